@@ -1,0 +1,473 @@
+// Memory-bound kernels of the training step (sm_100a): RMSNorm forward/backward,
+// SwiGLU forward/backward on separate tensors, in-place RoPE (forward or inverse),
+// embedding gather / scatter-add, the LM-head CE row reduction, the flat-buffer
+// AdamW update, and a squared L2 norm.  All use 16-byte vector accesses; none
+// allocates memory.
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <ATen/ATen.h>
+
+#include "common.cuh"
+#include "host_utils.h"
+
+namespace pb {
+
+template <typename T>
+__device__ __forceinline__ float to_f(T v);
+template <>
+__device__ __forceinline__ float to_f<float>(float v) { return v; }
+template <>
+__device__ __forceinline__ float to_f<__nv_bfloat16>(__nv_bfloat16 v) { return __bfloat162float(v); }
+
+template <typename T>
+__device__ __forceinline__ T from_f(float v);
+template <>
+__device__ __forceinline__ float from_f<float>(float v) { return v; }
+template <>
+__device__ __forceinline__ __nv_bfloat16 from_f<__nv_bfloat16>(float v) { return __float2bfloat16_rn(v); }
+
+// ------------------------------- RMSNorm ------------------------------------------
+// One warp per row.  y = x * rstd * w, rstd = 1/sqrt(mean(x^2) + eps).
+template <typename TI, typename TO>
+__global__ void rmsnorm_fwd_kernel(const TI* __restrict__ x, const float* __restrict__ w, TO* __restrict__ y,
+                                   float* __restrict__ rstd, int rows, int n, float eps) {
+  const int row = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+  if (row >= rows) return;
+  const TI* xr = x + static_cast<long>(row) * n;
+  float ss = 0.f;
+  for (int c = lane; c < n; c += 32) {
+    const float v = to_f(xr[c]);
+    ss += v * v;
+  }
+  ss = warp_sum(ss);
+  const float r = rsqrtf(ss / n + eps);
+  if (lane == 0) rstd[row] = r;
+  TO* yr = y + static_cast<long>(row) * n;
+  for (int c = lane; c < n; c += 32) yr[c] = from_f<TO>(to_f(xr[c]) * r * w[c]);
+}
+
+// dx = rstd * (g - xhat * mean(g * xhat)) [+ dres], g = dy * w; per-block partial dw.
+template <typename TI, typename TD>
+__global__ void rmsnorm_bwd_kernel(const TD* __restrict__ dy, const TI* __restrict__ x, const float* __restrict__ w,
+                                   const float* __restrict__ rstd, const float* __restrict__ dres,
+                                   float* __restrict__ dx, __nv_bfloat16* __restrict__ dx_bf16,
+                                   float* __restrict__ dw_part, int rows, int n, int rows_per_block) {
+  extern __shared__ float sdw[];
+  for (int c = threadIdx.x; c < n; c += blockDim.x) sdw[c] = 0.f;
+  __syncthreads();
+  const int warps = blockDim.x / 32;
+  const int lane = threadIdx.x % 32;
+  const int r0 = blockIdx.x * rows_per_block;
+  const int r1 = min(rows, r0 + rows_per_block);
+  for (int row = r0 + threadIdx.x / 32; row < r1; row += warps) {
+    const long off = static_cast<long>(row) * n;
+    const float r = rstd[row];
+    float dot = 0.f;
+    for (int c = lane; c < n; c += 32) dot += to_f(dy[off + c]) * w[c] * to_f(x[off + c]) * r;
+    dot = warp_sum(dot) / n;
+    for (int c = lane; c < n; c += 32) {
+      const float xh = to_f(x[off + c]) * r;
+      const float g = to_f(dy[off + c]);
+      float d = r * (g * w[c] - xh * dot);
+      if (dres != nullptr) d += dres[off + c];
+      dx[off + c] = d;
+      if (dx_bf16 != nullptr) dx_bf16[off + c] = __float2bfloat16_rn(d);
+      atomicAdd(&sdw[c], g * xh);
+    }
+  }
+  __syncthreads();
+  for (int c = threadIdx.x; c < n; c += blockDim.x) dw_part[static_cast<long>(blockIdx.x) * n + c] = sdw[c];
+}
+
+// dw[c] (+)= sum over partial rows.
+__global__ void reduce_cols_kernel(const float* __restrict__ part, int nparts, int n, float* __restrict__ out,
+                                   int accumulate) {
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= n) return;
+  float s = 0.f;
+  for (int p = 0; p < nparts; ++p) s += part[static_cast<long>(p) * n + c];
+  out[c] = accumulate ? out[c] + s : s;
+}
+
+std::vector<at::Tensor> rmsnorm_fwd(at::Tensor x, at::Tensor w, double eps, bool out_bf16) {
+  TORCH_CHECK(x.is_cuda() && x.is_contiguous() && w.is_contiguous() && w.scalar_type() == at::kFloat);
+  const c10::cuda::CUDAGuard guard(x.device());
+  const int n = x.size(-1);
+  const int rows = x.numel() / n;
+  auto y = at::empty(x.sizes(), x.options().dtype(out_bf16 ? at::kBFloat16 : x.scalar_type()));
+  auto rstd = at::empty({rows}, x.options().dtype(at::kFloat));
+  const int warps = 8;
+  dim3 grid((rows + warps - 1) / warps);
+  auto s = at::cuda::getCurrentCUDAStream();
+  if (rows == 0) return {y, rstd};
+  if (x.scalar_type() == at::kFloat) {
+    if (out_bf16)
+      rmsnorm_fwd_kernel<float, __nv_bfloat16><<<grid, warps * 32, 0, s>>>(
+          x.data_ptr<float>(), w.data_ptr<float>(), reinterpret_cast<__nv_bfloat16*>(y.data_ptr()),
+          rstd.data_ptr<float>(), rows, n, (float)eps);
+    else
+      rmsnorm_fwd_kernel<float, float><<<grid, warps * 32, 0, s>>>(x.data_ptr<float>(), w.data_ptr<float>(),
+                                                                   y.data_ptr<float>(), rstd.data_ptr<float>(),
+                                                                   rows, n, (float)eps);
+  } else {
+    TORCH_CHECK(x.scalar_type() == at::kBFloat16, "rmsnorm: fp32 or bf16 input");
+    rmsnorm_fwd_kernel<__nv_bfloat16, __nv_bfloat16><<<grid, warps * 32, 0, s>>>(
+        reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), w.data_ptr<float>(),
+        reinterpret_cast<__nv_bfloat16*>(y.data_ptr()), rstd.data_ptr<float>(), rows, n, (float)eps);
+  }
+  PB_CUDA_CHECK(cudaGetLastError());
+  return {y, rstd};
+}
+
+// Returns dx (fp32).  dw is written (or accumulated) into ``dw_out``.
+at::Tensor rmsnorm_bwd(at::Tensor dy, at::Tensor x, at::Tensor w, at::Tensor rstd, c10::optional<at::Tensor> dres,
+                       c10::optional<at::Tensor> dx_bf16, at::Tensor dw_out, bool accumulate_dw) {
+  TORCH_CHECK(dy.is_contiguous() && x.is_contiguous() && dy.numel() == x.numel());
+  const c10::cuda::CUDAGuard guard(x.device());
+  const int n = x.size(-1);
+  const int rows = x.numel() / n;
+  auto dx = at::empty(x.sizes(), x.options().dtype(at::kFloat));
+  if (rows == 0) return dx;
+  const int sms = num_sms(x.device().index());
+  const int nblocks = std::min(rows, 2 * sms);
+  const int rpb = (rows + nblocks - 1) / nblocks;
+  const int nb = (rows + rpb - 1) / rpb;
+  auto part = at::empty({nb, n}, x.options().dtype(at::kFloat));
+  auto s = at::cuda::getCurrentCUDAStream();
+  const float* dres_p = dres.has_value() ? dres->data_ptr<float>() : nullptr;
+  __nv_bfloat16* dxb = dx_bf16.has_value() ? reinterpret_cast<__nv_bfloat16*>(dx_bf16->data_ptr()) : nullptr;
+  const size_t smem = n * sizeof(float);
+  TORCH_CHECK(smem <= 48 * 1024, "rmsnorm_bwd: feature dim too large");
+#define PB_RMS_BWD(TI, TD)                                                                                  \
+  rmsnorm_bwd_kernel<TI, TD><<<nb, 256, smem, s>>>(                                                         \
+      reinterpret_cast<const TD*>(dy.data_ptr()), reinterpret_cast<const TI*>(x.data_ptr()), w.data_ptr<float>(), \
+      rstd.data_ptr<float>(), dres_p, dx.data_ptr<float>(), dxb, part.data_ptr<float>(), rows, n, rpb)
+  const bool xf = x.scalar_type() == at::kFloat, df = dy.scalar_type() == at::kFloat;
+  if (xf && df) PB_RMS_BWD(float, float);
+  else if (xf && !df) PB_RMS_BWD(float, __nv_bfloat16);
+  else if (!xf && df) PB_RMS_BWD(__nv_bfloat16, float);
+  else PB_RMS_BWD(__nv_bfloat16, __nv_bfloat16);
+#undef PB_RMS_BWD
+  PB_CUDA_CHECK(cudaGetLastError());
+  reduce_cols_kernel<<<(n + 255) / 256, 256, 0, s>>>(part.data_ptr<float>(), nb, n, dw_out.data_ptr<float>(),
+                                                       accumulate_dw ? 1 : 0);
+  PB_CUDA_CHECK(cudaGetLastError());
+  return dx;
+}
+
+// ------------------------------- SwiGLU -------------------------------------------
+template <typename T>
+__global__ void swiglu_fwd_kernel(const T* __restrict__ g, const T* __restrict__ u, T* __restrict__ h, long n) {
+  for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x) {
+    const float gv = to_f(g[i]);
+    h[i] = from_f<T>(gv * sigmoidf_(gv) * to_f(u[i]));
+  }
+}
+template <typename T>
+__global__ void swiglu_bwd_kernel(const T* __restrict__ g, const T* __restrict__ u, const T* __restrict__ dh,
+                                  T* __restrict__ dg, T* __restrict__ du, long n) {
+  for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x) {
+    const float gv = to_f(g[i]), uv = to_f(u[i]), d = to_f(dh[i]);
+    const float s = sigmoidf_(gv);
+    dg[i] = from_f<T>(d * uv * (s * (1.f + gv * (1.f - s))));
+    du[i] = from_f<T>(d * gv * s);
+  }
+}
+
+static int ew_grid(long n, int dev) { return (int)std::max<long>(1, std::min<long>((n + 255) / 256, 8L * num_sms(dev))); }
+
+at::Tensor swiglu_fwd(at::Tensor g, at::Tensor u) {
+  TORCH_CHECK(g.is_contiguous() && u.is_contiguous() && g.sizes() == u.sizes() && g.scalar_type() == u.scalar_type());
+  const c10::cuda::CUDAGuard guard(g.device());
+  auto h = at::empty_like(g);
+  const long n = g.numel();
+  if (n == 0) return h;
+  auto s = at::cuda::getCurrentCUDAStream();
+  const int grid = ew_grid(n, g.device().index());
+  if (g.scalar_type() == at::kFloat)
+    swiglu_fwd_kernel<float><<<grid, 256, 0, s>>>(g.data_ptr<float>(), u.data_ptr<float>(), h.data_ptr<float>(), n);
+  else
+    swiglu_fwd_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>(
+        reinterpret_cast<const __nv_bfloat16*>(g.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(u.data_ptr()),
+        reinterpret_cast<__nv_bfloat16*>(h.data_ptr()), n);
+  PB_CUDA_CHECK(cudaGetLastError());
+  return h;
+}
+
+std::vector<at::Tensor> swiglu_bwd(at::Tensor g, at::Tensor u, at::Tensor dh) {
+  const c10::cuda::CUDAGuard guard(g.device());
+  dh = dh.contiguous().to(g.scalar_type());
+  auto dg = at::empty_like(g), du = at::empty_like(u);
+  const long n = g.numel();
+  if (n == 0) return {dg, du};
+  auto s = at::cuda::getCurrentCUDAStream();
+  const int grid = ew_grid(n, g.device().index());
+  if (g.scalar_type() == at::kFloat)
+    swiglu_bwd_kernel<float><<<grid, 256, 0, s>>>(g.data_ptr<float>(), u.data_ptr<float>(), dh.data_ptr<float>(),
+                                                  dg.data_ptr<float>(), du.data_ptr<float>(), n);
+  else
+    swiglu_bwd_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>(
+        reinterpret_cast<const __nv_bfloat16*>(g.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(u.data_ptr()),
+        reinterpret_cast<const __nv_bfloat16*>(dh.data_ptr()), reinterpret_cast<__nv_bfloat16*>(dg.data_ptr()),
+        reinterpret_cast<__nv_bfloat16*>(du.data_ptr()), n);
+  PB_CUDA_CHECK(cudaGetLastError());
+  return {dg, du};
+}
+
+// ------------------------------- RoPE ---------------------------------------------
+// In place on x [T, ncols] (row pitch ld): every head of ``head_dim`` columns below
+// ``n_rope_cols`` is rotated by angle(pos[t], i); inverse = rotate by -angle.
+template <typename T>
+__global__ void rope_kernel(T* __restrict__ x, long ld, const int* __restrict__ pos, const float* __restrict__ cos_t,
+                            const float* __restrict__ sin_t, int rows, int n_rope_cols, int head_dim, int inverse,
+                            int n_pos) {
+  const int half = head_dim / 2;
+  const long pairs_per_row = n_rope_cols / 2;
+  const long total = static_cast<long>(rows) * pairs_per_row;
+  for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
+    const int row = static_cast<int>(i / pairs_per_row);
+    const int pr = static_cast<int>(i % pairs_per_row);
+    const int head = pr / half, j = pr % half;
+    const int p = min(max(pos[row], 0), n_pos - 1);
+    const float c = cos_t[static_cast<long>(p) * half + j];
+    const float s = inverse ? -sin_t[static_cast<long>(p) * half + j] : sin_t[static_cast<long>(p) * half + j];
+    T* base = x + row * ld + head * head_dim;
+    const float x1 = to_f(base[j]), x2 = to_f(base[j + half]);
+    base[j] = from_f<T>(x1 * c - x2 * s);
+    base[j + half] = from_f<T>(x2 * c + x1 * s);
+  }
+}
+
+void rope_apply(at::Tensor x, at::Tensor pos, at::Tensor cos_t, at::Tensor sin_t, int64_t n_rope_cols,
+                int64_t head_dim, bool inverse) {
+  TORCH_CHECK(x.dim() == 2 && x.stride(1) == 1 && pos.scalar_type() == at::kInt);
+  const c10::cuda::CUDAGuard guard(x.device());
+  const int rows = x.size(0);
+  const long total = (long)rows * (n_rope_cols / 2);
+  if (total == 0) return;
+  auto s = at::cuda::getCurrentCUDAStream();
+  const int grid = ew_grid(total, x.device().index());
+  if (x.scalar_type() == at::kFloat)
+    rope_kernel<float><<<grid, 256, 0, s>>>(x.data_ptr<float>(), x.stride(0), pos.data_ptr<int>(),
+                                            cos_t.data_ptr<float>(), sin_t.data_ptr<float>(), rows, (int)n_rope_cols,
+                                            (int)head_dim, inverse, (int)cos_t.size(0));
+  else
+    rope_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>(reinterpret_cast<__nv_bfloat16*>(x.data_ptr()), x.stride(0),
+                                                    pos.data_ptr<int>(), cos_t.data_ptr<float>(),
+                                                    sin_t.data_ptr<float>(), rows, (int)n_rope_cols, (int)head_dim,
+                                                    inverse, (int)cos_t.size(0));
+  PB_CUDA_CHECK(cudaGetLastError());
+}
+
+// ------------------------------- embedding ----------------------------------------
+// Ids outside [0, vocab) read row 0 and record status 501 (no out-of-range access).
+__device__ __forceinline__ int64_t checked_id(int64_t id, int64_t vocab, int* status) {
+  if (id < 0 || id >= vocab) {
+    report_error(status, 501);
+    return 0;
+  }
+  return id;
+}
+
+__global__ void embedding_fwd_kernel(const int64_t* __restrict__ ids, const float* __restrict__ w,
+                                     float* __restrict__ out, int rows, int d, int64_t vocab, int* status) {
+  const int d4 = d / 4;
+  const long total = static_cast<long>(rows) * d4;
+  for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
+    const int r = static_cast<int>(i / d4), c = static_cast<int>(i % d4);
+    reinterpret_cast<float4*>(out)[i] = reinterpret_cast<const float4*>(w + checked_id(ids[r], vocab, status) * d)[c];
+  }
+}
+
+__global__ void embedding_bwd_kernel(const int64_t* __restrict__ ids, const float* __restrict__ dx,
+                                     float* __restrict__ grad, int rows, int d, int64_t vocab, int* status) {
+  const int d4 = d / 4;
+  const long total = static_cast<long>(rows) * d4;
+  for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
+    const int r = static_cast<int>(i / d4), c = static_cast<int>(i % d4);
+    atomicAdd(reinterpret_cast<float4*>(grad + checked_id(ids[r], vocab, status) * d) + c,
+              reinterpret_cast<const float4*>(dx)[i]);
+  }
+}
+
+at::Tensor embedding_fwd(at::Tensor ids, at::Tensor w) {
+  TORCH_CHECK(ids.scalar_type() == at::kLong && w.scalar_type() == at::kFloat && w.size(1) % 4 == 0);
+  const c10::cuda::CUDAGuard guard(w.device());
+  ids = ids.contiguous();
+  const int rows = ids.numel(), d = w.size(1);
+  auto out = at::empty({rows, d}, w.options());
+  if (rows == 0) return out;
+  const long total = (long)rows * d / 4;
+  embedding_fwd_kernel<<<ew_grid(total, w.device().index()), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      ids.data_ptr<int64_t>(), w.data_ptr<float>(), out.data_ptr<float>(), rows, d, w.size(0),
+      status_ptr(w.device().index()));
+  PB_CUDA_CHECK(cudaGetLastError());
+  return out;
+}
+
+// grad (+)= scatter of dx rows; ``accumulate`` false zeroes ``grad`` first.
+void embedding_bwd(at::Tensor ids, at::Tensor dx, at::Tensor grad, bool accumulate) {
+  const c10::cuda::CUDAGuard guard(grad.device());
+  ids = ids.contiguous();
+  dx = dx.contiguous();
+  if (!accumulate) grad.zero_();
+  const int rows = ids.numel(), d = grad.size(1);
+  if (rows == 0) return;
+  const long total = (long)rows * d / 4;
+  embedding_bwd_kernel<<<ew_grid(total, grad.device().index()), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      ids.data_ptr<int64_t>(), dx.data_ptr<float>(), grad.data_ptr<float>(), rows, d, grad.size(0),
+      status_ptr(grad.device().index()));
+  PB_CUDA_CHECK(cudaGetLastError());
+}
+
+// ------------------------------- LM-head CE row reduction -------------------------
+// Combines the per-tile (max, sum exp) partials of each row into lse, and the summed
+// loss  lse - logit[target] + z * lse^2  over labelled rows.
+__global__ void ce_finalize_kernel(const float* __restrict__ pmax, const float* __restrict__ psum, int ntiles,
+                                   int rows, const float* __restrict__ tlogit, const int64_t* __restrict__ targets,
+                                   int64_t ignore_index, float z, float* __restrict__ lse, float* __restrict__ loss) {
+  const int r = blockIdx.x * blockDim.x + threadIdx.x;
+  float l = 0.f;
+  if (r < rows) {
+    float mx = -INFINITY;
+    for (int t = 0; t < ntiles; ++t) mx = fmaxf(mx, pmax[static_cast<long>(t) * rows + r]);
+    float se = 0.f;
+    for (int t = 0; t < ntiles; ++t) se += psum[static_cast<long>(t) * rows + r] * __expf(pmax[static_cast<long>(t) * rows + r] - mx);
+    const float ls = mx + logf(se);
+    lse[r] = ls;
+    if (targets[r] != ignore_index) l = ls - tlogit[r] + z * ls * ls;
+  }
+  l = warp_sum(l);
+  __shared__ float red[32];
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x / 32] = l;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float v = threadIdx.x < blockDim.x / 32 ? red[threadIdx.x] : 0.f;
+    v = warp_sum(v);
+    if (threadIdx.x == 0) atomicAdd(loss, v);
+  }
+}
+
+void ce_finalize(at::Tensor pmax, at::Tensor psum, at::Tensor tlogit, at::Tensor targets, int64_t ignore_index,
+                 double z, at::Tensor lse, at::Tensor loss) {
+  const c10::cuda::CUDAGuard guard(pmax.device());
+  const int ntiles = pmax.size(0), rows = pmax.size(1);
+  if (rows == 0) return;
+  ce_finalize_kernel<<<(rows + 255) / 256, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      pmax.data_ptr<float>(), psum.data_ptr<float>(), ntiles, rows, tlogit.data_ptr<float>(),
+      targets.data_ptr<int64_t>(), ignore_index, (float)z, lse.data_ptr<float>(), loss.data_ptr<float>());
+  PB_CUDA_CHECK(cudaGetLastError());
+}
+
+__global__ void ce_row_scale_kernel(const int64_t* __restrict__ targets, int64_t ignore_index,
+                                    const float* __restrict__ g, float* __restrict__ scale, int rows) {
+  const int r = blockIdx.x * blockDim.x + threadIdx.x;
+  if (r < rows) scale[r] = targets[r] != ignore_index ? *g : 0.f;
+}
+
+void ce_row_scale(at::Tensor targets, int64_t ignore_index, at::Tensor grad_out, at::Tensor scale) {
+  const c10::cuda::CUDAGuard guard(targets.device());
+  const int rows = targets.numel();
+  if (rows == 0) return;
+  ce_row_scale_kernel<<<(rows + 255) / 256, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      targets.data_ptr<int64_t>(), ignore_index, grad_out.data_ptr<float>(), scale.data_ptr<float>(), rows);
+  PB_CUDA_CHECK(cudaGetLastError());
+}
+
+// ------------------------------- optimizer ----------------------------------------
+// AdamW over flat fp32 buffers; the gradient is scaled by min(1, max_norm/(norm+1e-6))
+// when max_norm > 0, and nothing changes when the norm is not finite.
+__global__ void adamw_kernel(float* __restrict__ p, const float* __restrict__ g, float* __restrict__ m,
+                             float* __restrict__ v, __nv_bfloat16* __restrict__ shadow, long n,
+                             const float* __restrict__ norm, int* __restrict__ skipped, float lr, float b1, float b2,
+                             float eps, float wd, float bc1, float bc2, float max_norm) {
+  const float nv = *norm;
+  const bool bad = !isfinite(nv);
+  if (blockIdx.x == 0 && threadIdx.x == 0) *skipped = bad ? 1 : 0;
+  if (bad) return;
+  float gs = 1.f;
+  if (max_norm > 0.f) gs = fminf(1.f, max_norm / (nv + 1e-6f));
+  const float step = lr / bc1;
+  const float inv_sqrt_bc2 = rsqrtf(bc2);
+  const float decay = 1.f - lr * wd;
+  const long n4 = n / 4;
+  for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < n4; i += (long)gridDim.x * blockDim.x) {
+    float4 pv = reinterpret_cast<float4*>(p)[i];
+    const float4 gv = reinterpret_cast<const float4*>(g)[i];
+    float4 mv = reinterpret_cast<float4*>(m)[i];
+    float4 vv = reinterpret_cast<float4*>(v)[i];
+    float* pp = &pv.x;
+    const float* gg = &gv.x;
+    float* mm = &mv.x;
+    float* ww = &vv.x;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const float gk = gg[k] * gs;
+      mm[k] = b1 * mm[k] + (1.f - b1) * gk;
+      ww[k] = b2 * ww[k] + (1.f - b2) * gk * gk;
+      pp[k] = pp[k] * decay - step * mm[k] / (sqrtf(ww[k]) * inv_sqrt_bc2 + eps);
+    }
+    reinterpret_cast<float4*>(p)[i] = pv;
+    reinterpret_cast<float4*>(m)[i] = mv;
+    reinterpret_cast<float4*>(v)[i] = vv;
+    if (shadow != nullptr) {
+      uint2 o = make_uint2(pack_bf16x2(pv.x, pv.y), pack_bf16x2(pv.z, pv.w));
+      reinterpret_cast<uint2*>(shadow)[i] = o;
+    }
+  }
+  for (long i = n4 * 4 + blockIdx.x * (long)blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x) {
+    const float gk = g[i] * gs;
+    m[i] = b1 * m[i] + (1.f - b1) * gk;
+    v[i] = b2 * v[i] + (1.f - b2) * gk * gk;
+    p[i] = p[i] * decay - step * m[i] / (sqrtf(v[i]) * inv_sqrt_bc2 + eps);
+    if (shadow != nullptr) shadow[i] = __float2bfloat16_rn(p[i]);
+  }
+}
+
+void adamw_step(at::Tensor p, at::Tensor g, at::Tensor m, at::Tensor v, at::Tensor shadow, at::Tensor norm,
+                at::Tensor skipped, double lr, double b1, double b2, double eps, double wd, double bc1, double bc2,
+                double max_norm, bool write_shadow) {
+  const c10::cuda::CUDAGuard guard(p.device());
+  const long n = p.numel();
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(p.data_ptr()) % 16 == 0 && reinterpret_cast<uintptr_t>(g.data_ptr()) % 16 == 0);
+  adamw_kernel<<<4 * num_sms(p.device().index()), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      p.data_ptr<float>(), g.data_ptr<float>(), m.data_ptr<float>(), v.data_ptr<float>(),
+      write_shadow ? reinterpret_cast<__nv_bfloat16*>(shadow.data_ptr()) : nullptr, n, norm.data_ptr<float>(),
+      skipped.data_ptr<int>(), (float)lr, (float)b1, (float)b2, (float)eps, (float)wd, (float)bc1, (float)bc2,
+      (float)max_norm);
+  PB_CUDA_CHECK(cudaGetLastError());
+}
+
+__global__ void sumsq_kernel(const float* __restrict__ x, long n, float* __restrict__ out) {
+  float s = 0.f;
+  const long n4 = n / 4;
+  for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < n4; i += (long)gridDim.x * blockDim.x) {
+    const float4 v = reinterpret_cast<const float4*>(x)[i];
+    s += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+  }
+  for (long i = n4 * 4 + blockIdx.x * (long)blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x)
+    s += x[i] * x[i];
+  s = warp_sum(s);
+  __shared__ float red[32];
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x / 32] = s;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float t = threadIdx.x < blockDim.x / 32 ? red[threadIdx.x] : 0.f;
+    t = warp_sum(t);
+    if (threadIdx.x == 0) atomicAdd(out, t);
+  }
+}
+
+at::Tensor l2_norm(at::Tensor x) {
+  const c10::cuda::CUDAGuard guard(x.device());
+  auto acc = at::zeros({}, x.options().dtype(at::kFloat));
+  const long n = x.numel();
+  if (n > 0)
+    sumsq_kernel<<<2 * num_sms(x.device().index()), 512, 0, at::cuda::getCurrentCUDAStream()>>>(
+        x.data_ptr<float>(), n, acc.data_ptr<float>());
+  PB_CUDA_CHECK(cudaGetLastError());
+  return acc.sqrt();
+}
+
+}  // namespace pb

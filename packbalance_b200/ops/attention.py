@@ -1,0 +1,127 @@
+"""Document-masked causal GQA attention over a packed token stream.
+
+Layout: one bf16 buffer ``qkv`` of shape ``[T, (H + 2*Hkv) * D]`` (the fused QKV GEMM
+output, RoPE already applied to the q and k columns).  Token ``q`` attends to key
+``k`` iff ``doc_start[q] <= k <= q``; the kernel never touches a key tile that lies
+outside every document of its query tile.
+
+Work items are (query tile of 128 tokens, head) for the forward and (key tile, kv
+head) for the backward.  :func:`attention_plan` orders them by their number of
+key / query tiles, most expensive first, so the long documents that dominate the
+step start first and short ones fill the tail (the per-tile cost is the cost
+model's O(L^2) attention term at tile granularity).  The plan is built on the
+device with a few torch ops and no host synchronisation.
+"""
+
+from __future__ import annotations
+
+import math
+
+import torch
+
+from packbalance_b200.ops import _native
+from packbalance_b200.ops.reference import varlen_attention_reference
+
+TILE = 128
+
+
+def doc_end_from_start(doc_start: torch.Tensor) -> torch.Tensor:
+    t = doc_start.numel()
+    idx = torch.arange(t, device=doc_start.device, dtype=torch.int64)
+    last = torch.ones(t, device=doc_start.device, dtype=torch.bool)
+    if t > 1:
+        last[:-1] = doc_start[1:] != doc_start[:-1]
+    marks = torch.where(last, idx, torch.full_like(idx, t))
+    return torch.flip(torch.cummin(torch.flip(marks, (0,)), dim=0).values, (0,))
+
+
+def attention_plan(doc_start: torch.Tensor, n_heads: int, n_kv_heads: int) -> dict[str, torch.Tensor]:
+    """Cost-ordered work lists: ``fwd`` int32 [nq*H, 2] = (q tile, head);
+    ``bwd`` int32 [nk*Hkv, 3] = (kv tile, kv head, last q tile)."""
+    dev = doc_start.device
+    t = doc_start.numel()
+    n_tiles = -(-t // TILE)
+    tiles = torch.arange(n_tiles, device=dev, dtype=torch.int64)
+    ds = doc_start.to(torch.int64)
+    kv_lo = ds[tiles * TILE] // TILE
+    q_cost = tiles - kv_lo + 1
+    order = torch.argsort(q_cost, descending=True, stable=True)
+    heads = torch.arange(n_heads, device=dev, dtype=torch.int64)
+    fwd = torch.stack(
+        [order.repeat_interleave(n_heads), heads.repeat(n_tiles)], dim=1
+    ).to(torch.int32).contiguous()
+    de = doc_end_from_start(ds)
+    last_row = torch.clamp(tiles * TILE + TILE - 1, max=t - 1)
+    q_hi = de[last_row] // TILE
+    k_cost = q_hi - tiles + 1
+    korder = torch.argsort(k_cost, descending=True, stable=True)
+    kv_heads = torch.arange(n_kv_heads, device=dev, dtype=torch.int64)
+    bwd = torch.stack(
+        [korder.repeat_interleave(n_kv_heads), kv_heads.repeat(n_tiles), q_hi[korder].repeat_interleave(n_kv_heads)],
+        dim=1,
+    ).to(torch.int32).contiguous()
+    return {"fwd": fwd, "bwd": bwd, "doc_start": doc_start.to(torch.int32).contiguous()}
+
+
+def attn_forward_packed(
+    qkv: torch.Tensor, plan: dict, n_heads: int, n_kv_heads: int, head_dim: int
+) -> tuple[torch.Tensor, torch.Tensor]:
+    t = qkv.shape[0]
+    out = torch.empty(t, n_heads * head_dim, device=qkv.device, dtype=torch.bfloat16)
+    o, lse = _native.module().attn_fwd(
+        qkv, plan["doc_start"], plan["fwd"], n_heads, n_kv_heads, head_dim, 1.0 / math.sqrt(head_dim), out
+    )
+    return o, lse
+
+
+def attn_backward_packed(
+    qkv: torch.Tensor,
+    out: torch.Tensor,
+    dout: torch.Tensor,
+    lse: torch.Tensor,
+    plan: dict,
+    n_heads: int,
+    n_kv_heads: int,
+    head_dim: int,
+) -> torch.Tensor:
+    """Returns dqkv ``[T, (H + 2 Hkv) * D]`` bf16 (gradient w.r.t. the post-RoPE q/k)."""
+    t = qkv.shape[0]
+    dqkv = torch.empty_like(qkv)
+    dq_acc = torch.zeros(t, n_heads * head_dim, device=qkv.device, dtype=torch.float32)
+    delta = torch.empty(n_heads, t, device=qkv.device, dtype=torch.float32)
+    _native.module().attn_bwd(
+        qkv, out, dout.contiguous(), lse, plan["doc_start"], plan["bwd"], n_heads, n_kv_heads, head_dim,
+        1.0 / math.sqrt(head_dim), dqkv, dq_acc, delta,
+    )
+    return dqkv
+
+
+class _VarlenAttention(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, q, k, v, doc_start):
+        t, h, d = q.shape
+        hk = k.shape[1]
+        qkv = torch.cat([q.reshape(t, h * d), k.reshape(t, hk * d), v.reshape(t, hk * d)], dim=1)
+        qkv = qkv.to(torch.bfloat16).contiguous()
+        plan = attention_plan(doc_start, h, hk)
+        o, lse = attn_forward_packed(qkv, plan, h, hk, d)
+        ctx.save_for_backward(qkv, o, lse)
+        ctx.plan, ctx.dims, ctx.dtype = plan, (t, h, hk, d), q.dtype
+        return o.reshape(t, h, d).to(q.dtype)
+
+    @staticmethod
+    def backward(ctx, do):
+        qkv, o, lse = ctx.saved_tensors
+        t, h, hk, d = ctx.dims
+        dqkv = attn_backward_packed(qkv, o, do.reshape(t, h * d).to(torch.bfloat16), lse, ctx.plan, h, hk, d)
+        dq = dqkv[:, : h * d].reshape(t, h, d).to(ctx.dtype)
+        dk = dqkv[:, h * d : (h + hk) * d].reshape(t, hk, d).to(ctx.dtype)
+        dv = dqkv[:, (h + hk) * d :].reshape(t, hk, d).to(ctx.dtype)
+        return dq, dk, dv, None
+
+
+def varlen_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, doc_start: torch.Tensor) -> torch.Tensor:
+    """Token-major packed attention: q ``[T, H, D]``, k/v ``[T, Hkv, D]``."""
+    if q.is_cuda:
+        return _VarlenAttention.apply(q, k, v, doc_start)
+    return varlen_attention_reference(q, k, v, doc_start)

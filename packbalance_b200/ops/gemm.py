@@ -1,0 +1,142 @@
+"""Python side of the tcgen05 GEMM: tile-width choice, split-K and the Linear
+forward / dgrad / wgrad entry points.
+
+Operand conventions (all bf16, unit inner stride, 16-byte aligned rows):
+
+* ``linear_fwd(x[M,K], w[N,K])``      -> x @ w.T        (A K-major, B K-major)
+* ``linear_dgrad(dy[M,N], w[N,K])``   -> dy @ w         (A K-major, B MN-major)
+* ``linear_wgrad(dy[M,N], x[M,K])``   -> dy.T @ x, fp32 (A MN-major, B MN-major)
+"""
+
+from __future__ import annotations
+
+import math
+
+import torch
+
+from packbalance_b200.ops import _native
+
+EPI_BF16, EPI_F32, EPI_RESID, EPI_SWIGLU, EPI_ROPE, EPI_SWIGLU_BWD, EPI_ATOMIC_F32, EPI_CE_FWD, EPI_CE_BWD = range(9)
+
+_SM_COUNT: dict[int, int] = {}
+
+
+def sm_count(device: torch.device) -> int:
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    if idx not in _SM_COUNT:
+        _SM_COUNT[idx] = torch.cuda.get_device_properties(idx).multi_processor_count
+    return _SM_COUNT[idx]
+
+
+def pick_bn(m: int, n: int, sms: int, allowed=(256, 128, 64)) -> int:
+    """Tile width minimising (waves x per-tile cost); per-tile cost ~ BN + 64 models
+    the fixed prologue/epilogue share of a tile."""
+    best, best_cost = allowed[0], math.inf
+    m_tiles = -(-m // 128)
+    for bn in allowed:
+        tiles = m_tiles * -(-n // bn)
+        cost = -(-tiles // sms) * (bn + 64)
+        if cost < best_cost - 1e-9:
+            best, best_cost = bn, cost
+    return best
+
+
+def pick_splits(m: int, n: int, k: int, bn: int, sms: int) -> int:
+    """Split-K factor so that a small output grid still fills the GPU."""
+    tiles = -(-m // 128) * -(-n // bn)
+    if tiles >= sms // 2 or k < 1024:
+        return 1
+    return max(1, min(k // 512, sms // tiles))
+
+
+def gemm(
+    a: torch.Tensor,
+    b: torch.Tensor,
+    out: torch.Tensor,
+    m: int,
+    n: int,
+    k: int,
+    *,
+    a_mn: bool = False,
+    b_mn: bool = False,
+    epi: int = EPI_BF16,
+    bn: int | None = None,
+    splits: int = 1,
+    max_ctas: int = 0,
+    alpha: float = 1.0,
+    beta: bool = False,
+    res=None,
+    aux=None,
+    aux2=None,
+    pos=None,
+    cos=None,
+    sin=None,
+    head_dim: int = 0,
+    n_rope_cols: int = 0,
+    targets=None,
+    pmax=None,
+    psum=None,
+    tlogit=None,
+    lse=None,
+    row_scale=None,
+    z_coeff: float = 0.0,
+) -> torch.Tensor:
+    if bn is None:
+        width = n // 2 if epi == EPI_SWIGLU else n
+        bn = pick_bn(m, width if epi != EPI_SWIGLU else width * 2, sm_count(a.device))
+    _native.module().gemm_tc(
+        a, b, out, m, n, k, a_mn, b_mn, epi, bn, splits, max_ctas, alpha, beta,
+        res, aux, aux2, pos, cos, sin, head_dim, n_rope_cols, targets, pmax, psum, tlogit, lse, row_scale, z_coeff,
+    )
+    return out
+
+
+def linear_fwd(x: torch.Tensor, w: torch.Tensor, out_dtype: torch.dtype = torch.bfloat16) -> torch.Tensor:
+    m, k = x.shape
+    n = w.shape[0]
+    out = torch.empty(m, n, device=x.device, dtype=out_dtype)
+    return gemm(x, w, out, m, n, k, epi=EPI_BF16 if out_dtype == torch.bfloat16 else EPI_F32)
+
+
+def linear_dgrad(dy: torch.Tensor, w: torch.Tensor, out_dtype: torch.dtype = torch.bfloat16) -> torch.Tensor:
+    m, n = dy.shape
+    k = w.shape[1]
+    out = torch.empty(m, k, device=dy.device, dtype=out_dtype)
+    return gemm(dy, w, out, m, k, n, b_mn=True, epi=EPI_BF16 if out_dtype == torch.bfloat16 else EPI_F32)
+
+
+def linear_wgrad(dy: torch.Tensor, x: torch.Tensor, out: torch.Tensor | None = None, accumulate: bool = False) -> torch.Tensor:
+    m, n = dy.shape
+    k = x.shape[1]
+    if out is None:
+        out = torch.empty(n, k, device=dy.device, dtype=torch.float32)
+    return gemm(dy, x, out, n, k, m, a_mn=True, b_mn=True, epi=EPI_F32, beta=accumulate)
+
+
+class _Linear(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, w):
+        shape = x.shape
+        x2 = x.reshape(-1, shape[-1]).to(torch.bfloat16).contiguous()
+        wb = w.to(torch.bfloat16).contiguous()
+        ctx.save_for_backward(x2, wb)
+        ctx.shape, ctx.wdtype, ctx.xdtype = shape, w.dtype, x.dtype
+        return linear_fwd(x2, wb).reshape(*shape[:-1], w.shape[0])
+
+    @staticmethod
+    def backward(ctx, dy):
+        x2, wb = ctx.saved_tensors
+        dy2 = dy.reshape(-1, dy.shape[-1]).to(torch.bfloat16).contiguous()
+        dx = dw = None
+        if ctx.needs_input_grad[0]:
+            dx = linear_dgrad(dy2, wb).reshape(ctx.shape).to(ctx.xdtype)
+        if ctx.needs_input_grad[1]:
+            dw = linear_wgrad(dy2, x2).to(ctx.wdtype)
+        return dx, dw
+
+
+def linear(x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+    """``x @ w.T`` with bf16 tensor-core math on CUDA (fp32 math on CPU)."""
+    if not x.is_cuda:
+        return torch.nn.functional.linear(x, w)
+    return _Linear.apply(x, w)

@@ -1,0 +1,81 @@
+import pytest
+import torch
+import torch.nn.functional as F
+
+from packbalance_b200.config import DataConfig, ModelConfig
+from packbalance_b200.data.cost import FlopModel
+from packbalance_b200.data.dataset import PackedDataset
+from packbalance_b200.data.packer import build_packs
+from packbalance_b200.data.store import TokenStore
+from packbalance_b200.models.attention import doc_start_from_doc_ids, eager_attention
+from packbalance_b200.models.llama import LlamaModel
+from packbalance_b200.ops.attention import attention_plan, doc_end_from_start
+from packbalance_b200.ops.reference import varlen_attention_reference
+
+
+def test_eager_attention_matches_dense_mask() -> None:
+    torch.manual_seed(0)
+    q, k, v = (torch.randn(1, 2, 8, 4) for _ in range(3))
+    doc_ids = torch.tensor([[0, 0, 0, 1, 1, 2, 2, 2]])
+    mask = (doc_ids == doc_ids.T) & torch.tril(torch.ones(8, 8, dtype=torch.bool))
+    ref = F.scaled_dot_product_attention(q, k, v, attn_mask=mask[None, None])
+    torch.testing.assert_close(eager_attention(q, k, v, doc_ids), ref, atol=1e-5, rtol=1e-5)
+
+
+def test_varlen_reference_matches_eager_gqa() -> None:
+    torch.manual_seed(0)
+    t, h, hk, d = 40, 4, 2, 8
+    q, k, v = torch.randn(t, h, d), torch.randn(t, hk, d), torch.randn(t, hk, d)
+    doc_ids = torch.tensor([0] * 7 + [1] * 20 + [2] * 13)
+    ds = doc_start_from_doc_ids(doc_ids)
+    ref = eager_attention(q.transpose(0, 1)[None], k.transpose(0, 1)[None], v.transpose(0, 1)[None], doc_ids[None])
+    out = varlen_attention_reference(q, k, v, ds)
+    torch.testing.assert_close(out, ref[0].transpose(0, 1), atol=1e-5, rtol=1e-5)
+
+
+def test_packed_model_matches_isolated_documents(
+    store: TokenStore, data_cfg: DataConfig, model_cfg: ModelConfig, flop_model: FlopModel
+) -> None:
+    torch.manual_seed(0)
+    pack = next(p for p in build_packs(store, data_cfg, flop_model) if len(p.segments) >= 2)
+    item = PackedDataset(store, [pack], data_cfg)[0]
+    model = LlamaModel(model_cfg).eval()
+    with torch.no_grad():
+        packed = model(item["input_ids"][None], item["position_ids"][None], item["doc_ids"][None])
+        off = 0
+        for seg in pack.segments:
+            toks = torch.from_numpy(store.read(seg.start, seg.length))
+            iso = model(toks[None], torch.arange(seg.length)[None], torch.zeros(1, seg.length, dtype=torch.long))
+            torch.testing.assert_close(packed[0, off : off + seg.length], iso[0], atol=1e-5, rtol=1e-5)
+            off += seg.length
+
+
+def test_doc_start_and_end() -> None:
+    ids = torch.tensor([[0, 0, 1, 1, 1, -1], [0, 1, 1, 1, 2, 2]])
+    ds = doc_start_from_doc_ids(ids)
+    assert ds.tolist() == [0, 0, 2, 2, 2, 5, 6, 7, 7, 7, 10, 10]
+    assert doc_end_from_start(ds).tolist() == [1, 1, 4, 4, 4, 5, 6, 9, 9, 9, 11, 11]
+
+
+def test_attention_plan_orders_by_cost() -> None:
+    ds = torch.cat([torch.zeros(1024, dtype=torch.int32), torch.arange(1024, 1024 + 256, dtype=torch.int32)])
+    plan = attention_plan(ds, n_heads=2, n_kv_heads=1)
+    fwd = plan["fwd"]
+    assert fwd.shape == (10 * 2, 2)
+    # The last q tile of the 1024-token document sees 8 key tiles and comes first.
+    assert fwd[0, 0].item() == 7
+    bwd = plan["bwd"]
+    assert bwd.shape == (10, 3)
+    assert bwd[0].tolist() == [0, 0, 7]
+
+
+@pytest.mark.parametrize("backend", ["eager", "auto"])
+def test_generate_shape(model_cfg: ModelConfig, backend: str) -> None:
+    from dataclasses import replace
+
+    from packbalance_b200.models.llama import LlamaForCausalLM
+
+    torch.manual_seed(0)
+    model = LlamaForCausalLM(replace(model_cfg, attention_backend=backend))
+    out = model.generate(torch.randint(0, model_cfg.vocab_size, (1, 4)), max_new_tokens=4, temperature=0.0)
+    assert out.shape == (1, 8)

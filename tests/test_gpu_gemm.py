@@ -1,0 +1,102 @@
+"""tcgen05 GEMM numerics against fp32 PyTorch on the same bf16 inputs."""
+
+import pytest
+import torch
+
+from packbalance_b200.ops import _native
+from packbalance_b200.ops.gemm import (
+    EPI_ATOMIC_F32, EPI_BF16, EPI_F32, EPI_RESID, EPI_ROPE, EPI_SWIGLU, EPI_SWIGLU_BWD, gemm,
+)
+
+pytestmark = pytest.mark.gpu
+dev = "cuda"
+
+
+def _bf(*shape):
+    return (torch.randn(*shape, device=dev) * 0.5).to(torch.bfloat16)
+
+
+def _close(a, b, tol=2e-2):
+    torch.testing.assert_close(a.float(), b.float(), atol=tol * max(1.0, b.abs().max().item() * 0.05), rtol=tol)
+
+
+@pytest.mark.parametrize("bn", [64, 128, 256])
+@pytest.mark.parametrize("a_mn,b_mn", [(False, False), (False, True), (True, True), (True, False)])
+@pytest.mark.parametrize("mnk", [(256, 512, 256), (200, 136, 72), (1024, 768, 2048)])
+def test_gemm_majors(bn, a_mn, b_mn, mnk):
+    torch.manual_seed(0)
+    m, n, k = mnk
+    a = _bf(k, m) if a_mn else _bf(m, k)
+    b = _bf(k, n) if b_mn else _bf(n, k)
+    A = a.float().t() if a_mn else a.float()
+    B = b.float() if b_mn else b.float().t()
+    ref = A @ B
+    out = torch.empty(m, n, device=dev, dtype=torch.float32)
+    gemm(a, b, out, m, n, k, a_mn=a_mn, b_mn=b_mn, epi=EPI_F32, bn=bn)
+    _native.check_status()
+    _close(out, ref, 1e-2)
+    out16 = torch.empty(m, n, device=dev, dtype=torch.bfloat16)
+    gemm(a, b, out16, m, n, k, a_mn=a_mn, b_mn=b_mn, epi=EPI_BF16, bn=bn)
+    _close(out16, ref)
+
+
+def test_gemm_accumulate_residual_splitk():
+    torch.manual_seed(1)
+    m, n, k = 384, 256, 4096
+    a, b = _bf(m, k), _bf(n, k)
+    ref = a.float() @ b.float().t()
+    base = torch.randn(m, n, device=dev)
+    out = base.clone()
+    gemm(a, b, out, m, n, k, epi=EPI_F32, beta=True, bn=128)
+    _close(out, base + ref, 1e-2)
+    out2 = torch.empty(m, n, device=dev)
+    gemm(a, b, out2, m, n, k, epi=EPI_RESID, res=base, bn=256)
+    _close(out2, base + ref, 1e-2)
+    acc = torch.zeros(m, n, device=dev)
+    gemm(a, b, acc, m, n, k, epi=EPI_ATOMIC_F32, splits=4, bn=128)
+    _close(acc, ref, 1e-2)
+    _native.check_status()
+
+
+@pytest.mark.parametrize("bn", [64, 128, 256])
+def test_gemm_swiglu_and_backward(bn):
+    torch.manual_seed(2)
+    m, d, F = 320, 256, 384
+    x, w = _bf(m, d), _bf(2 * F, d)
+    h = torch.empty(m, F, device=dev, dtype=torch.bfloat16)
+    gu = torch.empty(m, 2 * F, device=dev, dtype=torch.bfloat16)
+    gemm(x, w, h, m, 2 * F, d, epi=EPI_SWIGLU, aux=gu, bn=bn)
+    full = x.float() @ w.float().t()
+    _close(gu, full)
+    g, u = gu.float()[:, :F], gu.float()[:, F:]
+    _close(h, torch.nn.functional.silu(g) * u)
+    # backward epilogue: dh = dy @ Wdown (Wdown [d, F]) then dg|du
+    dy, wd = _bf(m, d), _bf(d, F)
+    dgu = torch.empty(m, 2 * F, device=dev, dtype=torch.bfloat16)
+    gemm(dy, wd, dgu, m, F, d, b_mn=True, epi=EPI_SWIGLU_BWD, aux=gu, aux2=dgu, bn=bn)
+    dh = dy.float() @ wd.float()
+    s = torch.sigmoid(g)
+    _close(dgu[:, F:], dh * g * s)
+    _close(dgu[:, :F], dh * u * s * (1 + g * (1 - s)))
+    _native.check_status()
+
+
+@pytest.mark.parametrize("hd,bn", [(64, 128), (64, 256), (128, 256), (64, 64)])
+def test_gemm_rope_epilogue(hd, bn):
+    torch.manual_seed(3)
+    t, d, h, hk = 300, 256, 4, 2
+    n = (h + 2 * hk) * hd
+    x, w = _bf(t, d), _bf(n, d)
+    pos = torch.randint(0, 500, (t,), device=dev, dtype=torch.int32)
+    inv = 1.0 / (10000 ** (torch.arange(0, hd, 2, device=dev).float() / hd))
+    ang = torch.outer(torch.arange(512, device=dev).float(), inv)
+    cos, sin = ang.cos().contiguous(), ang.sin().contiguous()
+    out = torch.empty(t, n, device=dev, dtype=torch.bfloat16)
+    gemm(x, w, out, t, n, d, epi=EPI_ROPE, pos=pos, cos=cos, sin=sin, head_dim=hd, n_rope_cols=(h + hk) * hd, bn=bn)
+    y = (x.float() @ w.float().t()).view(t, -1, hd)
+    c, s = cos[pos.long()][:, None], sin[pos.long()][:, None]
+    half = hd // 2
+    rot = torch.cat([y[..., :half] * c - y[..., half:] * s, y[..., half:] * c + y[..., :half] * s], -1)
+    ref = torch.cat([rot[:, : h + hk], y[:, h + hk :]], 1).reshape(t, n)
+    _close(out, ref)
+    _native.check_status()
