@@ -56,7 +56,7 @@ def parse_args():
     ap.add_argument("--config", default=str(CONFIG))
     ap.add_argument("--mode", default="pack_ffd")
     ap.add_argument("--no-e2e", action="store_true")
-    ap.add_argument("--count-launches", action="store_true", default=True)
+    ap.add_argument("--no-count", action="store_true", help="skip the profiler pass that counts kernel launches")
     return ap.parse_args()
 
 
@@ -290,7 +290,7 @@ def run_ours(args, rank, world, dev) -> None:
         _ = time.perf_counter() - t0
 
     launches = None
-    if args.count_launches:
+    if not args.no_count:
         from torch.profiler import ProfilerActivity, profile
 
         with profile(activities=[ProfilerActivity.CUDA]) as prof:

@@ -79,7 +79,10 @@ struct FwdCfg {
   static constexpr int Q_OFF = 0;
   static constexpr int K_OFF = TILE_BYTES;             // 2 stages
   static constexpr int V_OFF = K_OFF + 2 * TILE_BYTES;  // 2 stages
-  static constexpr int SMEM = V_OFF + 2 * TILE_BYTES + 1024;
+  // At least 120 KB so that a second CTA (which would block in tcgen05.alloc on
+  // the fully allocated TMEM) is never co-scheduled on the same SM.
+  static constexpr int SMEM_USED = V_OFF + 2 * TILE_BYTES + 1024;
+  static constexpr int SMEM = SMEM_USED > 122880 ? SMEM_USED : 122880;
   static constexpr uint32_t S_COL = 0;    // two S buffers: 0, 128
   static constexpr uint32_t P_COL = 256;  // two P buffers (bf16 packed): 256, 320
   static constexpr uint32_t O_COL = 384;  // D columns
@@ -232,7 +235,7 @@ __global__ void __launch_bounds__(192, 1)
       bool ok = true;
       for (int j = 0; j < nkv; ++j) {
         const uint32_t g = kv_it + j;
-        if (!mbar_wait(&s_full[g & 1], (g >> 1) & 1, args.status, 208, &abort_sh)) {
+        if (!mbar_wait_warp(&s_full[g & 1], (g >> 1) & 1, args.status, 208, &abort_sh)) {
           ok = false;
           break;
         }
@@ -276,13 +279,14 @@ __global__ void __launch_bounds__(192, 1)
         // PV of the previous tile must be complete before O is rescaled or its P slot
         // (two tiles back) is overwritten.
         if (j > 0) {
-          if (!mbar_wait(&o_done, o_it & 1, args.status, 209, &abort_sh)) {
+          if (!mbar_wait_warp(&o_done, o_it & 1, args.status, 209, &abort_sh)) {
             ok = false;
             break;
           }
           ++o_it;
           tc_fence_after();
-          if (corr != 1.f) {
+          // Warp-uniform decision: the TMEM load/store below are .sync.aligned.
+          if (__any_sync(0xffffffff, corr != 1.f)) {
 #pragma unroll
             for (int c = 0; c < D; c += 16) {
               uint32_t ov[16];
@@ -310,7 +314,7 @@ __global__ void __launch_bounds__(192, 1)
       }
       if (!ok) break;
       // Epilogue: wait for the last PV, normalise and store.
-      if (!mbar_wait(&o_done, o_it & 1, args.status, 210, &abort_sh)) break;
+      if (!mbar_wait_warp(&o_done, o_it & 1, args.status, 210, &abort_sh)) break;
       ++o_it;
       tc_fence_after();
       const float inv = l > 0.f ? 1.f / l : 0.f;
@@ -354,8 +358,8 @@ struct BwdCfg {
   static constexpr int DO_OFF = 3 * TILE_BYTES;
   static constexpr int P_OFF = 4 * TILE_BYTES;      // P^T  [128 kv x 128 q] bf16, 32 KB
   static constexpr int DS_OFF = P_OFF + 32768;      // dS^T [128 kv x 128 q] bf16, 32 KB
-  static constexpr int VEC_OFF = DS_OFF + 32768;    // lse2[128], delta[128], doc_start[128]
-  static constexpr int SMEM = VEC_OFF + 3 * 512 + 1024;
+  static constexpr int VEC_OFF = DS_OFF + 32768;    // 2 x {lse2[128], delta[128], doc_start[128]}
+  static constexpr int SMEM = VEC_OFF + 2 * 3 * 512 + 1024;
   static constexpr uint32_t ST_COL = 0;    // S^T, later dQ
   static constexpr uint32_t DPT_COL = 128; // dP^T
   static constexpr uint32_t DV_COL = 256;
@@ -371,7 +375,7 @@ __global__ void __launch_bounds__(192, 1)
                     const AttnArgs args) {
   using C = BwdCfg<D>;
   __shared__ __align__(8) uint64_t kv_full, kv_empty, qd_full, qd_empty, st_full, ds_ready, mma2_done, dq_read,
-      acc_done, acc_free, drain_bar;
+      acc_done, acc_free, drain_bar, vec_bar;
   __shared__ uint32_t tmem_sh;
   __shared__ volatile int abort_sh;
   extern __shared__ uint8_t dyn[];
@@ -389,6 +393,7 @@ __global__ void __launch_bounds__(192, 1)
     mbar_init(&acc_done, 1);
     mbar_init(&acc_free, 4);
     mbar_init(&drain_bar, 1);
+    mbar_init(&vec_bar, 128);
     abort_sh = 0;
     fence_mbar_init();
   }
@@ -501,9 +506,7 @@ __global__ void __launch_bounds__(192, 1)
     const int q4 = warp & 3;
     const int r = q4 * 32 + lane;  // key row within the tile (and query row for dQ)
     const uint32_t lane_off = static_cast<uint32_t>(q4 * 32) << 16;
-    float* s_lse = reinterpret_cast<float*>(smem + C::VEC_OFF);
-    float* s_delta = s_lse + 128;
-    int* s_ds = reinterpret_cast<int*>(s_delta + 128);
+    float* vec_base = reinterpret_cast<float*>(smem + C::VEC_OFF);
     uint8_t* ptile = smem + C::P_OFF;
     uint8_t* dstile = smem + C::DS_OFF;
     uint32_t item_n = 0, qd_it = 0;
@@ -515,9 +518,13 @@ __global__ void __launch_bounds__(192, 1)
         const int h = hk * group + hh;
         for (int qt = kt; qt <= qhi; ++qt, ++qd_it) {
           const int q0 = qt * 128;
-          // Per-query vectors of this tile (the previous iteration finished reading them
-          // before it arrived on ds_ready, and the MMA warp consumed P/dS before dq).
-          asm volatile("bar.sync 1, 128;" ::: "memory");
+          // Per-query vectors of this tile, double-buffered by iteration parity.  Every
+          // thread arrives on vec_bar after writing its element; a thread can only be
+          // here once all threads passed the previous iteration's vec_bar, i.e. after
+          // they finished reading the buffer two iterations back.
+          float* s_lse = vec_base + (qd_it & 1) * 384;
+          float* s_delta = s_lse + 128;
+          int* s_ds = reinterpret_cast<int*>(s_delta + 128);
           {
             const int q = q0 + r;
             const bool qok = q < T;
@@ -525,8 +532,12 @@ __global__ void __launch_bounds__(192, 1)
             s_delta[r] = qok ? args.delta[static_cast<long>(h) * T + q] : 0.f;
             s_ds[r] = qok ? args.doc_start[q] : 0x7fffffff;
           }
-          asm volatile("bar.sync 1, 128;" ::: "memory");
-          if (!mbar_wait(&st_full, qd_it & 1, args.status, 229, &abort_sh)) {
+          mbar_arrive(&vec_bar);
+          if (!mbar_wait_warp(&vec_bar, qd_it & 1, args.status, 233, &abort_sh)) {
+            ok = false;
+            break;
+          }
+          if (!mbar_wait_warp(&st_full, qd_it & 1, args.status, 229, &abort_sh)) {
             ok = false;
             break;
           }
@@ -566,7 +577,7 @@ __global__ void __launch_bounds__(192, 1)
           __syncwarp();
           if (lane == 0) mbar_arrive(&ds_ready);
           // dQ rows (thread = query row) -> fp32 atomics.
-          if (!mbar_wait(&mma2_done, qd_it & 1, args.status, 231, &abort_sh)) {
+          if (!mbar_wait_warp(&mma2_done, qd_it & 1, args.status, 231, &abort_sh)) {
             ok = false;
             break;
           }
@@ -593,7 +604,7 @@ __global__ void __launch_bounds__(192, 1)
       }
       if (!ok) break;
       // dK (scaled) and dV of this key tile.
-      if (!mbar_wait(&acc_done, item_n & 1, args.status, 232, &abort_sh)) break;
+      if (!mbar_wait_warp(&acc_done, item_n & 1, args.status, 232, &abort_sh)) break;
       tc_fence_after();
       const int hcol_k = (H + hk) * D, hcol_v = (H + Hkv + hk) * D;
 #pragma unroll 1

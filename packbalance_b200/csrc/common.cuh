@@ -89,6 +89,18 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* s
   }
 }
 
+// Warp-collective bounded wait: lane 0 polls, the verdict is broadcast, so every lane
+// of the warp takes the same path afterwards (the tcgen05.ld/st that follow are
+// .sync.aligned and must never be reached by a subset of the warp).
+__device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, int* status, int code,
+                                               volatile int* abort) {
+  int ok = 1;
+  if ((threadIdx.x & 31) == 0) ok = mbar_wait(bar, parity, status, code, abort) ? 1 : 0;
+  ok = __shfl_sync(0xffffffff, ok, 0);
+  __syncwarp();
+  return ok != 0;
+}
+
 // ------------------------------- TMA ----------------------------------------------
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");

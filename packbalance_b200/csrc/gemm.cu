@@ -495,7 +495,7 @@ __global__ void __launch_bounds__(192, 1)
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
       int mb, nb, sp;
       tile_coords(args, tile, mb, nb, sp);
-      if (!mbar_wait(&accf_bar[acc], acc_phase, args.status, 106, &abort_sh)) break;
+      if (!mbar_wait_warp(&accf_bar[acc], acc_phase, args.status, 106, &abort_sh)) break;
       tc_fence_after();
       const int row = mb * C::BM + q * 32 + lane;
       const uint32_t tacc = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN;
