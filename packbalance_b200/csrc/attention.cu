@@ -66,9 +66,6 @@ struct AttnArgs {
   float* lse;          // [H, T] natural-log LSE
   // backward
   const float* delta;  // [H, T]
-  float* dq_acc;       // [T, H*D] fp32
-  __nv_bfloat16* dqkv;  // [T, (H+2Hkv)*D]
-  long ld_dqkv;
   int* status;
 };
 
@@ -349,32 +346,67 @@ __global__ void __launch_bounds__(192, 1)
 }
 
 // =================================== backward =====================================
+// Items = (key tile, query head, last query tile).  Warp roles (320 threads):
+//   0      TMA: K/V once per item, Q/dO per query tile (QSTAGES-deep ring)
+//   1      tcgen05.mma: S^T = K Q^T, dP^T = V dO^T; then dV += P^T dO, dK += dS^T Q,
+//          dQ = dS K
+//   2..5   P^T / dS^T, thread = key row; at item end dK/dV rows -> TMA reduce-add
+//          into the fp32 dK|dV accumulator (the GQA heads of a group add up there)
+//   6..9   dQ, thread = query row -> TMA reduce-add into the fp32 dQ accumulator
+// so the next tile's S^T/dP^T MMAs, this tile's dQ write-out and the next tile's
+// softmax-gradient math overlap.
 template <int D>
 struct BwdCfg {
   static constexpr int TILE_BYTES = 128 * D * 2;
+  static constexpr bool SPLIT_DQ = 256 + 3 * D <= 512;  // dQ in its own TMEM columns
+  static constexpr int QSTAGES = D == 64 ? 2 : 1;
+  static constexpr int DQ_SLOTS = D == 64 ? 2 : 1;      // 4 KB staging slots per dQ warp
   static constexpr int K_OFF = 0;
   static constexpr int V_OFF = TILE_BYTES;
-  static constexpr int Q_OFF = 2 * TILE_BYTES;
-  static constexpr int DO_OFF = 3 * TILE_BYTES;
-  static constexpr int P_OFF = 4 * TILE_BYTES;      // P^T  [128 kv x 128 q] bf16, 32 KB
-  static constexpr int DS_OFF = P_OFF + 32768;      // dS^T [128 kv x 128 q] bf16, 32 KB
-  static constexpr int VEC_OFF = DS_OFF + 32768;    // 2 x {lse2[128], delta[128], doc_start[128]}
+  static constexpr int Q_OFF = 2 * TILE_BYTES;  // stage s: Q at Q_OFF + 2*s*TILE, dO right after
+  static constexpr int P_OFF = Q_OFF + QSTAGES * 2 * TILE_BYTES;  // P^T  [128 kv x 128 q] bf16
+  static constexpr int DS_OFF = P_OFF + 32768;                   // dS^T [128 kv x 128 q] bf16
+  static constexpr int DQS_OFF = DS_OFF + 32768;                 // dQ staging, 4 warps
+  static constexpr int VEC_OFF = DQS_OFF + 4 * DQ_SLOTS * 4096;  // 2 x {lse2, delta, doc_start}[128]
   static constexpr int SMEM = VEC_OFF + 2 * 3 * 512 + 1024;
-  static constexpr uint32_t ST_COL = 0;    // S^T, later dQ
-  static constexpr uint32_t DPT_COL = 128; // dP^T
-  static constexpr uint32_t DV_COL = 256;
-  static constexpr uint32_t DK_COL = 256 + D;
+  static_assert(SMEM <= 232448, "shared memory budget");
+  static constexpr uint32_t ST_COL = 0;
+  static constexpr uint32_t DPT_COL = 128;
+  static constexpr uint32_t DQ_COL = SPLIT_DQ ? 256 : 0;
+  static constexpr uint32_t DK_COL = SPLIT_DQ ? 256 + D : 256;
+  static constexpr uint32_t DV_COL = DK_COL + D;
   static constexpr uint32_t IDESC_SQ = idesc_bf16_f32(128, 128, false, false);  // S^T, dP^T
-  static constexpr uint32_t IDESC_KV = idesc_bf16_f32(128, D, false, true);     // dV, dK: A K-major, B MN-major
-  static constexpr uint32_t IDESC_DQ = idesc_bf16_f32(128, D, true, true);      // dQ: A MN-major, B MN-major
+  static constexpr uint32_t IDESC_KV = idesc_bf16_f32(128, D, false, true);     // dV, dK
+  static constexpr uint32_t IDESC_DQ = idesc_bf16_f32(128, D, true, true);      // dQ
 };
 
+// 32 fp32 of this lane's row -> 128B-swizzled [32 x 32] fp32 staging box.
+__device__ __forceinline__ void stage_row_f32(uint8_t* s, const uint32_t (&v)[32], float scale) {
+  const int r = threadIdx.x & 31;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    float4 q = make_float4(__uint_as_float(v[4 * j]) * scale, __uint_as_float(v[4 * j + 1]) * scale,
+                           __uint_as_float(v[4 * j + 2]) * scale, __uint_as_float(v[4 * j + 3]) * scale);
+    *reinterpret_cast<float4*>(s + r * 128 + ((j ^ (r & 7)) << 4)) = q;
+  }
+}
+
+__device__ __forceinline__ void reduce_box(const CUtensorMap* map, const uint8_t* s, int col, int row) {
+  fence_async_smem();
+  __syncwarp();
+  if ((threadIdx.x & 31) == 0) {
+    tma_reduce_add_2d(map, s, col, row);
+    bulk_commit();
+  }
+}
+
 template <int D>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(320, 1)
     attn_bwd_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __grid_constant__ CUtensorMap tm_do,
+                    const __grid_constant__ CUtensorMap tm_dq, const __grid_constant__ CUtensorMap tm_dkv,
                     const AttnArgs args) {
   using C = BwdCfg<D>;
-  __shared__ __align__(8) uint64_t kv_full, kv_empty, qd_full, qd_empty, st_full, ds_ready, mma2_done, dq_read,
+  __shared__ __align__(8) uint64_t kv_full, kv_empty, qd_full[2], qd_empty[2], st_full, ds_ready, mma2_done, dq_free,
       acc_done, acc_free, drain_bar, vec_bar;
   __shared__ uint32_t tmem_sh;
   __shared__ volatile int abort_sh;
@@ -384,12 +416,14 @@ __global__ void __launch_bounds__(192, 1)
   if (threadIdx.x == 0) {
     mbar_init(&kv_full, 1);
     mbar_init(&kv_empty, 1);
-    mbar_init(&qd_full, 1);
-    mbar_init(&qd_empty, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&qd_full[i], 1);
+      mbar_init(&qd_empty[i], 1);
+    }
     mbar_init(&st_full, 1);
     mbar_init(&ds_ready, 4);
     mbar_init(&mma2_done, 1);
-    mbar_init(&dq_read, 4);
+    mbar_init(&dq_free, 4);
     mbar_init(&acc_done, 1);
     mbar_init(&acc_free, 4);
     mbar_init(&drain_bar, 1);
@@ -414,49 +448,51 @@ __global__ void __launch_bounds__(192, 1)
 
   if (warp == 0) {
     if (lane == 0) {
-      uint32_t item_n = 0, qd_it = 0;
+      uint32_t item_n = 0, g = 0;
       bool ok = true;
       for (int it = blockIdx.x; it < args.n_items && ok; it += gridDim.x, ++item_n) {
-        const int kt = args.items[3 * it], hk = args.items[3 * it + 1], qhi = args.items[3 * it + 2];
+        const int kt = args.items[3 * it], h = args.items[3 * it + 1], qhi = args.items[3 * it + 2];
+        const int hk = h / group;
         if (!mbar_wait(&kv_empty, (item_n & 1) ^ 1, args.status, 221, &abort_sh)) break;
         mbar_arrive_expect_tx(&kv_full, 2 * C::TILE_BYTES);
         load_tile_rows(smem + C::K_OFF, &tm_qkv, &kv_full, (H + hk) * D, kt * 128, D);
         load_tile_rows(smem + C::V_OFF, &tm_qkv, &kv_full, (H + Hkv + hk) * D, kt * 128, D);
-        for (int hh = 0; hh < group && ok; ++hh) {
-          const int h = hk * group + hh;
-          for (int qt = kt; qt <= qhi; ++qt, ++qd_it) {
-            if (!mbar_wait(&qd_empty, (qd_it & 1) ^ 1, args.status, 222, &abort_sh)) {
-              ok = false;
-              break;
-            }
-            mbar_arrive_expect_tx(&qd_full, 2 * C::TILE_BYTES);
-            load_tile_rows(smem + C::Q_OFF, &tm_qkv, &qd_full, h * D, qt * 128, D);
-            load_tile_rows(smem + C::DO_OFF, &tm_do, &qd_full, h * D, qt * 128, D);
+        for (int qt = kt; qt <= qhi; ++qt, ++g) {
+          const int s = g % C::QSTAGES;
+          const uint32_t ph = (g / C::QSTAGES) & 1;
+          if (!mbar_wait(&qd_empty[s], ph ^ 1, args.status, 222, &abort_sh)) {
+            ok = false;
+            break;
           }
+          mbar_arrive_expect_tx(&qd_full[s], 2 * C::TILE_BYTES);
+          uint8_t* qs = smem + C::Q_OFF + s * 2 * C::TILE_BYTES;
+          load_tile_rows(qs, &tm_qkv, &qd_full[s], h * D, qt * 128, D);
+          load_tile_rows(qs + C::TILE_BYTES, &tm_do, &qd_full[s], h * D, qt * 128, D);
         }
       }
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      uint32_t item_n = 0, qd_it = 0;
+      uint32_t item_n = 0, g = 0;
       bool ok = true;
       const uint32_t ka = smem_u32(smem + C::K_OFF), va = smem_u32(smem + C::V_OFF);
-      const uint32_t qa = smem_u32(smem + C::Q_OFF), da = smem_u32(smem + C::DO_OFF);
       const uint32_t pa = smem_u32(smem + C::P_OFF), dsa = smem_u32(smem + C::DS_OFF);
       for (int it = blockIdx.x; it < args.n_items && ok; it += gridDim.x, ++item_n) {
         const int kt = args.items[3 * it], qhi = args.items[3 * it + 2];
         if (!mbar_wait(&kv_full, item_n & 1, args.status, 223, &abort_sh)) break;
         if (!mbar_wait(&acc_free, (item_n & 1) ^ 1, args.status, 224, &abort_sh)) break;
         tc_fence_after();
-        bool first = true;
-        const int n_inner = group * (qhi - kt + 1);
-        for (int n = 0; n < n_inner; ++n, ++qd_it) {
-          if (!mbar_wait(&qd_full, qd_it & 1, args.status, 225, &abort_sh)) {
+        for (int qt = kt; qt <= qhi; ++qt, ++g) {
+          const int s = g % C::QSTAGES;
+          const uint32_t ph = (g / C::QSTAGES) & 1;
+          const uint32_t qa = smem_u32(smem + C::Q_OFF + s * 2 * C::TILE_BYTES);
+          const uint32_t da = qa + C::TILE_BYTES;
+          if (!mbar_wait(&qd_full[s], ph, args.status, 225, &abort_sh)) {
             ok = false;
             break;
           }
-          // S^T / dQ columns: the previous dQ must have been read out.
-          if (!mbar_wait(&dq_read, (qd_it & 1) ^ 1, args.status, 226, &abort_sh)) {
+          // Without separate dQ columns, dQ(g-1) lives where S^T(g) goes.
+          if (!C::SPLIT_DQ && g > 0 && !mbar_wait(&dq_free, (g - 1) & 1, args.status, 226, &abort_sh)) {
             ok = false;
             break;
           }
@@ -470,11 +506,12 @@ __global__ void __launch_bounds__(192, 1)
                     C::IDESC_SQ, kk > 0 ? 1u : 0u);
           }
           umma_commit(&st_full);
-          if (!mbar_wait(&ds_ready, qd_it & 1, args.status, 227, &abort_sh)) {
+          if (!mbar_wait(&ds_ready, g & 1, args.status, 227, &abort_sh)) {
             ok = false;
             break;
           }
           tc_fence_after();
+          const bool first = qt == kt;
 #pragma unroll
           for (int kk = 0; kk < 8; ++kk) {
             const uint32_t aoff = (kk >> 2) * 16384 + (kk & 3) * 32;  // K-major A over q (K dim)
@@ -485,15 +522,19 @@ __global__ void __launch_bounds__(192, 1)
             umma_ss(tmem + C::DK_COL, sdesc_sw128(dsa + aoff, 16, 1024), sdesc_sw128(qa + boff, 16384, 1024),
                     C::IDESC_KV, acc);
           }
+          if (C::SPLIT_DQ && g > 0 && !mbar_wait(&dq_free, (g - 1) & 1, args.status, 226, &abort_sh)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
 #pragma unroll
           for (int kk = 0; kk < 8; ++kk) {
             const uint32_t off = kk * 2048;  // 16 kv rows
-            umma_ss(tmem + C::ST_COL, sdesc_sw128(dsa + off, 16384, 1024), sdesc_sw128(ka + off, 16384, 1024),
+            umma_ss(tmem + C::DQ_COL, sdesc_sw128(dsa + off, 16384, 1024), sdesc_sw128(ka + off, 16384, 1024),
                     C::IDESC_DQ, kk > 0 ? 1u : 0u);
           }
           umma_commit(&mma2_done);
-          umma_commit(&qd_empty);
-          first = false;
+          umma_commit(&qd_empty[s]);
         }
         if (!ok) break;
         umma_commit(&acc_done);
@@ -502,137 +543,147 @@ __global__ void __launch_bounds__(192, 1)
       umma_commit(&drain_bar);
       mbar_wait(&drain_bar, 0, args.status, 228, nullptr);
     }
-  } else {
+  } else if (warp < 6) {
+    // ---------------- P^T / dS^T (thread = key row) ----------------
     const int q4 = warp & 3;
-    const int r = q4 * 32 + lane;  // key row within the tile (and query row for dQ)
+    const int r = q4 * 32 + lane;
     const uint32_t lane_off = static_cast<uint32_t>(q4 * 32) << 16;
     float* vec_base = reinterpret_cast<float*>(smem + C::VEC_OFF);
     uint8_t* ptile = smem + C::P_OFF;
     uint8_t* dstile = smem + C::DS_OFF;
-    uint32_t item_n = 0, qd_it = 0;
+    uint32_t item_n = 0, g = 0;
     bool ok = true;
     for (int it = blockIdx.x; it < args.n_items && ok; it += gridDim.x, ++item_n) {
-      const int kt = args.items[3 * it], hk = args.items[3 * it + 1], qhi = args.items[3 * it + 2];
+      const int kt = args.items[3 * it], h = args.items[3 * it + 1], qhi = args.items[3 * it + 2];
+      const int hk = h / group;
       const int kv = kt * 128 + r;
-      for (int hh = 0; hh < group && ok; ++hh) {
-        const int h = hk * group + hh;
-        for (int qt = kt; qt <= qhi; ++qt, ++qd_it) {
-          const int q0 = qt * 128;
-          // Per-query vectors of this tile, double-buffered by iteration parity.  Every
-          // thread arrives on vec_bar after writing its element; a thread can only be
-          // here once all threads passed the previous iteration's vec_bar, i.e. after
-          // they finished reading the buffer two iterations back.
-          float* s_lse = vec_base + (qd_it & 1) * 384;
-          float* s_delta = s_lse + 128;
-          int* s_ds = reinterpret_cast<int*>(s_delta + 128);
-          {
-            const int q = q0 + r;
-            const bool qok = q < T;
-            s_lse[r] = qok ? args.lse[static_cast<long>(h) * T + q] * kLog2e : INFINITY;
-            s_delta[r] = qok ? args.delta[static_cast<long>(h) * T + q] : 0.f;
-            s_ds[r] = qok ? args.doc_start[q] : 0x7fffffff;
-          }
-          mbar_arrive(&vec_bar);
-          if (!mbar_wait_warp(&vec_bar, qd_it & 1, args.status, 233, &abort_sh)) {
-            ok = false;
-            break;
-          }
-          if (!mbar_wait_warp(&st_full, qd_it & 1, args.status, 229, &abort_sh)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          // P/dS smem of the previous iteration was consumed by its MMAs: this thread
-          // waited for them (mma2_done) before reading that iteration's dQ.
-#pragma unroll 1
-          for (int c = 0; c < 4; ++c) {
-            uint32_t sv[32], dv[32];
-            tmem_ld32(tmem + lane_off + C::ST_COL + c * 32, sv);
-            tmem_ld32(tmem + lane_off + C::DPT_COL + c * 32, dv);
-            tmem_wait_ld();
-            uint32_t pp[16], dd[16];
-#pragma unroll
-            for (int i = 0; i < 16; ++i) {
-              float p2[2], d2[2];
-#pragma unroll
-              for (int e = 0; e < 2; ++e) {
-                const int j = c * 32 + 2 * i + e;
-                const int q = q0 + j;
-                const bool allowed = q >= kv && s_ds[j] <= kv;
-                const float p = allowed ? fast_exp2(__uint_as_float(sv[2 * i + e]) * args.scale_log2 - s_lse[j]) : 0.f;
-                p2[e] = p;
-                d2[e] = p * (__uint_as_float(dv[2 * i + e]) - s_delta[j]);
-              }
-              pp[i] = pack_bf16x2(p2[0], p2[1]);
-              dd[i] = pack_bf16x2(d2[0], d2[1]);
-            }
-#pragma unroll
-            for (int k = 0; k < 4; ++k) {
-              st_swz_chunk(ptile, r, c * 4 + k, make_uint4(pp[4 * k], pp[4 * k + 1], pp[4 * k + 2], pp[4 * k + 3]));
-              st_swz_chunk(dstile, r, c * 4 + k, make_uint4(dd[4 * k], dd[4 * k + 1], dd[4 * k + 2], dd[4 * k + 3]));
-            }
-          }
-          fence_proxy_async_smem();
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&ds_ready);
-          // dQ rows (thread = query row) -> fp32 atomics.
-          if (!mbar_wait_warp(&mma2_done, qd_it & 1, args.status, 231, &abort_sh)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
+      for (int qt = kt; qt <= qhi; ++qt, ++g) {
+        const int q0 = qt * 128;
+        // Per-query vectors, double-buffered by iteration parity (see vec_bar).
+        float* s_lse = vec_base + (g & 1) * 384;
+        float* s_delta = s_lse + 128;
+        int* s_ds = reinterpret_cast<int*>(s_delta + 128);
+        {
           const int q = q0 + r;
-#pragma unroll 1
-          for (int c = 0; c < D; c += 32) {
-            uint32_t v[32];
-            tmem_ld32(tmem + lane_off + C::ST_COL + c, v);
-            tmem_wait_ld();
-            if (q < T) {
-              float4* dst = reinterpret_cast<float4*>(args.dq_acc + static_cast<long>(q) * H * D + h * D + c);
-#pragma unroll
-              for (int i = 0; i < 8; ++i)
-                atomicAdd(dst + i, make_float4(__uint_as_float(v[4 * i]) * args.scale, __uint_as_float(v[4 * i + 1]) * args.scale,
-                                               __uint_as_float(v[4 * i + 2]) * args.scale,
-                                               __uint_as_float(v[4 * i + 3]) * args.scale));
-            }
-          }
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&dq_read);
+          const bool qok = q < T;
+          s_lse[r] = qok ? args.lse[static_cast<long>(h) * T + q] * kLog2e : INFINITY;
+          s_delta[r] = qok ? args.delta[static_cast<long>(h) * T + q] : 0.f;
+          s_ds[r] = qok ? args.doc_start[q] : 0x7fffffff;
         }
-      }
-      if (!ok) break;
-      // dK (scaled) and dV of this key tile.
-      if (!mbar_wait_warp(&acc_done, item_n & 1, args.status, 232, &abort_sh)) break;
-      tc_fence_after();
-      const int hcol_k = (H + hk) * D, hcol_v = (H + Hkv + hk) * D;
+        mbar_arrive(&vec_bar);
+        if (!mbar_wait_warp(&vec_bar, g & 1, args.status, 233, &abort_sh)) {
+          ok = false;
+          break;
+        }
+        if (!mbar_wait_warp(&st_full, g & 1, args.status, 229, &abort_sh)) {
+          ok = false;
+          break;
+        }
+        // The previous tile's dV/dK/dQ MMAs read P/dS from shared memory.
+        if (g > 0 && !mbar_wait_warp(&mma2_done, (g - 1) & 1, args.status, 230, &abort_sh)) {
+          ok = false;
+          break;
+        }
+        if (lane == 0) bulk_wait_read<0>();  // dK/dV staging of the previous item used the P area
+        __syncwarp();
+        tc_fence_after();
 #pragma unroll 1
-      for (int c = 0; c < D; c += 32) {
-        uint32_t kvv[32], vvv[32];
-        tmem_ld32(tmem + lane_off + C::DK_COL + c, kvv);
-        tmem_ld32(tmem + lane_off + C::DV_COL + c, vvv);
-        tmem_wait_ld();
-        if (kv < T) {
-          uint32_t pk[16], pv[16];
+        for (int c = 0; c < 4; ++c) {
+          uint32_t sv[32], dv[32];
+          tmem_ld32(tmem + lane_off + C::ST_COL + c * 32, sv);
+          tmem_ld32(tmem + lane_off + C::DPT_COL + c * 32, dv);
+          tmem_wait_ld();
+          uint32_t pp[16], dd[16];
 #pragma unroll
           for (int i = 0; i < 16; ++i) {
-            pk[i] = pack_bf16x2(__uint_as_float(kvv[2 * i]) * args.scale, __uint_as_float(kvv[2 * i + 1]) * args.scale);
-            pv[i] = pack_bf16x2(__uint_as_float(vvv[2 * i]), __uint_as_float(vvv[2 * i + 1]));
-          }
-          uint4* dk = reinterpret_cast<uint4*>(args.dqkv + static_cast<long>(kv) * args.ld_dqkv + hcol_k + c);
-          uint4* dvp = reinterpret_cast<uint4*>(args.dqkv + static_cast<long>(kv) * args.ld_dqkv + hcol_v + c);
+            float p2[2], d2[2];
 #pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            dk[i] = make_uint4(pk[4 * i], pk[4 * i + 1], pk[4 * i + 2], pk[4 * i + 3]);
-            dvp[i] = make_uint4(pv[4 * i], pv[4 * i + 1], pv[4 * i + 2], pv[4 * i + 3]);
+            for (int e = 0; e < 2; ++e) {
+              const int j = c * 32 + 2 * i + e;
+              const int q = q0 + j;
+              const bool allowed = q >= kv && s_ds[j] <= kv;
+              const float p = allowed ? fast_exp2(__uint_as_float(sv[2 * i + e]) * args.scale_log2 - s_lse[j]) : 0.f;
+              p2[e] = p;
+              d2[e] = p * (__uint_as_float(dv[2 * i + e]) - s_delta[j]);
+            }
+            pp[i] = pack_bf16x2(p2[0], p2[1]);
+            dd[i] = pack_bf16x2(d2[0], d2[1]);
+          }
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            st_swz_chunk(ptile, r, c * 4 + k, make_uint4(pp[4 * k], pp[4 * k + 1], pp[4 * k + 2], pp[4 * k + 3]));
+            st_swz_chunk(dstile, r, c * 4 + k, make_uint4(dd[4 * k], dd[4 * k + 1], dd[4 * k + 2], dd[4 * k + 3]));
           }
         }
+        fence_async_smem();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&ds_ready);
+      }
+      if (!ok) break;
+      // dK (scaled) and dV rows of this key tile -> fp32 accumulators (TMA reduce-add).
+      if (!mbar_wait_warp(&acc_done, item_n & 1, args.status, 232, &abort_sh)) break;
+      tc_fence_after();
+      uint8_t* stg = smem + C::P_OFF + q4 * 8192;  // P/dS are free once acc_done completed
+      int slot = 0;
+#pragma unroll 1
+      for (int c = 0; c < 2 * D; c += 32) {
+        const bool is_k = c < D;
+        uint32_t v[32];
+        tmem_ld32(tmem + lane_off + (is_k ? C::DK_COL + c : C::DV_COL + c - D), v);
+        tmem_wait_ld();
+        if (lane == 0) bulk_wait_read<1>();
+        __syncwarp();
+        uint8_t* sl = stg + slot * 4096;
+        stage_row_f32(sl, v, is_k ? args.scale : 1.f);
+        reduce_box(&tm_dkv, sl, is_k ? hk * D + c : (Hkv + hk) * D + c - D, kt * 128 + q4 * 32);
+        slot ^= 1;
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_free);
     }
+    if (lane == 0) bulk_wait_all<0>();
+    __syncwarp();
+  } else {
+    // ---------------- dQ write-out (thread = query row) ----------------
+    const int q4 = warp & 3;
+    const uint32_t lane_off = static_cast<uint32_t>(q4 * 32) << 16;
+    uint8_t* stg = smem + C::DQS_OFF + q4 * C::DQ_SLOTS * 4096;
+    int slot = 0;
+    uint32_t g = 0;
+    bool ok = true;
+    for (int it = blockIdx.x; it < args.n_items && ok; it += gridDim.x) {
+      const int kt = args.items[3 * it], h = args.items[3 * it + 1], qhi = args.items[3 * it + 2];
+      for (int qt = kt; qt <= qhi; ++qt, ++g) {
+        if (!mbar_wait_warp(&mma2_done, g & 1, args.status, 231, &abort_sh)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        uint32_t v[D];
+#pragma unroll
+        for (int c = 0; c < D; c += 32) tmem_ld32(tmem + lane_off + C::DQ_COL + c, *reinterpret_cast<uint32_t(*)[32]>(v + c));
+        tmem_wait_ld();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&dq_free);
+#pragma unroll
+        for (int c = 0; c < D; c += 32) {
+          if (lane == 0) {
+            if (C::DQ_SLOTS == 2) bulk_wait_read<1>();
+            else bulk_wait_read<0>();
+          }
+          __syncwarp();
+          uint8_t* sl = stg + slot * 4096;
+          stage_row_f32(sl, *reinterpret_cast<uint32_t(*)[32]>(v + c), args.scale);
+          reduce_box(&tm_dq, sl, h * D + c, qt * 128 + q4 * 32);
+          if (C::DQ_SLOTS == 2) slot ^= 1;
+        }
+      }
+    }
+    if (lane == 0) bulk_wait_all<0>();
+    __syncwarp();
   }
   tc_fence_before();
   __syncthreads();
@@ -642,33 +693,67 @@ __global__ void __launch_bounds__(192, 1)
   }
 }
 
-// delta[h, t] = sum_d O[t, h, d] * dO[t, h, d]
+// delta[h, t] = sum_d O[t, h, d] * dO[t, h, d]; one thread per (t, h), 16-byte loads.
 __global__ void attn_delta_kernel(const __nv_bfloat16* __restrict__ o, const __nv_bfloat16* __restrict__ dout,
                                   float* __restrict__ delta, int T, int H, int D) {
-  const long idx = blockIdx.x * (long)(blockDim.x / 32) + threadIdx.x / 32;  // (t, h) pair per warp
-  const int lane = threadIdx.x % 32;
+  const long idx = blockIdx.x * (long)blockDim.x + threadIdx.x;
   if (idx >= static_cast<long>(T) * H) return;
   const int t = static_cast<int>(idx / H), h = static_cast<int>(idx % H);
-  const __nv_bfloat16* a = o + static_cast<long>(t) * H * D + h * D;
-  const __nv_bfloat16* b = dout + static_cast<long>(t) * H * D + h * D;
+  const uint4* a = reinterpret_cast<const uint4*>(o + static_cast<long>(t) * H * D + h * D);
+  const uint4* b = reinterpret_cast<const uint4*>(dout + static_cast<long>(t) * H * D + h * D);
   float s = 0.f;
-  for (int d = lane * 2; d < D; d += 64) {
-    const float2 x = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(a + d));
-    const float2 y = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(b + d));
-    s += x.x * y.x + x.y * y.y;
+  for (int i = 0; i < D / 8; ++i) {
+    const uint4 x = a[i], y = b[i];
+    const uint32_t* xp = &x.x;
+    const uint32_t* yp = &y.x;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const float2 fx = unpack_bf16x2(xp[k]), fy = unpack_bf16x2(yp[k]);
+      s += fx.x * fy.x + fx.y * fy.y;
+    }
   }
-  s = warp_sum(s);
-  if (lane == 0) delta[static_cast<long>(h) * T + t] = s;
+  delta[static_cast<long>(h) * T + t] = s;
 }
 
-__global__ void dq_convert_kernel(const float* __restrict__ acc, __nv_bfloat16* __restrict__ dqkv, long ld, int T,
-                                  int HD) {
-  const long n = static_cast<long>(T) * HD / 2;
-  for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x) {
-    const long e = 2 * i;
-    const int t = static_cast<int>(e / HD), c = static_cast<int>(e % HD);
-    const float2 v = reinterpret_cast<const float2*>(acc)[i];
-    *reinterpret_cast<uint32_t*>(dqkv + t * ld + c) = pack_bf16x2(v.x, v.y);
+// dQ and dK (fp32 accumulators) -> bf16 into dqkv rotated back by the inverse RoPE
+// (the forward applied RoPE to q and k in the QKV GEMM epilogue); dV -> bf16.
+__global__ void dqkv_finalize_kernel(const float* __restrict__ dq_acc, const float* __restrict__ dkv_acc,
+                                     __nv_bfloat16* __restrict__ dqkv, long ld, const int* __restrict__ pos,
+                                     const float* __restrict__ cos_t, const float* __restrict__ sin_t, int n_pos,
+                                     int T, int H, int Hkv, int D) {
+  const int half = D / 2, g4 = half / 4;
+  const int heads = H + 2 * Hkv;
+  const long total = static_cast<long>(T) * heads * g4;
+  for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
+    const int t = static_cast<int>(i / (heads * g4));
+    const int rem = static_cast<int>(i % (heads * g4));
+    const int hs = rem / g4, j = (rem % g4) * 4;
+    const float* src = hs < H ? dq_acc + static_cast<long>(t) * H * D + hs * D
+                              : dkv_acc + static_cast<long>(t) * 2 * Hkv * D + (hs - H) * D;
+    const float4 a = *reinterpret_cast<const float4*>(src + j);
+    const float4 b = *reinterpret_cast<const float4*>(src + half + j);
+    float x1[4] = {a.x, a.y, a.z, a.w}, x2[4] = {b.x, b.y, b.z, b.w};
+    float y1[4], y2[4];
+    if (pos != nullptr && hs < H + Hkv) {
+      const int p = min(max(pos[t], 0), n_pos - 1);
+      const float4 c4 = *reinterpret_cast<const float4*>(cos_t + static_cast<long>(p) * half + j);
+      const float4 s4 = *reinterpret_cast<const float4*>(sin_t + static_cast<long>(p) * half + j);
+      const float cs[4] = {c4.x, c4.y, c4.z, c4.w}, sn[4] = {s4.x, s4.y, s4.z, s4.w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        y1[e] = x1[e] * cs[e] + x2[e] * sn[e];
+        y2[e] = x2[e] * cs[e] - x1[e] * sn[e];
+      }
+    } else {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        y1[e] = x1[e];
+        y2[e] = x2[e];
+      }
+    }
+    __nv_bfloat16* dst = dqkv + t * ld + hs * D;
+    *reinterpret_cast<uint2*>(dst + j) = make_uint2(pack_bf16x2(y1[0], y1[1]), pack_bf16x2(y1[2], y1[3]));
+    *reinterpret_cast<uint2*>(dst + half + j) = make_uint2(pack_bf16x2(y2[0], y2[1]), pack_bf16x2(y2[2], y2[3]));
   }
 }
 
@@ -717,21 +802,30 @@ std::vector<at::Tensor> attn_fwd(at::Tensor qkv, at::Tensor doc_start, at::Tenso
 
 void attn_bwd(at::Tensor qkv, at::Tensor out, at::Tensor dout, at::Tensor lse, at::Tensor doc_start,
               at::Tensor items, int64_t H, int64_t Hkv, int64_t D, double scale, at::Tensor dqkv, at::Tensor dq_acc,
-              at::Tensor delta) {
+              at::Tensor dkv_acc, at::Tensor delta, c10::optional<at::Tensor> pos, c10::optional<at::Tensor> cos_t,
+              c10::optional<at::Tensor> sin_t) {
   TORCH_CHECK(D == 64 || D == 128, "attention: head_dim must be 64 or 128");
   TORCH_CHECK(dout.is_contiguous() && dout.scalar_type() == at::kBFloat16 && out.is_contiguous());
-  TORCH_CHECK(dqkv.is_contiguous() && dq_acc.is_contiguous() && items.scalar_type() == at::kInt);
+  TORCH_CHECK(dqkv.is_contiguous() && dq_acc.is_contiguous() && dkv_acc.is_contiguous());
+  TORCH_CHECK(items.scalar_type() == at::kInt && items.dim() == 2 && items.size(1) == 3);
+  TORCH_CHECK(dq_acc.size(1) == H * D && dkv_acc.size(1) == 2 * Hkv * D, "attention: accumulator widths");
   const c10::cuda::CUDAGuard guard(qkv.device());
   const int T = qkv.size(0);
   if (T == 0) return;
   auto s = at::cuda::getCurrentCUDAStream();
+  PB_CUDA_CHECK(cudaMemsetAsync(dq_acc.data_ptr(), 0, dq_acc.numel() * sizeof(float), s));
+  PB_CUDA_CHECK(cudaMemsetAsync(dkv_acc.data_ptr(), 0, dkv_acc.numel() * sizeof(float), s));
   const long pairs = static_cast<long>(T) * H;
-  attn_delta_kernel<<<(pairs + 7) / 8, 256, 0, s>>>(reinterpret_cast<const __nv_bfloat16*>(out.data_ptr()),
-                                                    reinterpret_cast<const __nv_bfloat16*>(dout.data_ptr()),
-                                                    delta.data_ptr<float>(), T, (int)H, (int)D);
+  attn_delta_kernel<<<(pairs + 255) / 256, 256, 0, s>>>(reinterpret_cast<const __nv_bfloat16*>(out.data_ptr()),
+                                                      reinterpret_cast<const __nv_bfloat16*>(dout.data_ptr()),
+                                                      delta.data_ptr<float>(), T, (int)H, (int)D);
   PB_CUDA_CHECK(cudaGetLastError());
   CUtensorMap tq = make_tmap_bf16_2d(qkv.data_ptr(), qkv.size(1), T, qkv.stride(0) * 2, 64, 128);
   CUtensorMap td = make_tmap_bf16_2d(dout.data_ptr(), dout.size(1), T, dout.stride(0) * 2, 64, 128);
+  CUtensorMap tdq = make_tmap_2d(dq_acc.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_FLOAT32, dq_acc.size(1), T,
+                                 dq_acc.stride(0) * 4, 32, 32, CU_TENSOR_MAP_SWIZZLE_128B);
+  CUtensorMap tdkv = make_tmap_2d(dkv_acc.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_FLOAT32, dkv_acc.size(1), T,
+                                  dkv_acc.stride(0) * 4, 32, 32, CU_TENSOR_MAP_SWIZZLE_128B);
   AttnArgs a{};
   a.T = T;
   a.H = (int)H;
@@ -744,23 +838,24 @@ void attn_bwd(at::Tensor qkv, at::Tensor out, at::Tensor dout, at::Tensor lse, a
   a.n_items = items.size(0);
   a.lse = lse.data_ptr<float>();
   a.delta = delta.data_ptr<float>();
-  a.dq_acc = dq_acc.data_ptr<float>();
-  a.dqkv = reinterpret_cast<__nv_bfloat16*>(dqkv.data_ptr());
-  a.ld_dqkv = dqkv.stride(0);
   a.status = status_ptr(qkv.device().index());
   const int grid = std::min<int>(a.n_items, num_sms(qkv.device().index()));
   if (D == 64) {
     set_smem(attn_bwd_kernel<64>, BwdCfg<64>::SMEM);
-    attn_bwd_kernel<64><<<grid, 192, BwdCfg<64>::SMEM, s>>>(tq, td, a);
+    attn_bwd_kernel<64><<<grid, 320, BwdCfg<64>::SMEM, s>>>(tq, td, tdq, tdkv, a);
   } else {
     set_smem(attn_bwd_kernel<128>, BwdCfg<128>::SMEM);
-    attn_bwd_kernel<128><<<grid, 192, BwdCfg<128>::SMEM, s>>>(tq, td, a);
+    attn_bwd_kernel<128><<<grid, 320, BwdCfg<128>::SMEM, s>>>(tq, td, tdq, tdkv, a);
   }
   PB_CUDA_CHECK(cudaGetLastError());
-  const long n2 = static_cast<long>(T) * H * D / 2;
-  dq_convert_kernel<<<std::max<long>(1, std::min<long>((n2 + 255) / 256, 4L * num_sms(qkv.device().index()))), 256,
-                      0, s>>>(dq_acc.data_ptr<float>(), reinterpret_cast<__nv_bfloat16*>(dqkv.data_ptr()),
-                              dqkv.stride(0), T, (int)(H * D));
+  const long n4 = static_cast<long>(T) * (H + 2 * Hkv) * (D / 8);
+  dqkv_finalize_kernel<<<std::max<long>(1, std::min<long>((n4 + 255) / 256, 8L * num_sms(qkv.device().index()))),
+                         256, 0, s>>>(dq_acc.data_ptr<float>(), dkv_acc.data_ptr<float>(),
+                                      reinterpret_cast<__nv_bfloat16*>(dqkv.data_ptr()), dqkv.stride(0),
+                                      pos.has_value() ? pos->data_ptr<int>() : nullptr,
+                                      cos_t.has_value() ? cos_t->data_ptr<float>() : nullptr,
+                                      sin_t.has_value() ? sin_t->data_ptr<float>() : nullptr,
+                                      cos_t.has_value() ? (int)cos_t->size(0) : 1, T, (int)H, (int)Hkv, (int)D);
   PB_CUDA_CHECK(cudaGetLastError());
 }
 

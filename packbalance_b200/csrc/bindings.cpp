@@ -7,12 +7,15 @@
 
 namespace pb {
 void gemm_tc(at::Tensor a, at::Tensor b, at::Tensor out, int64_t M, int64_t N, int64_t K, bool a_mn, bool b_mn,
-             int64_t epi, int64_t bn, int64_t splits, int64_t max_ctas, double alpha, bool beta,
-             c10::optional<at::Tensor> res, c10::optional<at::Tensor> aux, c10::optional<at::Tensor> aux2,
-             c10::optional<at::Tensor> pos, c10::optional<at::Tensor> cos_t, c10::optional<at::Tensor> sin_t,
-             int64_t head_dim, int64_t n_rope_cols, c10::optional<at::Tensor> targets,
-             c10::optional<at::Tensor> pmax, c10::optional<at::Tensor> psum, c10::optional<at::Tensor> tlogit,
-             c10::optional<at::Tensor> lse, c10::optional<at::Tensor> row_scale, double z_coeff);
+             int64_t epi, int64_t bn, int64_t splits, int64_t max_ctas, double alpha,
+             c10::optional<at::Tensor> aux, c10::optional<at::Tensor> pos, c10::optional<at::Tensor> cos_t,
+             c10::optional<at::Tensor> sin_t, int64_t head_dim, int64_t n_rope_cols,
+             c10::optional<at::Tensor> targets, c10::optional<at::Tensor> pmax, c10::optional<at::Tensor> psum,
+             c10::optional<at::Tensor> tlogit, c10::optional<at::Tensor> lse, c10::optional<at::Tensor> row_scale,
+             double z_coeff);
+std::vector<at::Tensor> add_rmsnorm_fwd(at::Tensor x, c10::optional<at::Tensor> delta, at::Tensor w, double eps,
+                                        bool out_bf16);
+void swiglu_bwd_packed(at::Tensor dh, at::Tensor gu, at::Tensor dgu);
 std::vector<at::Tensor> rmsnorm_fwd(at::Tensor x, at::Tensor w, double eps, bool out_bf16);
 at::Tensor rmsnorm_bwd(at::Tensor dy, at::Tensor x, at::Tensor w, at::Tensor rstd, c10::optional<at::Tensor> dres,
                        c10::optional<at::Tensor> dx_bf16, at::Tensor dw_out, bool accumulate_dw);
@@ -34,7 +37,8 @@ std::vector<at::Tensor> attn_fwd(at::Tensor qkv, at::Tensor doc_start, at::Tenso
                                  int64_t n_kv_heads, int64_t head_dim, double scale, at::Tensor out);
 void attn_bwd(at::Tensor qkv, at::Tensor out, at::Tensor dout, at::Tensor lse, at::Tensor doc_start,
               at::Tensor kv_tiles, int64_t n_heads, int64_t n_kv_heads, int64_t head_dim, double scale,
-              at::Tensor dqkv, at::Tensor dq_acc, at::Tensor delta);
+              at::Tensor dqkv, at::Tensor dq_acc, at::Tensor dkv_acc, at::Tensor delta, c10::optional<at::Tensor> pos,
+              c10::optional<at::Tensor> cos_t, c10::optional<at::Tensor> sin_t);
 #endif
 #ifdef PB_WITH_COMM
 void comm_bindings(pybind11::module& m);
@@ -53,6 +57,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "packbalance_b200 native sm_100a kernels";
   m.def("gemm_tc", &pb::gemm_tc);
   m.def("rmsnorm_fwd", &pb::rmsnorm_fwd);
+  m.def("add_rmsnorm_fwd", &pb::add_rmsnorm_fwd);
+  m.def("swiglu_bwd_packed", &pb::swiglu_bwd_packed);
   m.def("rmsnorm_bwd", &pb::rmsnorm_bwd);
   m.def("swiglu_fwd", &pb::swiglu_fwd);
   m.def("swiglu_bwd", &pb::swiglu_bwd);

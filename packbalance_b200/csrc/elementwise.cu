@@ -27,97 +27,139 @@ template <>
 __device__ __forceinline__ __nv_bfloat16 from_f<__nv_bfloat16>(float v) { return __float2bfloat16_rn(v); }
 
 // ------------------------------- RMSNorm ------------------------------------------
-// One warp per row.  y = x * rstd * w, rstd = 1/sqrt(mean(x^2) + eps).
+// Vector helpers: 4 consecutive elements as fp32.
+__device__ __forceinline__ float4 ld4(const float* p) { return *reinterpret_cast<const float4*>(p); }
+__device__ __forceinline__ float4 ld4(const __nv_bfloat16* p) {
+  const uint2 u = *reinterpret_cast<const uint2*>(p);
+  const float2 a = unpack_bf16x2(u.x), b = unpack_bf16x2(u.y);
+  return make_float4(a.x, a.y, b.x, b.y);
+}
+__device__ __forceinline__ void st4(float* p, float4 v) { *reinterpret_cast<float4*>(p) = v; }
+__device__ __forceinline__ void st4(__nv_bfloat16* p, float4 v) {
+  *reinterpret_cast<uint2*>(p) = make_uint2(pack_bf16x2(v.x, v.y), pack_bf16x2(v.z, v.w));
+}
+
+// One warp per row (n % 4 == 0).  x = x_prev (+ delta); y = x * rstd * w with
+// rstd = 1/sqrt(mean(x^2) + eps).  ``x_out`` receives x when a delta is added.
 template <typename TI, typename TO>
-__global__ void rmsnorm_fwd_kernel(const TI* __restrict__ x, const float* __restrict__ w, TO* __restrict__ y,
+__global__ void add_rmsnorm_kernel(const TI* __restrict__ xp, const __nv_bfloat16* __restrict__ delta,
+                                   const float* __restrict__ w, float* __restrict__ x_out, TO* __restrict__ y,
                                    float* __restrict__ rstd, int rows, int n, float eps) {
   const int row = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
   if (row >= rows) return;
-  const TI* xr = x + static_cast<long>(row) * n;
+  const long off = static_cast<long>(row) * n;
   float ss = 0.f;
-  for (int c = lane; c < n; c += 32) {
-    const float v = to_f(xr[c]);
-    ss += v * v;
+  for (int c = lane * 4; c < n; c += 128) {
+    float4 v = ld4(xp + off + c);
+    if (delta != nullptr) {
+      const float4 d = ld4(delta + off + c);
+      v.x += d.x; v.y += d.y; v.z += d.z; v.w += d.w;
+      st4(x_out + off + c, v);
+    }
+    ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
   }
   ss = warp_sum(ss);
   const float r = rsqrtf(ss / n + eps);
   if (lane == 0) rstd[row] = r;
-  TO* yr = y + static_cast<long>(row) * n;
-  for (int c = lane; c < n; c += 32) yr[c] = from_f<TO>(to_f(xr[c]) * r * w[c]);
+  __syncwarp();
+  for (int c = lane * 4; c < n; c += 128) {
+    float4 v = delta != nullptr ? ld4(x_out + off + c) : ld4(xp + off + c);
+    const float4 g = ld4(w + c);
+    st4(y + off + c, make_float4(v.x * r * g.x, v.y * r * g.y, v.z * r * g.z, v.w * r * g.w));
+  }
 }
 
-// dx = rstd * (g - xhat * mean(g * xhat)) [+ dres], g = dy * w; per-block partial dw.
+// dx = rstd * (g - xhat * mean(g * xhat)) [+ dres], g = dy * w.  Each warp keeps its
+// own dw partial row in shared memory (lane-owned columns: no atomics, no bank
+// conflicts); the block's partial is added to dw_out with one atomic per column.
 template <typename TI, typename TD>
 __global__ void rmsnorm_bwd_kernel(const TD* __restrict__ dy, const TI* __restrict__ x, const float* __restrict__ w,
                                    const float* __restrict__ rstd, const float* __restrict__ dres,
                                    float* __restrict__ dx, __nv_bfloat16* __restrict__ dx_bf16,
-                                   float* __restrict__ dw_part, int rows, int n, int rows_per_block) {
-  extern __shared__ float sdw[];
-  for (int c = threadIdx.x; c < n; c += blockDim.x) sdw[c] = 0.f;
-  __syncthreads();
+                                   float* __restrict__ dw_out, int rows, int n) {
+  extern __shared__ float sdw[];  // [warps][n]
   const int warps = blockDim.x / 32;
-  const int lane = threadIdx.x % 32;
-  const int r0 = blockIdx.x * rows_per_block;
-  const int r1 = min(rows, r0 + rows_per_block);
-  for (int row = r0 + threadIdx.x / 32; row < r1; row += warps) {
+  const int wid = threadIdx.x / 32, lane = threadIdx.x % 32;
+  float* mine = sdw + static_cast<long>(wid) * n;
+  for (int c = lane * 4; c < n; c += 128) st4(mine + c, make_float4(0.f, 0.f, 0.f, 0.f));
+  for (int row = blockIdx.x * warps + wid; row < rows; row += gridDim.x * warps) {
     const long off = static_cast<long>(row) * n;
     const float r = rstd[row];
     float dot = 0.f;
-    for (int c = lane; c < n; c += 32) dot += to_f(dy[off + c]) * w[c] * to_f(x[off + c]) * r;
-    dot = warp_sum(dot) / n;
-    for (int c = lane; c < n; c += 32) {
-      const float xh = to_f(x[off + c]) * r;
-      const float g = to_f(dy[off + c]);
-      float d = r * (g * w[c] - xh * dot);
-      if (dres != nullptr) d += dres[off + c];
-      dx[off + c] = d;
-      if (dx_bf16 != nullptr) dx_bf16[off + c] = __float2bfloat16_rn(d);
-      atomicAdd(&sdw[c], g * xh);
+    for (int c = lane * 4; c < n; c += 128) {
+      const float4 g = ld4(dy + off + c), xv = ld4(x + off + c), wv = ld4(w + c);
+      dot += g.x * wv.x * xv.x + g.y * wv.y * xv.y + g.z * wv.z * xv.z + g.w * wv.w * xv.w;
+    }
+    dot = warp_sum(dot) * r / n;
+    for (int c = lane * 4; c < n; c += 128) {
+      const float4 g = ld4(dy + off + c), xv = ld4(x + off + c), wv = ld4(w + c);
+      float4 d = make_float4(r * (g.x * wv.x - xv.x * r * dot), r * (g.y * wv.y - xv.y * r * dot),
+                             r * (g.z * wv.z - xv.z * r * dot), r * (g.w * wv.w - xv.w * r * dot));
+      if (dres != nullptr) {
+        const float4 e = ld4(dres + off + c);
+        d.x += e.x; d.y += e.y; d.z += e.z; d.w += e.w;
+      }
+      st4(dx + off + c, d);
+      if (dx_bf16 != nullptr) st4(dx_bf16 + off + c, d);
+      float4 p = ld4(mine + c);
+      p.x += g.x * xv.x * r; p.y += g.y * xv.y * r; p.z += g.z * xv.z * r; p.w += g.w * xv.w * r;
+      st4(mine + c, p);
     }
   }
   __syncthreads();
-  for (int c = threadIdx.x; c < n; c += blockDim.x) dw_part[static_cast<long>(blockIdx.x) * n + c] = sdw[c];
+  for (int c = threadIdx.x; c < n; c += blockDim.x) {
+    float t = 0.f;
+    for (int k = 0; k < warps; ++k) t += sdw[static_cast<long>(k) * n + c];
+    atomicAdd(dw_out + c, t);
+  }
 }
 
-// dw[c] (+)= sum over partial rows.
-__global__ void reduce_cols_kernel(const float* __restrict__ part, int nparts, int n, float* __restrict__ out,
-                                   int accumulate) {
-  const int c = blockIdx.x * blockDim.x + threadIdx.x;
-  if (c >= n) return;
-  float s = 0.f;
-  for (int p = 0; p < nparts; ++p) s += part[static_cast<long>(p) * n + c];
-  out[c] = accumulate ? out[c] + s : s;
-}
-
-std::vector<at::Tensor> rmsnorm_fwd(at::Tensor x, at::Tensor w, double eps, bool out_bf16) {
+std::vector<at::Tensor> add_rmsnorm_fwd(at::Tensor x, c10::optional<at::Tensor> delta, at::Tensor w, double eps,
+                                        bool out_bf16) {
   TORCH_CHECK(x.is_cuda() && x.is_contiguous() && w.is_contiguous() && w.scalar_type() == at::kFloat);
   const c10::cuda::CUDAGuard guard(x.device());
   const int n = x.size(-1);
+  TORCH_CHECK(n % 4 == 0, "rmsnorm: feature dim must be a multiple of 4");
   const int rows = x.numel() / n;
   auto y = at::empty(x.sizes(), x.options().dtype(out_bf16 ? at::kBFloat16 : x.scalar_type()));
   auto rstd = at::empty({rows}, x.options().dtype(at::kFloat));
+  at::Tensor xo = x;
+  const __nv_bfloat16* dp = nullptr;
+  if (delta.has_value()) {
+    TORCH_CHECK(x.scalar_type() == at::kFloat && delta->scalar_type() == at::kBFloat16 && delta->is_contiguous() &&
+                    delta->numel() == x.numel(),
+                "add_rmsnorm: fp32 x and bf16 delta of the same shape");
+    xo = at::empty_like(x);
+    dp = reinterpret_cast<const __nv_bfloat16*>(delta->data_ptr());
+  }
+  if (rows == 0) return {xo, y, rstd};
   const int warps = 8;
   dim3 grid((rows + warps - 1) / warps);
   auto s = at::cuda::getCurrentCUDAStream();
-  if (rows == 0) return {y, rstd};
+  float* xop = delta.has_value() ? xo.data_ptr<float>() : nullptr;
   if (x.scalar_type() == at::kFloat) {
     if (out_bf16)
-      rmsnorm_fwd_kernel<float, __nv_bfloat16><<<grid, warps * 32, 0, s>>>(
-          x.data_ptr<float>(), w.data_ptr<float>(), reinterpret_cast<__nv_bfloat16*>(y.data_ptr()),
+      add_rmsnorm_kernel<float, __nv_bfloat16><<<grid, warps * 32, 0, s>>>(
+          x.data_ptr<float>(), dp, w.data_ptr<float>(), xop, reinterpret_cast<__nv_bfloat16*>(y.data_ptr()),
           rstd.data_ptr<float>(), rows, n, (float)eps);
     else
-      rmsnorm_fwd_kernel<float, float><<<grid, warps * 32, 0, s>>>(x.data_ptr<float>(), w.data_ptr<float>(),
-                                                                   y.data_ptr<float>(), rstd.data_ptr<float>(),
-                                                                   rows, n, (float)eps);
+      add_rmsnorm_kernel<float, float><<<grid, warps * 32, 0, s>>>(x.data_ptr<float>(), dp, w.data_ptr<float>(), xop,
+                                                                   y.data_ptr<float>(), rstd.data_ptr<float>(), rows,
+                                                                   n, (float)eps);
   } else {
-    TORCH_CHECK(x.scalar_type() == at::kBFloat16, "rmsnorm: fp32 or bf16 input");
-    rmsnorm_fwd_kernel<__nv_bfloat16, __nv_bfloat16><<<grid, warps * 32, 0, s>>>(
-        reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), w.data_ptr<float>(),
+    TORCH_CHECK(x.scalar_type() == at::kBFloat16 && !delta.has_value(), "rmsnorm: fp32 or bf16 input");
+    add_rmsnorm_kernel<__nv_bfloat16, __nv_bfloat16><<<grid, warps * 32, 0, s>>>(
+        reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), nullptr, w.data_ptr<float>(), nullptr,
         reinterpret_cast<__nv_bfloat16*>(y.data_ptr()), rstd.data_ptr<float>(), rows, n, (float)eps);
   }
   PB_CUDA_CHECK(cudaGetLastError());
-  return {y, rstd};
+  return {xo, y, rstd};
+}
+
+std::vector<at::Tensor> rmsnorm_fwd(at::Tensor x, at::Tensor w, double eps, bool out_bf16) {
+  auto r = add_rmsnorm_fwd(x, c10::nullopt, w, eps, out_bf16);
+  return {r[1], r[2]};
 }
 
 // Returns dx (fp32).  dw is written (or accumulated) into ``dw_out``.
@@ -126,23 +168,26 @@ at::Tensor rmsnorm_bwd(at::Tensor dy, at::Tensor x, at::Tensor w, at::Tensor rst
   TORCH_CHECK(dy.is_contiguous() && x.is_contiguous() && dy.numel() == x.numel());
   const c10::cuda::CUDAGuard guard(x.device());
   const int n = x.size(-1);
+  TORCH_CHECK(n % 4 == 0, "rmsnorm: feature dim must be a multiple of 4");
   const int rows = x.numel() / n;
   auto dx = at::empty(x.sizes(), x.options().dtype(at::kFloat));
-  if (rows == 0) return dx;
-  const int sms = num_sms(x.device().index());
-  const int nblocks = std::min(rows, 2 * sms);
-  const int rpb = (rows + nblocks - 1) / nblocks;
-  const int nb = (rows + rpb - 1) / rpb;
-  auto part = at::empty({nb, n}, x.options().dtype(at::kFloat));
   auto s = at::cuda::getCurrentCUDAStream();
+  if (!accumulate_dw) PB_CUDA_CHECK(cudaMemsetAsync(dw_out.data_ptr(), 0, n * sizeof(float), s));
+  if (rows == 0) return dx;
+  const int warps = 4;
+  const int nb = std::min((rows + warps - 1) / warps, 2 * num_sms(x.device().index()));
   const float* dres_p = dres.has_value() ? dres->data_ptr<float>() : nullptr;
   __nv_bfloat16* dxb = dx_bf16.has_value() ? reinterpret_cast<__nv_bfloat16*>(dx_bf16->data_ptr()) : nullptr;
-  const size_t smem = n * sizeof(float);
-  TORCH_CHECK(smem <= 48 * 1024, "rmsnorm_bwd: feature dim too large");
-#define PB_RMS_BWD(TI, TD)                                                                                  \
-  rmsnorm_bwd_kernel<TI, TD><<<nb, 256, smem, s>>>(                                                         \
-      reinterpret_cast<const TD*>(dy.data_ptr()), reinterpret_cast<const TI*>(x.data_ptr()), w.data_ptr<float>(), \
-      rstd.data_ptr<float>(), dres_p, dx.data_ptr<float>(), dxb, part.data_ptr<float>(), rows, n, rpb)
+  const size_t smem = static_cast<size_t>(warps) * n * sizeof(float);
+  TORCH_CHECK(smem <= 200 * 1024, "rmsnorm_bwd: feature dim too large");
+#define PB_RMS_BWD(TI, TD)                                                                                    \
+  do {                                                                                                        \
+    auto k = rmsnorm_bwd_kernel<TI, TD>;                                                                      \
+    if (smem > 48 * 1024) PB_CUDA_CHECK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)); \
+    k<<<nb, warps * 32, smem, s>>>(reinterpret_cast<const TD*>(dy.data_ptr()), reinterpret_cast<const TI*>(x.data_ptr()), \
+                                   w.data_ptr<float>(), rstd.data_ptr<float>(), dres_p, dx.data_ptr<float>(), dxb,      \
+                                   dw_out.data_ptr<float>(), rows, n);                                        \
+  } while (0)
   const bool xf = x.scalar_type() == at::kFloat, df = dy.scalar_type() == at::kFloat;
   if (xf && df) PB_RMS_BWD(float, float);
   else if (xf && !df) PB_RMS_BWD(float, __nv_bfloat16);
@@ -150,10 +195,50 @@ at::Tensor rmsnorm_bwd(at::Tensor dy, at::Tensor x, at::Tensor w, at::Tensor rst
   else PB_RMS_BWD(__nv_bfloat16, __nv_bfloat16);
 #undef PB_RMS_BWD
   PB_CUDA_CHECK(cudaGetLastError());
-  reduce_cols_kernel<<<(n + 255) / 256, 256, 0, s>>>(part.data_ptr<float>(), nb, n, dw_out.data_ptr<float>(),
-                                                       accumulate_dw ? 1 : 0);
-  PB_CUDA_CHECK(cudaGetLastError());
   return dx;
+}
+
+// SwiGLU backward on the packed layout: gu = [g | u] (bf16 [M, 2F]), dh (bf16 [M, F])
+// -> dgu = [dg | du] (bf16 [M, 2F]).  8 elements per thread.
+__global__ void swiglu_bwd_packed_kernel(const __nv_bfloat16* __restrict__ dh, const __nv_bfloat16* __restrict__ gu,
+                                         __nv_bfloat16* __restrict__ dgu, long rows, int F) {
+  const int f8 = F / 8;
+  const long total = rows * f8;
+  for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
+    const long r = i / f8;
+    const int c = static_cast<int>(i % f8) * 8;
+    const uint4 hv = *reinterpret_cast<const uint4*>(dh + r * F + c);
+    const uint4 gv = *reinterpret_cast<const uint4*>(gu + r * 2 * F + c);
+    const uint4 uv = *reinterpret_cast<const uint4*>(gu + r * 2 * F + F + c);
+    const uint32_t* hp = &hv.x;
+    const uint32_t* gp = &gv.x;
+    const uint32_t* up = &uv.x;
+    uint32_t dgo[4], duo[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const float2 d = unpack_bf16x2(hp[k]), g = unpack_bf16x2(gp[k]), u = unpack_bf16x2(up[k]);
+      const float s0 = sigmoidf_(g.x), s1 = sigmoidf_(g.y);
+      dgo[k] = pack_bf16x2(d.x * u.x * s0 * (1.f + g.x * (1.f - s0)), d.y * u.y * s1 * (1.f + g.y * (1.f - s1)));
+      duo[k] = pack_bf16x2(d.x * g.x * s0, d.y * g.y * s1);
+    }
+    *reinterpret_cast<uint4*>(dgu + r * 2 * F + c) = make_uint4(dgo[0], dgo[1], dgo[2], dgo[3]);
+    *reinterpret_cast<uint4*>(dgu + r * 2 * F + F + c) = make_uint4(duo[0], duo[1], duo[2], duo[3]);
+  }
+}
+
+void swiglu_bwd_packed(at::Tensor dh, at::Tensor gu, at::Tensor dgu) {
+  TORCH_CHECK(dh.is_contiguous() && gu.is_contiguous() && dgu.is_contiguous());
+  const c10::cuda::CUDAGuard guard(dh.device());
+  const long rows = dh.size(0);
+  const int F = dh.size(1);
+  TORCH_CHECK(F % 8 == 0 && gu.size(1) == 2 * F && dgu.size(1) == 2 * F);
+  const long total = rows * (F / 8);
+  if (total == 0) return;
+  swiglu_bwd_packed_kernel<<<(int)std::min<long>((total + 255) / 256, 16L * num_sms(dh.device().index())), 256, 0,
+                             at::cuda::getCurrentCUDAStream()>>>(
+      reinterpret_cast<const __nv_bfloat16*>(dh.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(gu.data_ptr()),
+      reinterpret_cast<__nv_bfloat16*>(dgu.data_ptr()), rows, F);
+  PB_CUDA_CHECK(cudaGetLastError());
 }
 
 // ------------------------------- SwiGLU -------------------------------------------

@@ -11,29 +11,31 @@
 // Kernel structure (one CTA per SM, persistent over output tiles of 128 x BN):
 //   warp 0      TMA producer: 128B-swizzled A/B tiles into a STAGES-deep smem ring
 //   warp 1      TMEM allocator + single-thread tcgen05.mma issuer (M=128, N=BN, K=16)
-//   warps 2..5  epilogue: tcgen05.ld of the accumulator (thread = row), fused math,
-//               global stores; two TMEM accumulators so tile i's epilogue overlaps
-//               tile i+1's MMAs.
+//   warps 2..5  epilogue, warp q owns TMEM lanes [32q, 32q+32) (= tile rows): each
+//               32-column chunk goes tcgen05.ld -> registers -> fused math -> swizzled
+//               smem staging slot -> TMA store (or TMA fp32 reduce-add), so global
+//               writes are full coalesced boxes issued asynchronously; two staging
+//               slots per warp and two TMEM accumulators overlap the epilogue of
+//               tile i with the MMAs of tile i+1.
 // Every mbarrier wait is bounded (common.cuh); a timeout records an error code in
 // the status word, the other roles stop, in-flight copies and MMAs are drained and
 // TMEM is freed before the CTA exits.
 //
-// Epilogues (runtime-selected, uniform per launch):
+// Epilogues (runtime-selected, uniform per launch; none reads global memory except
+// the CE row vectors and the RoPE tables):
 //   BF16        out(bf16) = alpha * acc
-//   F32         out(f32)  = alpha * acc (+ out when beta != 0)
-//   RESID       out(f32)  = res(f32) + acc                 (residual stream update)
-//   SWIGLU      B tile = [gate rows | up rows]; h = silu(g) * u (bf16) and the
-//               pre-activations are saved (bf16) for the backward pass
+//   F32         out(f32)  = alpha * acc
+//   ADD_F32     out(f32) += alpha * acc   (TMA reduce-add: accumulation and split-K)
+//   SWIGLU      B tile = [gate rows | up rows]; h = silu(g) * u and the rounded
+//               pre-activations g|u are stored (bf16) for the backward pass
 //   ROPE        out(bf16) = acc with half-split RoPE on the first n_rope_cols columns
 //               (per-row positions, fp32 cos/sin tables)
-//   SWIGLU_BWD  acc = dh; reads saved g|u and writes dg|du (bf16)
-//   ATOMIC_F32  out(f32) += acc via vector atomics (split-K partial sums)
 //   CE_FWD      per-row max / sum(exp) partials of the logits tile + target logit
 //   CE_BWD      dlogits(bf16) = (softmax(logit) * (1 + 2 z lse) - onehot) * row_scale
+#include <ATen/ATen.h>
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 #include <cudaTypedefs.h>
-#include <ATen/ATen.h>
 
 #include "common.cuh"
 #include "host_utils.h"
@@ -43,11 +45,9 @@ namespace pb {
 enum GemmEpi : int {
   EPI_BF16 = 0,
   EPI_F32 = 1,
-  EPI_RESID = 2,
+  EPI_ADD_F32 = 2,
   EPI_SWIGLU = 3,
   EPI_ROPE = 4,
-  EPI_SWIGLU_BWD = 5,
-  EPI_ATOMIC_F32 = 6,
   EPI_CE_FWD = 7,
   EPI_CE_BWD = 8,
 };
@@ -57,16 +57,7 @@ struct GemmArgs {
   int m_tiles, n_tiles, splits, kb_per_split, k_blocks;
   int epi;
   float alpha;
-  int beta;
-  void* out;
-  long ldo;
-  const float* res;
-  long ldr;
-  void* aux;  // SWIGLU: saved g|u (out); SWIGLU_BWD: saved g|u (in)
-  long ldaux;
-  void* aux2;  // SWIGLU_BWD: dg|du (out)
-  long ldaux2;
-  int F;  // half width of the gate|up matrices
+  int F;  // SWIGLU: width of h (gate|up matrices have 2F rows)
   const int* pos;
   const float* cos_t;
   const float* sin_t;
@@ -83,6 +74,8 @@ struct GemmArgs {
   int* status;
 };
 
+constexpr int kEpiWarpBytes = 8192;  // two 4 KB staging slots per epilogue warp
+
 template <int BN>
 struct GemmCfg {
   static constexpr int BM = 128;
@@ -91,8 +84,10 @@ struct GemmCfg {
   static constexpr int B_BYTES = BN * BK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int STAGES = BN == 256 ? 4 : (BN == 128 ? 6 : 8);
+  static constexpr int EPI_OFF = STAGES * STAGE_BYTES;
   static constexpr uint32_t TMEM_COLS = 2 * BN;
-  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024;
+  static constexpr int SMEM_BYTES = EPI_OFF + 4 * kEpiWarpBytes + 1024;
+  static_assert(SMEM_BYTES <= 232448, "shared memory budget");
 };
 
 __device__ __forceinline__ void tile_coords(const GemmArgs& a, int tile, int& mb, int& nb, int& sp) {
@@ -103,35 +98,54 @@ __device__ __forceinline__ void tile_coords(const GemmArgs& a, int tile, int& mb
 }
 
 // ------------------------------- epilogue helpers ---------------------------------
-__device__ __forceinline__ void store_bf16_32(__nv_bfloat16* dst, const float* v, int valid) {
-  uint32_t p[16];
+struct Stager {
+  uint8_t* base;  // this warp's 8 KB
+  int slot;
+  __device__ __forceinline__ uint8_t* acquire() {
+    // The store issued two slot-uses ago must have finished reading its slot.
+    if ((threadIdx.x & 31) == 0) bulk_wait_read<1>();
+    __syncwarp();
+    return base + slot * 4096;
+  }
+  __device__ __forceinline__ void release() { slot ^= 1; }
+};
+
+// 32 fp32 of this lane's row -> 128-byte row of a 128B-swizzled [32 x 32] fp32 box.
+__device__ __forceinline__ void stage_f32(uint8_t* s, const float (&v)[32], float scale) {
+  const int r = threadIdx.x & 31;
 #pragma unroll
-  for (int i = 0; i < 16; ++i) p[i] = pack_bf16x2(v[2 * i], v[2 * i + 1]);
-  if (valid >= 32) {
-    uint4* d = reinterpret_cast<uint4*>(dst);
-#pragma unroll
-    for (int i = 0; i < 4; ++i) d[i] = make_uint4(p[4 * i], p[4 * i + 1], p[4 * i + 2], p[4 * i + 3]);
-  } else {
-    for (int i = 0; i < valid; ++i) dst[i] = __float2bfloat16_rn(v[i]);
+  for (int j = 0; j < 8; ++j) {
+    float4 q = make_float4(v[4 * j] * scale, v[4 * j + 1] * scale, v[4 * j + 2] * scale, v[4 * j + 3] * scale);
+    *reinterpret_cast<float4*>(s + r * 128 + ((j ^ (r & 7)) << 4)) = q;
   }
 }
 
-__device__ __forceinline__ void load_bf16_32(const __nv_bfloat16* src, float* v, int valid) {
-  if (valid >= 32) {
-    const uint4* s = reinterpret_cast<const uint4*>(src);
+// 32 bf16 of this lane's row -> 64-byte row of a 64B-swizzled [32 x 32] bf16 box.
+__device__ __forceinline__ void stage_bf16(uint8_t* s, const float (&v)[32], float scale) {
+  const int r = threadIdx.x & 31;
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      uint4 q = s[i];
-      float2 f0 = unpack_bf16x2(q.x), f1 = unpack_bf16x2(q.y), f2 = unpack_bf16x2(q.z), f3 = unpack_bf16x2(q.w);
-      v[8 * i + 0] = f0.x; v[8 * i + 1] = f0.y; v[8 * i + 2] = f1.x; v[8 * i + 3] = f1.y;
-      v[8 * i + 4] = f2.x; v[8 * i + 5] = f2.y; v[8 * i + 6] = f3.x; v[8 * i + 7] = f3.y;
-    }
-  } else {
-    for (int i = 0; i < 32; ++i) v[i] = i < valid ? __bfloat162float(src[i]) : 0.f;
+  for (int j = 0; j < 4; ++j) {
+    uint4 q = make_uint4(pack_bf16x2(v[8 * j] * scale, v[8 * j + 1] * scale),
+                         pack_bf16x2(v[8 * j + 2] * scale, v[8 * j + 3] * scale),
+                         pack_bf16x2(v[8 * j + 4] * scale, v[8 * j + 5] * scale),
+                         pack_bf16x2(v[8 * j + 6] * scale, v[8 * j + 7] * scale));
+    *reinterpret_cast<uint4*>(s + r * 64 + ((j ^ ((r >> 1) & 3)) << 4)) = q;
   }
 }
 
-__device__ __forceinline__ void tmem_load_f32(uint32_t taddr, float* v) {
+enum StoreKind { ST_STORE = 0, ST_ADD = 1 };
+
+__device__ __forceinline__ void issue_store(const CUtensorMap* map, const uint8_t* s, int col, int row, int kind) {
+  fence_async_smem();
+  __syncwarp();
+  if ((threadIdx.x & 31) == 0) {
+    if (kind == ST_ADD) tma_reduce_add_2d(map, s, col, row);
+    else tma_store_2d(map, s, col, row);
+    bulk_commit();
+  }
+}
+
+__device__ __forceinline__ void tmem_load_f32(uint32_t taddr, float (&v)[32]) {
   uint32_t r[32];
   tmem_ld32(taddr, r);
   tmem_wait_ld();
@@ -139,63 +153,35 @@ __device__ __forceinline__ void tmem_load_f32(uint32_t taddr, float* v) {
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+__device__ __forceinline__ float bf16_round(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
+
+// Epilogue of one 128 x BN tile for the 32 rows [row0, row0 + 32) owned by this warp.
 template <int BN>
-__device__ void run_epilogue(const GemmArgs& a, uint32_t tacc, int row, int mb, int nb) {
+__device__ __forceinline__ void run_epilogue(const GemmArgs& a, const CUtensorMap* tm_out, const CUtensorMap* tm_aux,
+                                             Stager& st, uint32_t tacc, int row0, int nb) {
+  const int lane = threadIdx.x & 31;
+  const int row = row0 + lane;
   const bool row_ok = row < a.M;
   float v[32];
   switch (a.epi) {
     case EPI_BF16:
     case EPI_F32:
-    case EPI_RESID:
-    case EPI_ATOMIC_F32: {
-      const int n0 = nb * BN;
+    case EPI_ADD_F32: {
 #pragma unroll 1
       for (int c = 0; c < BN; c += 32) {
         tmem_load_f32(tacc + c, v);
-        const int col = n0 + c;
-        const int valid = min(32, a.N - col);
-        if (!row_ok || valid <= 0) continue;
-        if (a.epi == EPI_BF16) {
-#pragma unroll
-          for (int i = 0; i < 32; ++i) v[i] *= a.alpha;
-          store_bf16_32(reinterpret_cast<__nv_bfloat16*>(a.out) + row * a.ldo + col, v, valid);
-        } else if (a.epi == EPI_ATOMIC_F32) {
-          float* dst = reinterpret_cast<float*>(a.out) + row * a.ldo + col;
-          if (valid >= 32) {
-#pragma unroll
-            for (int i = 0; i < 8; ++i)
-              atomicAdd(reinterpret_cast<float4*>(dst) + i,
-                        make_float4(a.alpha * v[4 * i], a.alpha * v[4 * i + 1], a.alpha * v[4 * i + 2],
-                                    a.alpha * v[4 * i + 3]));
-          } else {
-            for (int i = 0; i < valid; ++i) atomicAdd(dst + i, a.alpha * v[i]);
-          }
-        } else {
-          float* dst = reinterpret_cast<float*>(a.out) + row * a.ldo + col;
-          const float* add = nullptr;
-          if (a.epi == EPI_RESID) add = a.res + row * a.ldr + col;
-          else if (a.beta) add = dst;
-          const float s = a.epi == EPI_RESID ? 1.f : a.alpha;
-          if (valid >= 32) {
-#pragma unroll
-            for (int i = 0; i < 8; ++i) {
-              float4 o = make_float4(s * v[4 * i], s * v[4 * i + 1], s * v[4 * i + 2], s * v[4 * i + 3]);
-              if (add != nullptr) {
-                float4 b = reinterpret_cast<const float4*>(add)[i];
-                o.x += b.x; o.y += b.y; o.z += b.z; o.w += b.w;
-              }
-              reinterpret_cast<float4*>(dst)[i] = o;
-            }
-          } else {
-            for (int i = 0; i < valid; ++i) dst[i] = s * v[i] + (add != nullptr ? add[i] : 0.f);
-          }
-        }
+        const int col = nb * BN + c;
+        if (col >= a.N) continue;  // uniform across the warp
+        uint8_t* s = st.acquire();
+        if (a.epi == EPI_BF16) stage_bf16(s, v, a.alpha);
+        else stage_f32(s, v, a.alpha);
+        issue_store(tm_out, s, col, row0, a.epi == EPI_ADD_F32 ? ST_ADD : ST_STORE);
+        st.release();
       }
       break;
     }
     case EPI_SWIGLU: {
-      // acc columns [0, BN/2) = gate, [BN/2, BN) = up, for output columns
-      // [nb*BN/2, (nb+1)*BN/2) of h.
+      // acc columns [0, BN/2) = gate, [BN/2, BN) = up, for h columns [nb*BN/2, ...).
       constexpr int HB = BN / 2;
       float u[32];
 #pragma unroll 1
@@ -203,119 +189,105 @@ __device__ void run_epilogue(const GemmArgs& a, uint32_t tacc, int row, int mb, 
         tmem_load_f32(tacc + c, v);
         tmem_load_f32(tacc + HB + c, u);
         const int col = nb * HB + c;
-        const int valid = min(32, a.F - col);
-        if (!row_ok || valid <= 0) continue;
-        __nv_bfloat16* gu = reinterpret_cast<__nv_bfloat16*>(a.aux) + row * a.ldaux;
+        if (col >= a.F) continue;
         // Round the pre-activations once and compute h from the rounded values, so
         // the backward pass (which reads the saved bf16 values) sees the same inputs.
-        store_bf16_32(gu + col, v, valid);
-        store_bf16_32(gu + a.F + col, u, valid);
-        float h[32];
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
-          const float g = __bfloat162float(__float2bfloat16_rn(v[i]));
-          const float up = __bfloat162float(__float2bfloat16_rn(u[i]));
-          h[i] = g * sigmoidf_(g) * up;
+          v[i] = bf16_round(v[i]);
+          u[i] = bf16_round(u[i]);
         }
-        store_bf16_32(reinterpret_cast<__nv_bfloat16*>(a.out) + row * a.ldo + col, h, valid);
-      }
-      break;
-    }
-    case EPI_SWIGLU_BWD: {
-      const int n0 = nb * BN;
-      float g[32], u[32];
-#pragma unroll 1
-      for (int c = 0; c < BN; c += 32) {
-        tmem_load_f32(tacc + c, v);
-        const int col = n0 + c;
-        const int valid = min(32, a.F - col);
-        if (!row_ok || valid <= 0) continue;
-        const __nv_bfloat16* gu = reinterpret_cast<const __nv_bfloat16*>(a.aux) + row * a.ldaux;
-        load_bf16_32(gu + col, g, valid);
-        load_bf16_32(gu + a.F + col, u, valid);
-        float dg[32], du[32];
+        uint8_t* s = st.acquire();
+        stage_bf16(s, v, 1.f);
+        issue_store(tm_aux, s, col, row0, ST_STORE);
+        st.release();
+        s = st.acquire();
+        stage_bf16(s, u, 1.f);
+        issue_store(tm_aux, s, a.F + col, row0, ST_STORE);
+        st.release();
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const float s = sigmoidf_(g[i]);
-          const float silu = g[i] * s;
-          du[i] = v[i] * silu;
-          dg[i] = v[i] * u[i] * (s * (1.f + g[i] * (1.f - s)));
-        }
-        __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(a.aux2) + row * a.ldaux2;
-        store_bf16_32(out + col, dg, valid);
-        store_bf16_32(out + a.F + col, du, valid);
+        for (int i = 0; i < 32; ++i) v[i] = v[i] * sigmoidf_(v[i]) * u[i];
+        s = st.acquire();
+        stage_bf16(s, v, 1.f);
+        issue_store(tm_out, s, col, row0, ST_STORE);
+        st.release();
       }
       break;
     }
     case EPI_ROPE: {
-      const int n0 = nb * BN;
       const int half = a.head_dim / 2;
       const int p = row_ok ? min(max(a.pos[row], 0), a.n_pos - 1) : 0;
       float w[32];
 #pragma unroll 1
       for (int hb = 0; hb < BN; hb += a.head_dim) {
-        const int hcol = n0 + hb;
+        const int hcol = nb * BN + hb;
         const bool rot = hcol < a.n_rope_cols;
 #pragma unroll 1
         for (int j = 0; j < half; j += 32) {
           tmem_load_f32(tacc + hb + j, v);
           tmem_load_f32(tacc + hb + half + j, w);
-          if (!row_ok || hcol >= a.N) continue;
+          if (hcol >= a.N) continue;
           if (rot) {
-            const float* cr = a.cos_t + (long)p * half + j;
-            const float* sr = a.sin_t + (long)p * half + j;
+            const float4* cr = reinterpret_cast<const float4*>(a.cos_t + static_cast<long>(p) * half + j);
+            const float4* sr = reinterpret_cast<const float4*>(a.sin_t + static_cast<long>(p) * half + j);
 #pragma unroll
-            for (int i = 0; i < 32; ++i) {
-              const float c = cr[i], s = sr[i];
-              const float x1 = v[i], x2 = w[i];
-              v[i] = x1 * c - x2 * s;
-              w[i] = x2 * c + x1 * s;
+            for (int i4 = 0; i4 < 8; ++i4) {
+              const float4 c4 = cr[i4], s4 = sr[i4];
+              const float cs[4] = {c4.x, c4.y, c4.z, c4.w};
+              const float sn[4] = {s4.x, s4.y, s4.z, s4.w};
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                const int i = 4 * i4 + e;
+                const float x1 = v[i], x2 = w[i];
+                v[i] = x1 * cs[e] - x2 * sn[e];
+                w[i] = x2 * cs[e] + x1 * sn[e];
+              }
             }
           }
-          __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(a.out) + row * a.ldo + hcol;
-          store_bf16_32(dst + j, v, 32);
-          store_bf16_32(dst + half + j, w, 32);
+          uint8_t* s = st.acquire();
+          stage_bf16(s, v, 1.f);
+          issue_store(tm_out, s, hcol + j, row0, ST_STORE);
+          st.release();
+          s = st.acquire();
+          stage_bf16(s, w, 1.f);
+          issue_store(tm_out, s, hcol + half + j, row0, ST_STORE);
+          st.release();
         }
       }
       break;
     }
     case EPI_CE_FWD: {
-      const int n0 = nb * BN;
       float mx = -INFINITY, se = 0.f;
       const int64_t tgt = row_ok ? a.targets[row] : -1;
 #pragma unroll 1
       for (int c = 0; c < BN; c += 32) {
         tmem_load_f32(tacc + c, v);
-        const int col = n0 + c;
+        const int col = nb * BN + c;
         const int valid = min(32, a.N - col);
-        if (!row_ok || valid <= 0) continue;
+        if (valid <= 0) continue;
         float cm = -INFINITY;
 #pragma unroll
-        for (int i = 0; i < 32; ++i)
-          if (i < valid) cm = fmaxf(cm, v[i]);
+        for (int i = 0; i < 32; ++i) cm = fmaxf(cm, i < valid ? v[i] : -INFINITY);
         const float nm = fmaxf(mx, cm);
         float s = 0.f;
 #pragma unroll
-        for (int i = 0; i < 32; ++i)
-          if (i < valid) s += __expf(v[i] - nm);
+        for (int i = 0; i < 32; ++i) s += i < valid ? __expf(v[i] - nm) : 0.f;
         se = se * __expf(mx - nm) + s;
         mx = nm;
         if (tgt >= col && tgt < col + valid) {
           float t = 0.f;
 #pragma unroll
-          for (int i = 0; i < 32; ++i)
-            if (tgt == col + i) t = v[i];
+          for (int i = 0; i < 32; ++i) t = (tgt == col + i) ? v[i] : t;
           a.tlogit[row] = t;
         }
       }
       if (row_ok) {
-        a.pmax[(long)nb * a.M + row] = mx;
-        a.psum[(long)nb * a.M + row] = se;
+        a.pmax[static_cast<long>(nb) * a.M + row] = mx;
+        a.psum[static_cast<long>(nb) * a.M + row] = se;
       }
       break;
     }
     case EPI_CE_BWD: {
-      const int n0 = nb * BN;
       float l = 0.f, scale = 0.f, zf = 1.f;
       int64_t tgt = -1;
       if (row_ok) {
@@ -327,16 +299,18 @@ __device__ void run_epilogue(const GemmArgs& a, uint32_t tacc, int row, int mb, 
 #pragma unroll 1
       for (int c = 0; c < BN; c += 32) {
         tmem_load_f32(tacc + c, v);
-        const int col = n0 + c;
-        const int valid = min(32, a.N - col);
-        if (!row_ok || valid <= 0) continue;
+        const int col = nb * BN + c;
+        if (col >= a.N) continue;
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
           float g = __expf(v[i] - l) * zf;
-          if (tgt == col + i) g -= 1.f;
+          g -= (tgt == col + i) ? 1.f : 0.f;
           v[i] = g * scale;
         }
-        store_bf16_32(reinterpret_cast<__nv_bfloat16*>(a.out) + row * a.ldo + col, v, valid);
+        uint8_t* s = st.acquire();
+        stage_bf16(s, v, 1.f);
+        issue_store(tm_out, s, col, row0, ST_STORE);
+        st.release();
       }
       break;
     }
@@ -349,6 +323,7 @@ __device__ void run_epilogue(const GemmArgs& a, uint32_t tacc, int row, int mb, 
 template <int BN, bool A_MN, bool B_MN>
 __global__ void __launch_bounds__(192, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
+                   const __grid_constant__ CUtensorMap tm_out, const __grid_constant__ CUtensorMap tm_aux,
                    const GemmArgs args) {
   using C = GemmCfg<BN>;
   constexpr uint32_t IDESC = idesc_bf16_f32(C::BM, BN, A_MN, B_MN);
@@ -396,8 +371,7 @@ __global__ void __launch_bounds__(192, 1)
     if (lane == 0) {
       int stage = 0;
       uint32_t phase = 0;
-      int issued[C::STAGES];
-      for (int s = 0; s < C::STAGES; ++s) issued[s] = -1;
+      uint32_t issued_mask = 0, issued_phase = 0;  // per stage: has a load, its phase
       bool ok = true;
       for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
         int mb, nb, sp;
@@ -431,7 +405,8 @@ __global__ void __launch_bounds__(192, 1)
 #pragma unroll
             for (int j = 0; j < BN / 64; ++j) tma_load_2d(sb + j * 8192, &tma_b, bar, nb * BN + j * 64, k0);
           }
-          issued[stage] = phase;
+          issued_mask |= 1u << stage;
+          issued_phase = (issued_phase & ~(1u << stage)) | (phase << stage);
           if (++stage == C::STAGES) {
             stage = 0;
             phase ^= 1;
@@ -441,7 +416,7 @@ __global__ void __launch_bounds__(192, 1)
       if (!ok) {
         // Drain: wait (bounded, once more) for the copies this thread issued.
         for (int s = 0; s < C::STAGES; ++s)
-          if (issued[s] >= 0) mbar_wait(&full_bar[s], issued[s], args.status, 102, nullptr);
+          if (issued_mask & (1u << s)) mbar_wait(&full_bar[s], (issued_phase >> s) & 1u, args.status, 102, nullptr);
       }
     }
   } else if (warp == 1) {
@@ -490,6 +465,7 @@ __global__ void __launch_bounds__(192, 1)
     }
   } else {
     const int q = warp & 3;
+    Stager st{smem + C::EPI_OFF + q * kEpiWarpBytes, 0};
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
@@ -497,15 +473,17 @@ __global__ void __launch_bounds__(192, 1)
       tile_coords(args, tile, mb, nb, sp);
       if (!mbar_wait_warp(&accf_bar[acc], acc_phase, args.status, 106, &abort_sh)) break;
       tc_fence_after();
-      const int row = mb * C::BM + q * 32 + lane;
       const uint32_t tacc = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN;
-      run_epilogue<BN>(args, tacc, row, mb, nb);
+      run_epilogue<BN>(args, &tm_out, &tm_aux, st, tacc, mb * C::BM + q * 32, nb);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acce_bar[acc]);
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1;
     }
+    // Bulk stores must have read their staging slots (and be complete) before exit.
+    if (lane == 0) bulk_wait_all<0>();
+    __syncwarp();
   }
   tc_fence_before();
   __syncthreads();
@@ -517,41 +495,53 @@ __global__ void __launch_bounds__(192, 1)
 
 // ------------------------------------ host ----------------------------------------
 template <int BN, bool A_MN, bool B_MN>
-static void launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& args, int grid,
-                        cudaStream_t stream) {
+static void launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& to, const CUtensorMap& tx,
+                        const GemmArgs& args, int grid, cudaStream_t stream) {
   using C = GemmCfg<BN>;
   auto kern = gemm_tc_kernel<BN, A_MN, B_MN>;
   static bool configured[64] = {false};
   int dev = 0;
-  cudaGetDevice(&dev);
+  PB_CUDA_CHECK(cudaGetDevice(&dev));
   if (!configured[dev]) {
     PB_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES));
     configured[dev] = true;
   }
-  kern<<<grid, 192, C::SMEM_BYTES, stream>>>(ta, tb, args);
+  kern<<<grid, 192, C::SMEM_BYTES, stream>>>(ta, tb, to, tx, args);
   PB_CUDA_CHECK(cudaGetLastError());
 }
 
 template <int BN>
-static void dispatch_major(bool a_mn, bool b_mn, const CUtensorMap& ta, const CUtensorMap& tb,
-                           const GemmArgs& args, int grid, cudaStream_t s) {
-  if (!a_mn && !b_mn) launch_gemm<BN, false, false>(ta, tb, args, grid, s);
-  else if (!a_mn && b_mn) launch_gemm<BN, false, true>(ta, tb, args, grid, s);
-  else if (a_mn && b_mn) launch_gemm<BN, true, true>(ta, tb, args, grid, s);
-  else launch_gemm<BN, true, false>(ta, tb, args, grid, s);
+static void dispatch_major(bool a_mn, bool b_mn, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& to,
+                           const CUtensorMap& tx, const GemmArgs& args, int grid, cudaStream_t s) {
+  if (!a_mn && !b_mn) launch_gemm<BN, false, false>(ta, tb, to, tx, args, grid, s);
+  else if (!a_mn && b_mn) launch_gemm<BN, false, true>(ta, tb, to, tx, args, grid, s);
+  else if (a_mn && b_mn) launch_gemm<BN, true, true>(ta, tb, to, tx, args, grid, s);
+  else launch_gemm<BN, true, false>(ta, tb, to, tx, args, grid, s);
 }
 
 static const void* opt_ptr(const c10::optional<at::Tensor>& t) { return t.has_value() ? t->data_ptr() : nullptr; }
 
+// Epilogue box over a 2-D output view: 32 x 32 elements, 128B (fp32) or 64B (bf16) swizzle.
+static CUtensorMap epi_map(const at::Tensor& t) {
+  TORCH_CHECK(t.dim() == 2 && t.stride(1) == 1, "gemm_tc: epilogue tensors must be 2-D row-major");
+  TORCH_CHECK((t.stride(0) * t.element_size()) % 16 == 0 && reinterpret_cast<uintptr_t>(t.data_ptr()) % 16 == 0,
+              "gemm_tc: epilogue tensor rows must be 16B aligned");
+  const bool f32 = t.scalar_type() == at::kFloat;
+  TORCH_CHECK(f32 || t.scalar_type() == at::kBFloat16, "gemm_tc: epilogue tensors are fp32 or bf16");
+  return make_tmap_2d(t.data_ptr(), f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
+                      t.size(1), t.size(0), t.stride(0) * t.element_size(), 32, 32,
+                      f32 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B);
+}
+
 // Python-facing entry.  ``a``/``b`` are 2-D bf16 views with unit inner stride; M, N, K
 // are the logical GEMM sizes (for SWIGLU N = 2F and ``b`` is the [2F, K] gate|up matrix).
 void gemm_tc(at::Tensor a, at::Tensor b, at::Tensor out, int64_t M, int64_t N, int64_t K, bool a_mn, bool b_mn,
-             int64_t epi, int64_t bn, int64_t splits, int64_t max_ctas, double alpha, bool beta,
-             c10::optional<at::Tensor> res, c10::optional<at::Tensor> aux, c10::optional<at::Tensor> aux2,
-             c10::optional<at::Tensor> pos, c10::optional<at::Tensor> cos_t, c10::optional<at::Tensor> sin_t,
-             int64_t head_dim, int64_t n_rope_cols, c10::optional<at::Tensor> targets,
-             c10::optional<at::Tensor> pmax, c10::optional<at::Tensor> psum, c10::optional<at::Tensor> tlogit,
-             c10::optional<at::Tensor> lse, c10::optional<at::Tensor> row_scale, double z_coeff) {
+             int64_t epi, int64_t bn, int64_t splits, int64_t max_ctas, double alpha,
+             c10::optional<at::Tensor> aux, c10::optional<at::Tensor> pos, c10::optional<at::Tensor> cos_t,
+             c10::optional<at::Tensor> sin_t, int64_t head_dim, int64_t n_rope_cols,
+             c10::optional<at::Tensor> targets, c10::optional<at::Tensor> pmax, c10::optional<at::Tensor> psum,
+             c10::optional<at::Tensor> tlogit, c10::optional<at::Tensor> lse, c10::optional<at::Tensor> row_scale,
+             double z_coeff) {
   TORCH_CHECK(a.is_cuda() && b.is_cuda(), "gemm_tc: CUDA tensors required");
   TORCH_CHECK(a.scalar_type() == at::kBFloat16 && b.scalar_type() == at::kBFloat16, "gemm_tc: bf16 operands");
   TORCH_CHECK(a.dim() == 2 && b.dim() == 2 && a.stride(1) == 1 && b.stride(1) == 1, "gemm_tc: 2-D row-major");
@@ -577,7 +567,7 @@ void gemm_tc(at::Tensor a, at::Tensor b, at::Tensor out, int64_t M, int64_t N, i
   g.M = (int)M;
   g.N = (int)N;
   g.K = (int)K;
-  g.F = swiglu || epi == EPI_SWIGLU_BWD ? (int)(swiglu ? N / 2 : N) : 0;
+  g.F = swiglu ? (int)(N / 2) : 0;
   g.m_tiles = (int)((M + 127) / 128);
   g.n_tiles = swiglu ? (int)((N / 2 + bn / 2 - 1) / (bn / 2)) : (int)((N + bn - 1) / bn);
   g.k_blocks = (int)((K + 63) / 64);
@@ -586,15 +576,6 @@ void gemm_tc(at::Tensor a, at::Tensor b, at::Tensor out, int64_t M, int64_t N, i
   g.splits = (g.k_blocks + g.kb_per_split - 1) / g.kb_per_split;
   g.epi = (int)epi;
   g.alpha = (float)alpha;
-  g.beta = beta ? 1 : 0;
-  g.out = out.data_ptr();
-  g.ldo = out.dim() == 2 ? out.stride(0) : 0;
-  g.res = static_cast<const float*>(opt_ptr(res));
-  g.ldr = res.has_value() ? res->stride(0) : 0;
-  g.aux = const_cast<void*>(opt_ptr(aux));
-  g.ldaux = aux.has_value() ? aux->stride(0) : 0;
-  g.aux2 = const_cast<void*>(opt_ptr(aux2));
-  g.ldaux2 = aux2.has_value() ? aux2->stride(0) : 0;
   g.pos = static_cast<const int*>(opt_ptr(pos));
   g.cos_t = static_cast<const float*>(opt_ptr(cos_t));
   g.sin_t = static_cast<const float*>(opt_ptr(sin_t));
@@ -612,15 +593,27 @@ void gemm_tc(at::Tensor a, at::Tensor b, at::Tensor out, int64_t M, int64_t N, i
   if (epi == EPI_ROPE) {
     TORCH_CHECK(head_dim % 64 == 0 && bn % head_dim == 0, "gemm_tc: RoPE needs head_dim % 64 == 0 and bn % head_dim == 0");
     TORCH_CHECK(N % head_dim == 0, "gemm_tc: RoPE output width must be whole heads");
+    TORCH_CHECK(cos_t.has_value() && sin_t.has_value() && pos.has_value(), "gemm_tc: RoPE tables");
   }
-  if (epi == EPI_SWIGLU) TORCH_CHECK((N / 2) % 8 == 0, "gemm_tc: SWIGLU F must be a multiple of 8");
-  if (g.splits > 1) TORCH_CHECK(epi == EPI_ATOMIC_F32, "gemm_tc: split-K needs the ATOMIC_F32 epilogue");
-  TORCH_CHECK(epi == EPI_CE_FWD || epi == EPI_ATOMIC_F32 || out.stride(-1) == 1, "gemm_tc: output must be row-major");
+  if (swiglu) {
+    TORCH_CHECK((N / 2) % 32 == 0, "gemm_tc: SWIGLU F must be a multiple of 32");
+    TORCH_CHECK(aux.has_value() && aux->size(1) == N && aux->size(0) == M, "gemm_tc: SWIGLU saves g|u in aux [M, 2F]");
+  }
+  if (g.splits > 1) TORCH_CHECK(epi == EPI_ADD_F32, "gemm_tc: split-K needs the ADD_F32 epilogue");
+  const bool has_out = epi != EPI_CE_FWD;
+  CUtensorMap to{}, tx{};
+  if (has_out) {
+    TORCH_CHECK(out.dim() == 2 && out.size(0) == M, "gemm_tc: out rows");
+    TORCH_CHECK(out.size(1) == (swiglu ? N / 2 : N), "gemm_tc: out columns");
+    TORCH_CHECK((epi == EPI_F32 || epi == EPI_ADD_F32) == (out.scalar_type() == at::kFloat),
+                "gemm_tc: fp32 output for F32/ADD_F32 epilogues, bf16 otherwise");
+    to = epi_map(out);
+  }
+  if (swiglu) tx = epi_map(*aux);
 
-  // TMA descriptors: 128-byte swizzle, 64-element (128 B) inner box.
-  const int bm_box = 128;
+  // Operand TMA descriptors: 128-byte swizzle, 64-element (128 B) inner box.
   CUtensorMap ta = a_mn ? make_tmap_bf16_2d(a.data_ptr(), M, K, a.stride(0) * 2, 64, 64)
-                        : make_tmap_bf16_2d(a.data_ptr(), K, M, a.stride(0) * 2, 64, bm_box);
+                        : make_tmap_bf16_2d(a.data_ptr(), K, M, a.stride(0) * 2, 64, 128);
   CUtensorMap tb;
   if (b_mn) tb = make_tmap_bf16_2d(b.data_ptr(), N, K, b.stride(0) * 2, 64, 64);
   else tb = make_tmap_bf16_2d(b.data_ptr(), K, N, b.stride(0) * 2, 64, swiglu ? bn / 2 : bn);
@@ -630,9 +623,9 @@ void gemm_tc(at::Tensor a, at::Tensor b, at::Tensor out, int64_t M, int64_t N, i
   if (max_ctas > 0) grid = std::min<int>(grid, (int)max_ctas);
   grid = std::max(grid, 1);
   cudaStream_t stream = at::cuda::getCurrentCUDAStream();
-  if (bn == 256) dispatch_major<256>(a_mn, b_mn, ta, tb, g, grid, stream);
-  else if (bn == 128) dispatch_major<128>(a_mn, b_mn, ta, tb, g, grid, stream);
-  else dispatch_major<64>(a_mn, b_mn, ta, tb, g, grid, stream);
+  if (bn == 256) dispatch_major<256>(a_mn, b_mn, ta, tb, to, tx, g, grid, stream);
+  else if (bn == 128) dispatch_major<128>(a_mn, b_mn, ta, tb, to, tx, g, grid, stream);
+  else dispatch_major<64>(a_mn, b_mn, ta, tb, to, tx, g, grid, stream);
 }
 
 }  // namespace pb

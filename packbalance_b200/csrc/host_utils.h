@@ -50,6 +50,23 @@ inline CUtensorMap make_tmap_bf16_2d(const void* ptr, int64_t inner, int64_t out
   return m;
 }
 
+// General 2-D tensor map (epilogue staging boxes): dtype, swizzle chosen by caller.
+inline CUtensorMap make_tmap_2d(const void* ptr, CUtensorMapDataType dtype, int64_t inner, int64_t outer,
+                                int64_t row_bytes, uint32_t box_inner, uint32_t box_outer,
+                                CUtensorMapSwizzle swizzle) {
+  CUtensorMap m;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(inner), static_cast<cuuint64_t>(outer)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(row_bytes)};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = tmap_encoder()(&m, dtype, 2, const_cast<void*>(ptr), dims, strides, box, estr,
+                              CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  TORCH_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled failed (", static_cast<int>(r), ") inner=", inner,
+              " outer=", outer, " pitch=", row_bytes);
+  return m;
+}
+
 inline int num_sms(int dev) {
   static int cache[64] = {0};
   if (cache[dev] == 0) PB_CUDA_CHECK(cudaDeviceGetAttribute(&cache[dev], cudaDevAttrMultiProcessorCount, dev));

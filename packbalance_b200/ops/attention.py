@@ -37,7 +37,8 @@ def doc_end_from_start(doc_start: torch.Tensor) -> torch.Tensor:
 
 def attention_plan(doc_start: torch.Tensor, n_heads: int, n_kv_heads: int) -> dict[str, torch.Tensor]:
     """Cost-ordered work lists: ``fwd`` int32 [nq*H, 2] = (q tile, head);
-    ``bwd`` int32 [nk*Hkv, 3] = (kv tile, kv head, last q tile)."""
+    ``bwd`` int32 [nk*H, 3] = (kv tile, q head, last q tile).  The GQA heads of a kv
+    head are separate backward items; their dK/dV add up in an fp32 accumulator."""
     dev = doc_start.device
     t = doc_start.numel()
     n_tiles = -(-t // TILE)
@@ -55,9 +56,8 @@ def attention_plan(doc_start: torch.Tensor, n_heads: int, n_kv_heads: int) -> di
     q_hi = de[last_row] // TILE
     k_cost = q_hi - tiles + 1
     korder = torch.argsort(k_cost, descending=True, stable=True)
-    kv_heads = torch.arange(n_kv_heads, device=dev, dtype=torch.int64)
     bwd = torch.stack(
-        [korder.repeat_interleave(n_kv_heads), kv_heads.repeat(n_tiles), q_hi[korder].repeat_interleave(n_kv_heads)],
+        [korder.repeat_interleave(n_heads), heads.repeat(n_tiles), q_hi[korder].repeat_interleave(n_heads)],
         dim=1,
     ).to(torch.int32).contiguous()
     return {"fwd": fwd, "bwd": bwd, "doc_start": doc_start.to(torch.int32).contiguous()}
@@ -83,15 +83,19 @@ def attn_backward_packed(
     n_heads: int,
     n_kv_heads: int,
     head_dim: int,
+    rope: tuple | None = None,
 ) -> torch.Tensor:
-    """Returns dqkv ``[T, (H + 2 Hkv) * D]`` bf16 (gradient w.r.t. the post-RoPE q/k)."""
+    """Returns dqkv ``[T, (H + 2 Hkv) * D]`` bf16.  With ``rope = (pos, cos, sin)`` the q
+    and k gradients are rotated back to the pre-RoPE frame (the gradient w.r.t. the QKV
+    GEMM output); without it they are w.r.t. the rotated q/k."""
     t = qkv.shape[0]
     dqkv = torch.empty_like(qkv)
-    dq_acc = torch.zeros(t, n_heads * head_dim, device=qkv.device, dtype=torch.float32)
+    dq_acc = torch.empty(t, n_heads * head_dim, device=qkv.device, dtype=torch.float32)
+    dkv_acc = torch.empty(t, 2 * n_kv_heads * head_dim, device=qkv.device, dtype=torch.float32)
     delta = torch.empty(n_heads, t, device=qkv.device, dtype=torch.float32)
     _native.module().attn_bwd(
         qkv, out, dout.contiguous(), lse, plan["doc_start"], plan["bwd"], n_heads, n_kv_heads, head_dim,
-        1.0 / math.sqrt(head_dim), dqkv, dq_acc, delta,
+        1.0 / math.sqrt(head_dim), dqkv, dq_acc, dkv_acc, delta, *(rope if rope is not None else (None, None, None)),
     )
     return dqkv
 

@@ -21,7 +21,7 @@ from __future__ import annotations
 import torch
 
 from packbalance_b200.ops import _native
-from packbalance_b200.ops.gemm import EPI_CE_BWD, EPI_CE_FWD, EPI_F32, gemm, pick_bn, sm_count
+from packbalance_b200.ops.gemm import EPI_ADD_F32, EPI_CE_BWD, EPI_CE_FWD, EPI_F32, gemm, linear_wgrad, pick_tiling, sm_count
 from packbalance_b200.ops.reference import chunked_linear_cross_entropy
 
 CE_TILE = 256
@@ -76,9 +76,13 @@ def lmhead_ce_backward(
         dl = dlog[:rows]
         gemm(x[r0:r1], w, dl, rows, v, d, epi=EPI_CE_BWD, bn=CE_TILE, targets=tgt[r0:r1], lse=lse[r0:r1],
              row_scale=scale[r0:r1], z_coeff=z_coeff)
-        gemm(dl, w, dx[r0:r1], rows, d, v, b_mn=True, epi=EPI_F32, bn=pick_bn(rows, d, sms))
-        gemm(dl, x[r0:r1], dw_out, v, d, rows, a_mn=True, b_mn=True, epi=EPI_F32,
-             beta=accumulate_dw or i > 0, bn=pick_bn(v, d, sms))
+        bn, splits = pick_tiling(rows, d, v, sms)
+        if splits > 1:
+            dx[r0:r1].zero_()
+            gemm(dl, w, dx[r0:r1], rows, d, v, b_mn=True, epi=EPI_ADD_F32, bn=bn, splits=splits)
+        else:
+            gemm(dl, w, dx[r0:r1], rows, d, v, b_mn=True, epi=EPI_F32, bn=bn)
+        linear_wgrad(dl, x[r0:r1], dw_out, accumulate=accumulate_dw or i > 0)
     return dx
 
 

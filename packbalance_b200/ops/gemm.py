@@ -1,4 +1,4 @@
-"""Python side of the tcgen05 GEMM: tile-width choice, split-K and the Linear
+"""Python side of the tcgen05 GEMM: tile-width / split-K choice and the Linear
 forward / dgrad / wgrad entry points.
 
 Operand conventions (all bf16, unit inner stride, 16-byte aligned rows):
@@ -16,7 +16,8 @@ import torch
 
 from packbalance_b200.ops import _native
 
-EPI_BF16, EPI_F32, EPI_RESID, EPI_SWIGLU, EPI_ROPE, EPI_SWIGLU_BWD, EPI_ATOMIC_F32, EPI_CE_FWD, EPI_CE_BWD = range(9)
+EPI_BF16, EPI_F32, EPI_ADD_F32, EPI_SWIGLU, EPI_ROPE = 0, 1, 2, 3, 4
+EPI_CE_FWD, EPI_CE_BWD = 7, 8
 
 _SM_COUNT: dict[int, int] = {}
 
@@ -28,25 +29,39 @@ def sm_count(device: torch.device) -> int:
     return _SM_COUNT[idx]
 
 
+# Relative tensor-pipe efficiency of a 128 x BN tile (narrow tiles reload the A tile
+# more often per FLOP and issue more, smaller MMAs), measured on the bench shapes.
+_TILE_EFF = {256: 1.0, 128: 0.75, 64: 0.45}
+
+
 def pick_bn(m: int, n: int, sms: int, allowed=(256, 128, 64)) -> int:
-    """Tile width minimising (waves x per-tile cost); per-tile cost ~ BN + 64 models
-    the fixed prologue/epilogue share of a tile."""
+    """Tile width minimising waves x per-tile time, per-tile time ~ (BN + 64) / eff(BN)."""
     best, best_cost = allowed[0], math.inf
     m_tiles = -(-m // 128)
     for bn in allowed:
         tiles = m_tiles * -(-n // bn)
-        cost = -(-tiles // sms) * (bn + 64)
+        cost = -(-tiles // sms) * (bn + 64) / _TILE_EFF[bn]
         if cost < best_cost - 1e-9:
             best, best_cost = bn, cost
     return best
 
 
-def pick_splits(m: int, n: int, k: int, bn: int, sms: int) -> int:
-    """Split-K factor so that a small output grid still fills the GPU."""
-    tiles = -(-m // 128) * -(-n // bn)
-    if tiles >= sms // 2 or k < 1024:
-        return 1
-    return max(1, min(k // 512, sms // tiles))
+def pick_tiling(m: int, n: int, k: int, sms: int, allowed=(256, 128, 64), max_splits: int = 8) -> tuple[int, int]:
+    """(BN, split-K) minimising an estimate of the busiest SM's work: per work unit
+    ``BN * (k / splits + 128)`` (the constant models the epilogue), times the number
+    of waves.  Split-K is only considered while it still adds idle SMs."""
+    best, best_cost = (allowed[0], 1), math.inf
+    m_tiles = -(-m // 128)
+    k_blocks = -(-k // 64)
+    for bn in allowed:
+        tiles = m_tiles * -(-n // bn)
+        for s in range(1, max_splits + 1):
+            if s > 1 and (k_blocks // s < 4 or tiles * (s - 1) >= sms):
+                break
+            cost = -(-(tiles * s) // sms) * bn * (k / s / _TILE_EFF[bn] + 128)
+            if cost < best_cost - 1e-9:
+                best, best_cost = (bn, s), cost
+    return best
 
 
 def gemm(
@@ -64,10 +79,7 @@ def gemm(
     splits: int = 1,
     max_ctas: int = 0,
     alpha: float = 1.0,
-    beta: bool = False,
-    res=None,
     aux=None,
-    aux2=None,
     pos=None,
     cos=None,
     sin=None,
@@ -81,12 +93,15 @@ def gemm(
     row_scale=None,
     z_coeff: float = 0.0,
 ) -> torch.Tensor:
+    """Launch the tcgen05 GEMM ``D[m, n] = sum_k A(m, k) B(n, k)`` with epilogue ``epi``."""
     if bn is None:
-        width = n // 2 if epi == EPI_SWIGLU else n
-        bn = pick_bn(m, width if epi != EPI_SWIGLU else width * 2, sm_count(a.device))
+        allowed = (256, 128, 64)
+        if epi == EPI_ROPE:
+            allowed = tuple(x for x in allowed if x % head_dim == 0)
+        bn = pick_bn(m, n, sm_count(a.device), allowed)
     _native.module().gemm_tc(
-        a, b, out, m, n, k, a_mn, b_mn, epi, bn, splits, max_ctas, alpha, beta,
-        res, aux, aux2, pos, cos, sin, head_dim, n_rope_cols, targets, pmax, psum, tlogit, lse, row_scale, z_coeff,
+        a, b, out, m, n, k, a_mn, b_mn, epi, bn, splits, max_ctas, alpha,
+        aux, pos, cos, sin, head_dim, n_rope_cols, targets, pmax, psum, tlogit, lse, row_scale, z_coeff,
     )
     return out
 
@@ -106,11 +121,18 @@ def linear_dgrad(dy: torch.Tensor, w: torch.Tensor, out_dtype: torch.dtype = tor
 
 
 def linear_wgrad(dy: torch.Tensor, x: torch.Tensor, out: torch.Tensor | None = None, accumulate: bool = False) -> torch.Tensor:
+    """``dy.T @ x`` in fp32 into ``out`` (overwritten, or added to when ``accumulate``);
+    split-K with TMA reduce-add when the output grid alone cannot fill the GPU."""
     m, n = dy.shape
     k = x.shape[1]
     if out is None:
         out = torch.empty(n, k, device=dy.device, dtype=torch.float32)
-    return gemm(dy, x, out, n, k, m, a_mn=True, b_mn=True, epi=EPI_F32, beta=accumulate)
+    bn, splits = pick_tiling(n, k, m, sm_count(dy.device))
+    if splits == 1 and not accumulate:
+        return gemm(dy, x, out, n, k, m, a_mn=True, b_mn=True, epi=EPI_F32, bn=bn)
+    if not accumulate:
+        out.zero_()
+    return gemm(dy, x, out, n, k, m, a_mn=True, b_mn=True, epi=EPI_ADD_F32, bn=bn, splits=splits)
 
 
 class _Linear(torch.autograd.Function):

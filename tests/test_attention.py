@@ -65,8 +65,8 @@ def test_attention_plan_orders_by_cost() -> None:
     # The last q tile of the 1024-token document sees 8 key tiles and comes first.
     assert fwd[0, 0].item() == 7
     bwd = plan["bwd"]
-    assert bwd.shape == (10, 3)
-    assert bwd[0].tolist() == [0, 0, 7]
+    assert bwd.shape == (10 * 2, 3)
+    assert bwd[0].tolist() == [0, 0, 7] and bwd[1].tolist() == [0, 1, 7]
 
 
 @pytest.mark.parametrize("backend", ["eager", "auto"])

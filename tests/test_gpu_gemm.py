@@ -4,9 +4,7 @@ import pytest
 import torch
 
 from packbalance_b200.ops import _native
-from packbalance_b200.ops.gemm import (
-    EPI_ATOMIC_F32, EPI_BF16, EPI_F32, EPI_RESID, EPI_ROPE, EPI_SWIGLU, EPI_SWIGLU_BWD, gemm,
-)
+from packbalance_b200.ops.gemm import EPI_ADD_F32, EPI_BF16, EPI_F32, EPI_ROPE, EPI_SWIGLU, gemm, linear_wgrad
 
 pytestmark = pytest.mark.gpu
 dev = "cuda"
@@ -40,26 +38,37 @@ def test_gemm_majors(bn, a_mn, b_mn, mnk):
     _close(out16, ref)
 
 
-def test_gemm_accumulate_residual_splitk():
+def test_gemm_accumulate_and_splitk():
     torch.manual_seed(1)
     m, n, k = 384, 256, 4096
     a, b = _bf(m, k), _bf(n, k)
     ref = a.float() @ b.float().t()
     base = torch.randn(m, n, device=dev)
     out = base.clone()
-    gemm(a, b, out, m, n, k, epi=EPI_F32, beta=True, bn=128)
+    gemm(a, b, out, m, n, k, epi=EPI_ADD_F32, bn=128)
     _close(out, base + ref, 1e-2)
-    out2 = torch.empty(m, n, device=dev)
-    gemm(a, b, out2, m, n, k, epi=EPI_RESID, res=base, bn=256)
-    _close(out2, base + ref, 1e-2)
     acc = torch.zeros(m, n, device=dev)
-    gemm(a, b, acc, m, n, k, epi=EPI_ATOMIC_F32, splits=4, bn=128)
+    gemm(a, b, acc, m, n, k, epi=EPI_ADD_F32, splits=4, bn=128)
     _close(acc, ref, 1e-2)
     _native.check_status()
 
 
+@pytest.mark.parametrize("shape", [(8192, 768, 768), (8192, 1280, 768), (8192, 768, 2048), (2048, 32000, 768)])
+@pytest.mark.parametrize("accumulate", [False, True])
+def test_linear_wgrad_splitk(shape, accumulate):
+    torch.manual_seed(4)
+    t, n, k = shape
+    dy, x = _bf(t, n), _bf(t, k)
+    ref = dy.float().t() @ x.float()
+    base = torch.randn(n, k, device=dev)
+    out = base.clone()
+    linear_wgrad(dy, x, out, accumulate=accumulate)
+    _native.check_status()
+    _close(out, ref + (base if accumulate else 0), 1e-2)
+
+
 @pytest.mark.parametrize("bn", [64, 128, 256])
-def test_gemm_swiglu_and_backward(bn):
+def test_gemm_swiglu(bn):
     torch.manual_seed(2)
     m, d, F = 320, 256, 384
     x, w = _bf(m, d), _bf(2 * F, d)
@@ -70,14 +79,12 @@ def test_gemm_swiglu_and_backward(bn):
     _close(gu, full)
     g, u = gu.float()[:, :F], gu.float()[:, F:]
     _close(h, torch.nn.functional.silu(g) * u)
-    # backward epilogue: dh = dy @ Wdown (Wdown [d, F]) then dg|du
-    dy, wd = _bf(m, d), _bf(d, F)
+    dh = _bf(m, F)
     dgu = torch.empty(m, 2 * F, device=dev, dtype=torch.bfloat16)
-    gemm(dy, wd, dgu, m, F, d, b_mn=True, epi=EPI_SWIGLU_BWD, aux=gu, aux2=dgu, bn=bn)
-    dh = dy.float() @ wd.float()
+    _native.module().swiglu_bwd_packed(dh, gu, dgu)
     s = torch.sigmoid(g)
-    _close(dgu[:, F:], dh * g * s)
-    _close(dgu[:, :F], dh * u * s * (1 + g * (1 - s)))
+    _close(dgu[:, F:], dh.float() * g * s)
+    _close(dgu[:, :F], dh.float() * u * s * (1 + g * (1 - s)))
     _native.check_status()
 
 

@@ -33,6 +33,19 @@ def test_rmsnorm_fwd_bwd():
     _native.check_status()
 
 
+def test_add_rmsnorm():
+    torch.manual_seed(0)
+    C = _native.module()
+    x = torch.randn(300, 768, device=dev)
+    delta = torch.randn(300, 768, device=dev).to(torch.bfloat16)
+    w = torch.randn(768, device=dev)
+    xo, y, rstd = C.add_rmsnorm_fwd(x, delta, w, 1e-5, True)
+    ref_x = x + delta.float()
+    torch.testing.assert_close(xo, ref_x)
+    torch.testing.assert_close(y.float(), rmsnorm_reference(ref_x, w, 1e-5), atol=2e-2, rtol=1e-2)
+    torch.testing.assert_close(rstd, torch.rsqrt(ref_x.square().mean(-1) + 1e-5), atol=1e-5, rtol=1e-5)
+
+
 def test_swiglu_fwd_bwd():
     torch.manual_seed(0)
     g, u, d = (torch.randn(64, 100, device=dev) for _ in range(3))
