@@ -60,7 +60,8 @@ struct AttnArgs {
   float scale_log2;  // softmax scale * log2(e)
   float scale;
   const int* doc_start;
-  const int* items;  // fwd: [n, 2] (q tile, head); bwd: [n, 3] (kv tile, kv head, last q tile)
+  const int* doc_end;  // last token of the document containing each token (backward)
+  const int* items;  // fwd: [n, 3] (q tile, head, first kv tile); bwd: [n, 3] (kv tile, head, last q tile)
   int n_items;
   __nv_bfloat16* out;  // fwd output [T, H*D]
   float* lse;          // [H, T] natural-log LSE
@@ -70,19 +71,26 @@ struct AttnArgs {
 };
 
 // =================================== forward ======================================
+// Two softmax warpgroups per query tile: group g owns key columns [64g, 64g + 64) of
+// every 128-wide key tile and runs its own online softmax (max, sum) with its own O
+// accumulator in TMEM; the two partial results are merged once at the end.  This
+// doubles the softmax warps per SM without any per-tile exchange between them.
 template <int D>
 struct FwdCfg {
   static constexpr int TILE_BYTES = 128 * D * 2;  // one 128-row tile of Q, K or V
   static constexpr int Q_OFF = 0;
   static constexpr int K_OFF = TILE_BYTES;             // 2 stages
   static constexpr int V_OFF = K_OFF + 2 * TILE_BYTES;  // 2 stages
+  static constexpr int STAT_OFF = V_OFF + 2 * TILE_BYTES;  // group-1 (max, sum) per row
   // At least 120 KB so that a second CTA (which would block in tcgen05.alloc on
   // the fully allocated TMEM) is never co-scheduled on the same SM.
-  static constexpr int SMEM_USED = V_OFF + 2 * TILE_BYTES + 1024;
+  static constexpr int SMEM_USED = STAT_OFF + 1024 + 1024;
   static constexpr int SMEM = SMEM_USED > 122880 ? SMEM_USED : 122880;
-  static constexpr uint32_t S_COL = 0;    // two S buffers: 0, 128
-  static constexpr uint32_t P_COL = 256;  // two P buffers (bf16 packed): 256, 320
-  static constexpr uint32_t O_COL = 384;  // D columns
+  static constexpr int S_BUFS = D == 64 ? 2 : 1;
+  static constexpr uint32_t S_COL = 0;                 // S_BUFS x 128 columns
+  static constexpr uint32_t P_COL = S_BUFS * 128;      // P[group][2] x 32 columns (64 bf16)
+  static constexpr uint32_t O_COL = P_COL + 128;       // O[group] x D columns
+  static_assert(O_COL + 2 * D <= 512, "TMEM budget");
   static constexpr uint32_t IDESC_S = idesc_bf16_f32(128, 128, false, false);
   static constexpr uint32_t IDESC_O = idesc_bf16_f32(128, D, false, true);
 };
@@ -93,12 +101,16 @@ __device__ __forceinline__ void load_tile_rows(void* dst, const CUtensorMap* map
     tma_load_2d(static_cast<uint8_t*>(dst) + c * 16384, map, bar, col0 + c * 64, row0);
 }
 
+__device__ __forceinline__ int3 ld_item(const int* items, int i) {
+  return make_int3(items[3 * i], items[3 * i + 1], items[3 * i + 2]);
+}
+
 template <int D>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(320, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tmap, const AttnArgs args) {
   using C = FwdCfg<D>;
-  __shared__ __align__(8) uint64_t q_full, q_empty, kv_full[2], kv_empty[2], s_full[2], p_ready, o_done, o_free,
-      drain_bar;
+  __shared__ __align__(8) uint64_t q_full, q_empty, kv_full[2], kv_empty[2], s_full[2], s_free, p_ready[2],
+      o_done[2], o_free, stats_ready, drain_bar;
   __shared__ uint32_t tmem_sh;
   __shared__ volatile int abort_sh;
   extern __shared__ uint8_t dyn[];
@@ -111,10 +123,12 @@ __global__ void __launch_bounds__(192, 1)
       mbar_init(&kv_full[i], 1);
       mbar_init(&kv_empty[i], 1);
       mbar_init(&s_full[i], 1);
+      mbar_init(&p_ready[i], 4);
+      mbar_init(&o_done[i], 1);
     }
-    mbar_init(&p_ready, 4);
-    mbar_init(&o_done, 1);
+    mbar_init(&s_free, 8);
     mbar_init(&o_free, 4);
+    mbar_init(&stats_ready, 4);
     mbar_init(&drain_bar, 1);
     abort_sh = 0;
     fence_mbar_init();
@@ -135,11 +149,12 @@ __global__ void __launch_bounds__(192, 1)
     if (lane == 0) {
       uint32_t kv_it = 0, q_it = 0;
       bool ok = true;
+      int3 nx = blockIdx.x < args.n_items ? ld_item(args.items, blockIdx.x) : make_int3(0, 0, 0);
       for (int it = blockIdx.x; it < args.n_items && ok; it += gridDim.x) {
-        const int qt = args.items[2 * it], h = args.items[2 * it + 1];
+        const int qt = nx.x, h = nx.y, kt0 = nx.z;
+        if (it + (int)gridDim.x < args.n_items) nx = ld_item(args.items, it + gridDim.x);
         const int hk = h / group;
         const int q0 = qt * 128;
-        const int kt0 = args.doc_start[q0] / 128;
         if (!mbar_wait(&q_empty, (q_it & 1) ^ 1, args.status, 201, &abort_sh)) break;
         mbar_arrive_expect_tx(&q_full, C::TILE_BYTES);
         load_tile_rows(smem + C::Q_OFF, &tmap, &q_full, h * D, q0, D);
@@ -158,18 +173,17 @@ __global__ void __launch_bounds__(192, 1)
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      uint32_t kv_it = 0, q_it = 0, p_it = 0, item_n = 0;
+      uint32_t kv_it = 0, q_it = 0, item_n = 0;
+      uint32_t p_it[2] = {0, 0};
       bool ok = true;
       const uint32_t qa = smem_u32(smem + C::Q_OFF);
+      int3 nx = blockIdx.x < args.n_items ? ld_item(args.items, blockIdx.x) : make_int3(0, 0, 0);
       for (int it = blockIdx.x; it < args.n_items && ok; it += gridDim.x, ++item_n) {
-        const int qt = args.items[2 * it];
-        const int q0 = qt * 128;
-        const int kt0 = args.doc_start[q0] / 128;
+        const int qt = nx.x, kt0 = nx.z;
+        if (it + (int)gridDim.x < args.n_items) nx = ld_item(args.items, it + gridDim.x);
         const int nkv = qt - kt0 + 1;
         if (!mbar_wait(&q_full, q_it & 1, args.status, 203, &abort_sh)) break;
         ++q_it;
-        // O of the previous item must have been read out before it is overwritten.
-        if (!mbar_wait(&o_free, (item_n & 1) ^ 1, args.status, 204, &abort_sh)) break;
         tc_fence_after();
         for (int j = 0; j <= nkv && ok; ++j) {
           if (j < nkv) {
@@ -179,34 +193,49 @@ __global__ void __launch_bounds__(192, 1)
               ok = false;
               break;
             }
+            // With one S buffer, both groups must have read S_{g-1}.
+            if (C::S_BUFS == 1 && g > 0 && !mbar_wait(&s_free, (g - 1) & 1, args.status, 211, &abort_sh)) {
+              ok = false;
+              break;
+            }
             tc_fence_after();
             const uint32_t ka = smem_u32(smem + C::K_OFF + s * C::TILE_BYTES);
-            const uint32_t sb = tmem + C::S_COL + (g & 1) * 128;
+            const uint32_t sb = tmem + C::S_COL + (g % C::S_BUFS) * 128;
 #pragma unroll
             for (int kk = 0; kk < D / 16; ++kk) {
               const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
               umma_ss(sb, sdesc_sw128(qa + off, 16, 1024), sdesc_sw128(ka + off, 16, 1024), C::IDESC_S,
                       kk > 0 ? 1u : 0u);
             }
-            umma_commit(&s_full[g & 1]);
+            umma_commit(&s_full[g % C::S_BUFS]);
             if (j == nkv - 1) umma_commit(&q_empty);
           }
           if (j > 0) {
             const uint32_t g = kv_it + j - 1;
-            if (!mbar_wait(&p_ready, p_it & 1, args.status, 206, &abort_sh)) {
+            const int s = g & 1;
+            const uint32_t va = smem_u32(smem + C::V_OFF + s * C::TILE_BYTES);
+            // The first PV overwrites O: the previous item's O must have been read out.
+            if (j == 1 && !mbar_wait(&o_free, (item_n & 1) ^ 1, args.status, 204, &abort_sh)) {
               ok = false;
               break;
             }
-            ++p_it;
-            tc_fence_after();
-            const int s = g & 1;
-            const uint32_t va = smem_u32(smem + C::V_OFF + s * C::TILE_BYTES);
-            const uint32_t pa = tmem + C::P_COL + (g & 1) * 64;
 #pragma unroll
-            for (int kk = 0; kk < 8; ++kk)
-              umma_ts(tmem + C::O_COL, pa + kk * 8, sdesc_sw128(va + kk * 2048, 16384, 1024), C::IDESC_O,
-                      (j > 1 || kk > 0) ? 1u : 0u);
-            umma_commit(&o_done);
+            for (int grp = 0; grp < 2; ++grp) {
+              if (!mbar_wait(&p_ready[grp], p_it[grp] & 1, args.status, 206, &abort_sh)) {
+                ok = false;
+                break;
+              }
+              ++p_it[grp];
+              tc_fence_after();
+              const uint32_t pa = tmem + C::P_COL + (grp * 2 + (g & 1)) * 32;
+#pragma unroll
+              for (int kk = 0; kk < 4; ++kk)
+                umma_ts(tmem + C::O_COL + grp * D, pa + kk * 8,
+                        sdesc_sw128(va + grp * 8192 + kk * 2048, 16384, 1024), C::IDESC_O,
+                        (j > 1 || kk > 0) ? 1u : 0u);
+              umma_commit(&o_done[grp]);
+            }
+            if (!ok) break;
             umma_commit(&kv_empty[s]);
           }
         }
@@ -216,45 +245,58 @@ __global__ void __launch_bounds__(192, 1)
       mbar_wait(&drain_bar, 0, args.status, 207, nullptr);
     }
   } else {
+    // ---------------- softmax groups (thread = query row) ----------------
+    const int grp = (warp - 2) / 4;  // 0: key columns 0-63, 1: key columns 64-127
     const int q4 = warp & 3;
     const int r = q4 * 32 + lane;
     const uint32_t lane_off = static_cast<uint32_t>(q4 * 32) << 16;
-    uint32_t kv_it = 0, o_it = 0, p_cnt = 0;
-    for (int it = blockIdx.x; it < args.n_items; it += gridDim.x) {
-      const int qt = args.items[2 * it], h = args.items[2 * it + 1];
+    float* stats = reinterpret_cast<float*>(smem + C::STAT_OFF);
+    uint32_t kv_it = 0, o_it = 0, item_n = 0;
+    int3 nx = blockIdx.x < args.n_items ? ld_item(args.items, blockIdx.x) : make_int3(0, 0, 0);
+    int nlo = (blockIdx.x < args.n_items && nx.x * 128 + r < T) ? args.doc_start[nx.x * 128 + r] : 0x7fffffff;
+    for (int it = blockIdx.x; it < args.n_items; it += gridDim.x, ++item_n) {
+      const int qt = nx.x, h = nx.y, kt0 = nx.z;
+      const int lo = nlo;
+      if (it + (int)gridDim.x < args.n_items) {
+        nx = ld_item(args.items, it + gridDim.x);
+        nlo = nx.x * 128 + r < T ? args.doc_start[nx.x * 128 + r] : 0x7fffffff;
+      }
       const int q0 = qt * 128;
-      const int kt0 = args.doc_start[q0] / 128;
       const int nkv = qt - kt0 + 1;
       const int q = q0 + r;
       const bool qok = q < T;
-      const int lo = qok ? args.doc_start[q] : 0x7fffffff;
       float m = -INFINITY, l = 0.f;
       bool ok = true;
       for (int j = 0; j < nkv; ++j) {
         const uint32_t g = kv_it + j;
-        if (!mbar_wait_warp(&s_full[g & 1], (g >> 1) & 1, args.status, 208, &abort_sh)) {
+        if (!mbar_wait_warp(&s_full[g % C::S_BUFS], (g / C::S_BUFS) & 1, args.status, 208, &abort_sh)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        const int kv0 = (kt0 + j) * 128;
-        float s[128];
+        const int kv0 = (kt0 + j) * 128 + grp * 64;
+        float s[64];
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
+        for (int c = 0; c < 2; ++c) {
           uint32_t v[32];
-          tmem_ld32(tmem + lane_off + C::S_COL + (g & 1) * 128 + c * 32, v);
+          tmem_ld32(tmem + lane_off + C::S_COL + (g % C::S_BUFS) * 128 + grp * 64 + c * 32, v);
           tmem_wait_ld();
 #pragma unroll
           for (int i = 0; i < 32; ++i) s[c * 32 + i] = __uint_as_float(v[i]) * args.scale_log2;
         }
-        const bool full = kv0 >= lo && kv0 + 127 <= q;
+        if (C::S_BUFS == 1) {
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&s_free);
+        }
+        const bool full = kv0 >= lo && kv0 + 63 <= q;
         float mx = -INFINITY;
         if (full) {
 #pragma unroll
-          for (int i = 0; i < 128; ++i) mx = fmaxf(mx, s[i]);
+          for (int i = 0; i < 64; ++i) mx = fmaxf(mx, s[i]);
         } else {
 #pragma unroll
-          for (int i = 0; i < 128; ++i) {
+          for (int i = 0; i < 64; ++i) {
             const int k = kv0 + i;
             if (k < lo || k > q) s[i] = -INFINITY;
             mx = fmaxf(mx, s[i]);
@@ -264,19 +306,19 @@ __global__ void __launch_bounds__(192, 1)
         const float base = m_new == -INFINITY ? 0.f : m_new;
         const float corr = fast_exp2(m - base);  // m == -inf -> 0
         float sum = 0.f;
-        uint32_t pk[64];
+        uint32_t pk[32];
 #pragma unroll
-        for (int i = 0; i < 64; ++i) {
+        for (int i = 0; i < 32; ++i) {
           const float p0 = fast_exp2(s[2 * i] - base);
           const float p1 = fast_exp2(s[2 * i + 1] - base);
           sum += p0 + p1;
           pk[i] = pack_bf16x2(p0, p1);
         }
         l = l * corr + sum;
-        // PV of the previous tile must be complete before O is rescaled or its P slot
-        // (two tiles back) is overwritten.
+        // The previous PV of this group must be complete before its O is rescaled or
+        // its P slot (two tiles back) is overwritten.
         if (j > 0) {
-          if (!mbar_wait_warp(&o_done, o_it & 1, args.status, 209, &abort_sh)) {
+          if (!mbar_wait_warp(&o_done[grp], o_it & 1, args.status, 209, &abort_sh)) {
             ok = false;
             break;
           }
@@ -287,53 +329,67 @@ __global__ void __launch_bounds__(192, 1)
 #pragma unroll
             for (int c = 0; c < D; c += 16) {
               uint32_t ov[16];
-              tmem_ld16(tmem + lane_off + C::O_COL + c, ov);
+              tmem_ld16(tmem + lane_off + C::O_COL + grp * D + c, ov);
               tmem_wait_ld();
 #pragma unroll
               for (int i = 0; i < 16; ++i) ov[i] = __float_as_uint(__uint_as_float(ov[i]) * corr);
-              tmem_st16(tmem + lane_off + C::O_COL + c, ov);
+              tmem_st16(tmem + lane_off + C::O_COL + grp * D + c, ov);
             }
           }
         }
         m = m_new;
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
+        for (int c = 0; c < 2; ++c) {
           uint32_t pv[16];
 #pragma unroll
           for (int i = 0; i < 16; ++i) pv[i] = pk[c * 16 + i];
-          tmem_st16(tmem + lane_off + C::P_COL + (g & 1) * 64 + c * 16, pv);
+          tmem_st16(tmem + lane_off + C::P_COL + (grp * 2 + (g & 1)) * 32 + c * 16, pv);
         }
         tmem_wait_st();
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&p_ready);
-        ++p_cnt;
+        if (lane == 0) mbar_arrive(&p_ready[grp]);
       }
       if (!ok) break;
-      // Epilogue: wait for the last PV, normalise and store.
-      if (!mbar_wait_warp(&o_done, o_it & 1, args.status, 210, &abort_sh)) break;
+      if (!mbar_wait_warp(&o_done[grp], o_it & 1, args.status, 210, &abort_sh)) break;
       ++o_it;
       tc_fence_after();
-      const float inv = l > 0.f ? 1.f / l : 0.f;
+      if (grp == 1) {
+        stats[2 * r] = m;
+        stats[2 * r + 1] = l;
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&stats_ready);
+      } else {
+        if (!mbar_wait_warp(&stats_ready, item_n & 1, args.status, 212, &abort_sh)) break;
+        const float mb = stats[2 * r], lb = stats[2 * r + 1];
+        const float mm = fmaxf(m, mb);
+        const float base = mm == -INFINITY ? 0.f : mm;
+        const float fa = fast_exp2(m - base), fb = fast_exp2(mb - base);
+        const float lt = l * fa + lb * fb;
+        const float inv = lt > 0.f ? 1.f / lt : 0.f;
+        const float sa = fa * inv, sbb = fb * inv;
 #pragma unroll
-      for (int c = 0; c < D; c += 16) {
-        uint32_t ov[16];
-        tmem_ld16(tmem + lane_off + C::O_COL + c, ov);
-        tmem_wait_ld();
-        if (qok) {
-          uint32_t pk[8];
+        for (int c = 0; c < D; c += 16) {
+          uint32_t oa[16], ob[16];
+          tmem_ld16(tmem + lane_off + C::O_COL + c, oa);
+          tmem_ld16(tmem + lane_off + C::O_COL + D + c, ob);
+          tmem_wait_ld();
+          if (qok) {
+            uint32_t pk[8];
 #pragma unroll
-          for (int i = 0; i < 8; ++i)
-            pk[i] = pack_bf16x2(__uint_as_float(ov[2 * i]) * inv, __uint_as_float(ov[2 * i + 1]) * inv);
-          uint4* dst = reinterpret_cast<uint4*>(args.out + static_cast<long>(q) * H * D + h * D + c);
-          dst[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-          dst[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+            for (int i = 0; i < 8; ++i)
+              pk[i] = pack_bf16x2(__uint_as_float(oa[2 * i]) * sa + __uint_as_float(ob[2 * i]) * sbb,
+                                  __uint_as_float(oa[2 * i + 1]) * sa + __uint_as_float(ob[2 * i + 1]) * sbb);
+            uint4* dst = reinterpret_cast<uint4*>(args.out + static_cast<long>(q) * H * D + h * D + c);
+            dst[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+            dst[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+          }
         }
+        if (qok) args.lse[static_cast<long>(h) * T + q] = lt > 0.f ? (base + __log2f(lt)) * kLn2 : -INFINITY;
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&o_free);
       }
-      if (qok) args.lse[static_cast<long>(h) * T + q] = l > 0.f ? (m + __log2f(l)) * kLn2 : -INFINITY;
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&o_free);
       kv_it += nkv;
     }
   }
@@ -350,9 +406,11 @@ __global__ void __launch_bounds__(192, 1)
 //   0      TMA: K/V once per item, Q/dO per query tile (QSTAGES-deep ring)
 //   1      tcgen05.mma: S^T = K Q^T, dP^T = V dO^T; then dV += P^T dO, dK += dS^T Q,
 //          dQ = dS K
-//   2..5   P^T / dS^T, thread = key row; at item end dK/dV rows -> TMA reduce-add
-//          into the fp32 dK|dV accumulator (the GQA heads of a group add up there)
-//   6..9   dQ, thread = query row -> TMA reduce-add into the fp32 dQ accumulator
+//   2..9   P^T / dS^T, thread = key row; warps 2-5 take query columns 0-63 and warps
+//          6-9 columns 64-127 (the gradient math needs no cross-column reduction);
+//          at item end dK (group 0) and dV (group 1) rows -> TMA reduce-add into the
+//          fp32 dK|dV accumulator (the GQA heads of a group add up there)
+//   10..13 dQ, thread = query row -> TMA reduce-add into the fp32 dQ accumulator
 // so the next tile's S^T/dP^T MMAs, this tile's dQ write-out and the next tile's
 // softmax-gradient math overlap.
 template <int D>
@@ -364,11 +422,11 @@ struct BwdCfg {
   static constexpr int K_OFF = 0;
   static constexpr int V_OFF = TILE_BYTES;
   static constexpr int Q_OFF = 2 * TILE_BYTES;  // stage s: Q at Q_OFF + 2*s*TILE, dO right after
-  static constexpr int P_OFF = Q_OFF + QSTAGES * 2 * TILE_BYTES;  // P^T  [128 kv x 128 q] bf16
+  static constexpr int VSTAGE_OFF = Q_OFF + QSTAGES * 2 * TILE_BYTES;  // stage s: lse[128], delta[128] fp32
+  static constexpr int P_OFF = VSTAGE_OFF + 2048;                      // P^T  [128 kv x 128 q] bf16
   static constexpr int DS_OFF = P_OFF + 32768;                   // dS^T [128 kv x 128 q] bf16
   static constexpr int DQS_OFF = DS_OFF + 32768;                 // dQ staging, 4 warps
-  static constexpr int VEC_OFF = DQS_OFF + 4 * DQ_SLOTS * 4096;  // 2 x {lse2, delta, doc_start}[128]
-  static constexpr int SMEM = VEC_OFF + 2 * 3 * 512 + 1024;
+  static constexpr int SMEM = DQS_OFF + 4 * DQ_SLOTS * 4096 + 1024;
   static_assert(SMEM <= 232448, "shared memory budget");
   static constexpr uint32_t ST_COL = 0;
   static constexpr uint32_t DPT_COL = 128;
@@ -401,13 +459,13 @@ __device__ __forceinline__ void reduce_box(const CUtensorMap* map, const uint8_t
 }
 
 template <int D>
-__global__ void __launch_bounds__(320, 1)
+__global__ void __launch_bounds__(448, 1)
     attn_bwd_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __grid_constant__ CUtensorMap tm_do,
                     const __grid_constant__ CUtensorMap tm_dq, const __grid_constant__ CUtensorMap tm_dkv,
                     const AttnArgs args) {
   using C = BwdCfg<D>;
   __shared__ __align__(8) uint64_t kv_full, kv_empty, qd_full[2], qd_empty[2], st_full, ds_ready, mma2_done, dq_free,
-      acc_done, acc_free, drain_bar, vec_bar;
+      acc_done, acc_free, drain_bar;
   __shared__ uint32_t tmem_sh;
   __shared__ volatile int abort_sh;
   extern __shared__ uint8_t dyn[];
@@ -421,13 +479,12 @@ __global__ void __launch_bounds__(320, 1)
       mbar_init(&qd_empty[i], 1);
     }
     mbar_init(&st_full, 1);
-    mbar_init(&ds_ready, 4);
+    mbar_init(&ds_ready, 8);
     mbar_init(&mma2_done, 1);
     mbar_init(&dq_free, 4);
     mbar_init(&acc_done, 1);
-    mbar_init(&acc_free, 4);
+    mbar_init(&acc_free, 8);
     mbar_init(&drain_bar, 1);
-    mbar_init(&vec_bar, 128);
     abort_sh = 0;
     fence_mbar_init();
   }
@@ -450,8 +507,10 @@ __global__ void __launch_bounds__(320, 1)
     if (lane == 0) {
       uint32_t item_n = 0, g = 0;
       bool ok = true;
+      int3 nx = blockIdx.x < args.n_items ? ld_item(args.items, blockIdx.x) : make_int3(0, 0, 0);
       for (int it = blockIdx.x; it < args.n_items && ok; it += gridDim.x, ++item_n) {
-        const int kt = args.items[3 * it], h = args.items[3 * it + 1], qhi = args.items[3 * it + 2];
+        const int kt = nx.x, h = nx.y, qhi = nx.z;
+        if (it + (int)gridDim.x < args.n_items) nx = ld_item(args.items, it + gridDim.x);
         const int hk = h / group;
         if (!mbar_wait(&kv_empty, (item_n & 1) ^ 1, args.status, 221, &abort_sh)) break;
         mbar_arrive_expect_tx(&kv_full, 2 * C::TILE_BYTES);
@@ -464,10 +523,15 @@ __global__ void __launch_bounds__(320, 1)
             ok = false;
             break;
           }
-          mbar_arrive_expect_tx(&qd_full[s], 2 * C::TILE_BYTES);
+          // Q, dO tiles and this tile's lse / delta rows (T % 4 == 0 keeps them 16B aligned).
+          const uint32_t vb = static_cast<uint32_t>(min(128, T - qt * 128)) * 4u;
+          mbar_arrive_expect_tx(&qd_full[s], 2 * C::TILE_BYTES + 2 * vb);
           uint8_t* qs = smem + C::Q_OFF + s * 2 * C::TILE_BYTES;
           load_tile_rows(qs, &tm_qkv, &qd_full[s], h * D, qt * 128, D);
           load_tile_rows(qs + C::TILE_BYTES, &tm_do, &qd_full[s], h * D, qt * 128, D);
+          uint8_t* vs = smem + C::VSTAGE_OFF + s * 1024;
+          bulk_load(vs, args.lse + static_cast<long>(h) * T + qt * 128, vb, &qd_full[s]);
+          bulk_load(vs + 512, args.delta + static_cast<long>(h) * T + qt * 128, vb, &qd_full[s]);
         }
       }
     }
@@ -477,8 +541,10 @@ __global__ void __launch_bounds__(320, 1)
       bool ok = true;
       const uint32_t ka = smem_u32(smem + C::K_OFF), va = smem_u32(smem + C::V_OFF);
       const uint32_t pa = smem_u32(smem + C::P_OFF), dsa = smem_u32(smem + C::DS_OFF);
+      int3 nx = blockIdx.x < args.n_items ? ld_item(args.items, blockIdx.x) : make_int3(0, 0, 0);
       for (int it = blockIdx.x; it < args.n_items && ok; it += gridDim.x, ++item_n) {
-        const int kt = args.items[3 * it], qhi = args.items[3 * it + 2];
+        const int kt = nx.x, qhi = nx.z;
+        if (it + (int)gridDim.x < args.n_items) nx = ld_item(args.items, it + gridDim.x);
         if (!mbar_wait(&kv_full, item_n & 1, args.status, 223, &abort_sh)) break;
         if (!mbar_wait(&acc_free, (item_n & 1) ^ 1, args.status, 224, &abort_sh)) break;
         tc_fence_after();
@@ -543,52 +609,53 @@ __global__ void __launch_bounds__(320, 1)
       umma_commit(&drain_bar);
       mbar_wait(&drain_bar, 0, args.status, 228, nullptr);
     }
-  } else if (warp < 6) {
+  } else if (warp < 10) {
     // ---------------- P^T / dS^T (thread = key row) ----------------
+    const int grp = (warp - 2) / 4;  // query columns [64 grp, 64 grp + 64)
     const int q4 = warp & 3;
     const int r = q4 * 32 + lane;
     const uint32_t lane_off = static_cast<uint32_t>(q4 * 32) << 16;
-    float* vec_base = reinterpret_cast<float*>(smem + C::VEC_OFF);
     uint8_t* ptile = smem + C::P_OFF;
     uint8_t* dstile = smem + C::DS_OFF;
     uint32_t item_n = 0, g = 0;
     bool ok = true;
+    int3 nx = blockIdx.x < args.n_items ? ld_item(args.items, blockIdx.x) : make_int3(0, 0, 0);
+    int nde = (blockIdx.x < args.n_items && nx.x * 128 + r < T) ? args.doc_end[nx.x * 128 + r] : -1;
     for (int it = blockIdx.x; it < args.n_items && ok; it += gridDim.x, ++item_n) {
-      const int kt = args.items[3 * it], h = args.items[3 * it + 1], qhi = args.items[3 * it + 2];
+      const int kt = nx.x, h = nx.y, qhi = nx.z;
+      // Key row kv is attended by queries q in [kv, doc_end(kv)] (none past T).
+      const int de = nde;
+      if (it + (int)gridDim.x < args.n_items) {
+        nx = ld_item(args.items, it + gridDim.x);
+        nde = nx.x * 128 + r < T ? args.doc_end[nx.x * 128 + r] : -1;
+      }
       const int hk = h / group;
       const int kv = kt * 128 + r;
       for (int qt = kt; qt <= qhi; ++qt, ++g) {
         const int q0 = qt * 128;
-        // Per-query vectors, double-buffered by iteration parity (see vec_bar).
-        float* s_lse = vec_base + (g & 1) * 384;
-        float* s_delta = s_lse + 128;
-        int* s_ds = reinterpret_cast<int*>(s_delta + 128);
-        {
-          const int q = q0 + r;
-          const bool qok = q < T;
-          s_lse[r] = qok ? args.lse[static_cast<long>(h) * T + q] * kLog2e : INFINITY;
-          s_delta[r] = qok ? args.delta[static_cast<long>(h) * T + q] : 0.f;
-          s_ds[r] = qok ? args.doc_start[q] : 0x7fffffff;
-        }
-        mbar_arrive(&vec_bar);
-        if (!mbar_wait_warp(&vec_bar, g & 1, args.status, 233, &abort_sh)) {
-          ok = false;
-          break;
-        }
+        const int s = g % C::QSTAGES;
         if (!mbar_wait_warp(&st_full, g & 1, args.status, 229, &abort_sh)) {
           ok = false;
           break;
         }
+        // The lse / delta rows arrived with the Q/dO stage (already complete here; the
+        // wait makes the bulk-copied data visible to this thread).
+        if (!mbar_wait_warp(&qd_full[s], (g / C::QSTAGES) & 1, args.status, 233, &abort_sh)) {
+          ok = false;
+          break;
+        }
+        const float* s_lse = reinterpret_cast<const float*>(smem + C::VSTAGE_OFF + s * 1024);
+        const float* s_delta = s_lse + 128;
         // The previous tile's dV/dK/dQ MMAs read P/dS from shared memory.
         if (g > 0 && !mbar_wait_warp(&mma2_done, (g - 1) & 1, args.status, 230, &abort_sh)) {
           ok = false;
           break;
         }
-        if (lane == 0) bulk_wait_read<0>();  // dK/dV staging of the previous item used the P area
+        if (lane == 0) bulk_wait_read<0>();  // dK/dV staging of the previous item used this group's P/dS half
         __syncwarp();
         tc_fence_after();
 #pragma unroll 1
-        for (int c = 0; c < 4; ++c) {
+        for (int c = 2 * grp; c < 2 * grp + 2; ++c) {
           uint32_t sv[32], dv[32];
           tmem_ld32(tmem + lane_off + C::ST_COL + c * 32, sv);
           tmem_ld32(tmem + lane_off + C::DPT_COL + c * 32, dv);
@@ -601,10 +668,11 @@ __global__ void __launch_bounds__(320, 1)
             for (int e = 0; e < 2; ++e) {
               const int j = c * 32 + 2 * i + e;
               const int q = q0 + j;
-              const bool allowed = q >= kv && s_ds[j] <= kv;
-              const float p = allowed ? fast_exp2(__uint_as_float(sv[2 * i + e]) * args.scale_log2 - s_lse[j]) : 0.f;
+              const bool allowed = q >= kv && q <= de;
+              const float p =
+                  allowed ? fast_exp2(__uint_as_float(sv[2 * i + e]) * args.scale_log2 - s_lse[j] * kLog2e) : 0.f;
               p2[e] = p;
-              d2[e] = p * (__uint_as_float(dv[2 * i + e]) - s_delta[j]);
+              d2[e] = allowed ? p * (__uint_as_float(dv[2 * i + e]) - s_delta[j]) : 0.f;  // select: delta past T is stale smem
             }
             pp[i] = pack_bf16x2(p2[0], p2[1]);
             dd[i] = pack_bf16x2(d2[0], d2[1]);
@@ -624,10 +692,11 @@ __global__ void __launch_bounds__(320, 1)
       // dK (scaled) and dV rows of this key tile -> fp32 accumulators (TMA reduce-add).
       if (!mbar_wait_warp(&acc_done, item_n & 1, args.status, 232, &abort_sh)) break;
       tc_fence_after();
-      uint8_t* stg = smem + C::P_OFF + q4 * 8192;  // P/dS are free once acc_done completed
+      // Staging in this group's own halves of the P and dS tiles (free after acc_done).
+      uint8_t* stg = smem + (q4 < 2 ? C::P_OFF : C::DS_OFF) + grp * 16384 + (q4 & 1) * 8192;
       int slot = 0;
 #pragma unroll 1
-      for (int c = 0; c < 2 * D; c += 32) {
+      for (int c = grp * D; c < grp * D + D; c += 32) {
         const bool is_k = c < D;
         uint32_t v[32];
         tmem_ld32(tmem + lane_off + (is_k ? C::DK_COL + c : C::DV_COL + c - D), v);
@@ -653,8 +722,10 @@ __global__ void __launch_bounds__(320, 1)
     int slot = 0;
     uint32_t g = 0;
     bool ok = true;
+    int3 nx = blockIdx.x < args.n_items ? ld_item(args.items, blockIdx.x) : make_int3(0, 0, 0);
     for (int it = blockIdx.x; it < args.n_items && ok; it += gridDim.x) {
-      const int kt = args.items[3 * it], h = args.items[3 * it + 1], qhi = args.items[3 * it + 2];
+      const int kt = nx.x, h = nx.y, qhi = nx.z;
+      if (it + (int)gridDim.x < args.n_items) nx = ld_item(args.items, it + gridDim.x);
       for (int qt = kt; qt <= qhi; ++qt, ++g) {
         if (!mbar_wait_warp(&mma2_done, g & 1, args.status, 231, &abort_sh)) {
           ok = false;
@@ -769,6 +840,7 @@ std::vector<at::Tensor> attn_fwd(at::Tensor qkv, at::Tensor doc_start, at::Tenso
   TORCH_CHECK(D == 64 || D == 128, "attention: head_dim must be 64 or 128");
   TORCH_CHECK(H % Hkv == 0 && qkv.size(1) == (H + 2 * Hkv) * D, "attention: qkv width");
   TORCH_CHECK(doc_start.scalar_type() == at::kInt && items.scalar_type() == at::kInt && items.is_contiguous());
+  TORCH_CHECK(items.dim() == 2 && items.size(1) == 3, "attention: forward items are (q tile, head, first kv tile)");
   const c10::cuda::CUDAGuard guard(qkv.device());
   const int T = qkv.size(0);
   auto lse = at::empty({H, T}, qkv.options().dtype(at::kFloat));
@@ -791,17 +863,17 @@ std::vector<at::Tensor> attn_fwd(at::Tensor qkv, at::Tensor doc_start, at::Tenso
   auto s = at::cuda::getCurrentCUDAStream();
   if (D == 64) {
     set_smem(attn_fwd_kernel<64>, FwdCfg<64>::SMEM);
-    attn_fwd_kernel<64><<<grid, 192, FwdCfg<64>::SMEM, s>>>(tm, a);
+    attn_fwd_kernel<64><<<grid, 320, FwdCfg<64>::SMEM, s>>>(tm, a);
   } else {
     set_smem(attn_fwd_kernel<128>, FwdCfg<128>::SMEM);
-    attn_fwd_kernel<128><<<grid, 192, FwdCfg<128>::SMEM, s>>>(tm, a);
+    attn_fwd_kernel<128><<<grid, 320, FwdCfg<128>::SMEM, s>>>(tm, a);
   }
   PB_CUDA_CHECK(cudaGetLastError());
   return {out, lse};
 }
 
 void attn_bwd(at::Tensor qkv, at::Tensor out, at::Tensor dout, at::Tensor lse, at::Tensor doc_start,
-              at::Tensor items, int64_t H, int64_t Hkv, int64_t D, double scale, at::Tensor dqkv, at::Tensor dq_acc,
+              at::Tensor doc_end, at::Tensor items, int64_t H, int64_t Hkv, int64_t D, double scale, at::Tensor dqkv, at::Tensor dq_acc,
               at::Tensor dkv_acc, at::Tensor delta, c10::optional<at::Tensor> pos, c10::optional<at::Tensor> cos_t,
               c10::optional<at::Tensor> sin_t) {
   TORCH_CHECK(D == 64 || D == 128, "attention: head_dim must be 64 or 128");
@@ -809,6 +881,8 @@ void attn_bwd(at::Tensor qkv, at::Tensor out, at::Tensor dout, at::Tensor lse, a
   TORCH_CHECK(dqkv.is_contiguous() && dq_acc.is_contiguous() && dkv_acc.is_contiguous());
   TORCH_CHECK(items.scalar_type() == at::kInt && items.dim() == 2 && items.size(1) == 3);
   TORCH_CHECK(dq_acc.size(1) == H * D && dkv_acc.size(1) == 2 * Hkv * D, "attention: accumulator widths");
+  TORCH_CHECK(qkv.size(0) % 4 == 0, "attention backward: token count must be a multiple of 4");
+  TORCH_CHECK(doc_end.scalar_type() == at::kInt && doc_end.numel() == qkv.size(0), "attention: doc_end");
   const c10::cuda::CUDAGuard guard(qkv.device());
   const int T = qkv.size(0);
   if (T == 0) return;
@@ -834,6 +908,7 @@ void attn_bwd(at::Tensor qkv, at::Tensor out, at::Tensor dout, at::Tensor lse, a
   a.scale = (float)scale;
   a.scale_log2 = (float)scale * kLog2e;
   a.doc_start = doc_start.data_ptr<int>();
+  a.doc_end = doc_end.data_ptr<int>();
   a.items = items.data_ptr<int>();
   a.n_items = items.size(0);
   a.lse = lse.data_ptr<float>();
@@ -842,10 +917,10 @@ void attn_bwd(at::Tensor qkv, at::Tensor out, at::Tensor dout, at::Tensor lse, a
   const int grid = std::min<int>(a.n_items, num_sms(qkv.device().index()));
   if (D == 64) {
     set_smem(attn_bwd_kernel<64>, BwdCfg<64>::SMEM);
-    attn_bwd_kernel<64><<<grid, 320, BwdCfg<64>::SMEM, s>>>(tq, td, tdq, tdkv, a);
+    attn_bwd_kernel<64><<<grid, 448, BwdCfg<64>::SMEM, s>>>(tq, td, tdq, tdkv, a);
   } else {
     set_smem(attn_bwd_kernel<128>, BwdCfg<128>::SMEM);
-    attn_bwd_kernel<128><<<grid, 320, BwdCfg<128>::SMEM, s>>>(tq, td, tdq, tdkv, a);
+    attn_bwd_kernel<128><<<grid, 448, BwdCfg<128>::SMEM, s>>>(tq, td, tdq, tdkv, a);
   }
   PB_CUDA_CHECK(cudaGetLastError());
   const long n4 = static_cast<long>(T) * (H + 2 * Hkv) * (D / 8);

@@ -36,8 +36,8 @@ at::Tensor l2_norm(at::Tensor x);
 std::vector<at::Tensor> attn_fwd(at::Tensor qkv, at::Tensor doc_start, at::Tensor tiles, int64_t n_heads,
                                  int64_t n_kv_heads, int64_t head_dim, double scale, at::Tensor out);
 void attn_bwd(at::Tensor qkv, at::Tensor out, at::Tensor dout, at::Tensor lse, at::Tensor doc_start,
-              at::Tensor kv_tiles, int64_t n_heads, int64_t n_kv_heads, int64_t head_dim, double scale,
-              at::Tensor dqkv, at::Tensor dq_acc, at::Tensor dkv_acc, at::Tensor delta, c10::optional<at::Tensor> pos,
+              at::Tensor doc_end, at::Tensor items, int64_t H, int64_t Hkv, int64_t D, double scale, at::Tensor dqkv,
+              at::Tensor dq_acc, at::Tensor dkv_acc, at::Tensor delta, c10::optional<at::Tensor> pos,
               c10::optional<at::Tensor> cos_t, c10::optional<at::Tensor> sin_t);
 #endif
 #ifdef PB_WITH_COMM

@@ -36,9 +36,10 @@ def doc_end_from_start(doc_start: torch.Tensor) -> torch.Tensor:
 
 
 def attention_plan(doc_start: torch.Tensor, n_heads: int, n_kv_heads: int) -> dict[str, torch.Tensor]:
-    """Cost-ordered work lists: ``fwd`` int32 [nq*H, 2] = (q tile, head);
+    """Cost-ordered work lists: ``fwd`` int32 [nq*H, 3] = (q tile, head, first kv tile);
     ``bwd`` int32 [nk*H, 3] = (kv tile, q head, last q tile).  The GQA heads of a kv
-    head are separate backward items; their dK/dV add up in an fp32 accumulator."""
+    head are separate backward items; their dK/dV add up in an fp32 accumulator.
+    Also returns ``doc_end`` (last token of each token's document)."""
     dev = doc_start.device
     t = doc_start.numel()
     n_tiles = -(-t // TILE)
@@ -49,7 +50,7 @@ def attention_plan(doc_start: torch.Tensor, n_heads: int, n_kv_heads: int) -> di
     order = torch.argsort(q_cost, descending=True, stable=True)
     heads = torch.arange(n_heads, device=dev, dtype=torch.int64)
     fwd = torch.stack(
-        [order.repeat_interleave(n_heads), heads.repeat(n_tiles)], dim=1
+        [order.repeat_interleave(n_heads), heads.repeat(n_tiles), kv_lo[order].repeat_interleave(n_heads)], dim=1
     ).to(torch.int32).contiguous()
     de = doc_end_from_start(ds)
     last_row = torch.clamp(tiles * TILE + TILE - 1, max=t - 1)
@@ -60,17 +61,50 @@ def attention_plan(doc_start: torch.Tensor, n_heads: int, n_kv_heads: int) -> di
         [korder.repeat_interleave(n_heads), heads.repeat(n_tiles), q_hi[korder].repeat_interleave(n_heads)],
         dim=1,
     ).to(torch.int32).contiguous()
-    return {"fwd": fwd, "bwd": bwd, "doc_start": doc_start.to(torch.int32).contiguous()}
+    return {
+        "fwd": fwd,
+        "bwd": bwd,
+        "doc_start": doc_start.to(torch.int32).contiguous(),
+        "doc_end": de.to(torch.int32).contiguous(),
+    }
+
+
+ALIGN = 8
+
+
+def _padded(plan: dict, n_heads: int, n_kv_heads: int, t: int) -> dict:
+    """Plan for ``t`` padded up to a multiple of ALIGN tokens (each pad token is its own
+    one-token document), cached in the plan."""
+    tp = -(-t // ALIGN) * ALIGN
+    if tp == t:
+        return plan
+    if "padded" not in plan:
+        ds = plan["doc_start"]
+        extra = torch.arange(t, tp, device=ds.device, dtype=torch.int32)
+        plan["padded"] = attention_plan(torch.cat([ds, extra]), n_heads, n_kv_heads)
+    return plan["padded"]
+
+
+def _pad_rows(x: torch.Tensor, rows: int) -> torch.Tensor:
+    if x.shape[0] == rows:
+        return x
+    return torch.cat([x, x.new_zeros(rows - x.shape[0], *x.shape[1:])])
 
 
 def attn_forward_packed(
     qkv: torch.Tensor, plan: dict, n_heads: int, n_kv_heads: int, head_dim: int
 ) -> tuple[torch.Tensor, torch.Tensor]:
+    """Returns (out ``[T, H*D]`` bf16, lse ``[H, T]`` fp32 natural log)."""
     t = qkv.shape[0]
-    out = torch.empty(t, n_heads * head_dim, device=qkv.device, dtype=torch.bfloat16)
+    pl = _padded(plan, n_heads, n_kv_heads, t)
+    tp = pl["doc_start"].numel()
+    qkv_p = _pad_rows(qkv, tp)
+    out = torch.empty(tp, n_heads * head_dim, device=qkv.device, dtype=torch.bfloat16)
     o, lse = _native.module().attn_fwd(
-        qkv, plan["doc_start"], plan["fwd"], n_heads, n_kv_heads, head_dim, 1.0 / math.sqrt(head_dim), out
+        qkv_p, pl["doc_start"], pl["fwd"], n_heads, n_kv_heads, head_dim, 1.0 / math.sqrt(head_dim), out
     )
+    if tp != t:
+        return o[:t], lse[:, :t].contiguous()
     return o, lse
 
 
@@ -89,15 +123,23 @@ def attn_backward_packed(
     and k gradients are rotated back to the pre-RoPE frame (the gradient w.r.t. the QKV
     GEMM output); without it they are w.r.t. the rotated q/k."""
     t = qkv.shape[0]
+    pl = _padded(plan, n_heads, n_kv_heads, t)
+    tp = pl["doc_start"].numel()
+    if tp != t:
+        qkv, out, dout = _pad_rows(qkv, tp), _pad_rows(out, tp), _pad_rows(dout, tp)
+        lse = torch.cat([lse, lse.new_zeros(lse.shape[0], tp - t)], dim=1)
+        if rope is not None:
+            rope = (_pad_rows(rope[0], tp), rope[1], rope[2])
     dqkv = torch.empty_like(qkv)
-    dq_acc = torch.empty(t, n_heads * head_dim, device=qkv.device, dtype=torch.float32)
-    dkv_acc = torch.empty(t, 2 * n_kv_heads * head_dim, device=qkv.device, dtype=torch.float32)
-    delta = torch.empty(n_heads, t, device=qkv.device, dtype=torch.float32)
+    dq_acc = torch.empty(tp, n_heads * head_dim, device=qkv.device, dtype=torch.float32)
+    dkv_acc = torch.empty(tp, 2 * n_kv_heads * head_dim, device=qkv.device, dtype=torch.float32)
+    delta = torch.empty(n_heads, tp, device=qkv.device, dtype=torch.float32)
     _native.module().attn_bwd(
-        qkv, out, dout.contiguous(), lse, plan["doc_start"], plan["bwd"], n_heads, n_kv_heads, head_dim,
-        1.0 / math.sqrt(head_dim), dqkv, dq_acc, dkv_acc, delta, *(rope if rope is not None else (None, None, None)),
+        qkv, out, dout.contiguous(), lse.contiguous(), pl["doc_start"], pl["doc_end"], pl["bwd"], n_heads,
+        n_kv_heads, head_dim, 1.0 / math.sqrt(head_dim), dqkv, dq_acc, dkv_acc, delta,
+        *(rope if rope is not None else (None, None, None)),
     )
-    return dqkv
+    return dqkv[:t] if tp != t else dqkv
 
 
 class _VarlenAttention(torch.autograd.Function):

@@ -61,9 +61,9 @@ def test_attention_plan_orders_by_cost() -> None:
     ds = torch.cat([torch.zeros(1024, dtype=torch.int32), torch.arange(1024, 1024 + 256, dtype=torch.int32)])
     plan = attention_plan(ds, n_heads=2, n_kv_heads=1)
     fwd = plan["fwd"]
-    assert fwd.shape == (10 * 2, 2)
+    assert fwd.shape == (10 * 2, 3)
     # The last q tile of the 1024-token document sees 8 key tiles and comes first.
-    assert fwd[0, 0].item() == 7
+    assert fwd[0].tolist() == [7, 0, 0] and fwd[-1].tolist() == [9, 1, 9]
     bwd = plan["bwd"]
     assert bwd.shape == (10 * 2, 3)
     assert bwd[0].tolist() == [0, 0, 7] and bwd[1].tolist() == [0, 1, 7]
