@@ -97,7 +97,7 @@ class DataParallel:
             from packbalance_b200.parallel.comm import FusedAllReduce
 
             try:
-                self.fused = FusedAllReduce(flat.grad, group=group)
+                self.fused = FusedAllReduce(flat.grad, group=group, flat=flat)
             except Exception as exc:  # peer memory unavailable
                 if backend == "fused":
                     raise
@@ -108,12 +108,13 @@ class DataParallel:
         self._norm_parts: list[torch.Tensor] = []
 
     def _make_buckets(self) -> list[tuple[int, int]]:
-        """Contiguous ranges of whole parameters, last parameters first (backward order)."""
+        """Contiguous ranges of whole parameters, last parameters first (backward order).
+        Bucket starts are 16-byte aligned (cuts only at offsets that are multiples of 4)."""
         buckets: list[tuple[int, int]] = []
         hi = self.flat.numel
         lo = hi
         for s in reversed(self.flat.slots):
-            if hi - s.offset > self.cap and lo < hi:
+            if hi - s.offset > self.cap and lo < hi and lo % 4 == 0:
                 buckets.append((lo, hi))
                 hi = lo
             lo = s.offset
@@ -123,6 +124,8 @@ class DataParallel:
     def start_step(self) -> None:
         self._issued = [False] * len(self.buckets)
         self._norm_parts = []
+        if self.fused is not None:
+            self.fused.start_step()
 
     def notify_ready(self, offset: int) -> None:
         """Every gradient at flat offset >= ``offset`` is final for this step: issue
@@ -144,7 +147,7 @@ class DataParallel:
             ctx = contextlib.nullcontext()
         with ctx:
             if self.fused is not None:
-                self._norm_parts.append(self.fused.all_reduce_mean(lo, hi))
+                self.fused.all_reduce_mean(lo, hi)
             else:
                 dist.all_reduce(view, op=dist.ReduceOp.SUM, group=self.group)
                 view.mul_(1.0 / self.world)
@@ -161,9 +164,13 @@ class DataParallel:
         if self.stream is not None:
             torch.cuda.current_stream().wait_stream(self.stream)
         if self.fused is not None:
-            self.fused.check()
-            return torch.stack(self._norm_parts).sum() if self._norm_parts else None
+            return self.fused.sumsq
         return None
+
+    def check(self) -> None:
+        """Raise if a fused all-reduce recorded a timeout (host synchronisation)."""
+        if self.fused is not None:
+            self.fused.check()
 
     def close(self) -> None:
         if self.fused is not None:

@@ -105,6 +105,16 @@ class FlatParameters:
     def slot(self, p: nn.Parameter) -> Slot:
         return self.by_param[id(p)]
 
+    def rebind_grad(self, buf: torch.Tensor) -> None:
+        """Move the flat gradient into ``buf`` (e.g. symmetric memory) and re-point every
+        parameter's ``.grad`` view at it."""
+        if buf.numel() != self.numel or buf.dtype != self.grad.dtype:
+            raise ValueError("replacement gradient buffer has the wrong size or dtype")
+        buf.copy_(self.grad)
+        self.grad = buf
+        for s in self.slots:
+            s.param.grad = buf[s.offset : s.offset + s.numel].view(s.shape)
+
     # ---- gradient write protocol -----------------------------------------------
     def zero_grad(self) -> None:
         """Start a new accumulation window: the next writer of each slot overwrites."""
