@@ -80,35 +80,47 @@ __device__ __forceinline__ bool cta_barrier(const ArArgs& a, int k, volatile int
   return ok && !*abort;
 }
 
-__global__ void __launch_bounds__(512) fused_allreduce_kernel(const ArArgs a) {
-  __shared__ volatile int abort_sh;
-  __shared__ float red[32];
-  if (threadIdx.x == 0) abort_sh = 0;
-  __syncthreads();
-  const int W = a.world;
-  const long n = a.hi - a.lo;
-  // chunk and per-CTA sub-range sizes (multiples of 4 floats for 16-byte accesses)
-  const long cs = ((n + W - 1) / W + 3) / 4 * 4;
-  const long sub = ((cs + gridDim.x - 1) / gridDim.x + 3) / 4 * 4;
+constexpr int kMaxWorld = 8;
+
+// Sub-range of chunk ``c`` owned by this CTA (same split on every rank).
+__device__ __forceinline__ void sub_range(const ArArgs& a, long cs, long sub, int c, long& s0, long& s1) {
+  const long c0 = a.lo + c * cs;
+  const long c1 = min(c0 + cs, a.hi);
+  s0 = min(c0 + static_cast<long>(blockIdx.x) * sub, c1);
+  s1 = min(s0 + sub, c1);
+}
+
+template <int W>
+__device__ __forceinline__ float reduce_phase(const ArArgs& a, long s0, long s1) {
+  // All W peer loads of a 16-byte group are issued before any is used, two groups per
+  // thread per iteration, so each thread keeps 2 * W loads in flight over NVLink.
   float ss = 0.f;
-  if (!cta_barrier(a, 0, &abort_sh)) return;
-  {
-    const long c0 = a.lo + a.rank * cs;
-    const long s0 = min(c0 + static_cast<long>(blockIdx.x) * sub, min(c0 + cs, a.hi));
-    const long s1 = min(s0 + sub, min(c0 + cs, a.hi));
-    float* mine = a.ptrs[a.rank];
-    for (long i = s0 + threadIdx.x * 4; i < s1; i += blockDim.x * 4) {
-      if (i + 3 < s1) {
-        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-        for (int p = 0; p < W; ++p) {
-          const float4 v = __ldcg(reinterpret_cast<const float4*>(a.ptrs[p] + i));
-          acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
+  float* mine = a.ptrs[a.rank];
+  const long step = static_cast<long>(blockDim.x) * 8;
+  for (long i = s0 + threadIdx.x * 4; i < s1; i += step) {
+    float4 v[2][W];
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      const long j = i + u * blockDim.x * 4;
+      if (j + 3 < s1) {
+#pragma unroll
+        for (int p = 0; p < W; ++p) v[u][p] = __ldcg(reinterpret_cast<const float4*>(a.ptrs[p] + j));
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      const long j = i + u * blockDim.x * 4;
+      if (j + 3 < s1) {
+        float4 acc = v[u][0];
+#pragma unroll
+        for (int p = 1; p < W; ++p) {
+          acc.x += v[u][p].x; acc.y += v[u][p].y; acc.z += v[u][p].z; acc.w += v[u][p].w;
         }
         acc.x *= a.scale; acc.y *= a.scale; acc.z *= a.scale; acc.w *= a.scale;
-        *reinterpret_cast<float4*>(mine + i) = acc;
+        *reinterpret_cast<float4*>(mine + j) = acc;
         ss += acc.x * acc.x + acc.y * acc.y + acc.z * acc.z + acc.w * acc.w;
-      } else {
-        for (long e = i; e < s1; ++e) {
+      } else if (j < s1) {
+        for (long e = j; e < s1; ++e) {
           float acc = 0.f;
           for (int p = 0; p < W; ++p) acc += __ldcg(a.ptrs[p] + e);
           acc *= a.scale;
@@ -118,28 +130,58 @@ __global__ void __launch_bounds__(512) fused_allreduce_kernel(const ArArgs a) {
       }
     }
   }
-  if (!cta_barrier(a, 1, &abort_sh)) return;
-  for (int step = 1; step < W; ++step) {
-    const int p = (a.rank + step) % W;
-    const long c0 = a.lo + p * cs;
-    const long s0 = min(c0 + static_cast<long>(blockIdx.x) * sub, min(c0 + cs, a.hi));
-    const long s1 = min(s0 + sub, min(c0 + cs, a.hi));
-    const float* src = a.ptrs[p];
-    float* dst = a.ptrs[a.rank];
-    for (long i = s0 + threadIdx.x * 4; i < s1; i += blockDim.x * 4) {
-      if (i + 3 < s1) {
-        const float4 v = __ldcg(reinterpret_cast<const float4*>(src + i));
-        *reinterpret_cast<float4*>(dst + i) = v;
-        ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+  return ss;
+}
+
+template <int W>
+__device__ __forceinline__ float gather_phase(const ArArgs& a, long cs, long sub) {
+  // Copy the other ranks' reduced chunks; for each position the W - 1 peer loads are
+  // in flight together.
+  float ss = 0.f;
+  float* mine = a.ptrs[a.rank];
+  long s0[W], s1[W];
+#pragma unroll
+  for (int p = 0; p < W; ++p) sub_range(a, cs, sub, p, s0[p], s1[p]);
+  for (long off = threadIdx.x * 4; off < sub; off += static_cast<long>(blockDim.x) * 4) {
+    float4 v[W];
+#pragma unroll
+    for (int p = 0; p < W; ++p)
+      if (p != a.rank && s0[p] + off + 3 < s1[p]) v[p] = __ldcg(reinterpret_cast<const float4*>(a.ptrs[p] + s0[p] + off));
+#pragma unroll
+    for (int p = 0; p < W; ++p) {
+      if (p == a.rank) continue;
+      const long j = s0[p] + off;
+      if (j + 3 < s1[p]) {
+        *reinterpret_cast<float4*>(mine + j) = v[p];
+        ss += v[p].x * v[p].x + v[p].y * v[p].y + v[p].z * v[p].z + v[p].w * v[p].w;
       } else {
-        for (long e = i; e < s1; ++e) {
-          const float v = __ldcg(src + e);
-          dst[e] = v;
-          ss += v * v;
+        for (long e = j; e < s1[p]; ++e) {
+          const float x = __ldcg(a.ptrs[p] + e);
+          mine[e] = x;
+          ss += x * x;
         }
       }
     }
   }
+  return ss;
+}
+
+template <int W>
+__global__ void __launch_bounds__(512) fused_allreduce_kernel(const ArArgs a) {
+  __shared__ volatile int abort_sh;
+  __shared__ float red[32];
+  if (threadIdx.x == 0) abort_sh = 0;
+  __syncthreads();
+  const long n = a.hi - a.lo;
+  // chunk and per-CTA sub-range sizes (multiples of 4 floats for 16-byte accesses)
+  const long cs = ((n + W - 1) / W + 3) / 4 * 4;
+  const long sub = ((cs + gridDim.x - 1) / gridDim.x + 3) / 4 * 4;
+  if (!cta_barrier(a, 0, &abort_sh)) return;
+  long s0, s1;
+  sub_range(a, cs, sub, a.rank, s0, s1);
+  float ss = reduce_phase<W>(a, s0, s1);
+  if (!cta_barrier(a, 1, &abort_sh)) return;
+  ss += gather_phase<W>(a, cs, sub);
   if (!cta_barrier(a, 2, &abort_sh)) return;
   ss = warp_sum(ss);
   if ((threadIdx.x & 31) == 0) red[threadIdx.x / 32] = ss;
@@ -149,6 +191,104 @@ __global__ void __launch_bounds__(512) fused_allreduce_kernel(const ArArgs a) {
     v = warp_sum(v);
     if (threadIdx.x == 0) atomicAdd(a.sumsq, v);
   }
+}
+
+// ----------------------------- NVLS (multimem) variant ----------------------------
+// With an NVLink multicast object bound over the symmetric buffers, one
+// multimem.ld_reduce returns the sum over all ranks (reduced inside the NVSwitch) and
+// one multimem.st writes the result into every rank's buffer.  Rank r handles chunk r:
+//   barrier 0 -> ld_reduce / scale / st over its chunk -> multimem.red of its squared
+//   norm into every rank's accumulator -> barrier 1
+// Per rank NVLink carries about (W - 1) / W of the bucket in each direction.
+__device__ __forceinline__ float4 mm_ld_reduce(const float* mc) {
+  float4 v;
+  asm volatile("multimem.ld_reduce.relaxed.sys.global.add.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "l"(mc)
+               : "memory");
+  return v;
+}
+__device__ __forceinline__ void mm_st(float* mc, float4 v) {
+  asm volatile("multimem.st.relaxed.sys.global.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(mc), "f"(v.x), "f"(v.y), "f"(v.z),
+               "f"(v.w)
+               : "memory");
+}
+__device__ __forceinline__ void mm_red_add(float* mc, float v) {
+  asm volatile("multimem.red.relaxed.sys.global.add.f32 [%0], %1;" ::"l"(mc), "f"(v) : "memory");
+}
+
+__global__ void __launch_bounds__(512) nvls_allreduce_kernel(const ArArgs a, float* mc, float* mc_sumsq) {
+  __shared__ volatile int abort_sh;
+  __shared__ float red[32];
+  if (threadIdx.x == 0) abort_sh = 0;
+  __syncthreads();
+  const int W = a.world;
+  const long n = a.hi - a.lo;
+  const long cs = ((n + W - 1) / W + 3) / 4 * 4;
+  const long sub = ((cs + gridDim.x - 1) / gridDim.x + 3) / 4 * 4;
+  if (!cta_barrier(a, 0, &abort_sh)) return;
+  long s0, s1;
+  sub_range(a, cs, sub, a.rank, s0, s1);
+  float ss = 0.f;
+  const long step = static_cast<long>(blockDim.x) * 16;
+  for (long i = s0 + threadIdx.x * 4; i < s1; i += step) {
+    float4 v[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const long j = i + u * blockDim.x * 4;
+      if (j + 3 < s1) v[u] = mm_ld_reduce(mc + j);
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const long j = i + u * blockDim.x * 4;
+      if (j + 3 < s1) {
+        float4 x = v[u];
+        x.x *= a.scale; x.y *= a.scale; x.z *= a.scale; x.w *= a.scale;
+        mm_st(mc + j, x);
+        ss += x.x * x.x + x.y * x.y + x.z * x.z + x.w * x.w;
+      } else if (j < s1) {
+        // ragged tail (bucket end not a multiple of 4): plain peer loads and stores
+        for (long e = j; e < s1; ++e) {
+          float acc = 0.f;
+          for (int p = 0; p < W; ++p) acc += __ldcg(a.ptrs[p] + e);
+          acc *= a.scale;
+          for (int p = 0; p < W; ++p) a.ptrs[p][e] = acc;
+          ss += acc * acc;
+        }
+      }
+    }
+  }
+  ss = warp_sum(ss);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x / 32] = ss;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float v = threadIdx.x < blockDim.x / 32 ? red[threadIdx.x] : 0.f;
+    v = warp_sum(v);
+    if (threadIdx.x == 0) mm_red_add(mc_sumsq, v);
+  }
+  cta_barrier(a, 1, &abort_sh);
+}
+
+void nvls_allreduce(int64_t ptrs_dev, int64_t pads_dev, int64_t pad_words, int64_t mc_ptr, int64_t mc_sumsq,
+                    int64_t lo, int64_t hi, int64_t rank, int64_t world, int64_t epoch, double scale,
+                    at::Tensor local_sumsq, int64_t ctas) {
+  TORCH_CHECK(lo % 4 == 0, "nvls_allreduce: bucket start must be 16-byte aligned");
+  TORCH_CHECK(2 * ctas * world <= pad_words, "nvls_allreduce: signal pad too small");
+  const c10::cuda::CUDAGuard guard(local_sumsq.device());
+  ArArgs a{};
+  a.ptrs = reinterpret_cast<float* const*>(ptrs_dev);
+  a.pads = reinterpret_cast<uint32_t* const*>(pads_dev);
+  a.lo = lo;
+  a.hi = hi;
+  a.rank = (int)rank;
+  a.world = (int)world;
+  a.epoch = static_cast<uint32_t>(epoch);
+  a.scale = (float)scale;
+  a.sumsq = local_sumsq.data_ptr<float>();
+  a.status = status_ptr(local_sumsq.device().index());
+  nvls_allreduce_kernel<<<(int)ctas, 512, 0, at::cuda::getCurrentCUDAStream()>>>(
+      a, reinterpret_cast<float*>(mc_ptr), reinterpret_cast<float*>(mc_sumsq));
+  PB_CUDA_CHECK(cudaGetLastError());
 }
 
 // ptrs_dev / pads_dev: device arrays of W uint64 addresses (from the symmetric-memory
@@ -170,10 +310,23 @@ void fused_allreduce(int64_t ptrs_dev, int64_t pads_dev, int64_t pad_words, int6
   a.scale = (float)scale;
   a.sumsq = sumsq.data_ptr<float>();
   a.status = status_ptr(sumsq.device().index());
-  fused_allreduce_kernel<<<(int)ctas, 512, 0, at::cuda::getCurrentCUDAStream()>>>(a);
+  auto st = at::cuda::getCurrentCUDAStream();
+  switch (world) {
+    case 2: fused_allreduce_kernel<2><<<(int)ctas, 512, 0, st>>>(a); break;
+    case 3: fused_allreduce_kernel<3><<<(int)ctas, 512, 0, st>>>(a); break;
+    case 4: fused_allreduce_kernel<4><<<(int)ctas, 512, 0, st>>>(a); break;
+    case 5: fused_allreduce_kernel<5><<<(int)ctas, 512, 0, st>>>(a); break;
+    case 6: fused_allreduce_kernel<6><<<(int)ctas, 512, 0, st>>>(a); break;
+    case 7: fused_allreduce_kernel<7><<<(int)ctas, 512, 0, st>>>(a); break;
+    case 8: fused_allreduce_kernel<8><<<(int)ctas, 512, 0, st>>>(a); break;
+    default: TORCH_CHECK(false, "fused_allreduce: world size 2..8 on one node");
+  }
   PB_CUDA_CHECK(cudaGetLastError());
 }
 
-void comm_bindings(pybind11::module& m) { m.def("fused_allreduce", &fused_allreduce); }
+void comm_bindings(pybind11::module& m) {
+  m.def("fused_allreduce", &fused_allreduce);
+  m.def("nvls_allreduce", &nvls_allreduce);
+}
 
 }  // namespace pb

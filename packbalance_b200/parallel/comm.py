@@ -6,7 +6,10 @@
 peer, plus a per-rank signal pad) and averages contiguous ranges of it with the native
 ``fused_allreduce`` kernel (``csrc/comm.cu``): reduce-scatter with the 1/W scale and the
 squared-norm partial fused in, then all-gather, synchronised by per-CTA flags in the
-peers' signal pads with bounded waits.  The rendezvous and the process group come from
+peers' signal pads with bounded waits.  When the driver binds an NVLink multicast
+object over the buffers, ``nvls_allreduce`` does the same with ``multimem.ld_reduce``
+(the NVSwitch sums the ranks' values) and ``multimem.st`` (the switch writes the
+result into every rank), which halves the NVLink traffic of the two-shot form.  The rendezvous and the process group come from
 ``torch.distributed`` (NCCL); the data never goes through NCCL.
 
 The squared norm of the averaged gradient accumulates in a device scalar across the
@@ -23,26 +26,46 @@ from packbalance_b200.ops import _native
 
 
 class FusedAllReduce:
-    CTAS = 32
+    """``mode``: "nvls" (multimem through the NVSwitch; default when the multicast
+    object is available), "p2p" (two-shot over peer loads) or "auto"."""
 
-    def __init__(self, grad: torch.Tensor, group: dist.ProcessGroup | None = None, flat=None) -> None:
+    CTAS = 64
+
+    def __init__(self, grad: torch.Tensor, group: dist.ProcessGroup | None = None, flat=None, mode: str | None = None) -> None:
+        import os
+
         import torch.distributed._symmetric_memory as symm_mem
 
         if not grad.is_cuda or grad.dtype != torch.float32:
             raise ValueError("fused all-reduce needs an fp32 CUDA gradient buffer")
         self.group = group if group is not None else dist.group.WORLD
-        buf = symm_mem.empty(grad.numel(), dtype=torch.float32, device=grad.device)
+        n = grad.numel()
+        # 16 trailing floats: the step's squared-norm accumulator (written via multicast).
+        full = symm_mem.empty(n + 16, dtype=torch.float32, device=grad.device)
+        full.zero_()
+        self.handle = symm_mem.rendezvous(full, self.group)
+        self.full = full
+        buf = full[:n]
         buf.copy_(grad)
-        self.handle = symm_mem.rendezvous(buf, self.group)
         self.buf = buf
         self.rank = self.handle.rank
         self.world = self.handle.world_size
+        if not 2 <= self.world <= 8:
+            raise RuntimeError("fused all-reduce covers 2..8 ranks of one node")
         self.pad_words = self.handle.signal_pad_size // 4
         self.ctas = min(self.CTAS, self.pad_words // (3 * self.world))
         if self.ctas < 1:
             raise RuntimeError("signal pad too small for the fused all-reduce")
         self.epoch = 0
-        self.sumsq = torch.zeros((), device=grad.device, dtype=torch.float32)
+        mode = mode or os.environ.get("PB_ALLREDUCE", "auto")
+        if int(getattr(self.handle, "offset", 0)) != 0:
+            raise RuntimeError("symmetric buffer must start at its allocation base")
+        mc = int(self.handle.multicast_ptr or 0)
+        self.mode = "nvls" if mode in ("auto", "nvls") and mc else "p2p"
+        if mode == "nvls" and self.mode != "nvls":
+            raise RuntimeError("NVLink multicast is not available for this group")
+        self.mc = mc
+        self.sumsq = full[n] if self.mode == "nvls" else torch.zeros((), device=grad.device, dtype=torch.float32)
         if flat is not None:
             flat.rebind_grad(buf)
         _native.module().fused_allreduce  # fail loudly if the extension lacks the kernel
@@ -53,10 +76,18 @@ class FusedAllReduce:
     def all_reduce_mean(self, lo: int, hi: int) -> torch.Tensor:
         """Average elements [lo, hi) of the gradient over all ranks (current stream)."""
         self.epoch += 1
-        _native.module().fused_allreduce(
-            self.handle.buffer_ptrs_dev, self.handle.signal_pad_ptrs_dev, self.pad_words, lo, hi, self.rank,
-            self.world, self.epoch, 1.0 / self.world, self.sumsq, self.ctas,
-        )
+        C = _native.module()
+        if self.mode == "nvls":
+            n = self.buf.numel()
+            C.nvls_allreduce(
+                self.handle.buffer_ptrs_dev, self.handle.signal_pad_ptrs_dev, self.pad_words, self.mc,
+                self.mc + 4 * n, lo, hi, self.rank, self.world, self.epoch, 1.0 / self.world, self.sumsq, self.ctas,
+            )
+        else:
+            C.fused_allreduce(
+                self.handle.buffer_ptrs_dev, self.handle.signal_pad_ptrs_dev, self.pad_words, lo, hi, self.rank,
+                self.world, self.epoch, 1.0 / self.world, self.sumsq, self.ctas,
+            )
         return self.sumsq
 
     def check(self) -> None:

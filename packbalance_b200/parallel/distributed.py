@@ -85,8 +85,12 @@ class DataParallel:
         bucket_cap_mb: float = 25.0,
         backend: str = "auto",
         group: dist.ProcessGroup | None = None,
+        overlap: bool | None = None,
     ) -> None:
         self.flat = flat
+        # Issue buckets during the backward pass (overlap) or all at once after it.
+        env = os.environ.get("PB_COMM_OVERLAP")
+        self.overlap = (env != "0") if overlap is None and env is not None else (True if overlap is None else overlap)
         self.group = group
         self.world = get_world_size() if dist.is_initialized() else 1
         self.cap = max(1, int(bucket_cap_mb * 1024 * 1024 // 4))
@@ -130,7 +134,7 @@ class DataParallel:
     def notify_ready(self, offset: int) -> None:
         """Every gradient at flat offset >= ``offset`` is final for this step: issue
         the buckets that lie entirely above it."""
-        if self.world <= 1:
+        if self.world <= 1 or not self.overlap:
             return
         for i, (lo, hi) in enumerate(self.buckets):
             if not self._issued[i] and lo >= offset:

@@ -36,7 +36,9 @@ WORKER = textwrap.dedent(
     ref = grad.clone()
     dist.all_reduce(ref)
     ref /= world
-    ar = FusedAllReduce(grad)
+    ar = FusedAllReduce(grad, mode=os.environ["PB_ALLREDUCE"])
+    if rank == 0:
+        print("mode", ar.mode)
     for step in range(3):
         ar.buf.copy_(grad)
         ar.start_step()
@@ -58,12 +60,13 @@ WORKER = textwrap.dedent(
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_fused_allreduce_matches_nccl(tmp_path):
+@pytest.mark.parametrize("mode", ["p2p", "auto"])
+def test_fused_allreduce_matches_nccl(tmp_path, mode):
     world = min(torch.cuda.device_count(), 8)
     script = tmp_path / "worker.py"
     script.write_text(WORKER)
     env = {**os.environ, "PB_ROOT": str(ROOT), "MASTER_ADDR": "127.0.0.1", "MASTER_PORT": str(_free_port()),
-           "NCCL_NVLS_ENABLE": "0"}
+           "NCCL_NVLS_ENABLE": "0", "PB_ALLREDUCE": mode}
     r = subprocess.run(
         ["timeout", "-k", "30", "240", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
          f"--nproc-per-node={world}", "--master-addr=127.0.0.1", f"--master-port={env['MASTER_PORT']}", str(script)],
@@ -71,6 +74,7 @@ def test_fused_allreduce_matches_nccl(tmp_path):
     )
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
     assert r.stdout.count("ok") == world
+    print(r.stdout[:200])
 
 
 def test_barrier_timeout_reports_status():
