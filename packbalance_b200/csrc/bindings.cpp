@@ -12,7 +12,7 @@ void gemm_tc(at::Tensor a, at::Tensor b, at::Tensor out, int64_t M, int64_t N, i
              c10::optional<at::Tensor> sin_t, int64_t head_dim, int64_t n_rope_cols,
              c10::optional<at::Tensor> targets, c10::optional<at::Tensor> pmax, c10::optional<at::Tensor> psum,
              c10::optional<at::Tensor> tlogit, c10::optional<at::Tensor> lse, c10::optional<at::Tensor> row_scale,
-             double z_coeff);
+             double z_coeff, std::vector<int64_t> ag);
 std::vector<at::Tensor> add_rmsnorm_fwd(at::Tensor x, c10::optional<at::Tensor> delta, at::Tensor w, double eps,
                                         bool out_bf16);
 void swiglu_bwd_packed(at::Tensor dh, at::Tensor gu, at::Tensor dgu);
@@ -32,17 +32,14 @@ void adamw_step(at::Tensor p, at::Tensor g, at::Tensor m, at::Tensor v, at::Tens
                 at::Tensor skipped, double lr, double b1, double b2, double eps, double wd, double bc1, double bc2,
                 double max_norm, bool write_shadow);
 at::Tensor l2_norm(at::Tensor x);
-#ifdef PB_WITH_ATTENTION
 std::vector<at::Tensor> attn_fwd(at::Tensor qkv, at::Tensor doc_start, at::Tensor tiles, int64_t n_heads,
                                  int64_t n_kv_heads, int64_t head_dim, double scale, at::Tensor out);
 void attn_bwd(at::Tensor qkv, at::Tensor out, at::Tensor dout, at::Tensor lse, at::Tensor doc_start,
               at::Tensor doc_end, at::Tensor items, int64_t H, int64_t Hkv, int64_t D, double scale, at::Tensor dqkv,
               at::Tensor dq_acc, at::Tensor dkv_acc, at::Tensor delta, c10::optional<at::Tensor> pos,
               c10::optional<at::Tensor> cos_t, c10::optional<at::Tensor> sin_t);
-#endif
-#ifdef PB_WITH_COMM
 void comm_bindings(pybind11::module& m);
-#endif
+void fsdp_bindings(pybind11::module& m);
 
 int64_t status_read(int64_t dev, bool clear) {
   int v = 0;
@@ -70,11 +67,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("adamw_step", &pb::adamw_step);
   m.def("l2_norm", &pb::l2_norm);
   m.def("status_read", &pb::status_read, pybind11::arg("dev"), pybind11::arg("clear") = true);
-#ifdef PB_WITH_ATTENTION
   m.def("attn_fwd", &pb::attn_fwd);
   m.def("attn_bwd", &pb::attn_bwd);
-#endif
-#ifdef PB_WITH_COMM
   pb::comm_bindings(m);
-#endif
+  pb::fsdp_bindings(m);
 }

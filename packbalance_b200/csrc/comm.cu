@@ -24,71 +24,11 @@
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/extension.h>
 
+#include "comm_common.cuh"
 #include "common.cuh"
 #include "host_utils.h"
 
 namespace pb {
-
-struct ArArgs {
-  float* const* ptrs;   // [W] peer buffer base pointers (device array)
-  uint32_t* const* pads;  // [W] peer signal pads (device array)
-  long lo, hi;
-  int rank, world;
-  uint32_t epoch;
-  float scale;
-  float* sumsq;
-  int* status;
-};
-
-__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
-  uint32_t v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
-
-// Barrier ``k`` between CTA ``blockIdx.x`` of every rank.  Slot (k, b, p) of rank r's pad
-// holds the last epoch in which rank p reached barrier k with CTA b.
-__device__ __forceinline__ bool cta_barrier(const ArArgs& a, int k, volatile int* abort) {
-  __syncthreads();
-  const int b = blockIdx.x;
-  const int W = a.world;
-  bool ok = true;
-  if (threadIdx.x < W) {
-    const int p = threadIdx.x;
-    const long slot_mine = (static_cast<long>(k) * gridDim.x + b) * W + a.rank;
-    __threadfence_system();
-    st_release_sys(a.pads[p] + slot_mine, a.epoch);
-    const uint32_t* watch = a.pads[a.rank] + (static_cast<long>(k) * gridDim.x + b) * W + p;
-    const uint64_t t0 = globaltimer();
-    while (static_cast<int>(ld_acquire_sys(watch) - a.epoch) < 0) {
-      if (*abort) {
-        ok = false;
-        break;
-      }
-      if (globaltimer() - t0 > PB_WAIT_TIMEOUT_NS / 2) {
-        report_error(a.status, 401 + 1000 * p);
-        *abort = 1;
-        ok = false;
-        break;
-      }
-    }
-  }
-  __syncthreads();
-  return ok && !*abort;
-}
-
-constexpr int kMaxWorld = 8;
-
-// Sub-range of chunk ``c`` owned by this CTA (same split on every rank).
-__device__ __forceinline__ void sub_range(const ArArgs& a, long cs, long sub, int c, long& s0, long& s1) {
-  const long c0 = a.lo + c * cs;
-  const long c1 = min(c0 + cs, a.hi);
-  s0 = min(c0 + static_cast<long>(blockIdx.x) * sub, c1);
-  s1 = min(s0 + sub, c1);
-}
 
 template <int W>
 __device__ __forceinline__ float reduce_phase(const ArArgs& a, long s0, long s1) {

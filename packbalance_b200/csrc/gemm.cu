@@ -12,6 +12,7 @@ namespace pb {
 template <int BN, bool A_MN, bool B_MN>
 static void launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& to, const CUtensorMap& tx,
                         const GemmArgs& args, int grid, cudaStream_t stream) {
+  const int threads = args.ag.world > 0 ? 256 : 192;
   using C = GemmCfg<BN>;
   auto kern = gemm_tc_kernel<BN, A_MN, B_MN>;
   static bool configured[64] = {false};
@@ -21,7 +22,7 @@ static void launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const CUte
     PB_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES));
     configured[dev] = true;
   }
-  kern<<<grid, 192, C::SMEM_BYTES, stream>>>(ta, tb, to, tx, args);
+  kern<<<grid, threads, C::SMEM_BYTES, stream>>>(ta, tb, to, tx, args);
   PB_CUDA_CHECK(cudaGetLastError());
 }
 
@@ -56,7 +57,7 @@ void gemm_tc(at::Tensor a, at::Tensor b, at::Tensor out, int64_t M, int64_t N, i
              c10::optional<at::Tensor> sin_t, int64_t head_dim, int64_t n_rope_cols,
              c10::optional<at::Tensor> targets, c10::optional<at::Tensor> pmax, c10::optional<at::Tensor> psum,
              c10::optional<at::Tensor> tlogit, c10::optional<at::Tensor> lse, c10::optional<at::Tensor> row_scale,
-             double z_coeff) {
+             double z_coeff, std::vector<int64_t> ag) {
   TORCH_CHECK(a.is_cuda() && b.is_cuda(), "gemm_tc: CUDA tensors required");
   TORCH_CHECK(a.scalar_type() == at::kBFloat16 && b.scalar_type() == at::kBFloat16, "gemm_tc: bf16 operands");
   TORCH_CHECK(a.dim() == 2 && b.dim() == 2 && a.stride(1) == 1 && b.stride(1) == 1, "gemm_tc: 2-D row-major");
@@ -133,6 +134,45 @@ void gemm_tc(at::Tensor a, at::Tensor b, at::Tensor out, int64_t M, int64_t N, i
   if (b_mn) tb = make_tmap_bf16_2d(b.data_ptr(), N, K, b.stride(0) * 2, 64, 64);
   else tb = make_tmap_bf16_2d(b.data_ptr(), K, N, b.stride(0) * 2, 64, swiglu ? bn / 2 : bn);
 
+  cudaStream_t stream0 = at::cuda::getCurrentCUDAStream();
+  if (!ag.empty()) {
+    // Fused all-gather of B: {src_ptrs_dev, dst, lo, hi, unit0, cs, b0, rank, world,
+    //                         piece_shift, flags, counter, epoch}
+    TORCH_CHECK(ag.size() == 13, "gemm_tc: ag spec has 13 fields");
+    TORCH_CHECK(!b_mn, "gemm_tc: the fused all-gather feeds a K-major B");
+    AgSpec& s = g.ag;
+    s.src = reinterpret_cast<const __nv_bfloat16* const*>(ag[0]);
+    s.dst = reinterpret_cast<__nv_bfloat16*>(ag[1]);
+    s.lo = ag[2];
+    s.hi = ag[3];
+    s.unit0 = ag[4];
+    s.cs = ag[5];
+    s.b0 = ag[6];
+    s.rank = (int)ag[7];
+    s.world = (int)ag[8];
+    s.piece_shift = (int)ag[9];
+    s.flags = reinterpret_cast<uint32_t*>(ag[10]);
+    s.counter = reinterpret_cast<int*>(ag[11]);
+    s.epoch = static_cast<uint32_t>(ag[12]);
+    TORCH_CHECK(s.world >= 2 && s.world <= 8 && s.rank >= 0 && s.rank < s.world, "gemm_tc: ag rank/world");
+    TORCH_CHECK(s.lo % 8 == 0 && s.hi % 8 == 0 && s.unit0 % 8 == 0 && s.cs % 8 == 0 && s.cs > 0,
+                "gemm_tc: ag ranges must be 16-byte aligned");
+    TORCH_CHECK(s.piece_shift >= 3 && s.piece_shift <= 24, "gemm_tc: ag piece size");
+    TORCH_CHECK(s.lo >= s.unit0 && s.hi <= s.unit0 + s.world * s.cs, "gemm_tc: ag range outside its unit");
+    TORCH_CHECK(reinterpret_cast<const char*>(b.data_ptr()) ==
+                    reinterpret_cast<const char*>(s.dst) + 2 * s.b0,
+                "gemm_tc: B must be the gathered buffer at element b0");
+    // Start with the tiles whose rows this rank owns (no wait), then follow the copy
+    // order, which starts right after this rank's own range.
+    const long own0 = s.unit0 + s.rank * s.cs, own1 = own0 + s.cs;
+    const int np = (int)((s.hi - s.lo + (1L << s.piece_shift) - 1) >> s.piece_shift);
+    s.rot = (own1 > s.lo && own1 < s.hi) ? (int)((own1 - s.lo) >> s.piece_shift) : 0;
+    if (s.rot >= np) s.rot = 0;
+    const long row = std::max<long>(0, (std::max(own0, s.lo) - s.b0) / K);
+    const long rows_per_tile = swiglu ? bn / 2 : bn;
+    g.n_rot = (int)(((swiglu ? row % (N / 2) : row) / rows_per_tile) % g.n_tiles);
+    PB_CUDA_CHECK(cudaMemsetAsync(s.counter, 0, sizeof(int), stream0));
+  }
   const int tiles = g.m_tiles * g.n_tiles * g.splits;
   int grid = std::min<int>(tiles, num_sms(a.device().index()));
   if (max_ctas > 0) grid = std::min<int>(grid, (int)max_ctas);

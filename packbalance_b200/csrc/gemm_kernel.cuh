@@ -11,6 +11,10 @@
 // Kernel structure (one CTA per SM, persistent over output tiles of 128 x BN):
 //   warp 0      TMA producer: 128B-swizzled A/B tiles into a STAGES-deep smem ring
 //   warp 1      TMEM allocator + single-thread tcgen05.mma issuer (M=128, N=BN, K=16)
+//   warps 6..7  (only in launches with a fused all-gather, 256 threads) copy warps that
+//               fetch the peer-owned parts of the sharded B operand into this GPU's
+//               gathered buffer while the MMAs run (ag_copy.cuh); the producer waits
+//               per B tile for the pieces it covers
 //   warps 2..5  epilogue, warp q owns TMEM lanes [32q, 32q+32) (= tile rows): each
 //               32-column chunk goes tcgen05.ld -> registers -> fused math -> swizzled
 //               smem staging slot -> TMA store (or TMA fp32 reduce-add), so global
@@ -36,6 +40,7 @@
 
 #include <cudaTypedefs.h>
 
+#include "ag_copy.cuh"
 #include "common.cuh"
 
 namespace pb {
@@ -70,6 +75,8 @@ struct GemmArgs {
   const float* row_scale;
   float z_coeff;
   int* status;
+  AgSpec ag;  // ag.world == 0: B is already local
+  int n_rot;  // n-blocks are visited starting at this one (wrapping)
 };
 
 constexpr int kEpiWarpBytes = 8192;  // two 4 KB staging slots per epilogue warp
@@ -92,7 +99,8 @@ __device__ __forceinline__ void tile_coords(const GemmArgs& a, int tile, int& mb
   sp = tile % a.splits;
   const int t = tile / a.splits;
   mb = t % a.m_tiles;
-  nb = t / a.m_tiles;
+  nb = t / a.m_tiles + a.n_rot;
+  if (nb >= a.n_tiles) nb -= a.n_tiles;
 }
 
 // ------------------------------- epilogue helpers ---------------------------------
@@ -319,7 +327,7 @@ __device__ __forceinline__ void run_epilogue(const GemmArgs& a, const CUtensorMa
 
 // ------------------------------------ kernel --------------------------------------
 template <int BN, bool A_MN, bool B_MN>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(256, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
                    const __grid_constant__ CUtensorMap tm_out, const __grid_constant__ CUtensorMap tm_aux,
                    const GemmArgs args) {
@@ -376,6 +384,20 @@ __global__ void __launch_bounds__(192, 1)
         tile_coords(args, tile, mb, nb, sp);
         const int kb0 = sp * args.kb_per_split;
         const int kb1 = min(args.k_blocks, kb0 + args.kb_per_split);
+        if (args.ag.world > 0) {
+          // The B rows of this tile must have been gathered (K-major B only).
+          const long K = args.K;
+          if (swiglu) {
+            const long r0 = static_cast<long>(nb) * (BN / 2), r1 = min(r0 + BN / 2, static_cast<long>(args.F));
+            ok = ag_wait_range(args.ag, args.ag.b0 + r0 * K, args.ag.b0 + r1 * K, args.status, 107, &abort_sh) &&
+                 ag_wait_range(args.ag, args.ag.b0 + (args.F + r0) * K, args.ag.b0 + (args.F + r1) * K, args.status,
+                               107, &abort_sh);
+          } else {
+            const long r0 = static_cast<long>(nb) * BN, r1 = min(r0 + BN, static_cast<long>(args.N));
+            ok = ag_wait_range(args.ag, args.ag.b0 + r0 * K, args.ag.b0 + r1 * K, args.status, 107, &abort_sh);
+          }
+          if (!ok) break;
+        }
         for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&empty_bar[stage], phase ^ 1, args.status, 101, &abort_sh)) {
             ok = false;
@@ -461,6 +483,8 @@ __global__ void __launch_bounds__(192, 1)
       umma_commit(&drain_bar);
       mbar_wait(&drain_bar, 0, args.status, 105, nullptr);
     }
+  } else if (warp >= 6) {
+    if (args.ag.world > 0) ag_copy_warp(args.ag);
   } else {
     const int q = warp & 3;
     Stager st{smem + C::EPI_OFF + q * kEpiWarpBytes, 0};

@@ -61,7 +61,7 @@ class _Embed(torch.autograd.Function):
         ctx.sc = sc
         ctx.ids = ids
         ctx.weight = weight
-        return _native.module().embedding_fwd(ids, weight)
+        return sc.flat.embedding(ids, weight)
 
     @staticmethod
     def backward(ctx, dx):
@@ -69,7 +69,7 @@ class _Embed(torch.autograd.Function):
         w = ctx.weight
         acc = flat.claim(w)
         _native.module().embedding_bwd(ctx.ids, dx.contiguous(), flat.grad_of(w), acc)
-        flat.ready(flat.slot(w).offset)
+        flat.ready_after(w)
         return None, None, None
 
 
@@ -85,15 +85,17 @@ class _Decoder(torch.autograd.Function):
         F = cfg.d_ff
         x, xn1, rstd1 = C.add_rmsnorm_fwd(x_prev, delta_prev, w_in, cfg.norm_eps, True)
         qkv = torch.empty(t, nqkv, device=x.device, dtype=torch.bfloat16)
+        ag = flat.gather_spec(wq, wk, wv)  # sharded weights: fetched inside this GEMM
         gemm(xn1, flat.shadow_of(wq, wk, wv), qkv, t, nqkv, d, epi=EPI_ROPE, pos=sc.pos, cos=sc.cos, sin=sc.sin,
-             head_dim=hd, n_rope_cols=(h + hk) * hd)
+             head_dim=hd, n_rope_cols=(h + hk) * hd, ag=ag)
         o, lse = attn_forward_packed(qkv, sc.plan, h, hk, hd)
         attn_out = torch.empty(t, d, device=x.device, dtype=torch.bfloat16)
         gemm(o, flat.shadow_of(wo), attn_out, t, d, h * hd, epi=EPI_BF16)
         x1, xn2, rstd2 = C.add_rmsnorm_fwd(x, attn_out, w_post, cfg.norm_eps, True)
         hmid = torch.empty(t, F, device=x.device, dtype=torch.bfloat16)
         gu = torch.empty(t, 2 * F, device=x.device, dtype=torch.bfloat16)
-        gemm(xn2, flat.shadow_of(wg, wu), hmid, t, 2 * F, d, epi=EPI_SWIGLU, aux=gu)
+        ag = flat.gather_spec(wg, wu)
+        gemm(xn2, flat.shadow_of(wg, wu), hmid, t, 2 * F, d, epi=EPI_SWIGLU, aux=gu, ag=ag)
         mlp_out = torch.empty(t, d, device=x.device, dtype=torch.bfloat16)
         gemm(hmid, flat.shadow_of(wd), mlp_out, t, d, F, epi=EPI_BF16)
         ctx.sc = sc
@@ -139,7 +141,7 @@ class _Decoder(torch.autograd.Function):
         _wgrad(flat, (wq, wk, wv), dqkv, xn1)
         dxb = torch.empty(t, d, device=dev, dtype=torch.bfloat16)
         dx = C.rmsnorm_bwd(dxn1, x, w_in, rstd1, dx1, dxb, flat.grad_of(w_in).view(-1), flat.claim(w_in))
-        flat.ready(flat.slot(w_in).offset)
+        flat.ready_after(w_in)
         return (dx, dxb if ctx.has_delta else None) + (None,) * 10
 
 
@@ -149,7 +151,8 @@ class _Head(torch.autograd.Function):
         cfg = sc.cfg
         C = _native.module()
         x, xf, rstd = C.add_rmsnorm_fwd(x_prev, delta_prev, w_norm, cfg.norm_eps, True)
-        loss, lse = lmhead_ce_forward(xf, sc.flat.shadow_of(w_lm), labels, -100, cfg.z_loss_coeff)
+        ag = sc.flat.gather_spec(w_lm)
+        loss, lse = lmhead_ce_forward(xf, sc.flat.shadow_of(w_lm), labels, -100, cfg.z_loss_coeff, ag=ag)
         ctx.sc = sc
         ctx.has_delta = delta_prev is not None
         ctx.saved = (x, xf, rstd, lse, labels)
@@ -170,14 +173,13 @@ class _Head(torch.autograd.Function):
         dxb = torch.empty(x.shape, device=x.device, dtype=torch.bfloat16)
         dx = _native.module().rmsnorm_bwd(dxf, x, w_norm, rstd, None, dxb, flat.grad_of(w_norm).view(-1),
                                           flat.claim(w_norm))
-        lm_off = flat.slot(w_norm).offset
-        if sc.model.lm_head is not None:
-            lm_off = min(lm_off, flat.slot(w_lm).offset)
-        flat.ready(lm_off)
+        flat.ready_after(w_norm)
         return dx, (dxb if ctx.has_delta else None), None, None, None, None
 
 
-def _ensure_flat(model) -> FlatParameters:
+def _ensure_flat(model):
+    """The model's parameter buffers: :class:`FlatParameters` (single GPU, DDP) or the
+    sharded layout of :mod:`packbalance_b200.parallel.sharded` (same interface)."""
     if model.flat is None:
         model.flat = FlatParameters(model)
     model.flat.refresh_shadow()

@@ -29,9 +29,15 @@ DLOGIT_CHUNK_BYTES = 256 * 1024 * 1024
 
 
 def lmhead_ce_forward(
-    x: torch.Tensor, w: torch.Tensor, targets: torch.Tensor, ignore_index: int = -100, z_coeff: float = 0.0
+    x: torch.Tensor,
+    w: torch.Tensor,
+    targets: torch.Tensor,
+    ignore_index: int = -100,
+    z_coeff: float = 0.0,
+    ag: list[int] | None = None,
 ) -> tuple[torch.Tensor, torch.Tensor]:
-    """Returns (summed loss, lse[T]).  ``x`` [T, d] bf16, ``w`` [V, d] bf16."""
+    """Returns (summed loss, lse[T]).  ``x`` [T, d] bf16, ``w`` [V, d] bf16.  ``ag``: the
+    sharded LM head is fetched inside the GEMM (see :func:`~packbalance_b200.ops.gemm.gemm`)."""
     t, d = x.shape
     v = w.shape[0]
     nt = -(-v // CE_TILE)
@@ -41,7 +47,7 @@ def lmhead_ce_forward(
     lse = torch.empty(t, device=x.device, dtype=torch.float32)
     loss = torch.zeros((), device=x.device, dtype=torch.float32)
     tgt = targets.reshape(-1).to(torch.int64).contiguous()
-    gemm(x, w, pmax, t, v, d, epi=EPI_CE_FWD, bn=CE_TILE, targets=tgt, pmax=pmax, psum=psum, tlogit=tlogit)
+    gemm(x, w, pmax, t, v, d, epi=EPI_CE_FWD, bn=CE_TILE, targets=tgt, pmax=pmax, psum=psum, tlogit=tlogit, ag=ag)
     _native.module().ce_finalize(pmax, psum, tlogit, tgt, ignore_index, float(z_coeff), lse, loss)
     return loss, lse
 

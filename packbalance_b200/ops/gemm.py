@@ -92,8 +92,13 @@ def gemm(
     lse=None,
     row_scale=None,
     z_coeff: float = 0.0,
+    ag: list[int] | None = None,
 ) -> torch.Tensor:
-    """Launch the tcgen05 GEMM ``D[m, n] = sum_k A(m, k) B(n, k)`` with epilogue ``epi``."""
+    """Launch the tcgen05 GEMM ``D[m, n] = sum_k A(m, k) B(n, k)`` with epilogue ``epi``.
+
+    ``ag``: fused all-gather of a sharded K-major B (13 ints, built by
+    :meth:`packbalance_b200.parallel.sharded.ShardedParameters.gather_spec`): copy warps
+    fetch the peer-owned rows of B into this GPU's gathered buffer during the GEMM."""
     if bn is None:
         allowed = (256, 128, 64)
         if epi == EPI_ROPE:
@@ -102,6 +107,7 @@ def gemm(
     _native.module().gemm_tc(
         a, b, out, m, n, k, a_mn, b_mn, epi, bn, splits, max_ctas, alpha,
         aux, pos, cos, sin, head_dim, n_rope_cols, targets, pmax, psum, tlogit, lse, row_scale, z_coeff,
+        ag or [],
     )
     return out
 

@@ -110,6 +110,7 @@ class DataParallel:
             self.stream = torch.cuda.Stream(priority=-1)
         self._issued: list[bool] = [False] * len(self.buckets)
         self._norm_parts: list[torch.Tensor] = []
+        self.hold = False  # set while a non-final microbatch runs its backward pass
 
     def _make_buckets(self) -> list[tuple[int, int]]:
         """Contiguous ranges of whole parameters, last parameters first (backward order).
@@ -134,7 +135,7 @@ class DataParallel:
     def notify_ready(self, offset: int) -> None:
         """Every gradient at flat offset >= ``offset`` is final for this step: issue
         the buckets that lie entirely above it."""
-        if self.world <= 1 or not self.overlap:
+        if self.world <= 1 or not self.overlap or self.hold:
             return
         for i, (lo, hi) in enumerate(self.buckets):
             if not self._issued[i] and lo >= offset:

@@ -37,7 +37,30 @@ class Slot:
     shape: torch.Size
 
 
-class FlatParameters:
+class GradWindow:
+    """First-writer-overwrites protocol of one accumulation window.
+
+    Kernels that produce a weight gradient call :meth:`claim` first: the first writer of
+    a window overwrites the gradient memory (no zeroing pass), later writers (the second
+    use of a tied weight, the next microbatch) accumulate."""
+
+    _fresh: set[int]
+
+    def begin_window(self) -> None:
+        """New window without clearing memory (every slot is overwritten first)."""
+        self._fresh.clear()
+
+    def claim(self, *params: nn.Parameter) -> bool:
+        """Return True if the caller must accumulate (an earlier writer this window)."""
+        key = id(params[0])
+        if key in self._fresh:
+            return True
+        for p in params:
+            self._fresh.add(id(p))
+        return False
+
+
+class FlatParameters(GradWindow):
     def __init__(self, module: nn.Module, *, with_shadow: bool | None = None) -> None:
         seen: set[int] = set()
         slots: list[Slot] = []
@@ -121,10 +144,6 @@ class FlatParameters:
         self._fresh.clear()
         self.grad.zero_()
 
-    def begin_window(self) -> None:
-        """New window without clearing memory (every slot is overwritten first)."""
-        self._fresh.clear()
-
     def finish_window(self) -> None:
         """Zero the gradient of every slot no writer claimed this window (a slot that
         is not written must not keep last step's values)."""
@@ -141,11 +160,18 @@ class FlatParameters:
     def ready_all(self) -> None:
         self.ready(0)
 
-    def claim(self, *params: nn.Parameter) -> bool:
-        """Return True if the caller must accumulate (an earlier writer this window)."""
-        key = id(params[0])
-        if key in self._fresh:
-            return True
-        for p in params:
-            self._fresh.add(id(p))
-        return False
+    def ready_after(self, p: nn.Parameter) -> None:
+        """The gradients of ``p`` and of every parameter registered after it are final
+        (the backward pass runs in reverse registration order)."""
+        self.ready(self.slot(p).offset)
+
+    # ---- hooks the sharded layout overrides ------------------------------------
+    def gather_spec(self, *params: nn.Parameter) -> list[int] | None:
+        """Fused all-gather spec for the GEMM that first reads ``params`` (none here:
+        every weight is local)."""
+        return None
+
+    def embedding(self, ids: torch.Tensor, weight: nn.Parameter) -> torch.Tensor:
+        from packbalance_b200.ops import _native
+
+        return _native.module().embedding_fwd(ids, weight)

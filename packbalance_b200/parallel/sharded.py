@@ -1,0 +1,498 @@
+"""Fully-sharded data parallelism over NVSwitch peer memory (native FSDP engine).
+
+Replaces the reference's FSDP2 wrapping (``train/distributed.py:42-51``: ``fully_shard``
+per decoder layer, then the root) for the native CUDA path.  Same sharding units (one
+per decoder layer, one for the embedding, one for an untied LM head); the collectives
+are this framework's own kernels:
+
+* **all-gather fused into the consuming GEMM.**  Each unit lives in a bf16 "gathered"
+  buffer in symmetric memory (same layout on every rank; rank p owns the p-th of W
+  equal chunks of every unit).  The first GEMM that reads a unit's weights in a step
+  (the QKV GEMM for q|k|v|o, the gate|up GEMM for gate|up|down, the LM-head GEMM for
+  the head) carries copy warps that fetch the peer-owned chunks over NVLink while its
+  MMAs run on the tiles that are already local (``csrc/ag_copy.cuh``).  The embedding
+  lookup reads its rows straight from the owners' fp32 master shards.
+* **reduce-scatter as each unit's backward finishes**, on a communication stream: rank
+  r sums chunk r of the unit's gradient over all ranks, scales by 1/W and keeps only
+  that chunk (fp32), plus its squared norm.
+* **reduce-scatter fused with the sharded AdamW**: the embedding unit, finished last,
+  is reduced by the optimizer kernel itself, which then exchanges the shards' squared
+  norms through peer memory, clips, runs AdamW on the fp32 master shard and writes
+  the bf16 copy of its chunk into the gathered buffer for the next step's fetches
+  (``csrc/fsdp.cu``).
+
+Memory per rank (B200 has 180 GB): bf16 weights 2 B/param (kept for the whole step,
+so the backward pass needs no second all-gather), fp32 gradient 4 B/param, and
+16 B/param / W of sharded fp32 master + moments + reduced gradient.  RMSNorm weights
+(a few KB per layer) stay replicated in fp32; their gradient is averaged with the
+fused all-reduce.
+
+Checkpoints use the reference's FSDP layout (``torch.distributed.checkpoint`` with
+``model.<name>`` and AdamW ``optimizer.state.<i>.*`` keys, full tensors).
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass, field
+from typing import Any
+
+import torch
+import torch.distributed as dist
+from torch import nn
+
+from packbalance_b200.ops import _native
+from packbalance_b200.parallel.flat import GradWindow, Slot
+
+ALIGN = 64  # elements; chunk boundaries stay 16-byte aligned in bf16 and fp32
+SYNC_WORDS = 16384  # per-CTA barrier slots (uint32) in the symmetric sync buffer
+PIECE_SHIFT = 14  # all-gather piece = 16384 bf16 = 32 KB
+
+
+@dataclass
+class Unit:
+    name: str
+    slots: list[Slot]
+    unit0: int = 0  # first element in gathered/gradient coordinates
+    cs: int = 0  # chunk size per rank
+    soff: int = 0  # offset of this rank's chunk in the shard buffers
+    order: int = 0  # position in model order (embedding 0, layers 1..L, head L+1)
+    span: int = 0  # elements of parameters (the rest up to W * cs is padding)
+    segments: list[tuple[int, int]] = field(default_factory=list)  # gather ranges (element lo, hi)
+
+
+def _units_of(model) -> tuple[list[Slot], list[Unit]]:
+    """Replicated RMSNorm weights and the sharded units, in model order."""
+    m = model.model
+    norms: list[nn.Parameter] = []
+    units: list[tuple[str, list[nn.Parameter]]] = [("embed", [m.embed_tokens.weight])]
+    for i, layer in enumerate(m.layers):
+        a, mlp = layer.self_attn, layer.mlp
+        norms += [layer.input_layernorm.weight, layer.post_attention_layernorm.weight]
+        units.append((f"layer{i}", [a.q_proj.weight, a.k_proj.weight, a.v_proj.weight, a.o_proj.weight,
+                                    mlp.gate_proj.weight, mlp.up_proj.weight, mlp.down_proj.weight]))
+    norms.append(m.norm.weight)
+    if model.lm_head is not None:
+        units.append(("head", [model.lm_head.weight]))
+    names = {id(p): n for n, p in model.named_parameters()}
+    covered = {id(p) for p in norms} | {id(p) for _, ps in units for p in ps}
+    missing = [n for n, p in model.named_parameters() if p.requires_grad and id(p) not in covered]
+    if missing:
+        raise ValueError(f"sharded layout does not cover parameters: {missing}")
+    rep = [Slot(names[id(p)], p, 0, p.numel(), p.shape) for p in norms]
+    out = [Unit(n, [Slot(names[id(p)], p, 0, p.numel(), p.shape) for p in ps], order=i) for i, (n, ps) in enumerate(units)]
+    return rep, out
+
+
+class ShardedParameters(GradWindow):
+    """Sharded parameter/gradient/optimizer-state buffers of one model (CUDA, W >= 2)."""
+
+    def __init__(self, model, group: dist.ProcessGroup | None = None, rs_ctas: int = 64) -> None:
+        import torch.distributed._symmetric_memory as symm_mem
+
+        self.group = group if group is not None else dist.group.WORLD
+        self.world = dist.get_world_size(self.group)
+        self.rank = dist.get_rank(self.group)
+        if not 2 <= self.world <= 8:
+            raise RuntimeError("the sharded engine covers 2..8 GPUs of one node")
+        first = next(model.parameters())
+        self.device = first.device
+        if self.device.type != "cuda":
+            raise RuntimeError("the sharded engine needs CUDA tensors")
+        self.model = model
+        W = self.world
+        rep, units = _units_of(model)
+
+        # ---- layout: [replicated norms | unit 0 | unit 1 | ...] ----------------------
+        off = 0
+        for s in rep:
+            s.offset = off
+            off += s.numel
+        self.rep_n = -(-off // ALIGN) * ALIGN
+        off = self.rep_n
+        soff = 0
+        for u in units:
+            u.unit0 = off
+            for s in u.slots:
+                s.offset = off
+                off += s.numel
+            span = off - u.unit0
+            padded = -(-span // (W * ALIGN)) * W * ALIGN
+            u.cs = padded // W
+            u.soff = soff
+            u.span = span
+            soff += u.cs
+            off = u.unit0 + padded
+        self.numel = off
+        self.shard_numel = soff
+        self.rep_slots = rep
+        self.units = units
+        self.embed_unit = units[0]
+        self.slots = rep + [s for u in units for s in u.slots]
+        self.by_param = {id(s.param): s for s in self.slots}
+        self.unit_of = {id(s.param): u for u in units for s in u.slots}
+        # gather segments: q..o and gate..down of a layer, whole unit otherwise
+        for u in units:
+            if u.name.startswith("layer"):
+                q, o, g, d = u.slots[0], u.slots[3], u.slots[4], u.slots[6]
+                u.segments = [(q.offset, o.offset + o.numel), (g.offset, d.offset + d.numel)]
+            else:
+                u.segments = [(u.unit0, u.unit0 + u.span)]
+        # norms (and, for the ready protocol, their layer's unit order)
+        self.rep_order = {}
+        for i, layer in enumerate(model.model.layers):
+            self.rep_order[id(layer.input_layernorm.weight)] = i + 1
+            self.rep_order[id(layer.post_attention_layernorm.weight)] = i + 1
+        self.rep_order[id(model.model.norm.weight)] = len(model.model.layers) + 1
+
+        # ---- buffers -------------------------------------------------------------------
+        dev = self.device
+        self.gathered = symm_mem.empty(self.numel, dtype=torch.bfloat16, device=dev)
+        self.grad = symm_mem.empty(self.numel, dtype=torch.float32, device=dev)
+        self.master = symm_mem.empty(max(self.shard_numel, 4), dtype=torch.float32, device=dev)
+        self.sync = symm_mem.empty(SYNC_WORDS + 64, dtype=torch.int32, device=dev)
+        self.grad.zero_()
+        self.master.zero_()
+        self.sync.zero_()
+        self.h_gath = symm_mem.rendezvous(self.gathered, self.group)
+        self.h_grad = symm_mem.rendezvous(self.grad, self.group)
+        self.h_master = symm_mem.rendezvous(self.master, self.group)
+        self.h_sync = symm_mem.rendezvous(self.sync, self.group)
+        for h in (self.h_gath, self.h_grad, self.h_master, self.h_sync):
+            if int(getattr(h, "offset", 0)) != 0:
+                raise RuntimeError("symmetric buffers must start at their allocation base")
+        self.xchg_ptrs = torch.tensor([int(p) + 4 * SYNC_WORDS for p in self.h_sync.buffer_ptrs], dtype=torch.int64,
+                                      device=dev)
+        self.exp_avg = torch.zeros(max(self.shard_numel, 4), dtype=torch.float32, device=dev)
+        self.exp_avg_sq = torch.zeros_like(self.exp_avg)
+        self.shard_grad = torch.zeros_like(self.exp_avg)
+        self.rep_data = torch.zeros(self.rep_n, dtype=torch.float32, device=dev)
+        self.rep_m = torch.zeros_like(self.rep_data)
+        self.rep_v = torch.zeros_like(self.rep_data)
+        self.sumsq = torch.zeros((), dtype=torch.float32, device=dev)
+        self.rep_sumsq = torch.zeros((), dtype=torch.float32, device=dev)
+        self.norm_out = torch.zeros((), dtype=torch.float32, device=dev)
+        self.skipped = torch.zeros((), dtype=torch.int32, device=dev)
+        self.arrive = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.go = torch.zeros(1, dtype=torch.int32, device=dev)
+        max_pieces = max(((hi - lo) >> PIECE_SHIFT) + 1 for u in units for lo, hi in u.segments)
+        self.ag_flags = torch.zeros(max_pieces, dtype=torch.int32, device=dev)
+        self.ag_counter = torch.zeros(4, dtype=torch.int32, device=dev)
+        self._epoch = 0  # barrier epochs (sync pads), one per collective launch
+        self._ag_epoch = 0
+        self._arrive_total = 0
+        self.rs_ctas = min(rs_ctas, SYNC_WORDS // (3 * W))
+        C = _native.module()
+        self.final_ctas = int(min(C.fsdp_adamw_max_ctas(W), SYNC_WORDS // (3 * W)))
+        self.comm = torch.cuda.Stream(device=dev, priority=-1)
+
+        # ---- initial values (every rank holds the same full init) ------------------
+        with torch.no_grad():
+            for s in rep:
+                self.rep_data[s.offset : s.offset + s.numel].copy_(s.param.detach().reshape(-1))
+            for u in units:
+                full = self._unit_from_params(u)
+                self.gathered[u.unit0 : u.unit0 + W * u.cs].copy_(full)
+                lo = self.rank * u.cs
+                self.master[u.soff : u.soff + u.cs].copy_(full[lo : lo + u.cs])
+        # parameters become views: norms -> replicated fp32, sharded -> gathered bf16
+        for s in rep:
+            s.param.data = self.rep_data[s.offset : s.offset + s.numel].view(s.shape)
+            s.param.grad = self.grad[s.offset : s.offset + s.numel].view(s.shape)
+        for u in units:
+            for s in u.slots:
+                s.param.grad = None
+                s.param.data = self.gathered[s.offset : s.offset + s.numel].view(s.shape)
+        self._segs = self._build_segments()
+        self._fresh: set[int] = set()
+        self._gathered_segs: set[tuple[int, int]] = {seg for u in units for seg in u.segments}
+        self._issued: set[int] = set()
+        self.ready_hook = None
+        self.hold_ready = False  # set while a non-final microbatch runs its backward pass
+
+    # ---- construction helpers ---------------------------------------------------------
+    def _unit_from_params(self, u: Unit) -> torch.Tensor:
+        full = torch.zeros(self.world * u.cs, dtype=torch.float32, device=self.device)
+        for s in u.slots:
+            o = s.offset - u.unit0
+            full[o : o + s.numel].copy_(s.param.detach().reshape(-1).float())
+        return full
+
+    def _build_segments(self) -> torch.Tensor:
+        rows = []
+        base = self.gathered.data_ptr()
+        for u in self.units:
+            rows.append([
+                self.master.data_ptr() + 4 * u.soff, self.exp_avg.data_ptr() + 4 * u.soff,
+                self.exp_avg_sq.data_ptr() + 4 * u.soff, self.shard_grad.data_ptr() + 4 * u.soff,
+                base + 2 * (u.unit0 + self.rank * u.cs), u.cs,
+            ])
+        rows.append([self.rep_data.data_ptr(), self.rep_m.data_ptr(), self.rep_v.data_ptr(),
+                     self.grad.data_ptr(), 0, self.rep_n])
+        return torch.tensor(rows, dtype=torch.int64, device=self.device)
+
+    # ---- views the fused model code uses -----------------------------------------------
+    def slot(self, p: nn.Parameter) -> Slot:
+        return self.by_param[id(p)]
+
+    def _span(self, buf: torch.Tensor, params) -> torch.Tensor:
+        slots = [self.by_param[id(p)] for p in params]
+        for a, b in zip(slots, slots[1:], strict=False):
+            if a.offset + a.numel != b.offset:
+                raise ValueError(f"parameters {a.name} and {b.name} are not adjacent")
+        cols = slots[0].shape[-1]
+        rows = sum(s.numel for s in slots) // cols
+        return buf[slots[0].offset : slots[0].offset + rows * cols].view(rows, cols)
+
+    def _segment(self, p: nn.Parameter) -> tuple[Unit, tuple[int, int]]:
+        u = self.unit_of[id(p)]
+        off = self.by_param[id(p)].offset
+        for seg in u.segments:
+            if seg[0] <= off < seg[1]:
+                return u, seg
+        raise AssertionError("parameter outside its unit's segments")
+
+    def _ag_spec(self, u: Unit, seg: tuple[int, int], b0: int) -> list[int]:
+        self._ag_epoch += 1
+        return [
+            int(self.h_gath.buffer_ptrs_dev), self.gathered.data_ptr(), seg[0], -(-seg[1] // 8) * 8, u.unit0, u.cs, b0,
+            self.rank, self.world, PIECE_SHIFT, self.ag_flags.data_ptr(), self.ag_counter.data_ptr(), self._ag_epoch,
+        ]
+
+    def gather_spec(self, *params: nn.Parameter) -> list[int] | None:
+        """Spec of the fused all-gather for the GEMM that reads ``params`` as its B
+        operand, or None when that segment is already local this step."""
+        if id(params[0]) not in self.unit_of:
+            return None
+        u, seg = self._segment(params[0])
+        if seg in self._gathered_segs:
+            return None
+        self._gathered_segs.add(seg)
+        return self._ag_spec(u, seg, self.by_param[id(params[0])].offset)
+
+    def _ensure_gathered(self, params) -> None:
+        for p in params:
+            if id(p) not in self.unit_of:
+                continue
+            u, seg = self._segment(p)
+            if seg not in self._gathered_segs:
+                self._gathered_segs.add(seg)
+                _native.module().fsdp_all_gather(self._ag_spec(u, seg, seg[0]), 2 * _sms(self.device))
+
+    def shadow_of(self, *params: nn.Parameter) -> torch.Tensor:
+        self._ensure_gathered(params)
+        return self._span(self.gathered, params)
+
+    def grad_of(self, *params: nn.Parameter) -> torch.Tensor:
+        return self._span(self.grad, params)
+
+    def embedding(self, ids: torch.Tensor, weight: nn.Parameter) -> torch.Tensor:
+        u = self.unit_of[id(weight)]
+        s = self.by_param[id(weight)]
+        return _native.module().fsdp_embedding_fwd(
+            ids, int(self.h_master.buffer_ptrs_dev), s.offset, u.unit0, u.cs, u.soff, s.shape[1], s.shape[0]
+        )
+
+    def refresh_shadow(self, force: bool = False) -> None:
+        """The gathered buffer is maintained by the fetches and the optimizer."""
+
+    # ---- gradient protocol -------------------------------------------------------------
+    def finish_window(self) -> None:
+        for s in self.slots:
+            if id(s.param) not in self._fresh:
+                self.grad[s.offset : s.offset + s.numel].zero_()
+                self._fresh.add(id(s.param))
+
+    def zero_grad(self) -> None:
+        self._fresh.clear()
+        self.grad.zero_()
+
+    def start_step(self) -> None:
+        """Called before the step's first backward: clears the norm accumulator."""
+        self._issued.clear()
+        self.sumsq.zero_()
+
+    def ready(self, offset: int) -> None:  # FlatParameters-compatible entry (unused)
+        pass
+
+    def ready_after(self, p: nn.Parameter) -> None:
+        """``p``'s unit and every later unit (model order) have final gradients: reduce-
+        scatter them now, except the embedding unit, which the optimizer kernel reduces."""
+        if self.hold_ready:
+            return
+        order = self.unit_of[id(p)].order if id(p) in self.unit_of else self.rep_order[id(p)]
+        for u in self.units:
+            if u.order >= order and u.order not in self._issued and u is not self.embed_unit:
+                self._issue_rs(u)
+
+    def _finish_unit(self, u: Unit) -> None:
+        for s in u.slots:
+            if id(s.param) not in self._fresh:
+                self.grad[s.offset : s.offset + s.numel].zero_()
+                self._fresh.add(id(s.param))
+
+    def _issue_rs(self, u: Unit) -> None:
+        self._issued.add(u.order)
+        self._finish_unit(u)
+        self.comm.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(self.comm):
+            self._epoch += 1
+            lo = u.unit0 + self.rank * u.cs
+            _native.module().fsdp_reduce_scatter(
+                int(self.h_grad.buffer_ptrs_dev), int(self.h_sync.buffer_ptrs_dev), SYNC_WORDS, lo, lo + u.cs,
+                self.shard_grad.data_ptr() + 4 * u.soff, self.rank, self.world, self._epoch, 1.0 / self.world,
+                self.sumsq, self.rs_ctas,
+            )
+
+    # ---- optimizer step -----------------------------------------------------------------
+    def optimizer_step(self, lr: float, b1: float, b2: float, eps: float, wd: float, bc1: float, bc2: float,
+                       max_norm: float) -> None:
+        """Finish the reduce-scatters, then the fused reduce-scatter + AdamW kernel.
+        Leaves the global gradient norm in ``norm_out`` and the skip flag in ``skipped``."""
+        C = _native.module()
+        self.finish_window()
+        for u in self.units:
+            if u.order not in self._issued and u is not self.embed_unit:
+                self._issue_rs(u)
+        self.comm.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(self.comm):
+            self.rep_sumsq.zero_()
+            self._epoch += 1
+            C.fused_allreduce(
+                int(self.h_grad.buffer_ptrs_dev), int(self.h_sync.buffer_ptrs_dev), SYNC_WORDS, 0, self.rep_n,
+                self.rank, self.world, self._epoch, 1.0 / self.world, self.rep_sumsq, min(8, self.rs_ctas),
+            )
+            self._epoch += 1
+            self._arrive_total += self.final_ctas
+            e = self.embed_unit
+            lo = e.unit0 + self.rank * e.cs
+            C.fsdp_adamw(
+                [int(self.h_grad.buffer_ptrs_dev), int(self.h_sync.buffer_ptrs_dev), SYNC_WORDS, self.rank,
+                 self.world, self._epoch, lo, lo + e.cs, self.shard_grad.data_ptr() + 4 * e.soff,
+                 self.rep_sumsq.data_ptr(), self.xchg_ptrs.data_ptr(), self.arrive.data_ptr(),
+                 self._arrive_total & 0xFFFFFFFF, self.go.data_ptr(), self._segs.data_ptr(), self._segs.shape[0],
+                 self.final_ctas],
+                [1.0 / self.world, lr, b1, b2, eps, wd, bc1, bc2, max_norm],
+                self.sumsq, self.norm_out, self.skipped,
+            )
+        torch.cuda.current_stream(self.device).wait_stream(self.comm)
+        self._issued.add(e.order)
+        self._gathered_segs.clear()
+
+    def check(self) -> None:
+        _native.check_status(self.device)
+
+    # ---- full (unsharded) state for checkpoints ------------------------------------------
+    def _gather_unit(self, buf: torch.Tensor, u: Unit) -> torch.Tensor:
+        out = torch.empty(self.world * u.cs, dtype=torch.float32, device=self.device)
+        dist.all_gather_into_tensor(out, buf[u.soff : u.soff + u.cs].contiguous(), group=self.group)
+        return out
+
+    def full_tensors(self, which: str = "param", owner_only: bool = False) -> dict[str, torch.Tensor]:
+        """Full fp32 CPU tensors keyed by parameter name (``which``: param, exp_avg,
+        exp_avg_sq).  Collective.  With ``owner_only`` a rank keeps only the tensors of
+        the parameters whose index i satisfies i % W == rank."""
+        shard = {"param": self.master, "exp_avg": self.exp_avg, "exp_avg_sq": self.exp_avg_sq}[which]
+        rep = {"param": self.rep_data, "exp_avg": self.rep_m, "exp_avg_sq": self.rep_v}[which]
+        index = {s.name: i for i, s in enumerate(self.model_order())}
+        keep = (lambda n: index[n] % self.world == self.rank) if owner_only else (lambda n: True)
+        out: dict[str, torch.Tensor] = {}
+        for s in self.rep_slots:
+            if keep(s.name):
+                out[s.name] = rep[s.offset : s.offset + s.numel].view(s.shape).cpu()
+        for u in self.units:
+            full = self._gather_unit(shard, u)
+            for s in u.slots:
+                if keep(s.name):
+                    o = s.offset - u.unit0
+                    out[s.name] = full[o : o + s.numel].view(s.shape).cpu()
+        return out
+
+    def load_full_tensors(self, tensors: dict[str, torch.Tensor], which: str = "param") -> None:
+        """Inverse of :meth:`full_tensors` (every rank passes full tensors of the
+        parameters it wants to set)."""
+        shard = {"param": self.master, "exp_avg": self.exp_avg, "exp_avg_sq": self.exp_avg_sq}[which]
+        rep = {"param": self.rep_data, "exp_avg": self.rep_m, "exp_avg_sq": self.rep_v}[which]
+        with torch.no_grad():
+            for s in self.rep_slots:
+                if s.name in tensors:
+                    rep[s.offset : s.offset + s.numel].copy_(tensors[s.name].reshape(-1))
+            for u in self.units:
+                c0, c1 = u.unit0 + self.rank * u.cs, u.unit0 + (self.rank + 1) * u.cs
+                for s in u.slots:
+                    if s.name not in tensors:
+                        continue
+                    t = tensors[s.name].reshape(-1).to(self.device, torch.float32)
+                    lo, hi = max(s.offset, c0), min(s.offset + s.numel, c1)
+                    if lo < hi:
+                        shard[u.soff + lo - c0 : u.soff + hi - c0].copy_(t[lo - s.offset : hi - s.offset])
+                    if which == "param":
+                        self.gathered[s.offset : s.offset + s.numel].copy_(t)
+        if which == "param":
+            self._gathered_segs = {seg for u in self.units for seg in u.segments}
+
+    def model_order(self) -> list[Slot]:
+        """Slots in ``model.named_parameters()`` order (the optimizer's param indices)."""
+        by_name = {s.name: s for s in self.slots}
+        return [by_name[n] for n, p in self.model.named_parameters() if n in by_name]
+
+
+def _sms(device: torch.device) -> int:
+    return torch.cuda.get_device_properties(device).multi_processor_count
+
+
+class ShardedAdamW(torch.optim.Optimizer):
+    """AdamW over :class:`ShardedParameters` (torch.optim.AdamW math and param groups;
+    the update itself is the fused reduce-scatter + AdamW kernel)."""
+
+    def __init__(self, sp: ShardedParameters, lr: float = 1e-3, betas: tuple[float, float] = (0.9, 0.999),
+                 eps: float = 1e-8, weight_decay: float = 1e-2) -> None:
+        defaults = dict(lr=lr, betas=betas, eps=eps, weight_decay=weight_decay, amsgrad=False, maximize=False,
+                        foreach=None, capturable=False, differentiable=False, fused=None)
+        super().__init__([s.param for s in sp.model_order()], defaults)
+        self.sp = sp
+        self.step_count = 0
+        self.last_skipped = sp.skipped
+
+    @torch.no_grad()
+    def step(self, closure=None, grad_norm: torch.Tensor | None = None, max_norm: float = 0.0):
+        loss = closure() if closure is not None else None
+        g = self.param_groups[0]
+        b1, b2 = g["betas"]
+        self.step_count += 1
+        t = self.step_count
+        self.sp.optimizer_step(float(g["lr"]), b1, b2, g["eps"], g["weight_decay"], 1.0 - b1**t, 1.0 - b2**t,
+                               float(max_norm))
+        return loss
+
+    @property
+    def grad_norm(self) -> torch.Tensor:
+        return self.sp.norm_out
+
+    # Checkpoint format: torch.optim.AdamW's (full tensors).  Collective.
+    def full_state_dict(self, owner_only: bool = False) -> dict[str, Any]:
+        m = self.sp.full_tensors("exp_avg", owner_only)
+        v = self.sp.full_tensors("exp_avg_sq", owner_only)
+        state = {}
+        for i, s in enumerate(self.sp.model_order()):
+            if s.name in m:
+                state[i] = {"step": torch.tensor(float(self.step_count)), "exp_avg": m[s.name],
+                            "exp_avg_sq": v[s.name]}
+        groups = [{k: v for k, v in self.param_groups[0].items() if k != "params"}]
+        groups[0]["params"] = list(range(len(self.sp.model_order())))
+        return {"state": state, "param_groups": groups}
+
+    def load_full_state_dict(self, sd: dict[str, Any]) -> None:
+        order = self.sp.model_order()
+        m, v, steps = {}, {}, []
+        for i, st in sd.get("state", {}).items():
+            name = order[int(i)].name
+            m[name], v[name] = st["exp_avg"], st["exp_avg_sq"]
+            steps.append(float(st["step"]))
+        self.sp.load_full_tensors(m, "exp_avg")
+        self.sp.load_full_tensors(v, "exp_avg_sq")
+        if steps:
+            self.step_count = int(max(steps))
+        for k, val in sd.get("param_groups", [{}])[0].items():
+            if k != "params":
+                self.param_groups[0][k] = val
+

@@ -70,9 +70,26 @@ class TrainEngine:
             self.model.gradient_checkpointing_enable()
         self.model.train()
         self.fsdp = bool(cfg.train.fsdp) and self.world > 1
-        if self.fsdp:
-            # Sharded path: torch FSDP2 over the module graph (per-layer units, then the
-            # root), AdamW on the DTensor shards, DCP checkpoints.
+        self.sharded = None
+        native_ok = device.type == "cuda" and self.model.uses_native_path(torch.empty(0, device=device))
+        if self.fsdp and native_ok:
+            # Native sharded path: per-unit shards in symmetric memory, all-gather fused
+            # into the consuming GEMMs, reduce-scatter fused with the sharded AdamW.
+            from packbalance_b200.parallel.sharded import ShardedAdamW, ShardedParameters
+
+            self.sharded = ShardedParameters(self.model)
+            self.model.flat = self.sharded
+            self.flat = self.sharded
+            self.dp = None
+            self.optimizer = ShardedAdamW(
+                self.sharded,
+                lr=cfg.train.lr,
+                betas=(cfg.train.beta1, cfg.train.beta2),
+                weight_decay=cfg.train.weight_decay,
+            )
+        elif self.fsdp:
+            # CPU (gloo) or eager path: torch FSDP2 over the module graph (per-layer
+            # units, then the root), AdamW on the DTensor shards, DCP checkpoints.
             from torch.distributed.fsdp import fully_shard
 
             self.model.native = False
@@ -133,6 +150,8 @@ class TrainEngine:
         if step_tokens <= 0:
             raise RuntimeError("step has no useful tokens")
         loss_scale = self.world / step_tokens
+        if self.sharded is not None:
+            return self._sharded_step(packs, loss_scale)
         if self.fsdp:
             return self._fsdp_step(packs, loss_scale)
         if self.native:
@@ -142,8 +161,11 @@ class TrainEngine:
         self.dp.start_step()
         groups = [concat_packs(packs)] if self.cfg.train.fuse_microbatches else packs
         local = torch.zeros((), device=self.device, dtype=torch.float32)
-        for batch in groups:
+        for i, batch in enumerate(groups):
+            # gradients are final only in the last microbatch's backward pass
+            self.dp.hold = i < len(groups) - 1
             local += self._forward_backward(to_device_batch(batch, self.device), loss_scale)
+        self.dp.hold = False
         if self.native:
             self.flat.finish_window()
         with record_function("packbalance/optimizer"):
@@ -154,6 +176,22 @@ class TrainEngine:
             self.optimizer.step(grad_norm=norm, max_norm=self.cfg.train.grad_clip)
             self.scheduler.step()
         return {"loss_sum": local, "grad_norm": norm}
+
+    def _sharded_step(self, packs: list[dict[str, Any]], loss_scale: float) -> dict[str, torch.Tensor]:
+        sp = self.sharded
+        sp.begin_window()
+        sp.start_step()
+        groups = [concat_packs(packs)] if self.cfg.train.fuse_microbatches else packs
+        local = torch.zeros((), device=self.device, dtype=torch.float32)
+        for i, batch in enumerate(groups):
+            # earlier microbatches only accumulate: no unit is final before the last one
+            sp.hold_ready = i < len(groups) - 1
+            local += self._forward_backward(to_device_batch(batch, self.device), loss_scale)
+        sp.hold_ready = False
+        with record_function("packbalance/optimizer"):
+            self.optimizer.step(max_norm=self.cfg.train.grad_clip)
+            self.scheduler.step()
+        return {"loss_sum": local, "grad_norm": sp.norm_out}
 
     def _fsdp_step(self, packs: list[dict[str, Any]], loss_scale: float) -> dict[str, torch.Tensor]:
         self.optimizer.zero_grad(set_to_none=True)

@@ -15,13 +15,9 @@ os.environ.setdefault("MAX_JOBS", str(os.cpu_count() or 4))
 
 ROOT = Path(__file__).parent
 CSRC = ROOT / "packbalance_b200" / "csrc"
-SOURCES = ["bindings.cpp", "gemm.cu", "elementwise.cu", "attention.cu", "comm.cu", "noalloc.cu"]
-SOURCES = [str((CSRC / s).relative_to(ROOT)) for s in SOURCES if (CSRC / s).exists()]
-DEFINES = []
-if any(s.endswith("attention.cu") for s in SOURCES):
-    DEFINES.append("-DPB_WITH_ATTENTION")
-if any(s.endswith("comm.cu") for s in SOURCES):
-    DEFINES.append("-DPB_WITH_COMM")
+SOURCES = ["bindings.cpp", "gemm.cu", "elementwise.cu", "attention.cu", "comm.cu", "fsdp.cu", "noalloc.cu"]
+SOURCES = [str((CSRC / s).relative_to(ROOT)) for s in SOURCES]
+DEFINES: list[str] = []
 
 NVCC_FLAGS = [
     "-gencode",

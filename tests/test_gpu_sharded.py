@@ -1,0 +1,101 @@
+"""Native sharded engine (fused all-gather GEMMs, reduce-scatter + sharded AdamW) against
+the native data-parallel engine on 2+ GPUs: same losses, gradient norms and weights."""
+
+import os
+import socket
+import subprocess
+import sys
+import textwrap
+from pathlib import Path
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+ROOT = Path(__file__).resolve().parents[1]
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return int(s.getsockname()[1])
+
+
+WORKER = textwrap.dedent(
+    """
+    import datetime, os, sys
+    from dataclasses import replace
+    from pathlib import Path
+    import torch, torch.distributed as dist
+    sys.path.insert(0, os.environ["PB_ROOT"])
+    from packbalance_b200.config import DataConfig, ModelConfig, PackBalanceConfig, TrainConfig
+    from packbalance_b200.data.cost import FlopModel
+    from packbalance_b200.data.dataset import PackedDataset
+    from packbalance_b200.data.packer import build_packs
+    from packbalance_b200.data.prepare import prepare_synthetic
+    from packbalance_b200.data.store import TokenStore
+    from packbalance_b200.ops import _native
+    from packbalance_b200.train.engine import TrainEngine
+
+    rank = int(os.environ["RANK"]); world = int(os.environ["WORLD_SIZE"])
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=60), device_id=dev)
+    tie = os.environ["PB_TIE"] == "1"
+    mcfg = ModelConfig(vocab_size=4096, d_model=256, n_layers=2, n_heads=4, n_kv_heads=2, d_ff=512, max_seq_len=512,
+                       tie_embeddings=tie, attention_backend="auto")
+    dcfg = DataConfig(dataset="synthetic", data_dir=os.path.join(os.environ["PB_TMP"], f"d{rank}"), seq_len=512,
+                      mode="pack_ffd", max_doc_len=512, min_doc_len=8, synthetic_num_docs=400, synthetic_mu=4.5,
+                      synthetic_sigma=0.8, synthetic_min_len=16, synthetic_max_len=900, synthetic_vocab_size=4096,
+                      num_workers=0, val_fraction=0.0, seed=3)
+    prepare_synthetic(dcfg, Path(dcfg.data_dir))
+    store = TokenStore.open(dcfg.data_dir)
+    packs = build_packs(store, dcfg, FlopModel.from_config(mcfg))
+    per = 2
+    ds = PackedDataset(store, packs, dcfg)
+    mine = [ds[i] for i in range(rank * per, (rank + 1) * per)]
+    tokens = sum(p.tokens for p in packs[: world * per])
+    base = PackBalanceConfig(model=mcfg, data=dcfg, train=TrainConfig(lr=3e-3, warmup_steps=1, max_steps=10,
+                                                                     grad_clip=0.5, dtype="bf16"))
+    torch.manual_seed(0)
+    ddp = TrainEngine(replace(base, train=replace(base.train, fsdp=False)), dev)
+    torch.manual_seed(0)
+    shd = TrainEngine(replace(base, train=replace(base.train, fsdp=True)), dev)
+    assert shd.sharded is not None
+    for step in range(3):
+        a = ddp.step(mine, tokens)
+        b = shd.step(mine, tokens)
+        torch.cuda.synchronize()
+        _native.check_status()
+        la, lb = a["loss_sum"].item(), b["loss_sum"].item()
+        na, nb = float(a["grad_norm"]), float(b["grad_norm"])
+        assert abs(la - lb) <= 2e-3 * abs(la), (step, la, lb)
+        assert abs(na - nb) <= 2e-3 * na, (step, na, nb)
+    full = shd.sharded.full_tensors("param")
+    ref = {n: p.detach().float().cpu() for n, p in ddp.model.named_parameters()}
+    worst = max((full[n] - ref[n]).abs().max().item() for n in ref)
+    assert worst < 2e-3, worst
+    shd.close(); ddp.close()
+    dist.barrier()
+    dist.destroy_process_group()
+    print("rank", rank, "ok", worst)
+    """
+)
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("tie", [True, False])
+def test_sharded_engine_matches_ddp(tmp_path, tie):
+    world = min(torch.cuda.device_count(), 4)
+    script = tmp_path / "worker.py"
+    script.write_text(WORKER)
+    port = str(_free_port())
+    env = {**os.environ, "PB_ROOT": str(ROOT), "PB_TMP": str(tmp_path), "PB_TIE": "1" if tie else "0",
+           "MASTER_ADDR": "127.0.0.1", "MASTER_PORT": port, "NCCL_NVLS_ENABLE": "0", "PB_ALLREDUCE": "p2p"}
+    r = subprocess.run(
+        ["timeout", "-k", "30", "300", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
+         f"--nproc-per-node={world}", "--master-addr=127.0.0.1", f"--master-port={port}", str(script)],
+        env=env, capture_output=True, text=True, timeout=360,
+    )
+    assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-4000:]
+    assert r.stdout.count(" ok ") == world
