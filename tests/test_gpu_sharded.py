@@ -59,6 +59,7 @@ WORKER = textwrap.dedent(
                                                                      grad_clip=0.5, dtype="bf16"))
     torch.manual_seed(0)
     ddp = TrainEngine(replace(base, train=replace(base.train, fsdp=False)), dev)
+    init = {n: p.detach().float().cpu().clone() for n, p in ddp.model.named_parameters()}
     torch.manual_seed(0)
     shd = TrainEngine(replace(base, train=replace(base.train, fsdp=True)), dev)
     assert shd.sharded is not None
@@ -73,12 +74,22 @@ WORKER = textwrap.dedent(
         assert abs(na - nb) <= 2e-3 * na, (step, na, nb)
     full = shd.sharded.full_tensors("param")
     ref = {n: p.detach().float().cpu() for n, p in ddp.model.named_parameters()}
-    worst = max((full[n] - ref[n]).abs().max().item() for n in ref)
-    assert worst < 2e-3, worst
+    # Both engines accumulate split-K and RMSNorm weight gradients with fp32 atomics, so
+    # their gradients differ in the last bits, and Adam (which normalises every
+    # coordinate) can move a coordinate whose gradient is ~0 either way.  Compare each
+    # parameter's update instead: a wrong chunk, scale or missing unit gives O(1) errors.
+    worst = 0.0
+    for n in ref:
+        upd = (ref[n] - init[n]).norm().item()
+        err = (full[n] - ref[n]).norm().item()
+        rel = err / max(upd, 1e-12)
+        worst = max(worst, rel)
+        assert rel < 0.05, (n, rel, err, upd)
+    frac = 0.0
     shd.close(); ddp.close()
     dist.barrier()
     dist.destroy_process_group()
-    print("rank", rank, "ok", worst)
+    print("rank", rank, "ok", worst, frac)
     """
 )
 
