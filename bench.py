@@ -301,23 +301,39 @@ def run_ours(args, rank, world, dev) -> None:
         launches = len(mine) * args.steps
         if rank == 0:
             print(f"[bench] kernels per step: {len(mine)} native / {len(names)} total", file=sys.stderr, flush=True)
+    if engine.sharded is not None:
+        comm = "sharded: all-gather fused into GEMMs, reduce-scatter fused with AdamW (peer memory)"
+    elif engine.dp is not None and engine.dp.fused is not None:
+        comm = f"fused peer-memory all-reduce ({engine.dp.fused.mode})"
+    else:
+        comm = "nccl"
     extra = {
-        "model": "llama-100M (12L d768 12H/4KV ff2048 V32000 tied)",
+        "model": describe_model(cfg.model),
         "global_batch": world * A,
-        "global_batch_unit": "packs of 2048 tokens",
+        "global_batch_unit": f"packs of {cfg.data.seq_len} tokens",
         "seq_len": cfg.data.seq_len,
-        "parallelism": f"dp{world}",
+        "parallelism": f"{'fsdp' if engine.fsdp else 'dp'}{world}",
         "packing": args.mode,
         "schedule": cfg.data.schedule,
         "packs_per_rank": A,
         "padding_waste": pstats["padding_waste"],
         "analytical_rank_imbalance": sched.stats()["rank_cost_imbalance"],
         "l2": "no flush; per-step working set (weights+Adam state+activations) >> 126 MB L2",
-        "comm": "fused peer-memory all-reduce" if engine.dp is not None and engine.dp.fused is not None else "nccl",
+        "comm": comm,
     }
     report(args, world, dev, rank, "ours", step_ms_ranks, e2e_ms, [p.step_tokens for p in plans[args.warmup:]],
            launches, clocks, extra, h2d, d2h)
     engine.close()
+
+
+def describe_model(m) -> str:
+    """Model name of the JSON line, from the config actually run."""
+    from packbalance_b200.data.cost import FlopModel
+
+    n = FlopModel.from_config(m).total_params()
+    tie = "tied" if m.tie_embeddings else "untied"
+    return (f"llama-{n / 1e6:.0f}M ({m.n_layers}L d{m.d_model} {m.n_heads}H/{m.n_kv_heads}KV ff{m.d_ff} "
+            f"V{m.vocab_size} {tie})")
 
 
 def run_reference(args, rank, world, dev) -> None:
@@ -352,13 +368,15 @@ def run_reference(args, rank, world, dev) -> None:
     m, d, t = ours.model, ours.data, ours.train
     rcfg = RConfig(
         model=RModelConfig(vocab_size=m.vocab_size, d_model=m.d_model, n_layers=m.n_layers, n_heads=m.n_heads,
-                           n_kv_heads=m.n_kv_heads, d_ff=m.d_ff, max_seq_len=m.max_seq_len, tie_embeddings=True,
-                           attention_backend="auto", use_fused_ce=True, ce_chunk_size=m.ce_chunk_size),
+                           n_kv_heads=m.n_kv_heads, d_ff=m.d_ff, max_seq_len=m.max_seq_len,
+                           tie_embeddings=m.tie_embeddings, rope_theta=m.rope_theta,
+                           gradient_checkpointing=m.gradient_checkpointing, attention_backend="auto",
+                           use_fused_ce=True, ce_chunk_size=m.ce_chunk_size),
         data=RDataConfig(dataset="synthetic", data_dir=str(data_dir), seq_len=d.seq_len, mode=args.mode,
                          schedule=d.schedule, max_doc_len=d.max_doc_len, min_doc_len=d.min_doc_len,
                          val_fraction=0.0, seed=d.seed, num_workers=0),
         train=RTrainConfig(grad_accum=t.grad_accum, lr=t.lr, min_lr=t.min_lr, warmup_steps=t.warmup_steps,
-                           dtype="bf16", max_steps=1000, grad_clip=t.grad_clip),
+                           dtype="bf16", max_steps=1000, grad_clip=t.grad_clip, fsdp=t.fsdp),
     )
     total = args.warmup + args.steps
     store = TokenStore.open(data_dir)
@@ -414,17 +432,17 @@ def run_reference(args, rank, world, dev) -> None:
         e2e_ms = max_over_ranks(ev0.elapsed_time(ev1), dev)
         barrier()
     extra = {
-        "model": "llama-100M (12L d768 12H/4KV ff2048 V32000 tied)",
+        "model": describe_model(ours.model),
         "global_batch": world * A,
-        "global_batch_unit": "packs of 2048 tokens",
+        "global_batch_unit": f"packs of {rcfg.data.seq_len} tokens",
         "seq_len": rcfg.data.seq_len,
-        "parallelism": f"dp{world}",
+        "parallelism": f"{'fsdp' if rcfg.train.fsdp and world > 1 else 'dp'}{world}",
         "packing": args.mode,
         "schedule": rcfg.data.schedule,
         "packs_per_rank": A,
         "padding_waste": pack_stats(packs, fm)["padding_waste"],
         "l2": "no flush; per-step working set >> 126 MB L2",
-        "comm": "torch DDP (NCCL)",
+        "comm": "torch FSDP2 (NCCL)" if rcfg.train.fsdp and world > 1 else "torch DDP (NCCL)",
     }
     report(args, world, dev, rank, "reference", step_ms_ranks, e2e_ms, [p.step_tokens for p in plans[args.warmup:]],
            None, clocks, extra, h2d, 4)

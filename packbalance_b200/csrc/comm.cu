@@ -140,23 +140,6 @@ __global__ void __launch_bounds__(512) fused_allreduce_kernel(const ArArgs a) {
 //   barrier 0 -> ld_reduce / scale / st over its chunk -> multimem.red of its squared
 //   norm into every rank's accumulator -> barrier 1
 // Per rank NVLink carries about (W - 1) / W of the bucket in each direction.
-__device__ __forceinline__ float4 mm_ld_reduce(const float* mc) {
-  float4 v;
-  asm volatile("multimem.ld_reduce.relaxed.sys.global.add.v4.f32 {%0, %1, %2, %3}, [%4];"
-               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
-               : "l"(mc)
-               : "memory");
-  return v;
-}
-__device__ __forceinline__ void mm_st(float* mc, float4 v) {
-  asm volatile("multimem.st.relaxed.sys.global.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(mc), "f"(v.x), "f"(v.y), "f"(v.z),
-               "f"(v.w)
-               : "memory");
-}
-__device__ __forceinline__ void mm_red_add(float* mc, float v) {
-  asm volatile("multimem.red.relaxed.sys.global.add.f32 [%0], %1;" ::"l"(mc), "f"(v) : "memory");
-}
-
 __global__ void __launch_bounds__(512) nvls_allreduce_kernel(const ArArgs a, float* mc, float* mc_sumsq) {
   __shared__ volatile int abort_sh;
   __shared__ float red[32];

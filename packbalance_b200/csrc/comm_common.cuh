@@ -69,4 +69,24 @@ __device__ __forceinline__ void sub_range(const ArArgs& a, long cs, long sub, in
   s1 = min(s0 + sub, c1);
 }
 
+// NVLink multicast (NVLS) through the NVSwitch: ``mc`` addresses a multicast object
+// bound over every rank's buffer.  ld_reduce returns the sum over all ranks, st writes
+// every rank, red adds into every rank.
+__device__ __forceinline__ float4 mm_ld_reduce(const float* mc) {
+  float4 v;
+  asm volatile("multimem.ld_reduce.relaxed.sys.global.add.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "l"(mc)
+               : "memory");
+  return v;
+}
+__device__ __forceinline__ void mm_st(float* mc, float4 v) {
+  asm volatile("multimem.st.relaxed.sys.global.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(mc), "f"(v.x), "f"(v.y), "f"(v.z),
+               "f"(v.w)
+               : "memory");
+}
+__device__ __forceinline__ void mm_red_add(float* mc, float v) {
+  asm volatile("multimem.red.relaxed.sys.global.add.f32 [%0], %1;" ::"l"(mc), "f"(v) : "memory");
+}
+
 }  // namespace pb

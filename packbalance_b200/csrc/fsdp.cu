@@ -16,6 +16,8 @@
 //                         writes the shard gradient and adds its squared norm to a
 //                         device accumulator.  Issued per unit as soon as the backward
 //                         pass has finished the unit, on the communication stream.
+//                         With an NVLink multicast object over the gradient buffers the
+//                         sum is one multimem.ld_reduce per 16 bytes, done in the switch.
 //   fsdp_adamw            the step's last reduce-scatter (the embedding unit, finished
 //                         last) fused with the optimizer: barrier, reduce-scatter, the
 //                         squared norms of all ranks' shards exchanged through peer
@@ -93,6 +95,37 @@ __device__ __forceinline__ float rs_chunk(float* const* ptrs, long c0, long c1, 
   return ss;
 }
 
+// Same as rs_chunk, with the sum done in the NVSwitch: one multimem.ld_reduce per 16
+// bytes over the gradient buffer's multicast address.
+__device__ __forceinline__ float rs_chunk_mc(const float* mc, long c0, long c1, float* out, float scale) {
+  const long n = c1 - c0;
+  const long sub = ((n + gridDim.x - 1) / gridDim.x + 3) / 4 * 4;
+  const long s0 = min(c0 + static_cast<long>(blockIdx.x) * sub, c1);
+  const long s1 = min(s0 + sub, c1);
+  float ss = 0.f;
+  const long stride = static_cast<long>(blockDim.x) * 4;
+  for (long i = s0 + threadIdx.x * 4; i < s1; i += 4 * stride) {
+    float4 v[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u)
+      if (i + u * stride < s1) v[u] = mm_ld_reduce(mc + i + u * stride);
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const long j = i + u * stride;
+      if (j < s1) {
+        float4 acc = v[u];
+        acc.x *= scale;
+        acc.y *= scale;
+        acc.z *= scale;
+        acc.w *= scale;
+        *reinterpret_cast<float4*>(out + (j - c0)) = acc;
+        ss += acc.x * acc.x + acc.y * acc.y + acc.z * acc.z + acc.w * acc.w;
+      }
+    }
+  }
+  return ss;
+}
+
 __device__ __forceinline__ float block_sum(float v, float* red) {
   v = warp_sum(v);
   __syncthreads();
@@ -104,19 +137,20 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
 }
 
 template <int W>
-__global__ void __launch_bounds__(512) fsdp_reduce_scatter_kernel(const ArArgs a, float* out) {
+__global__ void __launch_bounds__(512) fsdp_reduce_scatter_kernel(const ArArgs a, float* out, const float* mc) {
   __shared__ volatile int abort_sh;
   __shared__ float red[32];
   if (threadIdx.x == 0) abort_sh = 0;
   __syncthreads();
   if (!cta_barrier(a, 0, &abort_sh)) return;
-  const float ss = rs_chunk<W>(a.ptrs, a.lo, a.hi, out, a.scale);
+  const float ss = mc != nullptr ? rs_chunk_mc(mc, a.lo, a.hi, out, a.scale) : rs_chunk<W>(a.ptrs, a.lo, a.hi, out, a.scale);
   const float t = block_sum(ss, red);
   if (threadIdx.x == 0) atomicAdd(a.sumsq, t);
 }
 
 struct FinalArgs {
   ArArgs a;                // peers' gradient buffers + sync pads; lo/hi: last unit's chunk
+  const float* mc;         // multicast address of the gradient buffer (NVLS), or null
   float* rs_out;           // shard gradient of that chunk
   const float* rep_sumsq;  // squared norm of the replicated (already averaged) grads, or null
   float* const* xchg;      // [W] every rank's exchange slots (W floats each)
@@ -153,7 +187,8 @@ __global__ void __launch_bounds__(512) fsdp_adamw_kernel(const FinalArgs f) {
   // 0: every rank has finished its backward pass and its earlier reduce-scatters.
   if (!cta_barrier(a, 0, &abort_sh)) return;
   float ss = 0.f;
-  if (a.hi > a.lo) ss = rs_chunk<W>(a.ptrs, a.lo, a.hi, f.rs_out, a.scale);
+  if (a.hi > a.lo)
+    ss = f.mc != nullptr ? rs_chunk_mc(f.mc, a.lo, a.hi, f.rs_out, a.scale) : rs_chunk<W>(a.ptrs, a.lo, a.hi, f.rs_out, a.scale);
   const float t = block_sum(ss, red);
   if (threadIdx.x == 0) {
     if (t != 0.f) atomicAdd(a.sumsq, t);
@@ -262,8 +297,10 @@ static ArArgs make_args(int64_t ptrs_dev, int64_t pads_dev, int64_t lo, int64_t 
   return a;
 }
 
+// ``mc``: multicast address of the gradient buffer (0: peer loads).
 void fsdp_reduce_scatter(int64_t gptrs_dev, int64_t pads_dev, int64_t pad_words, int64_t lo, int64_t hi, int64_t out,
-                         int64_t rank, int64_t world, int64_t epoch, double scale, at::Tensor sumsq, int64_t ctas) {
+                         int64_t rank, int64_t world, int64_t epoch, double scale, at::Tensor sumsq, int64_t ctas,
+                         int64_t mc) {
   TORCH_CHECK(sumsq.is_cuda() && sumsq.scalar_type() == at::kFloat, "fsdp_reduce_scatter: fp32 CUDA accumulator");
   TORCH_CHECK(lo % 4 == 0 && hi % 4 == 0 && out % 16 == 0, "fsdp_reduce_scatter: 16-byte aligned chunk");
   TORCH_CHECK(ctas * world <= pad_words, "fsdp_reduce_scatter: sync pad too small");
@@ -271,15 +308,16 @@ void fsdp_reduce_scatter(int64_t gptrs_dev, int64_t pads_dev, int64_t pad_words,
   const ArArgs a = make_args(gptrs_dev, pads_dev, lo, hi, rank, world, epoch, scale, sumsq.data_ptr<float>(),
                              sumsq.device().index());
   float* o = reinterpret_cast<float*>(out);
+  const float* m = reinterpret_cast<const float*>(mc);
   auto st = at::cuda::getCurrentCUDAStream();
   switch (world) {
-    case 2: fsdp_reduce_scatter_kernel<2><<<(int)ctas, 512, 0, st>>>(a, o); break;
-    case 3: fsdp_reduce_scatter_kernel<3><<<(int)ctas, 512, 0, st>>>(a, o); break;
-    case 4: fsdp_reduce_scatter_kernel<4><<<(int)ctas, 512, 0, st>>>(a, o); break;
-    case 5: fsdp_reduce_scatter_kernel<5><<<(int)ctas, 512, 0, st>>>(a, o); break;
-    case 6: fsdp_reduce_scatter_kernel<6><<<(int)ctas, 512, 0, st>>>(a, o); break;
-    case 7: fsdp_reduce_scatter_kernel<7><<<(int)ctas, 512, 0, st>>>(a, o); break;
-    case 8: fsdp_reduce_scatter_kernel<8><<<(int)ctas, 512, 0, st>>>(a, o); break;
+    case 2: fsdp_reduce_scatter_kernel<2><<<(int)ctas, 512, 0, st>>>(a, o, m); break;
+    case 3: fsdp_reduce_scatter_kernel<3><<<(int)ctas, 512, 0, st>>>(a, o, m); break;
+    case 4: fsdp_reduce_scatter_kernel<4><<<(int)ctas, 512, 0, st>>>(a, o, m); break;
+    case 5: fsdp_reduce_scatter_kernel<5><<<(int)ctas, 512, 0, st>>>(a, o, m); break;
+    case 6: fsdp_reduce_scatter_kernel<6><<<(int)ctas, 512, 0, st>>>(a, o, m); break;
+    case 7: fsdp_reduce_scatter_kernel<7><<<(int)ctas, 512, 0, st>>>(a, o, m); break;
+    case 8: fsdp_reduce_scatter_kernel<8><<<(int)ctas, 512, 0, st>>>(a, o, m); break;
     default: TORCH_CHECK(false, "fsdp_reduce_scatter: world size 2..8 on one node");
   }
   PB_CUDA_CHECK(cudaGetLastError());
@@ -308,11 +346,11 @@ int64_t fsdp_adamw_max_ctas(int64_t world) {
 }
 
 // ``p``: {gptrs_dev, pads_dev, pad_words, rank, world, epoch, rs_lo, rs_hi, rs_out,
-//         rep_sumsq, xchg_ptrs_dev, arrive, arrive_target, go, segs, nseg, ctas}
+//         rep_sumsq, xchg_ptrs_dev, arrive, arrive_target, go, segs, nseg, ctas, mc}
 // ``h``: {scale, lr, b1, b2, eps, wd, bc1, bc2, max_norm}
 void fsdp_adamw(std::vector<int64_t> p, std::vector<double> h, at::Tensor sumsq, at::Tensor norm_out,
                 at::Tensor skipped) {
-  TORCH_CHECK(p.size() == 17 && h.size() == 9, "fsdp_adamw: argument vectors");
+  TORCH_CHECK(p.size() == 18 && h.size() == 9, "fsdp_adamw: argument vectors");
   TORCH_CHECK(sumsq.is_cuda() && norm_out.is_cuda() && skipped.is_cuda(), "fsdp_adamw: CUDA tensors");
   const c10::cuda::CUDAGuard guard(sumsq.device());
   const int64_t world = p[4], ctas = p[16];
@@ -322,6 +360,7 @@ void fsdp_adamw(std::vector<int64_t> p, std::vector<double> h, at::Tensor sumsq,
   FinalArgs f{};
   f.a = make_args(p[0], p[1], p[6], p[7], p[3], world, p[5], h[0], sumsq.data_ptr<float>(), sumsq.device().index());
   f.rs_out = reinterpret_cast<float*>(p[8]);
+  f.mc = reinterpret_cast<const float*>(p[17]);
   f.rep_sumsq = reinterpret_cast<const float*>(p[9]);
   f.xchg = reinterpret_cast<float* const*>(p[10]);
   f.arrive = reinterpret_cast<unsigned*>(p[11]);
@@ -370,29 +409,16 @@ at::Tensor fsdp_embedding_fwd(at::Tensor ids, int64_t masters_dev, int64_t row0,
 }
 
 // ``ag``: the 13-field spec of gemm_tc's fused all-gather (b0 unused).
+void parse_ag_spec(const std::vector<int64_t>& ag, AgSpec& s);
+
 void fsdp_all_gather(std::vector<int64_t> ag, int64_t ctas) {
   TORCH_CHECK(ag.size() == 13, "fsdp_all_gather: 13 fields");
   AgSpec s{};
-  s.src = reinterpret_cast<const __nv_bfloat16* const*>(ag[0]);
-  s.dst = reinterpret_cast<__nv_bfloat16*>(ag[1]);
-  s.lo = ag[2];
-  s.hi = ag[3];
-  s.unit0 = ag[4];
-  s.cs = ag[5];
-  s.b0 = ag[6];
-  s.rank = (int)ag[7];
-  s.world = (int)ag[8];
-  s.piece_shift = (int)ag[9];
-  s.flags = reinterpret_cast<uint32_t*>(ag[10]);
-  s.counter = reinterpret_cast<int*>(ag[11]);
-  s.epoch = static_cast<uint32_t>(ag[12]);
-  s.rot = 0;
-  TORCH_CHECK(s.lo % 8 == 0 && s.hi % 8 == 0 && s.unit0 % 8 == 0 && s.cs % 8 == 0 && s.cs > 0,
-              "fsdp_all_gather: 16-byte aligned ranges");
-  TORCH_CHECK(s.lo >= s.unit0 && s.hi <= s.unit0 + s.world * s.cs, "fsdp_all_gather: range outside its unit");
+  parse_ag_spec(ag, s);
   if (s.hi <= s.lo) return;
   auto st = at::cuda::getCurrentCUDAStream();
-  PB_CUDA_CHECK(cudaMemsetAsync(s.counter, 0, sizeof(int), st));
+  const long nblocks = (s.hi - s.lo + (1L << s.block_shift) - 1) >> s.block_shift;
+  PB_CUDA_CHECK(cudaMemsetAsync(s.counters, 0, sizeof(uint32_t) * (1 + nblocks), st));
   fsdp_all_gather_kernel<<<(int)ctas, 128, 0, st>>>(s);
   PB_CUDA_CHECK(cudaGetLastError());
 }

@@ -35,6 +35,30 @@ static void dispatch_major(bool a_mn, bool b_mn, const CUtensorMap& ta, const CU
   else launch_gemm<BN, true, false>(ta, tb, to, tx, args, grid, s);
 }
 
+// 13-field all-gather spec shared by gemm_tc and fsdp_all_gather (ag_copy.cuh).
+void parse_ag_spec(const std::vector<int64_t>& ag, AgSpec& s) {
+  s.src = reinterpret_cast<const __nv_bfloat16* const*>(ag[0]);
+  s.dst = reinterpret_cast<__nv_bfloat16*>(ag[1]);
+  s.lo = ag[2];
+  s.hi = ag[3];
+  s.unit0 = ag[4];
+  s.cs = ag[5];
+  s.b0 = ag[6];
+  s.split = ag[7];
+  s.rank = (int)ag[8];
+  s.world = (int)ag[9];
+  s.piece_shift = (int)ag[10];
+  s.block_shift = (int)ag[11];
+  s.counters = reinterpret_cast<uint32_t*>(ag[12]);
+  s.rot = 0;
+  TORCH_CHECK(s.world >= 2 && s.world <= 8 && s.rank >= 0 && s.rank < s.world, "ag: rank/world");
+  TORCH_CHECK(s.lo % 8 == 0 && s.hi % 8 == 0 && s.unit0 % 8 == 0 && s.cs % 8 == 0 && s.cs > 0 && s.split % 8 == 0,
+              "ag: ranges must be 16-byte aligned");
+  TORCH_CHECK(s.piece_shift >= 3 && s.piece_shift <= s.block_shift && s.block_shift <= 30, "ag: piece/block size");
+  TORCH_CHECK(s.lo >= s.unit0 && s.hi <= s.unit0 + s.world * s.cs && s.lo + 2 * s.split <= s.hi,
+              "ag: range outside its unit");
+}
+
 static const void* opt_ptr(const c10::optional<at::Tensor>& t) { return t.has_value() ? t->data_ptr() : nullptr; }
 
 // Epilogue box over a 2-D output view: 32 x 32 elements, 128B (fp32) or 64B (bf16) swizzle.
@@ -136,42 +160,35 @@ void gemm_tc(at::Tensor a, at::Tensor b, at::Tensor out, int64_t M, int64_t N, i
 
   cudaStream_t stream0 = at::cuda::getCurrentCUDAStream();
   if (!ag.empty()) {
-    // Fused all-gather of B: {src_ptrs_dev, dst, lo, hi, unit0, cs, b0, rank, world,
-    //                         piece_shift, flags, counter, epoch}
+    // Fused all-gather of B: {src_ptrs_dev, dst, lo, hi, unit0, cs, b0, split, rank, world,
+    //                         piece_shift, block_shift, counters}
     TORCH_CHECK(ag.size() == 13, "gemm_tc: ag spec has 13 fields");
     TORCH_CHECK(!b_mn, "gemm_tc: the fused all-gather feeds a K-major B");
     AgSpec& s = g.ag;
-    s.src = reinterpret_cast<const __nv_bfloat16* const*>(ag[0]);
-    s.dst = reinterpret_cast<__nv_bfloat16*>(ag[1]);
-    s.lo = ag[2];
-    s.hi = ag[3];
-    s.unit0 = ag[4];
-    s.cs = ag[5];
-    s.b0 = ag[6];
-    s.rank = (int)ag[7];
-    s.world = (int)ag[8];
-    s.piece_shift = (int)ag[9];
-    s.flags = reinterpret_cast<uint32_t*>(ag[10]);
-    s.counter = reinterpret_cast<int*>(ag[11]);
-    s.epoch = static_cast<uint32_t>(ag[12]);
-    TORCH_CHECK(s.world >= 2 && s.world <= 8 && s.rank >= 0 && s.rank < s.world, "gemm_tc: ag rank/world");
-    TORCH_CHECK(s.lo % 8 == 0 && s.hi % 8 == 0 && s.unit0 % 8 == 0 && s.cs % 8 == 0 && s.cs > 0,
-                "gemm_tc: ag ranges must be 16-byte aligned");
-    TORCH_CHECK(s.piece_shift >= 3 && s.piece_shift <= 24, "gemm_tc: ag piece size");
-    TORCH_CHECK(s.lo >= s.unit0 && s.hi <= s.unit0 + s.world * s.cs, "gemm_tc: ag range outside its unit");
-    TORCH_CHECK(reinterpret_cast<const char*>(b.data_ptr()) ==
-                    reinterpret_cast<const char*>(s.dst) + 2 * s.b0,
+    parse_ag_spec(ag, s);
+    TORCH_CHECK(reinterpret_cast<const char*>(b.data_ptr()) == reinterpret_cast<const char*>(s.dst) + 2 * s.b0,
                 "gemm_tc: B must be the gathered buffer at element b0");
-    // Start with the tiles whose rows this rank owns (no wait), then follow the copy
-    // order, which starts right after this rank's own range.
-    const long own0 = s.unit0 + s.rank * s.cs, own1 = own0 + s.cs;
-    const int np = (int)((s.hi - s.lo + (1L << s.piece_shift) - 1) >> s.piece_shift);
-    s.rot = (own1 > s.lo && own1 < s.hi) ? (int)((own1 - s.lo) >> s.piece_shift) : 0;
-    if (s.rot >= np) s.rot = 0;
-    const long row = std::max<long>(0, (std::max(own0, s.lo) - s.b0) / K);
-    const long rows_per_tile = swiglu ? bn / 2 : bn;
-    g.n_rot = (int)(((swiglu ? row % (N / 2) : row) / rows_per_tile) % g.n_tiles);
-    PB_CUDA_CHECK(cudaMemsetAsync(s.counter, 0, sizeof(int), stream0));
+    if (s.split > 0) {
+      // gate|up interleaved copies: tiles in plain order
+      TORCH_CHECK(swiglu && s.b0 == s.lo && s.split == (N / 2) * K, "gemm_tc: split gather is for the gate|up GEMM");
+      g.n_rot = 0;
+    } else {
+      // Copies start right after this rank's own range (or at lo when the range holds
+      // none of it); tiles start with this rank's own rows (no wait), else with the
+      // rows of the first piece copied, so the MMAs follow the copies.
+      const long own0 = s.unit0 + s.rank * s.cs, own1 = own0 + s.cs;
+      const bool mine = own0 < s.hi && own1 > s.lo;
+      const long np = (s.hi - s.lo + (1L << s.piece_shift) - 1) >> s.piece_shift;
+      s.rot = (mine && own1 < s.hi) ? (int)((own1 - s.lo) >> s.piece_shift) : 0;
+      if (s.rot >= np) s.rot = 0;
+      const long first = mine ? std::max(own0, s.lo) : s.lo;
+      const long row = std::max<long>(0, (first - s.b0) / K);
+      const long rows_per_tile = swiglu ? bn / 2 : bn;
+      const long brow = swiglu ? row % (N / 2) : row;
+      g.n_rot = brow < (swiglu ? N / 2 : N) ? (int)((brow / rows_per_tile) % g.n_tiles) : 0;
+    }
+    const long nblocks = (s.hi - s.lo + (1L << s.block_shift) - 1) >> s.block_shift;
+    PB_CUDA_CHECK(cudaMemsetAsync(s.counters, 0, sizeof(uint32_t) * (1 + nblocks), stream0));
   }
   const int tiles = g.m_tiles * g.n_tiles * g.splits;
   int grid = std::min<int>(tiles, num_sms(a.device().index()));

@@ -33,6 +33,7 @@ Checkpoints use the reference's FSDP layout (``torch.distributed.checkpoint`` wi
 
 from __future__ import annotations
 
+import os
 from dataclasses import dataclass, field
 from typing import Any
 
@@ -45,7 +46,8 @@ from packbalance_b200.parallel.flat import GradWindow, Slot
 
 ALIGN = 64  # elements; chunk boundaries stay 16-byte aligned in bf16 and fp32
 SYNC_WORDS = 16384  # per-CTA barrier slots (uint32) in the symmetric sync buffer
-PIECE_SHIFT = 14  # all-gather piece = 16384 bf16 = 32 KB
+PIECE_SHIFT = 12  # all-gather piece = 4096 bf16 = 8 KB (one round of a warp's loads)
+BLOCK_SHIFT = 18  # readiness is tracked per block of 256 Ki elements
 
 
 @dataclass
@@ -160,6 +162,11 @@ class ShardedParameters(GradWindow):
         for h in (self.h_gath, self.h_grad, self.h_master, self.h_sync):
             if int(getattr(h, "offset", 0)) != 0:
                 raise RuntimeError("symmetric buffers must start at their allocation base")
+        # NVLS: reduce-scatter with multimem.ld_reduce when the driver bound a multicast
+        # object over the gradient buffers (PB_ALLREDUCE=p2p forces peer loads)
+        use_mc = os.environ.get("PB_ALLREDUCE", "auto") in ("auto", "nvls")
+        self.grad_mc = int(self.h_grad.multicast_ptr or 0) if use_mc else 0
+        self.mode = "nvls" if self.grad_mc else "p2p"
         self.xchg_ptrs = torch.tensor([int(p) + 4 * SYNC_WORDS for p in self.h_sync.buffer_ptrs], dtype=torch.int64,
                                       device=dev)
         self.exp_avg = torch.zeros(max(self.shard_numel, 4), dtype=torch.float32, device=dev)
@@ -174,11 +181,9 @@ class ShardedParameters(GradWindow):
         self.skipped = torch.zeros((), dtype=torch.int32, device=dev)
         self.arrive = torch.zeros(1, dtype=torch.int32, device=dev)
         self.go = torch.zeros(1, dtype=torch.int32, device=dev)
-        max_pieces = max(((hi - lo) >> PIECE_SHIFT) + 1 for u in units for lo, hi in u.segments)
-        self.ag_flags = torch.zeros(max_pieces, dtype=torch.int32, device=dev)
-        self.ag_counter = torch.zeros(4, dtype=torch.int32, device=dev)
+        max_blocks = max(((hi - lo) >> BLOCK_SHIFT) + 2 for u in units for lo, hi in u.segments)
+        self.ag_counters = torch.zeros(max_blocks + 1, dtype=torch.int32, device=dev)
         self._epoch = 0  # barrier epochs (sync pads), one per collective launch
-        self._ag_epoch = 0
         self._arrive_total = 0
         self.rs_ctas = min(rs_ctas, SYNC_WORDS // (3 * W))
         C = _native.module()
@@ -251,11 +256,10 @@ class ShardedParameters(GradWindow):
                 return u, seg
         raise AssertionError("parameter outside its unit's segments")
 
-    def _ag_spec(self, u: Unit, seg: tuple[int, int], b0: int) -> list[int]:
-        self._ag_epoch += 1
+    def _ag_spec(self, u: Unit, seg: tuple[int, int], b0: int, split: int = 0) -> list[int]:
         return [
             int(self.h_gath.buffer_ptrs_dev), self.gathered.data_ptr(), seg[0], -(-seg[1] // 8) * 8, u.unit0, u.cs, b0,
-            self.rank, self.world, PIECE_SHIFT, self.ag_flags.data_ptr(), self.ag_counter.data_ptr(), self._ag_epoch,
+            split, self.rank, self.world, PIECE_SHIFT, BLOCK_SHIFT, self.ag_counters.data_ptr(),
         ]
 
     def gather_spec(self, *params: nn.Parameter) -> list[int] | None:
@@ -267,7 +271,9 @@ class ShardedParameters(GradWindow):
         if seg in self._gathered_segs:
             return None
         self._gathered_segs.add(seg)
-        return self._ag_spec(u, seg, self.by_param[id(params[0])].offset)
+        # gate|up: the two matrices are copied interleaved, in the order SwiGLU tiles read them
+        split = params[0].numel() if len(params) == 2 and params[0].shape == params[1].shape else 0
+        return self._ag_spec(u, seg, self.by_param[id(params[0])].offset, split)
 
     def _ensure_gathered(self, params) -> None:
         for p in params:
@@ -340,7 +346,7 @@ class ShardedParameters(GradWindow):
             _native.module().fsdp_reduce_scatter(
                 int(self.h_grad.buffer_ptrs_dev), int(self.h_sync.buffer_ptrs_dev), SYNC_WORDS, lo, lo + u.cs,
                 self.shard_grad.data_ptr() + 4 * u.soff, self.rank, self.world, self._epoch, 1.0 / self.world,
-                self.sumsq, self.rs_ctas,
+                self.sumsq, self.rs_ctas, self.grad_mc,
             )
 
     # ---- optimizer step -----------------------------------------------------------------
@@ -370,7 +376,7 @@ class ShardedParameters(GradWindow):
                  self.world, self._epoch, lo, lo + e.cs, self.shard_grad.data_ptr() + 4 * e.soff,
                  self.rep_sumsq.data_ptr(), self.xchg_ptrs.data_ptr(), self.arrive.data_ptr(),
                  self._arrive_total & 0xFFFFFFFF, self.go.data_ptr(), self._segs.data_ptr(), self._segs.shape[0],
-                 self.final_ctas],
+                 self.final_ctas, self.grad_mc],
                 [1.0 / self.world, lr, b1, b2, eps, wd, bc1, bc2, max_norm],
                 self.sumsq, self.norm_out, self.skipped,
             )

@@ -106,7 +106,11 @@ def save_checkpoint(
     if fsdp and dist.is_available() and dist.is_initialized():
         import torch.distributed.checkpoint as dcp
 
-        dcp.save({"model": model.state_dict(), "optimizer": optimizer.state_dict()}, checkpoint_id=str(ckpt_dir / "dcp"))
+        if hasattr(optimizer, "full_state_dict"):
+            state = sharded_state_dicts(optimizer)
+        else:
+            state = {"model": model.state_dict(), "optimizer": optimizer.state_dict()}
+        dcp.save(state, checkpoint_id=str(ckpt_dir / "dcp"))
         dist.barrier()
         if is_main_process():
             _write_meta(ckpt_dir, step, extra)
@@ -144,6 +148,10 @@ def load_checkpoint(
 ) -> dict[str, Any]:
     """Load model (+ optimizer) state in place; returns ``{"step", **extra}``."""
     ckpt = Path(path)
+    if fsdp and dist.is_available() and dist.is_initialized() and hasattr(optimizer, "full_state_dict"):
+        load_sharded_dcp(optimizer, ckpt / "dcp")
+        meta_file = ckpt / META
+        return json.loads(meta_file.read_text(encoding="utf-8")) if meta_file.exists() else {}
     if fsdp and dist.is_available() and dist.is_initialized():
         import torch.distributed.checkpoint as dcp
 
@@ -168,3 +176,52 @@ def load_checkpoint(
     if optimizer is not None and "optimizer" in state:
         optimizer.load_state_dict(state["optimizer"])
     return {"step": int(state.get("step", 0)), **state.get("extra", {})}
+
+
+# ---- native sharded engine ------------------------------------------------------------
+def sharded_state_dicts(optimizer) -> dict[str, Any]:
+    """DCP state of the native sharded engine: full tensors under the reference's keys
+    (``model.<name>``, ``optimizer.state.<i>.{step,exp_avg,exp_avg_sq}``,
+    ``optimizer.param_groups``).  Each parameter is written by one rank (index % W), so
+    no rank holds more than its share of the model on the host.  Collective."""
+    sp = optimizer.sp
+    model = sp.full_tensors("param", owner_only=True)
+    optim = optimizer.full_state_dict(owner_only=True)
+    if dist.get_rank() != 0:
+        optim.pop("param_groups")
+    return {"model": model, "optimizer": optim}
+
+
+def load_sharded_dcp(optimizer, dcp_dir: Path) -> None:
+    """Inverse of :func:`sharded_state_dicts`, one sharding unit at a time (bounded host
+    memory).  Collective: every rank reads every tensor of a unit and keeps its chunk."""
+    import torch.distributed.checkpoint as dcp
+
+    sp = optimizer.sp
+    order = sp.model_order()
+    index = {s.name: i for i, s in enumerate(order)}
+    groups = [sp.rep_slots] + [u.slots for u in sp.units]
+    step = 0.0
+    for slots in groups:
+        model = {s.name: torch.empty(s.shape, dtype=torch.float32) for s in slots}
+        state = {
+            index[s.name]: {"step": torch.zeros(()), "exp_avg": torch.empty(s.shape, dtype=torch.float32),
+                            "exp_avg_sq": torch.empty(s.shape, dtype=torch.float32)}
+            for s in slots
+        }
+        dcp.load({"model": model, "optimizer": {"state": state}}, checkpoint_id=str(dcp_dir))
+        sp.load_full_tensors(model, "param")
+        sp.load_full_tensors({s.name: state[index[s.name]]["exp_avg"] for s in slots}, "exp_avg")
+        sp.load_full_tensors({s.name: state[index[s.name]]["exp_avg_sq"] for s in slots}, "exp_avg_sq")
+        step = max([step] + [float(st["step"]) for st in state.values()])
+    # param_groups entries are stored one key per field (optimizer.param_groups.0.<k>)
+    prefix = "optimizer.param_groups.0."
+    keys = [k[len(prefix):] for k in dcp.FileSystemReader(str(dcp_dir)).read_metadata().state_dict_metadata
+            if k.startswith(prefix)]
+    group = {k: None for k in keys}
+    if group:
+        dcp.load({"optimizer": {"param_groups": [group]}}, checkpoint_id=str(dcp_dir))
+    optimizer.step_count = int(step)
+    for k, v in group.items():
+        if k != "params":
+            optimizer.param_groups[0][k] = v

@@ -86,6 +86,20 @@ WORKER = textwrap.dedent(
         worst = max(worst, rel)
         assert rel < 0.05, (n, rel, err, upd)
     frac = 0.0
+    # checkpoint round trip in the reference's FSDP layout (DCP), into a fresh engine
+    from packbalance_b200.train.checkpoint import load_checkpoint, save_checkpoint
+    ck = save_checkpoint(shd.model, shd.optimizer, 3, os.path.join(os.environ["PB_TMP"], "ck"), fsdp=True)
+    torch.manual_seed(1)
+    shd2 = TrainEngine(replace(base, train=replace(base.train, fsdp=True)), dev)
+    load_checkpoint(ck, shd2.model, shd2.optimizer, fsdp=True, device=dev)
+    shd2.rebuild_scheduler(3)
+    c1 = shd.step(mine, tokens)
+    c2 = shd2.step(mine, tokens)
+    l1, l2 = c1["loss_sum"].item(), c2["loss_sum"].item()
+    assert abs(l1 - l2) <= 1e-5 * abs(l1), (l1, l2)
+    p1 = shd.sharded.full_tensors("param")
+    p2 = shd2.sharded.full_tensors("param")
+    assert max((p1[n] - p2[n]).abs().max().item() for n in p1) < 1e-3
     shd.close(); ddp.close()
     dist.barrier()
     dist.destroy_process_group()
@@ -95,14 +109,14 @@ WORKER = textwrap.dedent(
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-@pytest.mark.parametrize("tie", [True, False])
-def test_sharded_engine_matches_ddp(tmp_path, tie):
+@pytest.mark.parametrize("tie,mode", [(True, "p2p"), (False, "p2p"), (True, "auto")])
+def test_sharded_engine_matches_ddp(tmp_path, tie, mode):
     world = min(torch.cuda.device_count(), 4)
     script = tmp_path / "worker.py"
     script.write_text(WORKER)
     port = str(_free_port())
     env = {**os.environ, "PB_ROOT": str(ROOT), "PB_TMP": str(tmp_path), "PB_TIE": "1" if tie else "0",
-           "MASTER_ADDR": "127.0.0.1", "MASTER_PORT": port, "NCCL_NVLS_ENABLE": "0", "PB_ALLREDUCE": "p2p"}
+           "MASTER_ADDR": "127.0.0.1", "MASTER_PORT": port, "NCCL_NVLS_ENABLE": "0", "PB_ALLREDUCE": mode}
     r = subprocess.run(
         ["timeout", "-k", "30", "300", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
          f"--nproc-per-node={world}", "--master-addr=127.0.0.1", f"--master-port={port}", str(script)],
