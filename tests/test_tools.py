@@ -1,0 +1,75 @@
+"""Command-line tools: benches, thesis validation, metrics plot (CPU)."""
+
+import json
+from pathlib import Path
+
+import pytest
+import yaml
+
+from packbalance_b200.config import config_to_dict, load_config
+
+
+@pytest.fixture
+def tiny_config(tmp_path: Path) -> Path:
+    cfg = load_config(Path(__file__).resolve().parents[1] / "configs" / "tiny.yaml")
+    d = config_to_dict(cfg)
+    d["data"]["data_dir"] = str(tmp_path / "data")
+    d["data"]["synthetic_num_docs"] = 400
+    d["train"]["output_dir"] = str(tmp_path / "out")
+    p = tmp_path / "cfg.yaml"
+    p.write_text(yaml.safe_dump(d), encoding="utf-8")
+    return p
+
+
+def test_bench_schedule_balanced_not_worse(tiny_config: Path, tmp_path: Path) -> None:
+    from packbalance_b200.profiling import bench_schedule
+
+    rows = bench_schedule.main(["--config", str(tiny_config), "--modes", "pack_ffd,isoflop", "--world-size", "4",
+                                "--output", str(tmp_path / "s.json")])
+    by = {(r["mode"], r["schedule"]): r for r in rows}
+    for mode in ("pack_ffd", "isoflop"):
+        assert by[(mode, "balanced")]["step_cost_cv"] <= by[(mode, "random")]["step_cost_cv"] + 1e-12
+    assert json.loads((tmp_path / "s.json").read_text())
+
+
+def test_bench_data_counts_tokens(tiny_config: Path, tmp_path: Path) -> None:
+    from packbalance_b200.profiling import bench_data
+
+    rows = bench_data.main(["--config", str(tiny_config), "--modes", "pad,pack_ffd", "--workers", "0",
+                            "--num-batches", "4", "--warmup", "1", "--output", str(tmp_path / "d.json")])
+    assert len(rows) == 2 and all(r["useful_tokens"] > 0 for r in rows)
+    pad = next(r for r in rows if r["mode"] == "pad")
+    assert pad["compute_tokens"] >= pad["useful_tokens"]
+
+
+def test_bench_train_cpu_step(tiny_config: Path, tmp_path: Path) -> None:
+    from packbalance_b200.profiling import bench_train
+
+    rows = bench_train.main(["--config", str(tiny_config), "--modes", "pack_ffd", "--steps", "1", "--warmup", "1",
+                             "--device", "cpu", "--output", str(tmp_path / "t.json")])
+    assert rows[0]["useful_tokens_per_s"] > 0 and rows[0]["timing"] == "wall clock"
+
+
+@pytest.mark.slow
+def test_prove_intuition_quick(tiny_config: Path, tmp_path: Path) -> None:
+    from packbalance_b200.profiling import prove_intuition
+
+    res = prove_intuition.main(["--config", str(tiny_config), "--output-dir", str(tmp_path / "thesis"), "--quick"])
+    assert res["packing"]["pad"]["padding_waste"] > res["packing"]["pack_ffd"]["padding_waste"]
+    assert res["packing"]["pad"]["flops_ratio_vs_pack_ffd"] > 1.0
+    assert res["doc_mask"]["correct_mask_max_abs_error"] < 1e-4 < res["doc_mask"]["broken_mask_max_abs_error"]
+    assert res["attention"]["fit_linear_plus_quadratic"]["r2"] > 0.9
+    assert (tmp_path / "thesis" / "report.md").exists()
+
+
+def test_plot_metrics_writes_svg(tmp_path: Path) -> None:
+    from packbalance_b200.utils import plot_metrics
+
+    log = tmp_path / "metrics.jsonl"
+    recs = [{"event": "start", "world_size": 1}]
+    recs += [{"step": i, "loss": 10.0 / (i + 1), "tokens_per_sec": 1000.0 + i} for i in range(1, 30)]
+    recs += [{"step": 10, "val_loss": 2.5}, {"event": "finish", "step": 29}]
+    log.write_text("\n".join(json.dumps(r) for r in recs), encoding="utf-8")
+    out = plot_metrics.main(["--metrics", str(log), "--output", str(tmp_path / "curve.png")])
+    text = out.read_text()
+    assert out.suffix == ".svg" and text.startswith("<svg") and text.count("<polyline") == 3
