@@ -330,7 +330,7 @@ def describe_model(m) -> str:
     """Model name of the JSON line, from the config actually run."""
     from packbalance_b200.data.cost import FlopModel
 
-    n = FlopModel.from_config(m).total_params()
+    n = FlopModel.from_config(m).total_params
     tie = "tied" if m.tie_embeddings else "untied"
     return (f"llama-{n / 1e6:.0f}M ({m.n_layers}L d{m.d_model} {m.n_heads}H/{m.n_kv_heads}KV ff{m.d_ff} "
             f"V{m.vocab_size} {tie})")

@@ -116,6 +116,107 @@ __global__ void rmsnorm_bwd_kernel(const TD* __restrict__ dy, const TI* __restri
   }
 }
 
+// Register-resident variants for n = 128 * CH (the common model widths): each warp
+// holds its row in registers, so x (and dy, dres) are read from HBM exactly once and
+// all loads of a row are issued before the first reduction; rows are strided over a
+// persistent grid.  The backward keeps each lane's dw partial (4 CH columns) in
+// registers across the warp's rows.
+template <int CH, typename TI, typename TO>
+__global__ void __launch_bounds__(256) add_rmsnorm_reg_kernel(const TI* __restrict__ xp,
+                                                               const __nv_bfloat16* __restrict__ delta,
+                                                               const float* __restrict__ w, float* __restrict__ x_out,
+                                                               TO* __restrict__ y, float* __restrict__ rstd, int rows,
+                                                               float eps) {
+  constexpr int n = 128 * CH;
+  const int lane = threadIdx.x & 31;
+  const int warps = blockDim.x / 32;
+  for (int row = blockIdx.x * warps + threadIdx.x / 32; row < rows; row += gridDim.x * warps) {
+    const long off = static_cast<long>(row) * n;
+    float4 v[CH];
+#pragma unroll
+    for (int k = 0; k < CH; ++k) v[k] = ld4(xp + off + lane * 4 + k * 128);
+    if (delta != nullptr) {
+#pragma unroll
+      for (int k = 0; k < CH; ++k) {
+        const float4 d = ld4(delta + off + lane * 4 + k * 128);
+        v[k].x += d.x; v[k].y += d.y; v[k].z += d.z; v[k].w += d.w;
+        st4(x_out + off + lane * 4 + k * 128, v[k]);
+      }
+    }
+    float ss = 0.f;
+#pragma unroll
+    for (int k = 0; k < CH; ++k) ss += v[k].x * v[k].x + v[k].y * v[k].y + v[k].z * v[k].z + v[k].w * v[k].w;
+    ss = warp_sum(ss);
+    const float r = rsqrtf(ss / n + eps);
+    if (lane == 0) rstd[row] = r;
+#pragma unroll
+    for (int k = 0; k < CH; ++k) {
+      const float4 g = ld4(w + lane * 4 + k * 128);
+      st4(y + off + lane * 4 + k * 128, make_float4(v[k].x * r * g.x, v[k].y * r * g.y, v[k].z * r * g.z, v[k].w * r * g.w));
+    }
+  }
+}
+
+template <int CH, typename TI, typename TD>
+__global__ void __launch_bounds__(256) rmsnorm_bwd_reg_kernel(const TD* __restrict__ dy, const TI* __restrict__ x,
+                                                               const float* __restrict__ w,
+                                                               const float* __restrict__ rstd,
+                                                               const float* __restrict__ dres, float* __restrict__ dx,
+                                                               __nv_bfloat16* __restrict__ dx_bf16,
+                                                               float* __restrict__ dw_out, int rows) {
+  constexpr int n = 128 * CH;
+  __shared__ float sdw[8][n];
+  const int lane = threadIdx.x & 31, wid = threadIdx.x / 32;
+  const int warps = blockDim.x / 32;
+  float4 acc[CH];
+#pragma unroll
+  for (int k = 0; k < CH; ++k) acc[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int row = blockIdx.x * warps + wid; row < rows; row += gridDim.x * warps) {
+    const long off = static_cast<long>(row) * n;
+    float4 g[CH], xv[CH], e[CH];
+#pragma unroll
+    for (int k = 0; k < CH; ++k) {
+      g[k] = ld4(dy + off + lane * 4 + k * 128);
+      xv[k] = ld4(x + off + lane * 4 + k * 128);
+    }
+    if (dres != nullptr) {
+#pragma unroll
+      for (int k = 0; k < CH; ++k) e[k] = ld4(dres + off + lane * 4 + k * 128);
+    }
+    const float r = rstd[row];
+    float dot = 0.f;
+#pragma unroll
+    for (int k = 0; k < CH; ++k) {
+      const float4 wv = ld4(w + lane * 4 + k * 128);
+      dot += g[k].x * wv.x * xv[k].x + g[k].y * wv.y * xv[k].y + g[k].z * wv.z * xv[k].z + g[k].w * wv.w * xv[k].w;
+    }
+    dot = warp_sum(dot) * r / n;
+#pragma unroll
+    for (int k = 0; k < CH; ++k) {
+      const float4 wv = ld4(w + lane * 4 + k * 128);
+      float4 d = make_float4(r * (g[k].x * wv.x - xv[k].x * r * dot), r * (g[k].y * wv.y - xv[k].y * r * dot),
+                             r * (g[k].z * wv.z - xv[k].z * r * dot), r * (g[k].w * wv.w - xv[k].w * r * dot));
+      if (dres != nullptr) {
+        d.x += e[k].x; d.y += e[k].y; d.z += e[k].z; d.w += e[k].w;
+      }
+      st4(dx + off + lane * 4 + k * 128, d);
+      if (dx_bf16 != nullptr) st4(dx_bf16 + off + lane * 4 + k * 128, d);
+      acc[k].x += g[k].x * xv[k].x * r;
+      acc[k].y += g[k].y * xv[k].y * r;
+      acc[k].z += g[k].z * xv[k].z * r;
+      acc[k].w += g[k].w * xv[k].w * r;
+    }
+  }
+#pragma unroll
+  for (int k = 0; k < CH; ++k) st4(&sdw[wid][lane * 4 + k * 128], acc[k]);
+  __syncthreads();
+  for (int c = threadIdx.x; c < n; c += blockDim.x) {
+    float t = 0.f;
+    for (int q = 0; q < warps; ++q) t += sdw[q][c];
+    atomicAdd(dw_out + c, t);
+  }
+}
+
 std::vector<at::Tensor> add_rmsnorm_fwd(at::Tensor x, c10::optional<at::Tensor> delta, at::Tensor w, double eps,
                                         bool out_bf16) {
   TORCH_CHECK(x.is_cuda() && x.is_contiguous() && w.is_contiguous() && w.scalar_type() == at::kFloat);
@@ -139,6 +240,23 @@ std::vector<at::Tensor> add_rmsnorm_fwd(at::Tensor x, c10::optional<at::Tensor> 
   dim3 grid((rows + warps - 1) / warps);
   auto s = at::cuda::getCurrentCUDAStream();
   float* xop = delta.has_value() ? xo.data_ptr<float>() : nullptr;
+  if (x.scalar_type() == at::kFloat && out_bf16 && n % 128 == 0 && n / 128 <= 32) {
+    const int g2 = std::min<int>((rows + warps - 1) / warps, 4 * num_sms(x.device().index()));
+    const float* xp = x.data_ptr<float>();
+    auto* yp = reinterpret_cast<__nv_bfloat16*>(y.data_ptr());
+    bool done = true;
+    switch (n / 128) {
+#define PB_FWD_CH(C) \
+  case C: add_rmsnorm_reg_kernel<C, float, __nv_bfloat16><<<g2, 256, 0, s>>>(xp, dp, w.data_ptr<float>(), xop, yp, rstd.data_ptr<float>(), rows, (float)eps); break;
+      PB_FWD_CH(2) PB_FWD_CH(4) PB_FWD_CH(6) PB_FWD_CH(8) PB_FWD_CH(12) PB_FWD_CH(16) PB_FWD_CH(32)
+#undef PB_FWD_CH
+      default: done = false;
+    }
+    if (done) {
+      PB_CUDA_CHECK(cudaGetLastError());
+      return {xo, y, rstd};
+    }
+  }
   if (x.scalar_type() == at::kFloat) {
     if (out_bf16)
       add_rmsnorm_kernel<float, __nv_bfloat16><<<grid, warps * 32, 0, s>>>(
@@ -175,6 +293,24 @@ at::Tensor rmsnorm_bwd(at::Tensor dy, at::Tensor x, at::Tensor w, at::Tensor rst
   auto s = at::cuda::getCurrentCUDAStream();
   if (!accumulate_dw) PB_CUDA_CHECK(cudaMemsetAsync(dw_out.data_ptr(), 0, n * sizeof(float), s));
   if (rows == 0) return dx;
+  if (x.scalar_type() == at::kFloat && dy.scalar_type() == at::kFloat && n % 128 == 0 && n / 128 <= 8) {
+    // one persistent wave: 1 CTA of 8 warps per SM for CH >= 6 (register-bound), else 2
+    const int g2 = std::min<int>((rows + 7) / 8, (n / 128 >= 6 ? 1 : 2) * num_sms(x.device().index()));
+    const float* dres_q = dres.has_value() ? dres->data_ptr<float>() : nullptr;
+    __nv_bfloat16* dxq = dx_bf16.has_value() ? reinterpret_cast<__nv_bfloat16*>(dx_bf16->data_ptr()) : nullptr;
+    bool done = true;
+    switch (n / 128) {
+#define PB_BWD_CH(C) \
+  case C: rmsnorm_bwd_reg_kernel<C, float, float><<<g2, 256, 0, s>>>(dy.data_ptr<float>(), x.data_ptr<float>(), w.data_ptr<float>(), rstd.data_ptr<float>(), dres_q, dx.data_ptr<float>(), dxq, dw_out.data_ptr<float>(), rows); break;
+      PB_BWD_CH(2) PB_BWD_CH(4) PB_BWD_CH(6) PB_BWD_CH(8)
+#undef PB_BWD_CH
+      default: done = false;
+    }
+    if (done) {
+      PB_CUDA_CHECK(cudaGetLastError());
+      return dx;
+    }
+  }
   const int warps = 4;
   const int nb = std::min((rows + warps - 1) / warps, 2 * num_sms(x.device().index()));
   const float* dres_p = dres.has_value() ? dres->data_ptr<float>() : nullptr;

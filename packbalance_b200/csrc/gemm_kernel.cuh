@@ -104,16 +104,23 @@ __device__ __forceinline__ void tile_coords(const GemmArgs& a, int tile, int& mb
 }
 
 // ------------------------------- epilogue helpers ---------------------------------
+// Per-warp staging ring in shared memory for the epilogue's TMA stores: 4 slots of
+// 2 KB (a 32 x 32 bf16 box) or 2 slots of 4 KB (a 32 x 32 fp32 box), so up to 3 (or 1)
+// stores are in flight while the next box is staged.
 struct Stager {
   uint8_t* base;  // this warp's 8 KB
   int slot;
+  bool wide;  // fp32 boxes
   __device__ __forceinline__ uint8_t* acquire() {
-    // The store issued two slot-uses ago must have finished reading its slot.
-    if ((threadIdx.x & 31) == 0) bulk_wait_read<1>();
+    // The store that last used this slot must have finished reading it.
+    if ((threadIdx.x & 31) == 0) {
+      if (wide) bulk_wait_read<1>();
+      else bulk_wait_read<3>();
+    }
     __syncwarp();
-    return base + slot * 4096;
+    return base + slot * (wide ? 4096 : 2048);
   }
-  __device__ __forceinline__ void release() { slot ^= 1; }
+  __device__ __forceinline__ void release() { slot = (slot + 1) & (wide ? 1 : 3); }
 };
 
 // 32 fp32 of this lane's row -> 128-byte row of a 128B-swizzled [32 x 32] fp32 box.
@@ -159,6 +166,19 @@ __device__ __forceinline__ void tmem_load_f32(uint32_t taddr, float (&v)[32]) {
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+// Two 32-column TMEM loads behind one wait.
+__device__ __forceinline__ void tmem_load_f32x2(uint32_t ta, float (&v)[32], uint32_t tb, float (&w)[32]) {
+  uint32_t r[32], q[32];
+  tmem_ld32(ta, r);
+  tmem_ld32(tb, q);
+  tmem_wait_ld();
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    v[i] = __uint_as_float(r[i]);
+    w[i] = __uint_as_float(q[i]);
+  }
+}
+
 __device__ __forceinline__ float bf16_round(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
 
 // Epilogue of one 128 x BN tile for the 32 rows [row0, row0 + 32) owned by this warp.
@@ -192,8 +212,7 @@ __device__ __forceinline__ void run_epilogue(const GemmArgs& a, const CUtensorMa
       float u[32];
 #pragma unroll 1
       for (int c = 0; c < HB; c += 32) {
-        tmem_load_f32(tacc + c, v);
-        tmem_load_f32(tacc + HB + c, u);
+        tmem_load_f32x2(tacc + c, v, tacc + HB + c, u);
         const int col = nb * HB + c;
         if (col >= a.F) continue;
         // Round the pre-activations once and compute h from the rounded values, so
@@ -212,7 +231,7 @@ __device__ __forceinline__ void run_epilogue(const GemmArgs& a, const CUtensorMa
         issue_store(tm_aux, s, a.F + col, row0, ST_STORE);
         st.release();
 #pragma unroll
-        for (int i = 0; i < 32; ++i) v[i] = v[i] * sigmoidf_(v[i]) * u[i];
+        for (int i = 0; i < 32; ++i) v[i] = __fdividef(v[i] * u[i], 1.f + __expf(-v[i]));
         s = st.acquire();
         stage_bf16(s, v, 1.f);
         issue_store(tm_out, s, col, row0, ST_STORE);
@@ -224,14 +243,48 @@ __device__ __forceinline__ void run_epilogue(const GemmArgs& a, const CUtensorMa
       const int half = a.head_dim / 2;
       const int p = row_ok ? min(max(a.pos[row], 0), a.n_pos - 1) : 0;
       float w[32];
+      if (half == 32) {
+        // head_dim 64: this row's 32 (cos, sin) pairs serve every head of the tile
+        float cs[32], sn[32];
+        const float4* cr = reinterpret_cast<const float4*>(a.cos_t + static_cast<long>(p) * half);
+        const float4* sr = reinterpret_cast<const float4*>(a.sin_t + static_cast<long>(p) * half);
+#pragma unroll
+        for (int i4 = 0; i4 < 8; ++i4) {
+          const float4 c4 = cr[i4], s4 = sr[i4];
+          cs[4 * i4] = c4.x; cs[4 * i4 + 1] = c4.y; cs[4 * i4 + 2] = c4.z; cs[4 * i4 + 3] = c4.w;
+          sn[4 * i4] = s4.x; sn[4 * i4 + 1] = s4.y; sn[4 * i4 + 2] = s4.z; sn[4 * i4 + 3] = s4.w;
+        }
+#pragma unroll 1
+        for (int hb = 0; hb < BN; hb += 64) {
+          const int hcol = nb * BN + hb;
+          tmem_load_f32x2(tacc + hb, v, tacc + hb + 32, w);
+          if (hcol >= a.N) continue;
+          if (hcol < a.n_rope_cols) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+              const float x1 = v[i], x2 = w[i];
+              v[i] = x1 * cs[i] - x2 * sn[i];
+              w[i] = x2 * cs[i] + x1 * sn[i];
+            }
+          }
+          uint8_t* s = st.acquire();
+          stage_bf16(s, v, 1.f);
+          issue_store(tm_out, s, hcol, row0, ST_STORE);
+          st.release();
+          s = st.acquire();
+          stage_bf16(s, w, 1.f);
+          issue_store(tm_out, s, hcol + 32, row0, ST_STORE);
+          st.release();
+        }
+        break;
+      }
 #pragma unroll 1
       for (int hb = 0; hb < BN; hb += a.head_dim) {
         const int hcol = nb * BN + hb;
         const bool rot = hcol < a.n_rope_cols;
 #pragma unroll 1
         for (int j = 0; j < half; j += 32) {
-          tmem_load_f32(tacc + hb + j, v);
-          tmem_load_f32(tacc + hb + half + j, w);
+          tmem_load_f32x2(tacc + hb + j, v, tacc + hb + half + j, w);
           if (hcol >= a.N) continue;
           if (rot) {
             const float4* cr = reinterpret_cast<const float4*>(a.cos_t + static_cast<long>(p) * half + j);
@@ -487,7 +540,7 @@ __global__ void __launch_bounds__(256, 1)
     if (args.ag.world > 0) ag_copy_warp(args.ag);
   } else {
     const int q = warp & 3;
-    Stager st{smem + C::EPI_OFF + q * kEpiWarpBytes, 0};
+    Stager st{smem + C::EPI_OFF + q * kEpiWarpBytes, 0, args.epi == EPI_F32 || args.epi == EPI_ADD_F32};
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {

@@ -73,7 +73,7 @@ def run(args) -> list[dict]:
     from packbalance_b200.ops import _native
     from packbalance_b200.ops.attention import attention_plan, attn_backward_packed, attn_forward_packed
     from packbalance_b200.ops.cross_entropy import linear_cross_entropy
-    from packbalance_b200.ops.gemm import EPI_BF16, gemm, linear_wgrad
+    from packbalance_b200.ops.gemm import EPI_BF16, EPI_ROPE, EPI_SWIGLU, gemm, linear_wgrad
     from packbalance_b200.ops.reference import rmsnorm_reference, swiglu_reference
     from packbalance_b200.ops.rmsnorm import rmsnorm
     from packbalance_b200.ops.swiglu import swiglu
@@ -132,6 +132,32 @@ def run(args) -> list[dict]:
             gw = torch.empty(n, k, device=dev)
             add(f"gemm_wgrad_{name}", timeit(lambda: linear_wgrad(dy, a, gw), args.iters, args.warmup),
                 flops=2.0 * m * n * k, shape=[n, k, m])
+        # the fused forward epilogues of the training step
+        m, k = t, 768
+        a = torch.randn(m, k, device=dev).to(torch.bfloat16)
+        wgu = torch.randn(4096, k, device=dev).to(torch.bfloat16)
+        h = torch.empty(m, 2048, device=dev, dtype=torch.bfloat16)
+        gu = torch.empty(m, 4096, device=dev, dtype=torch.bfloat16)
+        add("gemm_fwd_gateup_swiglu", timeit(lambda: gemm(a, wgu, h, m, 4096, k, epi=EPI_SWIGLU, aux=gu), args.iters,
+                                             args.warmup), flops=2.0 * m * 4096 * k, shape=[m, 4096, k])
+        wqkv = torch.randn(1280, k, device=dev).to(torch.bfloat16)
+        qkv = torch.empty(m, 1280, device=dev, dtype=torch.bfloat16)
+        pos = (torch.arange(m, device=dev) % 2048).to(torch.int32)
+        inv = 1.0 / (10000.0 ** (torch.arange(0, 64, 2, device=dev).float() / 64))
+        ang = torch.outer(torch.arange(2048, device=dev).float(), inv)
+        cos, sin = torch.cat([ang, ang], -1).cos(), torch.cat([ang, ang], -1).sin()
+        add("gemm_fwd_qkv_rope", timeit(lambda: gemm(a, wqkv, qkv, m, 1280, k, epi=EPI_ROPE, pos=pos, cos=cos, sin=sin,
+                                                     head_dim=64, n_rope_cols=1024), args.iters, args.warmup),
+            flops=2.0 * m * 1280 * k, shape=[m, 1280, k])
+        # large square GEMM: the kernel's main loop against cuBLAS (library baseline)
+        n = 8192
+        a = torch.randn(n, n, device=dev).to(torch.bfloat16)
+        b = torch.randn(n, n, device=dev).to(torch.bfloat16)
+        o = torch.empty(n, n, device=dev, dtype=torch.bfloat16)
+        add("gemm_8192_sm100", timeit(lambda: gemm(a, b, o, n, n, n, epi=EPI_BF16), args.iters, args.warmup),
+            flops=2.0 * n ** 3, shape=[n, n, n])
+        add("gemm_8192_cublas", timeit(lambda: torch.matmul(a, b.t(), out=o), args.iters, args.warmup),
+            flops=2.0 * n ** 3, shape=[n, n, n])
     if "attn_fwd" in cases or "attn_bwd" in cases:
         h, hk, d = 12, 4, 64
         lengths = bench_doc_lengths(args.tokens * 4)

@@ -46,6 +46,35 @@ def test_add_rmsnorm():
     torch.testing.assert_close(rstd, torch.rsqrt(ref_x.square().mean(-1) + 1e-5), atol=1e-5, rtol=1e-5)
 
 
+@pytest.mark.parametrize("n", [256, 512, 768, 1024, 2048, 4096, 800])
+def test_rmsnorm_widths_fused_residual(n):
+    """Register-resident kernels (n = 128 k) and the generic fallback, with the fused
+    residual add (forward) and residual gradient + bf16 copy (backward)."""
+    torch.manual_seed(n)
+    C = _native.module()
+    rows = 1000
+    x = torch.randn(rows, n, device=dev)
+    delta = torch.randn(rows, n, device=dev).to(torch.bfloat16)
+    w = torch.randn(n, device=dev)
+    xo, y, rstd = C.add_rmsnorm_fwd(x, delta, w, 1e-5, True)
+    ref_x = x + delta.float()
+    torch.testing.assert_close(xo, ref_x)
+    torch.testing.assert_close(y.float(), rmsnorm_reference(ref_x, w, 1e-5), atol=3e-2, rtol=1e-2)
+    dy = torch.randn(rows, n, device=dev)
+    dres = torch.randn(rows, n, device=dev)
+    xr, wr = ref_x.clone().requires_grad_(), w.clone().requires_grad_()
+    rmsnorm_reference(xr, wr, 1e-5).backward(dy)
+    dxb = torch.empty(rows, n, device=dev, dtype=torch.bfloat16)
+    dw = torch.full((n,), 7.0, device=dev)
+    dx = C.rmsnorm_bwd(dy, xo, w, rstd, dres, dxb, dw, False)
+    torch.testing.assert_close(dx, xr.grad + dres, atol=1e-3, rtol=1e-4)
+    torch.testing.assert_close(dxb.float(), dx, atol=3e-2, rtol=1e-2)
+    torch.testing.assert_close(dw, wr.grad, atol=2e-3, rtol=1e-4)
+    C.rmsnorm_bwd(dy, xo, w, rstd, None, None, dw, True)  # accumulate
+    torch.testing.assert_close(dw, 2 * wr.grad, atol=4e-3, rtol=1e-4)
+    _native.check_status()
+
+
 def test_swiglu_fwd_bwd():
     torch.manual_seed(0)
     g, u, d = (torch.randn(64, 100, device=dev) for _ in range(3))
