@@ -178,6 +178,9 @@ class TrainConfig:
     # concatenation (document masking keeps packs independent).  The loss and the
     # gradient are those of the microbatch loop; only the launch count changes.
     fuse_microbatches: bool = True
+    # Capture the native single-GPU / data-parallel step in a CUDA graph and replay it
+    # (inputs copied into static buffers); steps with a new input shape run eagerly.
+    cuda_graphs: bool = True
     # Skip the optimizer step when the gradient norm is not finite.
     skip_nonfinite_steps: bool = True
 

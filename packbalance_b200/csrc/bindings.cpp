@@ -30,7 +30,7 @@ void ce_finalize(at::Tensor pmax, at::Tensor psum, at::Tensor tlogit, at::Tensor
 void ce_row_scale(at::Tensor targets, int64_t ignore_index, at::Tensor grad_out, at::Tensor scale);
 void adamw_step(at::Tensor p, at::Tensor g, at::Tensor m, at::Tensor v, at::Tensor shadow, at::Tensor norm,
                 at::Tensor skipped, double lr, double b1, double b2, double eps, double wd, double bc1, double bc2,
-                double max_norm, bool write_shadow);
+                double max_norm, bool write_shadow, c10::optional<at::Tensor> hparams);
 at::Tensor l2_norm(at::Tensor x);
 std::vector<at::Tensor> attn_fwd(at::Tensor qkv, at::Tensor doc_start, at::Tensor tiles, int64_t n_heads,
                                  int64_t n_kv_heads, int64_t head_dim, double scale, at::Tensor out);

@@ -32,15 +32,17 @@ namespace pb {
 
 template <int W>
 __device__ __forceinline__ float reduce_phase(const ArArgs& a, long s0, long s1) {
-  // All W peer loads of a 16-byte group are issued before any is used, two groups per
-  // thread per iteration, so each thread keeps 2 * W loads in flight over NVLink.
+  // All W peer loads of a 16-byte group are issued before any is used, G groups per
+  // thread per iteration (G W <= 8 keeps the data in 32 registers), so each thread keeps
+  // G W loads in flight over NVLink.
+  constexpr int G = W <= 4 ? 2 : 1;
   float ss = 0.f;
   float* mine = a.ptrs[a.rank];
-  const long step = static_cast<long>(blockDim.x) * 8;
+  const long step = static_cast<long>(blockDim.x) * 4 * G;
   for (long i = s0 + threadIdx.x * 4; i < s1; i += step) {
-    float4 v[2][W];
+    float4 v[G][W];
 #pragma unroll
-    for (int u = 0; u < 2; ++u) {
+    for (int u = 0; u < G; ++u) {
       const long j = i + u * blockDim.x * 4;
       if (j + 3 < s1) {
 #pragma unroll
@@ -48,7 +50,7 @@ __device__ __forceinline__ float reduce_phase(const ArArgs& a, long s0, long s1)
       }
     }
 #pragma unroll
-    for (int u = 0; u < 2; ++u) {
+    for (int u = 0; u < G; ++u) {
       const long j = i + u * blockDim.x * 4;
       if (j + 3 < s1) {
         float4 acc = v[u][0];
@@ -107,7 +109,7 @@ __device__ __forceinline__ float gather_phase(const ArArgs& a, long cs, long sub
 }
 
 template <int W>
-__global__ void __launch_bounds__(512) fused_allreduce_kernel(const ArArgs a) {
+__global__ void __launch_bounds__(kCommThreads, kCommMinBlocks) fused_allreduce_kernel(const ArArgs a) {
   __shared__ volatile int abort_sh;
   __shared__ float red[32];
   if (threadIdx.x == 0) abort_sh = 0;
@@ -140,7 +142,8 @@ __global__ void __launch_bounds__(512) fused_allreduce_kernel(const ArArgs a) {
 //   barrier 0 -> ld_reduce / scale / st over its chunk -> multimem.red of its squared
 //   norm into every rank's accumulator -> barrier 1
 // Per rank NVLink carries about (W - 1) / W of the bucket in each direction.
-__global__ void __launch_bounds__(512) nvls_allreduce_kernel(const ArArgs a, float* mc, float* mc_sumsq) {
+__global__ void __launch_bounds__(kCommThreads, kCommMinBlocks) nvls_allreduce_kernel(const ArArgs a, float* mc,
+                                                                                     float* mc_sumsq) {
   __shared__ volatile int abort_sh;
   __shared__ float red[32];
   if (threadIdx.x == 0) abort_sh = 0;
@@ -194,7 +197,7 @@ __global__ void __launch_bounds__(512) nvls_allreduce_kernel(const ArArgs a, flo
 
 void nvls_allreduce(int64_t ptrs_dev, int64_t pads_dev, int64_t pad_words, int64_t mc_ptr, int64_t mc_sumsq,
                     int64_t lo, int64_t hi, int64_t rank, int64_t world, int64_t epoch, double scale,
-                    at::Tensor local_sumsq, int64_t ctas) {
+                    at::Tensor local_sumsq, int64_t ctas, int64_t epoch_base) {
   TORCH_CHECK(lo % 4 == 0, "nvls_allreduce: bucket start must be 16-byte aligned");
   TORCH_CHECK(2 * ctas * world <= pad_words, "nvls_allreduce: signal pad too small");
   const c10::cuda::CUDAGuard guard(local_sumsq.device());
@@ -206,10 +209,11 @@ void nvls_allreduce(int64_t ptrs_dev, int64_t pads_dev, int64_t pad_words, int64
   a.rank = (int)rank;
   a.world = (int)world;
   a.epoch = static_cast<uint32_t>(epoch);
+  a.epoch_base = reinterpret_cast<const uint32_t*>(epoch_base);
   a.scale = (float)scale;
   a.sumsq = local_sumsq.data_ptr<float>();
   a.status = status_ptr(local_sumsq.device().index());
-  nvls_allreduce_kernel<<<(int)ctas, 512, 0, at::cuda::getCurrentCUDAStream()>>>(
+  nvls_allreduce_kernel<<<(int)ctas, kCommThreads, 0, at::cuda::getCurrentCUDAStream()>>>(
       a, reinterpret_cast<float*>(mc_ptr), reinterpret_cast<float*>(mc_sumsq));
   PB_CUDA_CHECK(cudaGetLastError());
 }
@@ -217,7 +221,7 @@ void nvls_allreduce(int64_t ptrs_dev, int64_t pads_dev, int64_t pad_words, int64
 // ptrs_dev / pads_dev: device arrays of W uint64 addresses (from the symmetric-memory
 // rendezvous).  ``pad_words`` is the signal pad size in uint32 words.
 void fused_allreduce(int64_t ptrs_dev, int64_t pads_dev, int64_t pad_words, int64_t lo, int64_t hi, int64_t rank,
-                     int64_t world, int64_t epoch, double scale, at::Tensor sumsq, int64_t ctas) {
+                     int64_t world, int64_t epoch, double scale, at::Tensor sumsq, int64_t ctas, int64_t epoch_base) {
   TORCH_CHECK(sumsq.is_cuda() && sumsq.scalar_type() == at::kFloat);
   TORCH_CHECK(lo % 4 == 0, "fused_allreduce: bucket start must be 16-byte aligned");
   TORCH_CHECK(3 * ctas * world <= pad_words, "fused_allreduce: signal pad too small for ", ctas, " CTAs");
@@ -230,24 +234,37 @@ void fused_allreduce(int64_t ptrs_dev, int64_t pads_dev, int64_t pad_words, int6
   a.rank = (int)rank;
   a.world = (int)world;
   a.epoch = static_cast<uint32_t>(epoch);
+  a.epoch_base = reinterpret_cast<const uint32_t*>(epoch_base);
   a.scale = (float)scale;
   a.sumsq = sumsq.data_ptr<float>();
   a.status = status_ptr(sumsq.device().index());
   auto st = at::cuda::getCurrentCUDAStream();
   switch (world) {
-    case 2: fused_allreduce_kernel<2><<<(int)ctas, 512, 0, st>>>(a); break;
-    case 3: fused_allreduce_kernel<3><<<(int)ctas, 512, 0, st>>>(a); break;
-    case 4: fused_allreduce_kernel<4><<<(int)ctas, 512, 0, st>>>(a); break;
-    case 5: fused_allreduce_kernel<5><<<(int)ctas, 512, 0, st>>>(a); break;
-    case 6: fused_allreduce_kernel<6><<<(int)ctas, 512, 0, st>>>(a); break;
-    case 7: fused_allreduce_kernel<7><<<(int)ctas, 512, 0, st>>>(a); break;
-    case 8: fused_allreduce_kernel<8><<<(int)ctas, 512, 0, st>>>(a); break;
+    case 2: fused_allreduce_kernel<2><<<(int)ctas, kCommThreads, 0, st>>>(a); break;
+    case 3: fused_allreduce_kernel<3><<<(int)ctas, kCommThreads, 0, st>>>(a); break;
+    case 4: fused_allreduce_kernel<4><<<(int)ctas, kCommThreads, 0, st>>>(a); break;
+    case 5: fused_allreduce_kernel<5><<<(int)ctas, kCommThreads, 0, st>>>(a); break;
+    case 6: fused_allreduce_kernel<6><<<(int)ctas, kCommThreads, 0, st>>>(a); break;
+    case 7: fused_allreduce_kernel<7><<<(int)ctas, kCommThreads, 0, st>>>(a); break;
+    case 8: fused_allreduce_kernel<8><<<(int)ctas, kCommThreads, 0, st>>>(a); break;
     default: TORCH_CHECK(false, "fused_allreduce: world size 2..8 on one node");
   }
   PB_CUDA_CHECK(cudaGetLastError());
 }
 
+__global__ void epoch_bump_kernel(uint32_t* base, uint32_t inc) { *base += inc; }
+
+// Adds ``inc`` to the device epoch base (stream-ordered, capturable in a CUDA graph).
+void epoch_bump(at::Tensor base, int64_t inc) {
+  TORCH_CHECK(base.is_cuda() && base.scalar_type() == at::kInt && base.numel() >= 1, "epoch_bump: int32 CUDA tensor");
+  const c10::cuda::CUDAGuard guard(base.device());
+  epoch_bump_kernel<<<1, 1, 0, at::cuda::getCurrentCUDAStream()>>>(reinterpret_cast<uint32_t*>(base.data_ptr()),
+                                                                     static_cast<uint32_t>(inc));
+  PB_CUDA_CHECK(cudaGetLastError());
+}
+
 void comm_bindings(pybind11::module& m) {
+  m.def("epoch_bump", &epoch_bump);
   m.def("fused_allreduce", &fused_allreduce);
   m.def("nvls_allreduce", &nvls_allreduce);
 }

@@ -14,6 +14,9 @@ struct ArArgs {
   long lo, hi;
   int rank, world;
   uint32_t epoch;
+  // When set, the launch's epoch is epoch + *epoch_base: the base is bumped on the
+  // device once per training step, so a captured CUDA graph replays with fresh epochs.
+  const uint32_t* epoch_base;
   float scale;
   float* sumsq;
   int* status;
@@ -28,6 +31,10 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
   return v;
 }
 
+__device__ __forceinline__ uint32_t launch_epoch(const ArArgs& a) {
+  return a.epoch + (a.epoch_base != nullptr ? *a.epoch_base : 0u);
+}
+
 // Barrier ``k`` between CTA ``blockIdx.x`` of every rank.  Slot (k, b, p) of rank r's pad
 // holds the last epoch in which rank p reached barrier k with CTA b.
 __device__ __forceinline__ bool cta_barrier(const ArArgs& a, int k, volatile int* abort) {
@@ -38,11 +45,12 @@ __device__ __forceinline__ bool cta_barrier(const ArArgs& a, int k, volatile int
   if (threadIdx.x < W) {
     const int p = threadIdx.x;
     const long slot_mine = (static_cast<long>(k) * gridDim.x + b) * W + a.rank;
+    const uint32_t ep = launch_epoch(a);
     __threadfence_system();
-    st_release_sys(a.pads[p] + slot_mine, a.epoch);
+    st_release_sys(a.pads[p] + slot_mine, ep);
     const uint32_t* watch = a.pads[a.rank] + (static_cast<long>(k) * gridDim.x + b) * W + p;
     const uint64_t t0 = globaltimer();
-    while (static_cast<int>(ld_acquire_sys(watch) - a.epoch) < 0) {
+    while (static_cast<int>(ld_acquire_sys(watch) - ep) < 0) {
       if (*abort) {
         ok = false;
         break;
@@ -60,6 +68,13 @@ __device__ __forceinline__ bool cta_barrier(const ArArgs& a, int k, volatile int
 }
 
 constexpr int kMaxWorld = 8;
+
+// Collective kernels run beside the compute kernels of the backward pass.  Small CTAs
+// with a capped register budget (128 threads x <= 64 registers = 8 K registers) fit
+// next to a resident GEMM or attention CTA on the same SM, so communication never
+// evicts compute from an SM; bandwidth comes from many such CTAs.
+constexpr int kCommThreads = 128;
+constexpr int kCommMinBlocks = 8;
 
 // Sub-range of chunk ``c`` owned by this CTA (same split on every rank).
 __device__ __forceinline__ void sub_range(const ArArgs& a, long cs, long sub, int c, long& s0, long& s1) {

@@ -575,7 +575,12 @@ void ce_row_scale(at::Tensor targets, int64_t ignore_index, at::Tensor grad_out,
 __global__ void adamw_kernel(float* __restrict__ p, const float* __restrict__ g, float* __restrict__ m,
                              float* __restrict__ v, __nv_bfloat16* __restrict__ shadow, long n,
                              const float* __restrict__ norm, int* __restrict__ skipped, float lr, float b1, float b2,
-                             float eps, float wd, float bc1, float bc2, float max_norm) {
+                             float eps, float wd, float bc1, float bc2, float max_norm, const float* __restrict__ hp) {
+  if (hp != nullptr) {  // per-step values from device memory (CUDA-graph replay)
+    lr = hp[0];
+    bc1 = hp[1];
+    bc2 = hp[2];
+  }
   const float nv = *norm;
   const bool bad = !isfinite(nv);
   if (blockIdx.x == 0 && threadIdx.x == 0) *skipped = bad ? 1 : 0;
@@ -619,9 +624,11 @@ __global__ void adamw_kernel(float* __restrict__ p, const float* __restrict__ g,
   }
 }
 
+// ``hparams`` (optional, device fp32 [3]): lr, bc1, bc2 read by the kernel instead of
+// the host values, so a captured CUDA graph picks up each step's schedule.
 void adamw_step(at::Tensor p, at::Tensor g, at::Tensor m, at::Tensor v, at::Tensor shadow, at::Tensor norm,
                 at::Tensor skipped, double lr, double b1, double b2, double eps, double wd, double bc1, double bc2,
-                double max_norm, bool write_shadow) {
+                double max_norm, bool write_shadow, c10::optional<at::Tensor> hparams) {
   const c10::cuda::CUDAGuard guard(p.device());
   const long n = p.numel();
   TORCH_CHECK(reinterpret_cast<uintptr_t>(p.data_ptr()) % 16 == 0 && reinterpret_cast<uintptr_t>(g.data_ptr()) % 16 == 0);
@@ -629,7 +636,7 @@ void adamw_step(at::Tensor p, at::Tensor g, at::Tensor m, at::Tensor v, at::Tens
       p.data_ptr<float>(), g.data_ptr<float>(), m.data_ptr<float>(), v.data_ptr<float>(),
       write_shadow ? reinterpret_cast<__nv_bfloat16*>(shadow.data_ptr()) : nullptr, n, norm.data_ptr<float>(),
       skipped.data_ptr<int>(), (float)lr, (float)b1, (float)b2, (float)eps, (float)wd, (float)bc1, (float)bc2,
-      (float)max_norm);
+      (float)max_norm, hparams.has_value() ? hparams->data_ptr<float>() : nullptr);
   PB_CUDA_CHECK(cudaGetLastError());
 }
 

@@ -62,17 +62,18 @@ __device__ __forceinline__ float rs_chunk(float* const* ptrs, long c0, long c1, 
   const long sub = ((n + gridDim.x - 1) / gridDim.x + 3) / 4 * 4;
   const long s0 = min(c0 + static_cast<long>(blockIdx.x) * sub, c1);
   const long s1 = min(s0 + sub, c1);
+  constexpr int G = W <= 4 ? 2 : 1;  // G W <= 8 loads of 16 bytes in flight per thread
   float ss = 0.f;
   const long stride = static_cast<long>(blockDim.x) * 4;
-  for (long i = s0 + threadIdx.x * 4; i < s1; i += 2 * stride) {
-    float4 v[2][W];
+  for (long i = s0 + threadIdx.x * 4; i < s1; i += G * stride) {
+    float4 v[G][W];
 #pragma unroll
-    for (int u = 0; u < 2; ++u)
+    for (int u = 0; u < G; ++u)
 #pragma unroll
       for (int p = 0; p < W; ++p)
         if (i + u * stride < s1) v[u][p] = __ldcg(reinterpret_cast<const float4*>(ptrs[p] + i + u * stride));
 #pragma unroll
-    for (int u = 0; u < 2; ++u) {
+    for (int u = 0; u < G; ++u) {
       const long j = i + u * stride;
       if (j < s1) {
         float4 acc = v[u][0];
@@ -137,7 +138,8 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
 }
 
 template <int W>
-__global__ void __launch_bounds__(512) fsdp_reduce_scatter_kernel(const ArArgs a, float* out, const float* mc) {
+__global__ void __launch_bounds__(kCommThreads, kCommMinBlocks) fsdp_reduce_scatter_kernel(const ArArgs a, float* out,
+                                                                                          const float* mc) {
   __shared__ volatile int abort_sh;
   __shared__ float red[32];
   if (threadIdx.x == 0) abort_sh = 0;
@@ -211,11 +213,11 @@ __global__ void __launch_bounds__(512) fsdp_adamw_kernel(const FinalArgs f) {
       *f.norm_out = nv;
       *f.skipped = isfinite(nv) ? 0 : 1;
       __threadfence();
-      st_release_gpu(f.go, a.epoch);
+      st_release_gpu(f.go, launch_epoch(a));
     }
   }
   if (threadIdx.x == 0) {
-    go_ok = spin_until(f.go, a.epoch, a.status, 403) ? 1 : 0;
+    go_ok = spin_until(f.go, launch_epoch(a), a.status, 403) ? 1 : 0;
     norm_sh = *reinterpret_cast<volatile float*>(f.norm_out);
   }
   __syncthreads();
@@ -311,13 +313,13 @@ void fsdp_reduce_scatter(int64_t gptrs_dev, int64_t pads_dev, int64_t pad_words,
   const float* m = reinterpret_cast<const float*>(mc);
   auto st = at::cuda::getCurrentCUDAStream();
   switch (world) {
-    case 2: fsdp_reduce_scatter_kernel<2><<<(int)ctas, 512, 0, st>>>(a, o, m); break;
-    case 3: fsdp_reduce_scatter_kernel<3><<<(int)ctas, 512, 0, st>>>(a, o, m); break;
-    case 4: fsdp_reduce_scatter_kernel<4><<<(int)ctas, 512, 0, st>>>(a, o, m); break;
-    case 5: fsdp_reduce_scatter_kernel<5><<<(int)ctas, 512, 0, st>>>(a, o, m); break;
-    case 6: fsdp_reduce_scatter_kernel<6><<<(int)ctas, 512, 0, st>>>(a, o, m); break;
-    case 7: fsdp_reduce_scatter_kernel<7><<<(int)ctas, 512, 0, st>>>(a, o, m); break;
-    case 8: fsdp_reduce_scatter_kernel<8><<<(int)ctas, 512, 0, st>>>(a, o, m); break;
+    case 2: fsdp_reduce_scatter_kernel<2><<<(int)ctas, kCommThreads, 0, st>>>(a, o, m); break;
+    case 3: fsdp_reduce_scatter_kernel<3><<<(int)ctas, kCommThreads, 0, st>>>(a, o, m); break;
+    case 4: fsdp_reduce_scatter_kernel<4><<<(int)ctas, kCommThreads, 0, st>>>(a, o, m); break;
+    case 5: fsdp_reduce_scatter_kernel<5><<<(int)ctas, kCommThreads, 0, st>>>(a, o, m); break;
+    case 6: fsdp_reduce_scatter_kernel<6><<<(int)ctas, kCommThreads, 0, st>>>(a, o, m); break;
+    case 7: fsdp_reduce_scatter_kernel<7><<<(int)ctas, kCommThreads, 0, st>>>(a, o, m); break;
+    case 8: fsdp_reduce_scatter_kernel<8><<<(int)ctas, kCommThreads, 0, st>>>(a, o, m); break;
     default: TORCH_CHECK(false, "fsdp_reduce_scatter: world size 2..8 on one node");
   }
   PB_CUDA_CHECK(cudaGetLastError());

@@ -186,13 +186,16 @@ def _ensure_flat(model):
     return model.flat
 
 
-def fused_causal_lm_forward(model, input_ids, labels, position_ids, doc_start) -> CausalLMOutput:
+def fused_causal_lm_forward(model, input_ids, labels, position_ids, doc_start, attn_plan=None) -> CausalLMOutput:
     cfg = model.cfg
     flat = _ensure_flat(model)
     ids = input_ids.reshape(-1).contiguous()
     pos32 = position_ids.reshape(-1).to(torch.int32).contiguous()
-    doc_start = doc_start.reshape(-1).to(device=ids.device, dtype=torch.int32).contiguous()
-    plan = attention_plan(doc_start, cfg.n_heads, cfg.n_kv_heads)
+    if attn_plan is not None:
+        plan = attn_plan  # built on the host with the batch
+    else:
+        doc_start = doc_start.reshape(-1).to(device=ids.device, dtype=torch.int32).contiguous()
+        plan = attention_plan(doc_start, cfg.n_heads, cfg.n_kv_heads)
     sc = StepContext(model, flat, pos32, plan)
     m = model.model
     x = _Embed.apply(ids, m.embed_tokens.weight, sc)

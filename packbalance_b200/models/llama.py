@@ -185,7 +185,12 @@ class LlamaForCausalLM(nn.Module):
         doc_ids: torch.Tensor | None = None,
         block_mask=None,
         doc_start: torch.Tensor | None = None,
+        attn_plan: dict | None = None,
     ) -> CausalLMOutput:
+        """Reference signature plus ``doc_start`` (first token of each token's document)
+        and ``attn_plan`` (the attention work lists of
+        :func:`packbalance_b200.ops.attention.attention_plan_host`, already on the
+        device), both optional and used only by the native path."""
         if input_ids.dim() == 1:
             input_ids = input_ids.unsqueeze(0)
             labels = labels.unsqueeze(0) if labels is not None else None
@@ -198,11 +203,11 @@ class LlamaForCausalLM(nn.Module):
         if self.uses_native_path(input_ids):
             from packbalance_b200.models.fused import fused_causal_lm_forward
 
-            if doc_start is None:
+            if doc_start is None and attn_plan is None:
                 doc_start = (
                     block_mask if isinstance(block_mask, torch.Tensor) else doc_start_from_doc_ids(doc_ids)
                 )
-            return fused_causal_lm_forward(self, input_ids, labels, position_ids, doc_start)
+            return fused_causal_lm_forward(self, input_ids, labels, position_ids, doc_start, attn_plan)
         hidden = self.model(input_ids, position_ids, doc_ids, block_mask)
         if labels is None:
             return CausalLMOutput(logits=hidden @ self.lm_head_weight.t(), hidden_states=hidden)

@@ -9,14 +9,18 @@ Work items are (query tile of 128 tokens, head) for the forward and (key tile, k
 head) for the backward.  :func:`attention_plan` orders them by their number of
 key / query tiles, most expensive first, so the long documents that dominate the
 step start first and short ones fill the tail (the per-tile cost is the cost
-model's O(L^2) attention term at tile granularity).  The plan is built on the
-device with a few torch ops and no host synchronisation.
+model's O(L^2) attention term at tile granularity).  :func:`attention_plan_host`
+builds the plan with numpy next to the rest of the batch on the host (the trainer
+ships it with the step's inputs); :func:`attention_plan` builds the same plan on the
+device with a few torch ops and no host synchronisation, for batches that arrive
+without one.
 """
 
 from __future__ import annotations
 
 import math
 
+import numpy as np
 import torch
 
 from packbalance_b200.ops import _native
@@ -70,6 +74,43 @@ def attention_plan(doc_start: torch.Tensor, n_heads: int, n_kv_heads: int) -> di
 
 
 ALIGN = 8
+
+
+def _plan_np(ds: np.ndarray, n_heads: int) -> dict[str, np.ndarray]:
+    t = ds.shape[0]
+    n_tiles = -(-t // TILE)
+    tiles = np.arange(n_tiles, dtype=np.int64)
+    kv_lo = ds[tiles * TILE].astype(np.int64) // TILE
+    order = np.argsort(-(tiles - kv_lo + 1), kind="stable")
+    heads = np.arange(n_heads, dtype=np.int64)
+    fwd = np.stack([np.repeat(order, n_heads), np.tile(heads, n_tiles), np.repeat(kv_lo[order], n_heads)], axis=1)
+    last = np.ones(t, dtype=bool)
+    last[:-1] = ds[1:] != ds[:-1]
+    marks = np.where(last, np.arange(t), t)
+    de = np.minimum.accumulate(marks[::-1])[::-1]
+    q_hi = de[np.minimum(tiles * TILE + TILE - 1, t - 1)] // TILE
+    korder = np.argsort(-(q_hi - tiles + 1), kind="stable")
+    bwd = np.stack([np.repeat(korder, n_heads), np.tile(heads, n_tiles), np.repeat(q_hi[korder], n_heads)], axis=1)
+    return {"fwd": fwd.astype(np.int32), "bwd": bwd.astype(np.int32), "doc_start": ds.astype(np.int32),
+            "doc_end": de.astype(np.int32)}
+
+
+def attention_plan_host(doc_start, n_heads: int) -> dict:
+    """:func:`attention_plan` on the host (numpy; CPU tensors out), including the
+    ALIGN-padded variant when the token count is not a multiple of ALIGN."""
+    ds = np.asarray(doc_start.cpu() if isinstance(doc_start, torch.Tensor) else doc_start).astype(np.int64).reshape(-1)
+    plan: dict = {k: torch.from_numpy(v) for k, v in _plan_np(ds, n_heads).items()}
+    t = ds.shape[0]
+    tp = -(-t // ALIGN) * ALIGN
+    if tp != t:
+        padded = np.concatenate([ds, np.arange(t, tp, dtype=np.int64)])
+        plan["padded"] = {k: torch.from_numpy(v) for k, v in _plan_np(padded, n_heads).items()}
+    return plan
+
+
+def plan_to_device(plan: dict, device: torch.device) -> dict:
+    return {k: (plan_to_device(v, device) if isinstance(v, dict) else v.to(device, non_blocking=True))
+            for k, v in plan.items()}
 
 
 def _padded(plan: dict, n_heads: int, n_kv_heads: int, t: int) -> dict:

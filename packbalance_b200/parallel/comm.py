@@ -29,7 +29,8 @@ class FusedAllReduce:
     """``mode``: "nvls" (multimem through the NVSwitch; default when the multicast
     object is available), "p2p" (two-shot over peer loads) or "auto"."""
 
-    CTAS = 64
+    CTAS = 148  # small CTAs (csrc/comm_common.cuh: 128 threads), about one per SM
+    SYNC_WORDS = 16384
 
     def __init__(self, grad: torch.Tensor, group: dist.ProcessGroup | None = None, flat=None, mode: str | None = None) -> None:
         import os
@@ -45,6 +46,11 @@ class FusedAllReduce:
         full.zero_()
         self.handle = symm_mem.rendezvous(full, self.group)
         self.full = full
+        # per-CTA barrier slots: a symmetric buffer of our own (the default signal pad
+        # is too small for one CTA per SM at W = 8)
+        self.sync = symm_mem.empty(self.SYNC_WORDS, dtype=torch.int32, device=grad.device)
+        self.sync.zero_()
+        self.h_sync = symm_mem.rendezvous(self.sync, self.group)
         buf = full[:n]
         buf.copy_(grad)
         self.buf = buf
@@ -52,11 +58,14 @@ class FusedAllReduce:
         self.world = self.handle.world_size
         if not 2 <= self.world <= 8:
             raise RuntimeError("fused all-reduce covers 2..8 ranks of one node")
-        self.pad_words = self.handle.signal_pad_size // 4
+        self.pad_words = self.SYNC_WORDS
         self.ctas = min(self.CTAS, self.pad_words // (3 * self.world))
         if self.ctas < 1:
             raise RuntimeError("signal pad too small for the fused all-reduce")
-        self.epoch = 0
+        # Barrier epochs: a device base bumped by EPOCH_STRIDE at every step start plus the
+        # launch's index within the step, so a captured graph replays with fresh epochs.
+        self.epoch_base = torch.zeros(1, dtype=torch.int32, device=grad.device)
+        self._k = 0
         mode = mode or os.environ.get("PB_ALLREDUCE", "auto")
         if int(getattr(self.handle, "offset", 0)) != 0:
             raise RuntimeError("symmetric buffer must start at its allocation base")
@@ -70,23 +79,31 @@ class FusedAllReduce:
             flat.rebind_grad(buf)
         _native.module().fused_allreduce  # fail loudly if the extension lacks the kernel
 
+    EPOCH_STRIDE = 64  # launches per step, at most
+
     def start_step(self) -> None:
+        """Stream-ordered start of a step's reductions (zero the norm, new epoch base)."""
         self.sumsq.zero_()
+        _native.module().epoch_bump(self.epoch_base, self.EPOCH_STRIDE)
+        self._k = 0
 
     def all_reduce_mean(self, lo: int, hi: int) -> torch.Tensor:
         """Average elements [lo, hi) of the gradient over all ranks (current stream)."""
-        self.epoch += 1
+        self._k += 1
+        if self._k >= self.EPOCH_STRIDE:
+            raise RuntimeError("more all-reduce launches in one step than the epoch stride allows")
         C = _native.module()
+        base = self.epoch_base.data_ptr()
         if self.mode == "nvls":
             n = self.buf.numel()
             C.nvls_allreduce(
-                self.handle.buffer_ptrs_dev, self.handle.signal_pad_ptrs_dev, self.pad_words, self.mc,
-                self.mc + 4 * n, lo, hi, self.rank, self.world, self.epoch, 1.0 / self.world, self.sumsq, self.ctas,
+                self.handle.buffer_ptrs_dev, self.h_sync.buffer_ptrs_dev, self.pad_words, self.mc,
+                self.mc + 4 * n, lo, hi, self.rank, self.world, self._k, 1.0 / self.world, self.sumsq, self.ctas, base,
             )
         else:
             C.fused_allreduce(
-                self.handle.buffer_ptrs_dev, self.handle.signal_pad_ptrs_dev, self.pad_words, lo, hi, self.rank,
-                self.world, self.epoch, 1.0 / self.world, self.sumsq, self.ctas,
+                self.handle.buffer_ptrs_dev, self.h_sync.buffer_ptrs_dev, self.pad_words, lo, hi, self.rank,
+                self.world, self._k, 1.0 / self.world, self.sumsq, self.ctas, base,
             )
         return self.sumsq
 
@@ -95,3 +112,4 @@ class FusedAllReduce:
 
     def close(self) -> None:
         self.handle = None
+        self.h_sync = None

@@ -45,9 +45,11 @@ class FlatAdamW(torch.optim.Optimizer):
         self._bind_state()
 
     def _bind_state(self) -> None:
+        # one shared CPU scalar for every parameter's "step" entry, updated in place
+        self._step_t = torch.tensor(float(self.step_count))
         for s in self.flat.slots:
             self.state[s.param] = {
-                "step": torch.tensor(float(self.step_count)),
+                "step": self._step_t,
                 "exp_avg": self.exp_avg[s.offset : s.offset + s.numel].view(s.shape),
                 "exp_avg_sq": self.exp_avg_sq[s.offset : s.offset + s.numel].view(s.shape),
             }
@@ -74,9 +76,12 @@ class FlatAdamW(torch.optim.Optimizer):
         self._bind_state()
 
     @torch.no_grad()
-    def step(self, closure=None, grad_norm: torch.Tensor | None = None, max_norm: float = 0.0):
+    def step(self, closure=None, grad_norm: torch.Tensor | None = None, max_norm: float = 0.0,
+             hparams: torch.Tensor | None = None):
         """One update.  ``grad_norm`` (device scalar) enables clipping to ``max_norm``
-        and the non-finite skip; without it gradients are used as they are."""
+        and the non-finite skip; without it gradients are used as they are.  ``hparams``
+        (CUDA, fp32 [3]): lr and the two bias corrections read on the device, for
+        captured CUDA graphs (the caller keeps them current)."""
         loss = closure() if closure is not None else None
         group = self.param_groups[0]
         lr, (b1, b2), eps, wd = group["lr"], group["betas"], group["eps"], group["weight_decay"]
@@ -95,7 +100,7 @@ class FlatAdamW(torch.optim.Optimizer):
                 norm, self.last_skipped,
                 float(lr), float(b1), float(b2), float(eps), float(wd),
                 float(bc1), float(bc2), float(max_norm if grad_norm is not None else 0.0),
-                flat.shadow is not None,
+                flat.shadow is not None, hparams,
             )
             flat.mark_shadow_fresh()
         else:
@@ -115,9 +120,37 @@ class FlatAdamW(torch.optim.Optimizer):
             self.exp_avg_sq.mul_(b2).addcmul_(g, g, value=1.0 - b2)
             denom = (self.exp_avg_sq.sqrt() / math.sqrt(bc2)).add_(eps)
             flat.data.addcdiv_(self.exp_avg, denom, value=-lr / bc1)
-        for s in flat.slots:
-            self.state[s.param]["step"] = torch.tensor(float(self.step_count))
+        self._step_t.fill_(float(self.step_count))
         return loss
+
+
+    # ---- CUDA-graph support --------------------------------------------------------
+    def launch(self, grad_norm: torch.Tensor, max_norm: float, hparams: torch.Tensor) -> None:
+        """The update kernel alone, with lr and bias corrections read from ``hparams`` on
+        the device (captured into a CUDA graph); the host-side step count is advanced
+        by the caller (see :meth:`sync_step_state`)."""
+        from packbalance_b200.ops import _native
+
+        group = self.param_groups[0]
+        flat = self.flat
+        b1, b2 = group["betas"]
+        _native.module().adamw_step(
+            flat.data, flat.grad, self.exp_avg, self.exp_avg_sq,
+            flat.shadow if flat.shadow is not None else flat.data, grad_norm, self.last_skipped,
+            0.0, float(b1), float(b2), float(group["eps"]), float(group["weight_decay"]), 1.0, 1.0,
+            float(max_norm), flat.shadow is not None, hparams,
+        )
+        flat.mark_shadow_fresh()
+
+    def sync_step_state(self) -> None:
+        """Refresh the per-parameter ``step`` entries after a replayed update."""
+        self._step_t.fill_(float(self.step_count))
+
+    def state_dict(self) -> dict[str, Any]:
+        sd = super().state_dict()
+        for st in sd["state"].values():  # independent step tensors, as torch.optim.AdamW has
+            st["step"] = st["step"].clone()
+        return sd
 
 
 def global_grad_norm(flat: FlatParameters) -> torch.Tensor:

@@ -88,7 +88,7 @@ def _units_of(model) -> tuple[list[Slot], list[Unit]]:
 class ShardedParameters(GradWindow):
     """Sharded parameter/gradient/optimizer-state buffers of one model (CUDA, W >= 2)."""
 
-    def __init__(self, model, group: dist.ProcessGroup | None = None, rs_ctas: int = 64) -> None:
+    def __init__(self, model, group: dist.ProcessGroup | None = None, rs_ctas: int = 148) -> None:
         import torch.distributed._symmetric_memory as symm_mem
 
         self.group = group if group is not None else dist.group.WORLD
@@ -365,7 +365,7 @@ class ShardedParameters(GradWindow):
             self._epoch += 1
             C.fused_allreduce(
                 int(self.h_grad.buffer_ptrs_dev), int(self.h_sync.buffer_ptrs_dev), SYNC_WORDS, 0, self.rep_n,
-                self.rank, self.world, self._epoch, 1.0 / self.world, self.rep_sumsq, min(8, self.rs_ctas),
+                self.rank, self.world, self._epoch, 1.0 / self.world, self.rep_sumsq, min(16, self.rs_ctas), 0,
             )
             self._epoch += 1
             self._arrive_total += self.final_ctas

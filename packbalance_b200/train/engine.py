@@ -13,12 +13,20 @@ scalars (no host synchronisation):
    averages them bucket by bucket as layers finish;
 4. global gradient norm, clipping and AdamW run as device kernels; a non-finite
    norm skips the update.
+
+On the native CUDA path without sharding, the whole step (forward, backward, the
+gradient all-reduce launches on their side stream, norm and AdamW) is captured once
+in a CUDA graph per input signature and replayed: the step's inputs are copied into
+the graph's static buffers, and the per-step scalars (loss scale, learning rate, bias
+corrections) live in device memory, so one launch replaces several hundred and the
+host no longer paces the GPU.
 """
 
 from __future__ import annotations
 
 import contextlib
 import math
+import os
 from typing import Any
 
 import torch
@@ -28,6 +36,7 @@ from torch.profiler import record_function
 from packbalance_b200.config import PackBalanceConfig
 from packbalance_b200.data.dataset import concat_packs
 from packbalance_b200.models.llama import LlamaForCausalLM
+from packbalance_b200.ops.attention import attention_plan_host, plan_to_device
 from packbalance_b200.parallel.distributed import DataParallel
 from packbalance_b200.parallel.flat import FlatParameters
 from packbalance_b200.parallel.optim import FlatAdamW, global_grad_norm
@@ -49,8 +58,69 @@ def make_lr_lambda(cfg: PackBalanceConfig):
     return lr_lambda
 
 
+def _signature(batch: dict[str, Any]) -> tuple:
+    sig = []
+    for k in sorted(batch):
+        v = batch[k]
+        if isinstance(v, torch.Tensor):
+            sig.append((k, tuple(v.shape), v.dtype))
+        elif isinstance(v, dict):
+            sig.append((k, _signature(v)))
+    return tuple(sig)
+
+
+def _copy_into(dst: dict[str, Any], src: dict[str, Any]) -> None:
+    for k, v in dst.items():
+        if isinstance(v, torch.Tensor):
+            v.copy_(src[k], non_blocking=True)
+        elif isinstance(v, dict):
+            _copy_into(v, src[k])
+
+
+def _clone_tensors(batch: dict[str, Any]) -> dict[str, Any]:
+    out: dict[str, Any] = {}
+    for k, v in batch.items():
+        if isinstance(v, torch.Tensor):
+            out[k] = v.clone()
+        elif isinstance(v, dict):
+            out[k] = _clone_tensors(v)
+    return out
+
+
+class _GraphedStep:
+    """One captured native step with static input buffers (see the module docstring)."""
+
+    def __init__(self, engine: "TrainEngine", batch: dict[str, Any]) -> None:
+        dev = engine.device
+        self.static = _clone_tensors(batch)
+        self.loss_scale = torch.ones((), device=dev, dtype=torch.float32)
+        self.hp = torch.zeros(3, device=dev, dtype=torch.float32)  # lr, bias corrections 1 and 2
+        self.hp_host = torch.zeros(3, dtype=torch.float32).pin_memory()
+        engine.flat.refresh_shadow()
+        torch.cuda.synchronize(dev)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            self.out = engine._native_body([self.static], self.loss_scale, self.hp)
+
+    def run(self, batch: dict[str, Any], loss_scale: float, hp: tuple[float, float, float]) -> dict[str, torch.Tensor]:
+        _copy_into(self.static, batch)
+        self.loss_scale.fill_(loss_scale)
+        self.hp_host[0], self.hp_host[1], self.hp_host[2] = hp
+        self.hp.copy_(self.hp_host, non_blocking=True)
+        self.graph.replay()
+        return {k: v.clone() for k, v in self.out.items()}
+
+
 def to_device_batch(batch: dict[str, Any], device: torch.device) -> dict[str, Any]:
-    return {k: (v.to(device, non_blocking=True) if isinstance(v, torch.Tensor) else v) for k, v in batch.items()}
+    out: dict[str, Any] = {}
+    for k, v in batch.items():
+        if isinstance(v, torch.Tensor):
+            out[k] = v.to(device, non_blocking=True)
+        elif k == "attn_plan" and isinstance(v, dict):
+            out[k] = plan_to_device(v, device)
+        else:
+            out[k] = v
+    return out
 
 
 class TrainEngine:
@@ -118,6 +188,13 @@ class TrainEngine:
             )
         self.scheduler = self.make_scheduler(start_step)
         self.native = self.model.uses_native_path(torch.empty(0, device=device))
+        self._graphs: dict[tuple, _GraphedStep] = {}
+        self._eager_seen: dict[tuple, int] = {}
+        env = os.environ.get("PB_CUDA_GRAPHS")
+        self.use_graphs = (
+            cfg.train.cuda_graphs and (env != "0") and self.native and self.sharded is None and not self.fsdp
+            and device.type == "cuda" and (self.world == 1 or (self.dp is not None and self.dp.fused is not None))
+        )
         amp = get_autocast_dtype(cfg.train.dtype) if device.type == "cuda" and not self.native else None
         self.autocast = (lambda: torch.autocast("cuda", dtype=amp)) if amp is not None else contextlib.nullcontext
 
@@ -131,6 +208,16 @@ class TrainEngine:
             g.setdefault("initial_lr", self.cfg.train.lr)
         self.scheduler = self.make_scheduler(start_step)
 
+    def prepare_batch(self, batch: dict[str, Any]) -> dict[str, Any]:
+        """Host-side preprocessing of a (concatenated) batch: on the native path, the
+        attention work lists are built on the host from ``doc_start`` and travel with
+        the batch's host->device copy."""
+        if self.native and "attn_plan" not in batch and isinstance(batch.get("doc_start"), torch.Tensor) \
+                and not batch["doc_start"].is_cuda:
+            batch = dict(batch)
+            batch["attn_plan"] = attention_plan_host(batch["doc_start"], self.cfg.model.n_heads)
+        return batch
+
     def _forward_backward(self, batch: dict[str, Any], loss_scale: float) -> torch.Tensor:
         with record_function("packbalance/forward"), self.autocast():
             out = self.model(
@@ -139,6 +226,7 @@ class TrainEngine:
                 position_ids=batch["position_ids"].unsqueeze(0),
                 doc_ids=batch["doc_ids"].unsqueeze(0),
                 doc_start=batch.get("doc_start"),
+                attn_plan=batch.get("attn_plan"),
             )
         loss = out.loss
         with record_function("packbalance/backward"):
@@ -154,17 +242,45 @@ class TrainEngine:
             return self._sharded_step(packs, loss_scale)
         if self.fsdp:
             return self._fsdp_step(packs, loss_scale)
+        groups = [concat_packs(packs)] if self.cfg.train.fuse_microbatches else packs
+        if self.use_graphs and len(groups) == 1:
+            batch = self.prepare_batch(groups[0])
+            sig = _signature(batch)
+            g = self._graphs.get(sig)
+            if g is None and self._eager_seen.get(sig, 0) >= 2:
+                # warmed up (allocator pools, kernel attributes, lazy buffers): capture
+                g = self._graphs[sig] = _GraphedStep(self, to_device_batch(batch, self.device))
+            if g is not None:
+                opt = self.optimizer
+                grp = opt.param_groups[0]
+                b1, b2 = grp["betas"]
+                opt.step_count += 1
+                t = opt.step_count
+                out = g.run(batch, loss_scale, (float(grp["lr"]), 1.0 - b1**t, 1.0 - b2**t))
+                opt.sync_step_state()
+                self.scheduler.step()
+                return out
+            self._eager_seen[sig] = self._eager_seen.get(sig, 0) + 1
+            groups = [batch]
+        out = self._native_body([to_device_batch(self.prepare_batch(b), self.device) for b in groups], loss_scale)
+        self.scheduler.step()
+        return out
+
+    def _native_body(self, batches: list[dict[str, Any]], loss_scale, hparams: torch.Tensor | None = None
+                     ) -> dict[str, torch.Tensor]:
+        """Forward + backward of this rank's batches (device), gradient averaging, norm,
+        clipping and AdamW.  ``loss_scale`` and ``hparams`` may be device tensors (graph
+        capture); with ``hparams`` the optimizer's host-side step count is left alone."""
         if self.native:
             self.flat.begin_window()
         else:
             self.flat.zero_grad()
         self.dp.start_step()
-        groups = [concat_packs(packs)] if self.cfg.train.fuse_microbatches else packs
         local = torch.zeros((), device=self.device, dtype=torch.float32)
-        for i, batch in enumerate(groups):
+        for i, batch in enumerate(batches):
             # gradients are final only in the last microbatch's backward pass
-            self.dp.hold = i < len(groups) - 1
-            local += self._forward_backward(to_device_batch(batch, self.device), loss_scale)
+            self.dp.hold = i < len(batches) - 1
+            local += self._forward_backward(batch, loss_scale)
         self.dp.hold = False
         if self.native:
             self.flat.finish_window()
@@ -173,8 +289,10 @@ class TrainEngine:
             if not self.native:
                 self.flat.ready_all()
             norm = sq.sqrt() if sq is not None else global_grad_norm(self.flat)
-            self.optimizer.step(grad_norm=norm, max_norm=self.cfg.train.grad_clip)
-            self.scheduler.step()
+            if hparams is None:
+                self.optimizer.step(grad_norm=norm, max_norm=self.cfg.train.grad_clip)
+            else:
+                self.optimizer.launch(norm, self.cfg.train.grad_clip, hparams)
         return {"loss_sum": local, "grad_norm": norm}
 
     def _sharded_step(self, packs: list[dict[str, Any]], loss_scale: float) -> dict[str, torch.Tensor]:
@@ -186,7 +304,7 @@ class TrainEngine:
         for i, batch in enumerate(groups):
             # earlier microbatches only accumulate: no unit is final before the last one
             sp.hold_ready = i < len(groups) - 1
-            local += self._forward_backward(to_device_batch(batch, self.device), loss_scale)
+            local += self._forward_backward(to_device_batch(self.prepare_batch(batch), self.device), loss_scale)
         sp.hold_ready = False
         with record_function("packbalance/optimizer"):
             self.optimizer.step(max_norm=self.cfg.train.grad_clip)

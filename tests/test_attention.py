@@ -79,3 +79,28 @@ def test_generate_shape(model_cfg: ModelConfig, backend: str) -> None:
     model = LlamaForCausalLM(replace(model_cfg, attention_backend=backend))
     out = model.generate(torch.randint(0, model_cfg.vocab_size, (1, 4)), max_new_tokens=4, temperature=0.0)
     assert out.shape == (1, 8)
+
+
+def test_host_plan_matches_device_plan() -> None:
+    """The numpy plan the trainer builds with the batch equals the torch plan."""
+    import numpy as np
+
+    from packbalance_b200.ops.attention import attention_plan, attention_plan_host
+
+    rng = np.random.default_rng(3)
+    for t in (1000, 1024, 4099):
+        lens, tot = [], 0
+        while tot < t:
+            n = int(min(rng.integers(1, 700), t - tot))
+            lens.append(n)
+            tot += n
+        ds = np.concatenate([np.full(n, s) for n, s in zip(lens, np.cumsum([0] + lens[:-1]))]).astype(np.int32)
+        dev = attention_plan(torch.from_numpy(ds), 6, 2)
+        host = attention_plan_host(ds, 6)
+        for k in ("fwd", "bwd", "doc_start", "doc_end"):
+            assert torch.equal(dev[k], host[k]), (t, k)
+        if t % 8:
+            padded = np.concatenate([ds, np.arange(t, -(-t // 8) * 8)]).astype(np.int32)
+            devp = attention_plan(torch.from_numpy(padded), 6, 2)
+            for k in ("fwd", "bwd", "doc_start", "doc_end"):
+                assert torch.equal(devp[k], host["padded"][k]), (t, k)

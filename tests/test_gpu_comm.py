@@ -90,7 +90,7 @@ def test_barrier_timeout_reports_status():
     pad_ptrs = torch.tensor([pads[0].data_ptr(), pads[1].data_ptr()], device=dev, dtype=torch.int64)
     sumsq = torch.zeros((), device=dev)
     C.status_read(dev.index or 0, True)
-    C.fused_allreduce(ptrs.data_ptr(), pad_ptrs.data_ptr(), pads.shape[1], 0, 1024, 0, 2, 1, 0.5, sumsq, 4)
+    C.fused_allreduce(ptrs.data_ptr(), pad_ptrs.data_ptr(), pads.shape[1], 0, 1024, 0, 2, 1, 0.5, sumsq, 4, 0)
     torch.cuda.synchronize()
     code = C.status_read(dev.index or 0, True)
     assert code == 401 + 1000 * 1, code

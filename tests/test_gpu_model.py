@@ -81,3 +81,46 @@ def test_engine_steps_reduce_loss():
         losses.append(float(out["loss_sum"]) / (2 * toks))
     _native.check_status()
     assert losses[-1] < losses[0] * 0.8, losses
+
+
+def test_cuda_graph_step_matches_eager_step():
+    """The captured-and-replayed training step gives the eager step's losses, norms and
+    weights (graphs are captured on the third step of an input signature)."""
+    from packbalance_b200.data.dataset import doc_starts_from_ids
+    from packbalance_b200.train.engine import TrainEngine
+
+    cfg = _cfg()
+    g = torch.Generator().manual_seed(5)
+    batches = []
+    for s in range(6):
+        lengths, tot = [], 0
+        while tot < 1024:
+            n = min(int(torch.randint(20, 400, (1,), generator=g)), 1024 - tot)
+            lengths.append(n)
+            tot += n
+        ids, labels, pos, doc = _batch(1024, cfg.vocab_size, lengths, device="cpu")
+        batches.append({"input_ids": ids, "labels": labels, "position_ids": pos, "doc_ids": doc,
+                        "doc_start": torch.from_numpy(doc_starts_from_ids(doc.numpy()))})
+    engines = []
+    for graphs in (False, True):
+        torch.manual_seed(0)
+        tc = TrainConfig(lr=1e-3, warmup_steps=2, max_steps=20, grad_clip=1.0, cuda_graphs=graphs)
+        engines.append(TrainEngine(PackBalanceConfig(model=cfg, train=tc), torch.device("cuda")))
+    assert engines[1].use_graphs and not engines[0].use_graphs
+    e0, e1 = engines
+    for b in batches:
+        # same starting state each step, so gradient noise from fp32 atomics is not
+        # amplified by Adam over several steps
+        for dst, src in ((e1.flat.data, e0.flat.data), (e1.flat.shadow, e0.flat.shadow),
+                         (e1.optimizer.exp_avg, e0.optimizer.exp_avg), (e1.optimizer.exp_avg_sq, e0.optimizer.exp_avg_sq)):
+            dst.copy_(src)
+        e1.flat.mark_shadow_fresh()
+        before = e0.flat.data.clone()
+        outs = [e.step([b], 900) for e in engines]
+        torch.testing.assert_close(outs[1]["loss_sum"], outs[0]["loss_sum"], rtol=1e-5, atol=1e-4)
+        torch.testing.assert_close(outs[1]["grad_norm"], outs[0]["grad_norm"], rtol=1e-4, atol=1e-5)
+        upd = (e0.flat.data - before).norm()
+        err = (e1.flat.data - e0.flat.data).norm()
+        assert err < 0.02 * upd, (float(err), float(upd))
+    assert len(e1._graphs) == 1
+    _native.check_status()
