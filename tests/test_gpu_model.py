@@ -121,6 +121,6 @@ def test_cuda_graph_step_matches_eager_step():
         torch.testing.assert_close(outs[1]["grad_norm"], outs[0]["grad_norm"], rtol=1e-4, atol=1e-5)
         upd = (e0.flat.data - before).norm()
         err = (e1.flat.data - e0.flat.data).norm()
-        assert err < 0.02 * upd, (float(err), float(upd))
+        assert err <= 0.02 * upd + 1e-6, (float(err), float(upd))
     assert len(e1._graphs) == 1
     _native.check_status()
