@@ -99,54 +99,86 @@ def gather(values: list[float], dev) -> list[list[float]]:
 
 
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled every 200 ms during the timed region."""
+    """SM clocks and clock-event (throttle) reasons of the job's GPUs, polled every 10 ms
+    through NVML in a background thread during the timed region (read-only queries).
+    Falls back to ``nvidia-smi -lms 50`` when NVML is unavailable."""
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = (("hw_slowdown", "nvmlClocksEventReasonHwSlowdown"),
+               ("hw_thermal_slowdown", "nvmlClocksEventReasonHwThermalSlowdown"),
+               ("sw_thermal_slowdown", "nvmlClocksEventReasonSwThermalSlowdown"),
+               ("sw_power_cap", "nvmlClocksEventReasonSwPowerCap"))
 
-    def __init__(self, enabled: bool) -> None:
+    def __init__(self, enabled: bool, gpus: list[int] | None = None) -> None:
+        import threading
+
+        self.samples: list[tuple[int, float, float, set]] = []
         self.proc = None
-        if enabled:
+        self.thread = None
+        self.stop_flag = threading.Event()
+        if not enabled:
+            return
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            handles = [(i, pynvml.nvmlDeviceGetHandleByIndex(i)) for i in (gpus or [0])]
+            masks = [(name, getattr(pynvml, attr)) for name, attr in self.REASONS]
+
+            def poll() -> None:
+                while not self.stop_flag.is_set():
+                    for i, h in handles:
+                        try:
+                            sm = pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM)
+                            mx = pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM)
+                            r = pynvml.nvmlDeviceGetCurrentClocksEventReasons(h)
+                        except pynvml.NVMLError:
+                            continue
+                        self.samples.append((i, float(sm), float(mx), {n for n, m in masks if r & m}))
+                    self.stop_flag.wait(0.01)
+
+            self.thread = threading.Thread(target=poll, daemon=True)
+            self.thread.start()
+        except Exception:  # no NVML: nvidia-smi
+            fields = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+                      "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+                      "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
             try:
                 self.proc = subprocess.Popen(
-                    ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200"],
+                    ["nvidia-smi", f"--query-gpu={fields}", "--format=csv,noheader,nounits", "-lms", "50"],
                     stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True,
                 )
             except (OSError, ValueError):
                 self.proc = None
 
     def stop(self, gpus: list[int]) -> dict:
-        if self.proc is None:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
-        self.proc.terminate()
-        try:
-            out, _ = self.proc.communicate(timeout=10)
-        except subprocess.TimeoutExpired:
-            self.proc.kill()
-            out, _ = self.proc.communicate()
-        sm, mx, reasons = [], [], set()
-        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
-        for row in csv.reader(io.StringIO(out)):
+        if self.thread is not None:
+            self.stop_flag.set()
+            self.thread.join(timeout=5)
+        elif self.proc is not None:
+            self.proc.terminate()
             try:
-                idx = int(row[0])
-            except (ValueError, IndexError):
-                continue
-            if idx not in gpus:
-                continue
-            try:
-                sm.append(float(row[1]))
-                mx.append(float(row[2]))
-            except ValueError:
-                continue
-            for name, val in zip(names, row[5:9]):
-                if val.strip().lower() == "active":
-                    reasons.add(name)
+                out, _ = self.proc.communicate(timeout=10)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            for row in csv.reader(io.StringIO(out)):
+                try:
+                    idx, sm, mx = int(row[0]), float(row[1]), float(row[2])
+                except (ValueError, IndexError):
+                    continue
+                names = {n for (n, _), v in zip(self.REASONS, row[5:9]) if v.strip().lower() == "active"}
+                self.samples.append((idx, sm, mx, names))
+        else:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+        rows = [r for r in self.samples if r[0] in gpus]
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+        reasons = set().union(*(r[3] for r in rows))
         return {
-            "sm_mhz": float(np.median(sm)) if sm else None,
-            "sm_max_mhz": max(mx) if mx else None,
+            "sm_mhz": float(np.median([r[1] for r in rows])),
+            "sm_max_mhz": max(r[2] for r in rows),
             "reasons": sorted(reasons),
-            "samples": len(sm),
+            "samples": len(rows),
         }
 
 
@@ -263,7 +295,7 @@ def run_ours(args, rank, world, dev) -> None:
     torch.cuda.synchronize()
     _native.check_status(dev)
 
-    sampler = ClockSampler(rank == 0)
+    sampler = ClockSampler(rank == 0, clocks_gpus(world))
     timed = list(range(args.warmup, total))
     ms = time_steps(lambda i: engine.step([dev_batches[timed[i]]], plans[timed[i]].step_tokens), args.steps, dev)
     clocks = sampler.stop(clocks_gpus(world))
@@ -416,7 +448,7 @@ def run_reference(args, rank, world, dev) -> None:
     for i in range(args.warmup):
         ref_step(dev_batches[i], plans[i].step_tokens, False)
     torch.cuda.synchronize()
-    sampler = ClockSampler(rank == 0)
+    sampler = ClockSampler(rank == 0, clocks_gpus(world))
     ms = time_steps(lambda i: ref_step(dev_batches[args.warmup + i], plans[args.warmup + i].step_tokens, False),
                     args.steps, dev)
     clocks = sampler.stop(clocks_gpus(world))
