@@ -772,11 +772,20 @@ __global__ void attn_delta_kernel(const __nv_bfloat16* __restrict__ o, const __n
   const int t = static_cast<int>(idx / H), h = static_cast<int>(idx % H);
   const uint4* a = reinterpret_cast<const uint4*>(o + static_cast<long>(t) * H * D + h * D);
   const uint4* b = reinterpret_cast<const uint4*>(dout + static_cast<long>(t) * H * D + h * D);
+  // all loads of the row (D <= 128: at most 16 + 16 of 16 bytes) before any use
+  uint4 x[16], y[16];
+#pragma unroll
+  for (int i = 0; i < 16; ++i)
+    if (i < D / 8) {
+      x[i] = a[i];
+      y[i] = b[i];
+    }
   float s = 0.f;
-  for (int i = 0; i < D / 8; ++i) {
-    const uint4 x = a[i], y = b[i];
-    const uint32_t* xp = &x.x;
-    const uint32_t* yp = &y.x;
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    if (i >= D / 8) break;
+    const uint32_t* xp = &x[i].x;
+    const uint32_t* yp = &y[i].x;
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
       const float2 fx = unpack_bf16x2(xp[k]), fy = unpack_bf16x2(yp[k]);

@@ -548,7 +548,7 @@ void ce_finalize(at::Tensor pmax, at::Tensor psum, at::Tensor tlogit, at::Tensor
   const c10::cuda::CUDAGuard guard(pmax.device());
   const int ntiles = pmax.size(0), rows = pmax.size(1);
   if (rows == 0) return;
-  ce_finalize_kernel<<<(rows + 255) / 256, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+  ce_finalize_kernel<<<ce_finalize_blocks(rows), kCeRows * kCeGroups, 0, at::cuda::getCurrentCUDAStream()>>>(
       pmax.data_ptr<float>(), psum.data_ptr<float>(), ntiles, rows, tlogit.data_ptr<float>(),
       targets.data_ptr<int64_t>(), ignore_index, (float)z, lse.data_ptr<float>(), loss.data_ptr<float>());
   PB_CUDA_CHECK(cudaGetLastError());

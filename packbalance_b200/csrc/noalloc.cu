@@ -198,7 +198,7 @@ extern "C" int pb_lmhead_ce_forward_noalloc(const void* x, const void* w, const 
   const long tiles = static_cast<long>(g.m_tiles) * g.n_tiles;
   const int grid = static_cast<int>(tiles < st->sms ? tiles : st->sms);
   gemm_tc_kernel<kTile, false, false><<<grid, 192, GemmCfg<kTile>::SMEM_BYTES, stream>>>(ta, tb, unused, unused, g);
-  ce_finalize_kernel<<<(T + 255) / 256, 256, 0, stream>>>(pmax, psum, static_cast<int>(ntiles), T, tlogit, targets,
+  ce_finalize_kernel<<<ce_finalize_blocks(T), kCeRows * kCeGroups, 0, stream>>>(pmax, psum, static_cast<int>(ntiles), T, tlogit, targets,
                                                           ignore_index, z_coeff, lse_out, loss_out);
   if ((e = cudaGetLastError()) != cudaSuccess) return fail(1, "kernel launch: %s", cudaGetErrorString(e));
   return 0;

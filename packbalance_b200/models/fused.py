@@ -49,10 +49,47 @@ class StepContext:
         self.sin = rot.sin_cached
 
 
+_WGRAD_STREAMS: dict[int, torch.cuda.Stream] = {}
+# Weight gradients go to a side stream only while a CUDA graph is being captured: in a
+# graph the fork/join costs nothing at run time; eagerly, the host-side stream and
+# allocator bookkeeping per GEMM costs more than the overlap gains.
+ASYNC_WGRAD = False
+
+
+def _dev_index(device: torch.device) -> int:
+    return device.index if device.index is not None else torch.cuda.current_device()
+
+
+def _wgrad_stream(device: torch.device) -> torch.cuda.Stream | None:
+    if device.type != "cuda":
+        return None
+    idx = _dev_index(device)
+    if idx not in _WGRAD_STREAMS:
+        _WGRAD_STREAMS[idx] = torch.cuda.Stream(device=idx)
+    return _WGRAD_STREAMS[idx]
+
+
 def _wgrad(flat: FlatParameters, params, dy: torch.Tensor, x: torch.Tensor) -> None:
-    """Weight gradient ``dy.T @ x`` of a group of adjacent params into the flat buffer."""
+    """Weight gradient ``dy.T @ x`` of a group of adjacent params into the flat buffer,
+    on a side stream: the weight gradients of a layer depend on nothing the rest of the
+    backward pass computes, so they fill the SMs the dgrad / attention kernels leave idle
+    (wave tails).  The layer joins the side stream before it reports its gradients."""
     acc = flat.claim(*params)
-    linear_wgrad(dy, x, flat.grad_of(*params), accumulate=acc)
+    ws = _wgrad_stream(dy.device) if ASYNC_WGRAD else None
+    if ws is None:
+        linear_wgrad(dy, x, flat.grad_of(*params), accumulate=acc)
+        return
+    ws.wait_stream(torch.cuda.current_stream(dy.device))
+    with torch.cuda.stream(ws):
+        linear_wgrad(dy, x, flat.grad_of(*params), accumulate=acc)
+    dy.record_stream(ws)
+    x.record_stream(ws)
+
+
+def _join_wgrads(device: torch.device) -> None:
+    ws = _WGRAD_STREAMS.get(_dev_index(device)) if ASYNC_WGRAD and device.type == "cuda" else None
+    if ws is not None:
+        torch.cuda.current_stream(device).wait_stream(ws)
 
 
 class _Embed(torch.autograd.Function):
@@ -141,6 +178,7 @@ class _Decoder(torch.autograd.Function):
         _wgrad(flat, (wq, wk, wv), dqkv, xn1)
         dxb = torch.empty(t, d, device=dev, dtype=torch.bfloat16)
         dx = C.rmsnorm_bwd(dxn1, x, w_in, rstd1, dx1, dxb, flat.grad_of(w_in).view(-1), flat.claim(w_in))
+        _join_wgrads(dev)
         flat.ready_after(w_in)
         return (dx, dxb if ctx.has_delta else None) + (None,) * 10
 

@@ -98,9 +98,15 @@ class _GraphedStep:
         self.hp_host = torch.zeros(3, dtype=torch.float32).pin_memory()
         engine.flat.refresh_shadow()
         torch.cuda.synchronize(dev)
+        from packbalance_b200.models import fused
+
         self.graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(self.graph):
-            self.out = engine._native_body([self.static], self.loss_scale, self.hp)
+        fused.ASYNC_WGRAD = True  # weight gradients on a parallel branch of the graph
+        try:
+            with torch.cuda.graph(self.graph):
+                self.out = engine._native_body([self.static], self.loss_scale, self.hp)
+        finally:
+            fused.ASYNC_WGRAD = False
 
     def run(self, batch: dict[str, Any], loss_scale: float, hp: tuple[float, float, float]) -> dict[str, torch.Tensor]:
         _copy_into(self.static, batch)

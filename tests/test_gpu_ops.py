@@ -108,12 +108,18 @@ def test_embedding_and_adamw_and_norm():
     norm = g.norm()
     ref.grad = g * min(1.0, 0.5 / (norm.item() + 1e-6))
     opt.step()
+    p0 = p.clone()
     m, v = torch.zeros_like(p), torch.zeros_like(p)
     sh = torch.empty(1003, device=dev, dtype=torch.bfloat16)
     skipped = torch.zeros((), device=dev, dtype=torch.int32)
-    C.adamw_step(p, g, m, v, sh, norm, skipped, 1e-2, 0.9, 0.95, 1e-8, 0.1, 0.1, 1 - 0.95, 0.5, True)
+    C.adamw_step(p, g, m, v, sh, norm, skipped, 1e-2, 0.9, 0.95, 1e-8, 0.1, 0.1, 1 - 0.95, 0.5, True, None)
     torch.testing.assert_close(p, ref.detach(), atol=1e-6, rtol=1e-5)
     torch.testing.assert_close(sh.float(), p.to(torch.bfloat16).float())
+    # lr and bias corrections from device memory (the CUDA-graph path): same update
+    p2, m2, v2 = p0.clone(), torch.zeros_like(p), torch.zeros_like(p)
+    hp = torch.tensor([1e-2, 0.1, 1 - 0.95], device=dev)
+    C.adamw_step(p2, g, m2, v2, sh, norm, skipped, 0.0, 0.9, 0.95, 1e-8, 0.1, 1.0, 1.0, 0.5, True, hp)
+    torch.testing.assert_close(p2, p, atol=0, rtol=0)
     _native.check_status()
 
 
