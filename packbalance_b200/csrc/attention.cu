@@ -465,7 +465,7 @@ __global__ void __launch_bounds__(448, 1)
                     const AttnArgs args) {
   using C = BwdCfg<D>;
   __shared__ __align__(8) uint64_t kv_full, kv_empty, qd_full[2], qd_empty[2], st_full, ds_ready, mma2_done, dq_free,
-      acc_done, acc_free, drain_bar;
+      acc_done, acc_free, drain_bar, st_free, dpt_free;
   __shared__ uint32_t tmem_sh;
   __shared__ volatile int abort_sh;
   extern __shared__ uint8_t dyn[];
@@ -485,6 +485,8 @@ __global__ void __launch_bounds__(448, 1)
     mbar_init(&acc_done, 1);
     mbar_init(&acc_free, 8);
     mbar_init(&drain_bar, 1);
+    mbar_init(&st_free, 8);   // the gradient warps have read S^T out of TMEM
+    mbar_init(&dpt_free, 8);  // ... and dP^T
     abort_sh = 0;
     fence_mbar_init();
   }
@@ -541,43 +543,61 @@ __global__ void __launch_bounds__(448, 1)
       bool ok = true;
       const uint32_t ka = smem_u32(smem + C::K_OFF), va = smem_u32(smem + C::V_OFF);
       const uint32_t pa = smem_u32(smem + C::P_OFF), dsa = smem_u32(smem + C::DS_OFF);
+      // S^T(gx) = K Q^T and dP^T(gx) = V dO^T of global tile gx: each overwrites its TMEM
+      // columns once the gradient warps have read out tile gx - 1's.
+      auto issue_st = [&](uint32_t gx) -> bool {
+        const int sx = gx % C::QSTAGES;
+        const uint32_t qa = smem_u32(smem + C::Q_OFF + sx * 2 * C::TILE_BYTES);
+        const uint32_t da = qa + C::TILE_BYTES;
+        if (!mbar_wait(&qd_full[sx], (gx / C::QSTAGES) & 1, args.status, 225, &abort_sh)) return false;
+        // Without separate dQ columns, dQ(gx-1) lives where S^T(gx) goes.
+        if (!C::SPLIT_DQ && gx > 0 && !mbar_wait(&dq_free, (gx - 1) & 1, args.status, 226, &abort_sh)) return false;
+        if (gx > 0 && !mbar_wait(&st_free, (gx - 1) & 1, args.status, 234, &abort_sh)) return false;
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
+          umma_ss(tmem + C::ST_COL, sdesc_sw128(ka + off, 16, 1024), sdesc_sw128(qa + off, 16, 1024), C::IDESC_SQ,
+                  kk > 0 ? 1u : 0u);
+        }
+        if (gx > 0 && !mbar_wait(&dpt_free, (gx - 1) & 1, args.status, 235, &abort_sh)) return false;
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
+          umma_ss(tmem + C::DPT_COL, sdesc_sw128(va + off, 16, 1024), sdesc_sw128(da + off, 16, 1024), C::IDESC_SQ,
+                  kk > 0 ? 1u : 0u);
+        }
+        umma_commit(&st_full);
+        return true;
+      };
       int3 nx = blockIdx.x < args.n_items ? ld_item(args.items, blockIdx.x) : make_int3(0, 0, 0);
       for (int it = blockIdx.x; it < args.n_items && ok; it += gridDim.x, ++item_n) {
         const int kt = nx.x, qhi = nx.z;
         if (it + (int)gridDim.x < args.n_items) nx = ld_item(args.items, it + gridDim.x);
         if (!mbar_wait(&kv_full, item_n & 1, args.status, 223, &abort_sh)) break;
+        // dK / dV accumulators and the staging smem of the previous item must be free
+        // before this item's first S^T (whose completion lets the gradient warps write
+        // the P^T / dS^T tiles that double as that staging).
         if (!mbar_wait(&acc_free, (item_n & 1) ^ 1, args.status, 224, &abort_sh)) break;
-        tc_fence_after();
+        if (!issue_st(g)) break;
         for (int qt = kt; qt <= qhi; ++qt, ++g) {
           const int s = g % C::QSTAGES;
-          const uint32_t ph = (g / C::QSTAGES) & 1;
           const uint32_t qa = smem_u32(smem + C::Q_OFF + s * 2 * C::TILE_BYTES);
           const uint32_t da = qa + C::TILE_BYTES;
-          if (!mbar_wait(&qd_full[s], ph, args.status, 225, &abort_sh)) {
+          // The next tile's S^T / dP^T go to the tensor pipe now, so they run while the
+          // gradient warps compute this tile's P^T / dS^T.  (With dQ in the S^T columns
+          // the order must stay tile by tile.)
+          if (C::SPLIT_DQ && qt < qhi && !issue_st(g + 1)) {
             ok = false;
             break;
           }
-          // Without separate dQ columns, dQ(g-1) lives where S^T(g) goes.
-          if (!C::SPLIT_DQ && g > 0 && !mbar_wait(&dq_free, (g - 1) & 1, args.status, 226, &abort_sh)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-#pragma unroll
-          for (int kk = 0; kk < D / 16; ++kk) {
-            const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
-            umma_ss(tmem + C::ST_COL, sdesc_sw128(ka + off, 16, 1024), sdesc_sw128(qa + off, 16, 1024), C::IDESC_SQ,
-                    kk > 0 ? 1u : 0u);
-            umma_ss(tmem + C::DPT_COL, sdesc_sw128(va + off, 16, 1024), sdesc_sw128(da + off, 16, 1024),
-                    C::IDESC_SQ, kk > 0 ? 1u : 0u);
-          }
-          umma_commit(&st_full);
           if (!mbar_wait(&ds_ready, g & 1, args.status, 227, &abort_sh)) {
             ok = false;
             break;
           }
-          tc_fence_after();
           const bool first = qt == kt;
+          tc_fence_after();
 #pragma unroll
           for (int kk = 0; kk < 8; ++kk) {
             const uint32_t aoff = (kk >> 2) * 16384 + (kk & 3) * 32;  // K-major A over q (K dim)
@@ -601,6 +621,10 @@ __global__ void __launch_bounds__(448, 1)
           }
           umma_commit(&mma2_done);
           umma_commit(&qd_empty[s]);
+          if (!C::SPLIT_DQ && qt < qhi && !issue_st(g + 1)) {
+            ok = false;
+            break;
+          }
         }
         if (!ok) break;
         umma_commit(&acc_done);
@@ -646,42 +670,69 @@ __global__ void __launch_bounds__(448, 1)
         }
         const float* s_lse = reinterpret_cast<const float*>(smem + C::VSTAGE_OFF + s * 1024);
         const float* s_delta = s_lse + 128;
+        tc_fence_after();
+        // S^T -> P^T (bf16, this group's 64 query columns), then release S^T's TMEM
+        // columns so the next tile's S^T MMA can run while this tile's gradient math does.
+        // dS^T below uses the same bf16 P^T that the dV MMA reads (registers: 14 warps
+        // leave 128 per thread).
+        uint32_t pp[32];
+#pragma unroll
+        for (int cc = 0; cc < 2; ++cc) {
+          uint32_t sv[32];
+          tmem_ld32(tmem + lane_off + C::ST_COL + grp * 64 + cc * 32, sv);
+          tmem_wait_ld();
+          if (cc == 1) {
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&st_free);
+          }
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            float p2[2];
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+              const int j = grp * 64 + cc * 32 + 2 * i + e;
+              const int q = q0 + j;
+              const bool allowed = q >= kv && q <= de;
+              p2[e] = allowed ? fast_exp2(__uint_as_float(sv[2 * i + e]) * args.scale_log2 - s_lse[j] * kLog2e) : 0.f;
+            }
+            pp[cc * 16 + i] = pack_bf16x2(p2[0], p2[1]);
+          }
+        }
         // The previous tile's dV/dK/dQ MMAs read P/dS from shared memory.
         if (g > 0 && !mbar_wait_warp(&mma2_done, (g - 1) & 1, args.status, 230, &abort_sh)) {
           ok = false;
           break;
         }
-        if (lane == 0) bulk_wait_read<0>();  // dK/dV staging of the previous item used this group's P/dS half
+        if (lane == 0) bulk_wait_read<0>();  // dK/dV staging of the previous item used these tiles
         __syncwarp();
-        tc_fence_after();
-#pragma unroll 1
-        for (int c = 2 * grp; c < 2 * grp + 2; ++c) {
-          uint32_t sv[32], dv[32];
-          tmem_ld32(tmem + lane_off + C::ST_COL + c * 32, sv);
-          tmem_ld32(tmem + lane_off + C::DPT_COL + c * 32, dv);
+#pragma unroll
+        for (int k = 0; k < 8; ++k)
+          st_swz_chunk(ptile, r, grp * 8 + k, make_uint4(pp[4 * k], pp[4 * k + 1], pp[4 * k + 2], pp[4 * k + 3]));
+        // dP^T -> dS^T = P^T (dP^T - delta), 32 columns at a time
+#pragma unroll
+        for (int cc = 0; cc < 2; ++cc) {
+          uint32_t dv[32];
+          tmem_ld32(tmem + lane_off + C::DPT_COL + grp * 64 + cc * 32, dv);
           tmem_wait_ld();
-          uint32_t pp[16], dd[16];
+          if (cc == 1) {
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&dpt_free);
+          }
+          uint32_t dd[16];
 #pragma unroll
           for (int i = 0; i < 16; ++i) {
-            float p2[2], d2[2];
-#pragma unroll
-            for (int e = 0; e < 2; ++e) {
-              const int j = c * 32 + 2 * i + e;
-              const int q = q0 + j;
-              const bool allowed = q >= kv && q <= de;
-              const float p =
-                  allowed ? fast_exp2(__uint_as_float(sv[2 * i + e]) * args.scale_log2 - s_lse[j] * kLog2e) : 0.f;
-              p2[e] = p;
-              d2[e] = allowed ? p * (__uint_as_float(dv[2 * i + e]) - s_delta[j]) : 0.f;  // select: delta past T is stale smem
-            }
-            pp[i] = pack_bf16x2(p2[0], p2[1]);
-            dd[i] = pack_bf16x2(d2[0], d2[1]);
+            const float2 p = unpack_bf16x2(pp[cc * 16 + i]);
+            const int j = grp * 64 + cc * 32 + 2 * i;
+            // select (not multiply): delta past T is stale smem; masked P is exactly 0
+            const float d0 = p.x != 0.f ? p.x * (__uint_as_float(dv[2 * i]) - s_delta[j]) : 0.f;
+            const float d1 = p.y != 0.f ? p.y * (__uint_as_float(dv[2 * i + 1]) - s_delta[j + 1]) : 0.f;
+            dd[i] = pack_bf16x2(d0, d1);
           }
 #pragma unroll
-          for (int k = 0; k < 4; ++k) {
-            st_swz_chunk(ptile, r, c * 4 + k, make_uint4(pp[4 * k], pp[4 * k + 1], pp[4 * k + 2], pp[4 * k + 3]));
-            st_swz_chunk(dstile, r, c * 4 + k, make_uint4(dd[4 * k], dd[4 * k + 1], dd[4 * k + 2], dd[4 * k + 3]));
-          }
+          for (int k = 0; k < 4; ++k)
+            st_swz_chunk(dstile, r, grp * 8 + cc * 4 + k, make_uint4(dd[4 * k], dd[4 * k + 1], dd[4 * k + 2], dd[4 * k + 3]));
         }
         fence_async_smem();
         tc_fence_before();
@@ -708,6 +759,9 @@ __global__ void __launch_bounds__(448, 1)
         reduce_box(&tm_dkv, sl, is_k ? hk * D + c : (Hkv + hk) * D + c - D, kt * 128 + q4 * 32);
         slot ^= 1;
       }
+      // The staging areas overlap other warps' P^T / dS^T rows: they may be rewritten
+      // (next item) only after these stores have read them; acc_free orders that.
+      if (lane == 0) bulk_wait_read<0>();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_free);
