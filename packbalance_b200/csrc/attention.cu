@@ -75,6 +75,8 @@ struct AttnArgs {
 // every 128-wide key tile and runs its own online softmax (max, sum) with its own O
 // accumulator in TMEM; the two partial results are merged once at the end.  This
 // doubles the softmax warps per SM without any per-tile exchange between them.
+constexpr float kLazyRescaleLog2 = 8.f;  // forward: rescale O only when the max grows > 2^8
+
 template <int D>
 struct FwdCfg {
   static constexpr int TILE_BYTES = 128 * D * 2;  // one 128-row tile of Q, K or V
@@ -109,8 +111,11 @@ template <int D>
 __global__ void __launch_bounds__(320, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tmap, const AttnArgs args) {
   using C = FwdCfg<D>;
-  __shared__ __align__(8) uint64_t q_full, q_empty, kv_full[2], kv_empty[2], s_full[2], s_free, p_ready[2],
-      o_done[2], o_free, stats_ready, drain_bar;
+  // p_ready / o_done [group][P slot] (tile g uses slot g & 1): one barrier per slot, so
+  // with the softmax groups running up to two tiles ahead of the P V products no
+  // barrier ever completes a second phase before its first has been waited for.
+  __shared__ __align__(8) uint64_t q_full, q_empty, kv_full[2], kv_empty[2], s_full[2], s_free, p_ready[2][2],
+      o_done[2][2], o_free, stats_ready, drain_bar;
   __shared__ uint32_t tmem_sh;
   __shared__ volatile int abort_sh;
   extern __shared__ uint8_t dyn[];
@@ -123,8 +128,10 @@ __global__ void __launch_bounds__(320, 1)
       mbar_init(&kv_full[i], 1);
       mbar_init(&kv_empty[i], 1);
       mbar_init(&s_full[i], 1);
-      mbar_init(&p_ready[i], 4);
-      mbar_init(&o_done[i], 1);
+      mbar_init(&p_ready[i][0], 4);
+      mbar_init(&p_ready[i][1], 4);
+      mbar_init(&o_done[i][0], 1);
+      mbar_init(&o_done[i][1], 1);
     }
     mbar_init(&s_free, 8);
     mbar_init(&o_free, 4);
@@ -174,7 +181,6 @@ __global__ void __launch_bounds__(320, 1)
   } else if (warp == 1) {
     if (lane == 0) {
       uint32_t kv_it = 0, q_it = 0, item_n = 0;
-      uint32_t p_it[2] = {0, 0};
       bool ok = true;
       const uint32_t qa = smem_u32(smem + C::Q_OFF);
       int3 nx = blockIdx.x < args.n_items ? ld_item(args.items, blockIdx.x) : make_int3(0, 0, 0);
@@ -221,11 +227,10 @@ __global__ void __launch_bounds__(320, 1)
             }
 #pragma unroll
             for (int grp = 0; grp < 2; ++grp) {
-              if (!mbar_wait(&p_ready[grp], p_it[grp] & 1, args.status, 206, &abort_sh)) {
+              if (!mbar_wait(&p_ready[grp][g & 1], (g >> 1) & 1, args.status, 206, &abort_sh)) {
                 ok = false;
                 break;
               }
-              ++p_it[grp];
               tc_fence_after();
               const uint32_t pa = tmem + C::P_COL + (grp * 2 + (g & 1)) * 32;
 #pragma unroll
@@ -233,7 +238,7 @@ __global__ void __launch_bounds__(320, 1)
                 umma_ts(tmem + C::O_COL + grp * D, pa + kk * 8,
                         sdesc_sw128(va + grp * 8192 + kk * 2048, 16384, 1024), C::IDESC_O,
                         (j > 1 || kk > 0) ? 1u : 0u);
-              umma_commit(&o_done[grp]);
+              umma_commit(&o_done[grp][g & 1]);
             }
             if (!ok) break;
             umma_commit(&kv_empty[s]);
@@ -251,7 +256,7 @@ __global__ void __launch_bounds__(320, 1)
     const int r = q4 * 32 + lane;
     const uint32_t lane_off = static_cast<uint32_t>(q4 * 32) << 16;
     float* stats = reinterpret_cast<float*>(smem + C::STAT_OFF);
-    uint32_t kv_it = 0, o_it = 0, item_n = 0;
+    uint32_t kv_it = 0, item_n = 0;
     int3 nx = blockIdx.x < args.n_items ? ld_item(args.items, blockIdx.x) : make_int3(0, 0, 0);
     int nlo = (blockIdx.x < args.n_items && nx.x * 128 + r < T) ? args.doc_start[nx.x * 128 + r] : 0x7fffffff;
     for (int it = blockIdx.x; it < args.n_items; it += gridDim.x, ++item_n) {
@@ -267,6 +272,7 @@ __global__ void __launch_bounds__(320, 1)
       const bool qok = q < T;
       float m = -INFINITY, l = 0.f;
       bool ok = true;
+      uint32_t pv_waited = 0;  // o_done phases of this item waited so far
       for (int j = 0; j < nkv; ++j) {
         const uint32_t g = kv_it + j;
         if (!mbar_wait_warp(&s_full[g % C::S_BUFS], (g / C::S_BUFS) & 1, args.status, 208, &abort_sh)) {
@@ -302,9 +308,15 @@ __global__ void __launch_bounds__(320, 1)
             mx = fmaxf(mx, s[i]);
           }
         }
+        // Lazy rescaling: the exponent base only moves when the running max grows by more
+        // than 2^8 (or on the first finite max), so most tiles neither touch O nor wait
+        // for the previous P V product.  Exact: O and l always share the base, and
+        // P <= 2^8 stays well inside bf16 / fp32 range.
         const float m_new = fmaxf(m, mx);
-        const float base = m_new == -INFINITY ? 0.f : m_new;
-        const float corr = fast_exp2(m - base);  // m == -inf -> 0
+        const bool need = m != -INFINITY && m_new > m + kLazyRescaleLog2;
+        const bool rescale = __any_sync(0xffffffff, need);  // warp-uniform: TMEM ops below
+        const float base = (rescale || m == -INFINITY) ? (m_new == -INFINITY ? 0.f : m_new) : m;
+        const float corr = m == -INFINITY ? 0.f : fast_exp2(m - base);  // 1 when the base stays
         float sum = 0.f;
         uint32_t pk[32];
 #pragma unroll
@@ -315,29 +327,31 @@ __global__ void __launch_bounds__(320, 1)
           pk[i] = pack_bf16x2(p0, p1);
         }
         l = l * corr + sum;
-        // The previous PV of this group must be complete before its O is rescaled or
-        // its P slot (two tiles back) is overwritten.
-        if (j > 0) {
-          if (!mbar_wait_warp(&o_done[grp], o_it & 1, args.status, 209, &abort_sh)) {
+        // P V products of this item that must be complete: tiles <= j - 2 (their P slot is
+        // reused now) and, to rescale O, tile j - 1 too, waited tile by tile in order.
+        const uint32_t need_done = rescale ? j : (j > 0 ? j - 1 : 0);
+        while (pv_waited < need_done) {
+          const uint32_t t = kv_it + pv_waited;
+          if (!mbar_wait_warp(&o_done[grp][t & 1], (t >> 1) & 1, args.status, 209, &abort_sh)) {
             ok = false;
             break;
           }
-          ++o_it;
-          tc_fence_after();
-          // Warp-uniform decision: the TMEM load/store below are .sync.aligned.
-          if (__any_sync(0xffffffff, corr != 1.f)) {
+          ++pv_waited;
+        }
+        if (!ok) break;
+        tc_fence_after();
+        if (rescale && j > 0) {
 #pragma unroll
-            for (int c = 0; c < D; c += 16) {
-              uint32_t ov[16];
-              tmem_ld16(tmem + lane_off + C::O_COL + grp * D + c, ov);
-              tmem_wait_ld();
+          for (int c = 0; c < D; c += 16) {
+            uint32_t ov[16];
+            tmem_ld16(tmem + lane_off + C::O_COL + grp * D + c, ov);
+            tmem_wait_ld();
 #pragma unroll
-              for (int i = 0; i < 16; ++i) ov[i] = __float_as_uint(__uint_as_float(ov[i]) * corr);
-              tmem_st16(tmem + lane_off + C::O_COL + grp * D + c, ov);
-            }
+            for (int i = 0; i < 16; ++i) ov[i] = __float_as_uint(__uint_as_float(ov[i]) * corr);
+            tmem_st16(tmem + lane_off + C::O_COL + grp * D + c, ov);
           }
         }
-        m = m_new;
+        m = m_new == -INFINITY ? m : base;
 #pragma unroll
         for (int c = 0; c < 2; ++c) {
           uint32_t pv[16];
@@ -348,11 +362,18 @@ __global__ void __launch_bounds__(320, 1)
         tmem_wait_st();
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&p_ready[grp]);
+        if (lane == 0) mbar_arrive(&p_ready[grp][g & 1]);
       }
       if (!ok) break;
-      if (!mbar_wait_warp(&o_done[grp], o_it & 1, args.status, 210, &abort_sh)) break;
-      ++o_it;
+      while (pv_waited < static_cast<uint32_t>(nkv)) {  // every P V of the item
+        const uint32_t t = kv_it + pv_waited;
+        if (!mbar_wait_warp(&o_done[grp][t & 1], (t >> 1) & 1, args.status, 210, &abort_sh)) {
+          ok = false;
+          break;
+        }
+        ++pv_waited;
+      }
+      if (!ok) break;
       tc_fence_after();
       if (grp == 1) {
         stats[2 * r] = m;
