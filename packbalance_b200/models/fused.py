@@ -47,6 +47,8 @@ class StepContext:
         rot = model.model.rotary
         self.cos = rot.cos_cached
         self.sin = rot.sin_cached
+        # reference flag (model/llama.py:153-163): recompute each layer in its backward
+        self.checkpoint = bool(model.model.gradient_checkpointing and model.training)
 
 
 _WGRAD_STREAMS: dict[int, torch.cuda.Stream] = {}
@@ -110,35 +112,48 @@ class _Embed(torch.autograd.Function):
         return None, None, None
 
 
+def _layer_forward(x_prev, delta_prev, params, sc: StepContext):
+    """One decoder layer forward; returns (x1, mlp_out, saved activations)."""
+    w_in, wq, wk, wv, wo, w_post, wg, wu, wd = params
+    cfg = sc.cfg
+    flat = sc.flat
+    C = _native.module()
+    t, d = x_prev.shape
+    h, hk, hd = cfg.n_heads, cfg.n_kv_heads, cfg.head_dim
+    nqkv = (h + 2 * hk) * hd
+    F = cfg.d_ff
+    x, xn1, rstd1 = C.add_rmsnorm_fwd(x_prev, delta_prev, w_in, cfg.norm_eps, True)
+    qkv = torch.empty(t, nqkv, device=x.device, dtype=torch.bfloat16)
+    ag = flat.gather_spec(wq, wk, wv)  # sharded weights: fetched inside this GEMM
+    gemm(xn1, flat.shadow_of(wq, wk, wv), qkv, t, nqkv, d, epi=EPI_ROPE, pos=sc.pos, cos=sc.cos, sin=sc.sin,
+         head_dim=hd, n_rope_cols=(h + hk) * hd, ag=ag)
+    o, lse = attn_forward_packed(qkv, sc.plan, h, hk, hd)
+    attn_out = torch.empty(t, d, device=x.device, dtype=torch.bfloat16)
+    gemm(o, flat.shadow_of(wo), attn_out, t, d, h * hd, epi=EPI_BF16)
+    x1, xn2, rstd2 = C.add_rmsnorm_fwd(x, attn_out, w_post, cfg.norm_eps, True)
+    hmid = torch.empty(t, F, device=x.device, dtype=torch.bfloat16)
+    gu = torch.empty(t, 2 * F, device=x.device, dtype=torch.bfloat16)
+    ag = flat.gather_spec(wg, wu)
+    gemm(xn2, flat.shadow_of(wg, wu), hmid, t, 2 * F, d, epi=EPI_SWIGLU, aux=gu, ag=ag)
+    mlp_out = torch.empty(t, d, device=x.device, dtype=torch.bfloat16)
+    gemm(hmid, flat.shadow_of(wd), mlp_out, t, d, F, epi=EPI_BF16)
+    return x1, mlp_out, (x, xn1, rstd1, qkv, o, lse, x1, xn2, rstd2, gu, hmid)
+
+
 class _Decoder(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x_prev, delta_prev, w_in, wq, wk, wv, wo, w_post, wg, wu, wd, sc: StepContext):
-        cfg = sc.cfg
-        flat = sc.flat
-        C = _native.module()
-        t, d = x_prev.shape
-        h, hk, hd = cfg.n_heads, cfg.n_kv_heads, cfg.head_dim
-        nqkv = (h + 2 * hk) * hd
-        F = cfg.d_ff
-        x, xn1, rstd1 = C.add_rmsnorm_fwd(x_prev, delta_prev, w_in, cfg.norm_eps, True)
-        qkv = torch.empty(t, nqkv, device=x.device, dtype=torch.bfloat16)
-        ag = flat.gather_spec(wq, wk, wv)  # sharded weights: fetched inside this GEMM
-        gemm(xn1, flat.shadow_of(wq, wk, wv), qkv, t, nqkv, d, epi=EPI_ROPE, pos=sc.pos, cos=sc.cos, sin=sc.sin,
-             head_dim=hd, n_rope_cols=(h + hk) * hd, ag=ag)
-        o, lse = attn_forward_packed(qkv, sc.plan, h, hk, hd)
-        attn_out = torch.empty(t, d, device=x.device, dtype=torch.bfloat16)
-        gemm(o, flat.shadow_of(wo), attn_out, t, d, h * hd, epi=EPI_BF16)
-        x1, xn2, rstd2 = C.add_rmsnorm_fwd(x, attn_out, w_post, cfg.norm_eps, True)
-        hmid = torch.empty(t, F, device=x.device, dtype=torch.bfloat16)
-        gu = torch.empty(t, 2 * F, device=x.device, dtype=torch.bfloat16)
-        ag = flat.gather_spec(wg, wu)
-        gemm(xn2, flat.shadow_of(wg, wu), hmid, t, 2 * F, d, epi=EPI_SWIGLU, aux=gu, ag=ag)
-        mlp_out = torch.empty(t, d, device=x.device, dtype=torch.bfloat16)
-        gemm(hmid, flat.shadow_of(wd), mlp_out, t, d, F, epi=EPI_BF16)
+        params = (w_in, wq, wk, wv, wo, w_post, wg, wu, wd)
+        x1, mlp_out, saved = _layer_forward(x_prev, delta_prev, params, sc)
         ctx.sc = sc
         ctx.has_delta = delta_prev is not None
-        ctx.params = (w_in, wq, wk, wv, wo, w_post, wg, wu, wd)
-        ctx.saved = (x, xn1, rstd1, qkv, o, lse, x1, xn2, rstd2, gu, hmid)
+        ctx.params = params
+        if sc.checkpoint:
+            # activation checkpointing: keep only the layer inputs, recompute in backward
+            ctx.saved = None
+            ctx.inputs = (x_prev, delta_prev)
+        else:
+            ctx.saved = saved
         return x1, mlp_out
 
     @staticmethod
@@ -148,6 +163,9 @@ class _Decoder(torch.autograd.Function):
         flat = sc.flat
         C = _native.module()
         w_in, wq, wk, wv, wo, w_post, wg, wu, wd = ctx.params
+        if ctx.saved is None:  # checkpointed: recompute this layer's activations
+            ctx.saved = _layer_forward(*ctx.inputs, ctx.params, sc)[2]
+            ctx.inputs = None
         x, xn1, rstd1, qkv, o, lse, x1, xn2, rstd2, gu, hmid = ctx.saved
         ctx.saved = None
         t, d = x.shape

@@ -124,3 +124,28 @@ def test_cuda_graph_step_matches_eager_step():
         assert err <= 0.02 * upd + 1e-6, (float(err), float(upd))
     assert len(e1._graphs) == 1
     _native.check_status()
+
+
+def test_activation_checkpointing_native_path():
+    """With the reference's gradient_checkpointing flag the native path recomputes each
+    layer in its backward: same loss and (up to fp32 atomics) the same gradients."""
+    torch.manual_seed(0)
+    cfg = _cfg()
+    lengths = [300, 211, 489]
+    ids, labels, pos, doc = _batch(sum(lengths), cfg.vocab_size, lengths)
+    model = LlamaForCausalLM(cfg).cuda()
+    flat = FlatParameters(model)
+    model.flat = flat
+    losses, grads = [], []
+    for ckpt in (False, True):
+        model.model.gradient_checkpointing = ckpt
+        flat.begin_window()
+        out = model(ids[None], labels=labels[None], position_ids=pos[None], doc_ids=doc[None])
+        out.loss.backward()
+        flat.finish_window()
+        losses.append(float(out.loss))
+        grads.append(flat.grad.clone())
+    _native.check_status()
+    assert losses[0] == losses[1]
+    rel = (grads[1] - grads[0]).norm() / grads[0].norm()
+    assert rel < 1e-4, float(rel)
