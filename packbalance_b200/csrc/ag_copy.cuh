@@ -132,7 +132,7 @@ __device__ __forceinline__ void ag_copy_warp(const AgSpec& s) {
     for (long e = e0; e < e1;) {
       const int p = static_cast<int>((e - s.unit0) / s.cs);
       const long seg_end = min(e1, s.unit0 + (p + 1) * s.cs);
-      if (p != s.rank) ag_copy_span(s.src[p] + e, s.dst + e, seg_end - e);
+      if (p != s.rank && PB_BOUNDS_OK(p >= 0 && p < s.world, nullptr, 0)) ag_copy_span(s.src[p] + e, s.dst + e, seg_end - e);
       e = seg_end;
     }
     fence_proxy_async_global();

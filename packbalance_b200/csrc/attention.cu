@@ -107,6 +107,15 @@ __device__ __forceinline__ int3 ld_item(const int* items, int i) {
   return make_int3(items[3 * i], items[3 * i + 1], items[3 * i + 2]);
 }
 
+// Debug builds: an item outside the token range / head count is reported (status 240)
+// and replaced by an empty one on a valid tile.
+__device__ __forceinline__ int3 checked_item(int3 it, int T, int H, int* status) {
+  const int nt = (T + 127) / 128;
+  if (!PB_BOUNDS_OK(it.x >= 0 && it.x < nt && it.y >= 0 && it.y < H && it.z >= 0 && it.z < nt, status, 240))
+    return make_int3(0, 0, 0);
+  return it;
+}
+
 template <int D>
 __global__ void __launch_bounds__(320, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tmap, const AttnArgs args) {
@@ -156,10 +165,10 @@ __global__ void __launch_bounds__(320, 1)
     if (lane == 0) {
       uint32_t kv_it = 0, q_it = 0;
       bool ok = true;
-      int3 nx = blockIdx.x < args.n_items ? ld_item(args.items, blockIdx.x) : make_int3(0, 0, 0);
+      int3 nx = blockIdx.x < args.n_items ? checked_item(ld_item(args.items, blockIdx.x), args.T, args.H, args.status) : make_int3(0, 0, 0);
       for (int it = blockIdx.x; it < args.n_items && ok; it += gridDim.x) {
         const int qt = nx.x, h = nx.y, kt0 = nx.z;
-        if (it + (int)gridDim.x < args.n_items) nx = ld_item(args.items, it + gridDim.x);
+        if (it + (int)gridDim.x < args.n_items) nx = checked_item(ld_item(args.items, it + gridDim.x), args.T, args.H, args.status);
         const int hk = h / group;
         const int q0 = qt * 128;
         if (!mbar_wait(&q_empty, (q_it & 1) ^ 1, args.status, 201, &abort_sh)) break;
@@ -183,10 +192,10 @@ __global__ void __launch_bounds__(320, 1)
       uint32_t kv_it = 0, q_it = 0, item_n = 0;
       bool ok = true;
       const uint32_t qa = smem_u32(smem + C::Q_OFF);
-      int3 nx = blockIdx.x < args.n_items ? ld_item(args.items, blockIdx.x) : make_int3(0, 0, 0);
+      int3 nx = blockIdx.x < args.n_items ? checked_item(ld_item(args.items, blockIdx.x), args.T, args.H, args.status) : make_int3(0, 0, 0);
       for (int it = blockIdx.x; it < args.n_items && ok; it += gridDim.x, ++item_n) {
         const int qt = nx.x, kt0 = nx.z;
-        if (it + (int)gridDim.x < args.n_items) nx = ld_item(args.items, it + gridDim.x);
+        if (it + (int)gridDim.x < args.n_items) nx = checked_item(ld_item(args.items, it + gridDim.x), args.T, args.H, args.status);
         const int nkv = qt - kt0 + 1;
         if (!mbar_wait(&q_full, q_it & 1, args.status, 203, &abort_sh)) break;
         ++q_it;
@@ -257,13 +266,13 @@ __global__ void __launch_bounds__(320, 1)
     const uint32_t lane_off = static_cast<uint32_t>(q4 * 32) << 16;
     float* stats = reinterpret_cast<float*>(smem + C::STAT_OFF);
     uint32_t kv_it = 0, item_n = 0;
-    int3 nx = blockIdx.x < args.n_items ? ld_item(args.items, blockIdx.x) : make_int3(0, 0, 0);
+    int3 nx = blockIdx.x < args.n_items ? checked_item(ld_item(args.items, blockIdx.x), args.T, args.H, args.status) : make_int3(0, 0, 0);
     int nlo = (blockIdx.x < args.n_items && nx.x * 128 + r < T) ? args.doc_start[nx.x * 128 + r] : 0x7fffffff;
     for (int it = blockIdx.x; it < args.n_items; it += gridDim.x, ++item_n) {
       const int qt = nx.x, h = nx.y, kt0 = nx.z;
       const int lo = nlo;
       if (it + (int)gridDim.x < args.n_items) {
-        nx = ld_item(args.items, it + gridDim.x);
+        nx = checked_item(ld_item(args.items, it + gridDim.x), args.T, args.H, args.status);
         nlo = nx.x * 128 + r < T ? args.doc_start[nx.x * 128 + r] : 0x7fffffff;
       }
       const int q0 = qt * 128;
@@ -530,10 +539,10 @@ __global__ void __launch_bounds__(448, 1)
     if (lane == 0) {
       uint32_t item_n = 0, g = 0;
       bool ok = true;
-      int3 nx = blockIdx.x < args.n_items ? ld_item(args.items, blockIdx.x) : make_int3(0, 0, 0);
+      int3 nx = blockIdx.x < args.n_items ? checked_item(ld_item(args.items, blockIdx.x), args.T, args.H, args.status) : make_int3(0, 0, 0);
       for (int it = blockIdx.x; it < args.n_items && ok; it += gridDim.x, ++item_n) {
         const int kt = nx.x, h = nx.y, qhi = nx.z;
-        if (it + (int)gridDim.x < args.n_items) nx = ld_item(args.items, it + gridDim.x);
+        if (it + (int)gridDim.x < args.n_items) nx = checked_item(ld_item(args.items, it + gridDim.x), args.T, args.H, args.status);
         const int hk = h / group;
         if (!mbar_wait(&kv_empty, (item_n & 1) ^ 1, args.status, 221, &abort_sh)) break;
         mbar_arrive_expect_tx(&kv_full, 2 * C::TILE_BYTES);
@@ -592,10 +601,10 @@ __global__ void __launch_bounds__(448, 1)
         umma_commit(&st_full);
         return true;
       };
-      int3 nx = blockIdx.x < args.n_items ? ld_item(args.items, blockIdx.x) : make_int3(0, 0, 0);
+      int3 nx = blockIdx.x < args.n_items ? checked_item(ld_item(args.items, blockIdx.x), args.T, args.H, args.status) : make_int3(0, 0, 0);
       for (int it = blockIdx.x; it < args.n_items && ok; it += gridDim.x, ++item_n) {
         const int kt = nx.x, qhi = nx.z;
-        if (it + (int)gridDim.x < args.n_items) nx = ld_item(args.items, it + gridDim.x);
+        if (it + (int)gridDim.x < args.n_items) nx = checked_item(ld_item(args.items, it + gridDim.x), args.T, args.H, args.status);
         if (!mbar_wait(&kv_full, item_n & 1, args.status, 223, &abort_sh)) break;
         // dK / dV accumulators and the staging smem of the previous item must be free
         // before this item's first S^T (whose completion lets the gradient warps write
@@ -664,14 +673,14 @@ __global__ void __launch_bounds__(448, 1)
     uint8_t* dstile = smem + C::DS_OFF;
     uint32_t item_n = 0, g = 0;
     bool ok = true;
-    int3 nx = blockIdx.x < args.n_items ? ld_item(args.items, blockIdx.x) : make_int3(0, 0, 0);
+    int3 nx = blockIdx.x < args.n_items ? checked_item(ld_item(args.items, blockIdx.x), args.T, args.H, args.status) : make_int3(0, 0, 0);
     int nde = (blockIdx.x < args.n_items && nx.x * 128 + r < T) ? args.doc_end[nx.x * 128 + r] : -1;
     for (int it = blockIdx.x; it < args.n_items && ok; it += gridDim.x, ++item_n) {
       const int kt = nx.x, h = nx.y, qhi = nx.z;
       // Key row kv is attended by queries q in [kv, doc_end(kv)] (none past T).
       const int de = nde;
       if (it + (int)gridDim.x < args.n_items) {
-        nx = ld_item(args.items, it + gridDim.x);
+        nx = checked_item(ld_item(args.items, it + gridDim.x), args.T, args.H, args.status);
         nde = nx.x * 128 + r < T ? args.doc_end[nx.x * 128 + r] : -1;
       }
       const int hk = h / group;
@@ -797,10 +806,10 @@ __global__ void __launch_bounds__(448, 1)
     int slot = 0;
     uint32_t g = 0;
     bool ok = true;
-    int3 nx = blockIdx.x < args.n_items ? ld_item(args.items, blockIdx.x) : make_int3(0, 0, 0);
+    int3 nx = blockIdx.x < args.n_items ? checked_item(ld_item(args.items, blockIdx.x), args.T, args.H, args.status) : make_int3(0, 0, 0);
     for (int it = blockIdx.x; it < args.n_items && ok; it += gridDim.x) {
       const int kt = nx.x, h = nx.y, qhi = nx.z;
-      if (it + (int)gridDim.x < args.n_items) nx = ld_item(args.items, it + gridDim.x);
+      if (it + (int)gridDim.x < args.n_items) nx = checked_item(ld_item(args.items, it + gridDim.x), args.T, args.H, args.status);
       for (int qt = kt; qt <= qhi; ++qt, ++g) {
         if (!mbar_wait_warp(&mma2_done, g & 1, args.status, 231, &abort_sh)) {
           ok = false;

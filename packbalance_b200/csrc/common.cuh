@@ -33,6 +33,16 @@ __device__ __forceinline__ void report_error(int* status, int code) {
   if (status != nullptr) atomicCAS(status, 0, code);
 }
 
+// Debug builds (PB_DEBUG_BOUNDS, see setup.py) check the indices that kernels derive
+// from their inputs (work-item lists, owner ranks, token ids) before using them: a
+// failed check records ``code`` in the status word and the access is skipped (no trap).
+// Release builds compile the checks away.
+#ifdef PB_DEBUG_BOUNDS
+#define PB_BOUNDS_OK(cond, status, code) ((cond) ? true : (::pb::report_error((status), (code)), false))
+#else
+#define PB_BOUNDS_OK(cond, status, code) true
+#endif
+
 __device__ __forceinline__ uint64_t globaltimer() {
   uint64_t t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));

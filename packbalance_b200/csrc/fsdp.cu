@@ -275,6 +275,7 @@ __global__ void fsdp_embedding_kernel(const int64_t* __restrict__ ids, long T, f
   for (int j = lane * 4; j < d; j += 128) {
     const long e = row0 + id * d + j;
     const int p = static_cast<int>((e - unit0) / cs);
+    if (!PB_BOUNDS_OK(p >= 0 && p < kMaxWorld, status, 502)) continue;
     const float* src = masters[p] + soff + (e - unit0 - p * cs);
     *reinterpret_cast<float4*>(o + j) = __ldcg(reinterpret_cast<const float4*>(src));
   }

@@ -17,7 +17,10 @@ ROOT = Path(__file__).parent
 CSRC = ROOT / "packbalance_b200" / "csrc"
 SOURCES = ["bindings.cpp", "gemm.cu", "elementwise.cu", "attention.cu", "comm.cu", "fsdp.cu", "noalloc.cu"]
 SOURCES = [str((CSRC / s).relative_to(ROOT)) for s in SOURCES]
-DEFINES: list[str] = []
+# PB_DEBUG_BOUNDS=1 builds the index checks of csrc/common.cuh (PB_BOUNDS_OK) into the
+# kernels: a bad work item, owner rank or token id is reported through the device status
+# word and its access skipped.  Rebuild without it for normal use.
+DEFINES: list[str] = ["-DPB_DEBUG_BOUNDS"] if os.environ.get("PB_DEBUG_BOUNDS") == "1" else []
 
 NVCC_FLAGS = [
     "-gencode",
