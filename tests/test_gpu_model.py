@@ -148,4 +148,4 @@ def test_activation_checkpointing_native_path():
     _native.check_status()
     assert losses[0] == losses[1]
     rel = (grads[1] - grads[0]).norm() / grads[0].norm()
-    assert rel < 1e-4, float(rel)
+    assert rel < 5e-3, float(rel)  # fp32 atomics + bf16 roundings of gradients; a missed recompute is O(1)
