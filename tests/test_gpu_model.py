@@ -146,6 +146,6 @@ def test_activation_checkpointing_native_path():
         losses.append(float(out.loss))
         grads.append(flat.grad.clone())
     _native.check_status()
-    assert losses[0] == losses[1]
+    assert abs(losses[0] - losses[1]) <= 1e-6 * abs(losses[0])  # loss sum uses fp32 atomics
     rel = (grads[1] - grads[0]).norm() / grads[0].norm()
     assert rel < 5e-3, float(rel)  # fp32 atomics + bf16 roundings of gradients; a missed recompute is O(1)
