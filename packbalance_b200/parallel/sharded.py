@@ -85,6 +85,48 @@ def _units_of(model) -> tuple[list[Slot], list[Unit]]:
     return rep, out
 
 
+@dataclass
+class Layout:
+    rep: list[Slot]  # replicated RMSNorm weights (fp32), at the front
+    units: list[Unit]
+    rep_n: int  # elements of the replicated region (padded)
+    numel: int  # gathered / gradient buffer elements
+    shard_numel: int  # elements of one rank's shard
+
+
+def plan_layout(model, world: int) -> Layout:
+    """Element layout of the gathered and gradient buffers: the replicated norms, then
+    every unit padded to a multiple of ``world * ALIGN`` and cut into ``world`` equal
+    chunks (rank p owns chunk p; its shard holds its chunks of all units in order)."""
+    rep, units = _units_of(model)
+    off = 0
+    for s in rep:
+        s.offset = off
+        off += s.numel
+    rep_n = -(-off // ALIGN) * ALIGN
+    off = rep_n
+    soff = 0
+    for u in units:
+        u.unit0 = off
+        for s in u.slots:
+            s.offset = off
+            off += s.numel
+        u.span = off - u.unit0
+        padded = -(-u.span // (world * ALIGN)) * world * ALIGN
+        u.cs = padded // world
+        u.soff = soff
+        soff += u.cs
+        off = u.unit0 + padded
+        # gather segments: q..o and gate..down of a layer (the QKV and gate|up GEMMs fetch
+        # them), the whole unit otherwise
+        if u.name.startswith("layer"):
+            q, o, g, d = u.slots[0], u.slots[3], u.slots[4], u.slots[6]
+            u.segments = [(q.offset, o.offset + o.numel), (g.offset, d.offset + d.numel)]
+        else:
+            u.segments = [(u.unit0, u.unit0 + u.span)]
+    return Layout(rep, units, rep_n, off, soff)
+
+
 class ShardedParameters(GradWindow):
     """Sharded parameter/gradient/optimizer-state buffers of one model (CUDA, W >= 2)."""
 
@@ -102,43 +144,15 @@ class ShardedParameters(GradWindow):
             raise RuntimeError("the sharded engine needs CUDA tensors")
         self.model = model
         W = self.world
-        rep, units = _units_of(model)
-
-        # ---- layout: [replicated norms | unit 0 | unit 1 | ...] ----------------------
-        off = 0
-        for s in rep:
-            s.offset = off
-            off += s.numel
-        self.rep_n = -(-off // ALIGN) * ALIGN
-        off = self.rep_n
-        soff = 0
-        for u in units:
-            u.unit0 = off
-            for s in u.slots:
-                s.offset = off
-                off += s.numel
-            span = off - u.unit0
-            padded = -(-span // (W * ALIGN)) * W * ALIGN
-            u.cs = padded // W
-            u.soff = soff
-            u.span = span
-            soff += u.cs
-            off = u.unit0 + padded
-        self.numel = off
-        self.shard_numel = soff
+        layout = plan_layout(model, W)
+        self.rep_n, self.numel, self.shard_numel = layout.rep_n, layout.numel, layout.shard_numel
+        rep, units = layout.rep, layout.units
         self.rep_slots = rep
         self.units = units
         self.embed_unit = units[0]
         self.slots = rep + [s for u in units for s in u.slots]
         self.by_param = {id(s.param): s for s in self.slots}
         self.unit_of = {id(s.param): u for u in units for s in u.slots}
-        # gather segments: q..o and gate..down of a layer, whole unit otherwise
-        for u in units:
-            if u.name.startswith("layer"):
-                q, o, g, d = u.slots[0], u.slots[3], u.slots[4], u.slots[6]
-                u.segments = [(q.offset, o.offset + o.numel), (g.offset, d.offset + d.numel)]
-            else:
-                u.segments = [(u.unit0, u.unit0 + u.span)]
         # norms (and, for the ready protocol, their layer's unit order)
         self.rep_order = {}
         for i, layer in enumerate(model.model.layers):

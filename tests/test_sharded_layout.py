@@ -1,0 +1,46 @@
+"""Layout of the native sharded engine (host-side arithmetic, CPU)."""
+
+from dataclasses import replace
+
+import pytest
+
+from packbalance_b200.config import ModelConfig
+from packbalance_b200.models.llama import LlamaForCausalLM
+from packbalance_b200.parallel.sharded import ALIGN, plan_layout
+
+
+@pytest.mark.parametrize("world", [2, 3, 8])
+@pytest.mark.parametrize("tie", [True, False])
+def test_layout_covers_every_parameter_once(model_cfg: ModelConfig, world: int, tie: bool) -> None:
+    model = LlamaForCausalLM(replace(model_cfg, tie_embeddings=tie))
+    lay = plan_layout(model, world)
+    names = [n for n, p in model.named_parameters()]
+    slots = lay.rep + [s for u in lay.units for s in u.slots]
+    assert sorted(s.name for s in slots) == sorted(names)
+    # non-overlapping, in increasing order, norms first
+    spans = sorted((s.offset, s.offset + s.numel) for s in slots)
+    assert all(a[1] <= b[0] for a, b in zip(spans, spans[1:]))
+    assert all(s.offset + s.numel <= lay.rep_n for s in lay.rep)
+    assert all(s.name.endswith("norm.weight") for s in lay.rep)
+    soff = 0
+    for u in lay.units:
+        assert u.unit0 % ALIGN == 0 and u.cs % ALIGN == 0 and u.cs * world >= u.span
+        assert u.soff == soff
+        soff += u.cs
+        assert all(u.unit0 <= s.offset and s.offset + s.numel <= u.unit0 + u.span for s in u.slots)
+        # gather segments lie in the unit and cover every weight of it
+        covered = sum(hi - lo for lo, hi in u.segments)
+        assert covered == u.span and all(u.unit0 <= lo < hi <= u.unit0 + u.span for lo, hi in u.segments)
+    assert soff == lay.shard_numel
+    assert lay.units[0].name == "embed" and (lay.units[-1].name == "head") == (not tie)
+
+
+def test_layer_segments_follow_the_fused_gemms(model_cfg: ModelConfig) -> None:
+    model = LlamaForCausalLM(model_cfg)
+    lay = plan_layout(model, 2)
+    layer = next(u for u in lay.units if u.name == "layer0")
+    names = [s.name.split(".")[-2] for s in layer.slots]
+    assert names == ["q_proj", "k_proj", "v_proj", "o_proj", "gate_proj", "up_proj", "down_proj"]
+    (qlo, qhi), (glo, ghi) = layer.segments
+    assert qlo == layer.slots[0].offset and qhi == layer.slots[3].offset + layer.slots[3].numel
+    assert glo == layer.slots[4].offset and ghi == layer.slots[6].offset + layer.slots[6].numel
