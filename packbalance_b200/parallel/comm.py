@@ -3,14 +3,21 @@
 :class:`FusedAllReduce` moves the flat fp32 gradient buffer of
 :class:`~packbalance_b200.parallel.flat.FlatParameters` into symmetric memory
 (``torch.distributed._symmetric_memory``: one allocation per rank, mapped into every
-peer, plus a per-rank signal pad) and averages contiguous ranges of it with the native
-``fused_allreduce`` kernel (``csrc/comm.cu``): reduce-scatter with the 1/W scale and the
-squared-norm partial fused in, then all-gather, synchronised by per-CTA flags in the
-peers' signal pads with bounded waits.  When the driver binds an NVLink multicast
-object over the buffers, ``nvls_allreduce`` does the same with ``multimem.ld_reduce``
-(the NVSwitch sums the ranks' values) and ``multimem.st`` (the switch writes the
-result into every rank), which halves the NVLink traffic of the two-shot form.  The rendezvous and the process group come from
-``torch.distributed`` (NCCL); the data never goes through NCCL.
+peer) and averages contiguous ranges (buckets) of it with native kernels
+(``csrc/comm.cu``):
+
+* ``nvls_allreduce`` when the driver binds an NVLink multicast object over the
+  buffers: ``multimem.ld_reduce`` (the NVSwitch sums the ranks' values) and
+  ``multimem.st`` (the switch writes the result into every rank), the 1/W scale and the
+  squared norm fused in;
+* ``fused_allreduce`` otherwise: two-shot reduce-scatter / all-gather with peer loads.
+
+Both synchronise through per-CTA flags in a symmetric sync buffer (release/acquire at
+system scope, bounded waits).  Barrier epochs come from a device counter bumped once
+per step (:meth:`start_step`) plus the launch's index within the step, so a captured
+CUDA graph replays with fresh epochs.  The kernels use small CTAs that fit beside the
+backward pass's GEMM and attention CTAs on the same SMs.  The rendezvous and the
+process group come from ``torch.distributed`` (NCCL); the data never goes through NCCL.
 
 The squared norm of the averaged gradient accumulates in a device scalar across the
 buckets of a step, which gives gradient clipping its global norm without a separate

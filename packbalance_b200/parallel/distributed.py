@@ -10,10 +10,10 @@ owns no hooks inside autograd; gradients live in the flat buffer of
 :class:`~packbalance_b200.parallel.flat.FlatParameters` and are averaged bucket by
 bucket over contiguous ranges of that buffer:
 
-* CUDA + peer memory available: the fused all-reduce kernel
-  (:mod:`packbalance_b200.parallel.comm`), which loads every peer's bucket over
-  NVLink, sums in fp32, scales by 1/W and also returns the squared L2 norm of the
-  result for gradient clipping;
+* CUDA + peer memory available: the fused all-reduce kernels
+  (:mod:`packbalance_b200.parallel.comm`: NVLS multimem or peer loads), which sum in
+  fp32, scale by 1/W and also return the squared L2 norm of the result for gradient
+  clipping;
 * otherwise ``torch.distributed.all_reduce`` (NCCL on GPU, gloo on CPU).
 
 Buckets are issued in reverse layer order as soon as the backward pass has written
