@@ -130,6 +130,10 @@ def to_device_batch(batch: dict[str, Any], device: torch.device) -> dict[str, An
 
 
 class TrainEngine:
+    # Captured step graphs kept (each holds its own activation memory pool); inputs of
+    # other shapes run eagerly.
+    MAX_GRAPHS = 4
+
     def __init__(
         self,
         cfg: PackBalanceConfig,
@@ -253,7 +257,7 @@ class TrainEngine:
             batch = self.prepare_batch(groups[0])
             sig = _signature(batch)
             g = self._graphs.get(sig)
-            if g is None and self._eager_seen.get(sig, 0) >= 2:
+            if g is None and self._eager_seen.get(sig, 0) >= 2 and len(self._graphs) < self.MAX_GRAPHS:
                 # warmed up (allocator pools, kernel attributes, lazy buffers): capture
                 g = self._graphs[sig] = _GraphedStep(self, to_device_batch(batch, self.device))
             if g is not None:
