@@ -102,12 +102,13 @@ void gemm_tc(at::Tensor a, at::Tensor b, at::Tensor out, int64_t M, int64_t N, i
   TORCH_CHECK(reinterpret_cast<uintptr_t>(a.data_ptr()) % 16 == 0 && reinterpret_cast<uintptr_t>(b.data_ptr()) % 16 == 0,
               "gemm_tc: operands must be 16B aligned");
   TORCH_CHECK(!(swiglu && b_mn), "gemm_tc: SWIGLU needs a K-major B");
+  const bool swiglu_bwd = epi == EPI_SWIGLU_BWD;
 
   GemmArgs g{};
   g.M = (int)M;
   g.N = (int)N;
   g.K = (int)K;
-  g.F = swiglu ? (int)(N / 2) : 0;
+  g.F = swiglu ? (int)(N / 2) : (swiglu_bwd ? (int)N : 0);
   g.m_tiles = (int)((M + 127) / 128);
   g.n_tiles = swiglu ? (int)((N / 2 + bn / 2 - 1) / (bn / 2)) : (int)((N + bn - 1) / bn);
   g.k_blocks = (int)((K + 63) / 64);
@@ -139,12 +140,20 @@ void gemm_tc(at::Tensor a, at::Tensor b, at::Tensor out, int64_t M, int64_t N, i
     TORCH_CHECK((N / 2) % 32 == 0, "gemm_tc: SWIGLU F must be a multiple of 32");
     TORCH_CHECK(aux.has_value() && aux->size(1) == N && aux->size(0) == M, "gemm_tc: SWIGLU saves g|u in aux [M, 2F]");
   }
+  if (swiglu_bwd) {
+    TORCH_CHECK(N % 32 == 0, "gemm_tc: SWIGLU_BWD F must be a multiple of 32");
+    TORCH_CHECK(aux.has_value() && aux->is_contiguous() && aux->scalar_type() == at::kBFloat16 &&
+                    aux->size(0) == M && aux->size(1) == 2 * N,
+                "gemm_tc: SWIGLU_BWD reads the saved g|u from aux (bf16 [M, 2F], contiguous)");
+    TORCH_CHECK(reinterpret_cast<uintptr_t>(aux->data_ptr()) % 16 == 0, "gemm_tc: aux must be 16B aligned");
+    g.gu = reinterpret_cast<const __nv_bfloat16*>(aux->data_ptr());
+  }
   if (g.splits > 1) TORCH_CHECK(epi == EPI_ADD_F32, "gemm_tc: split-K needs the ADD_F32 epilogue");
   const bool has_out = epi != EPI_CE_FWD;
   CUtensorMap to{}, tx{};
   if (has_out) {
     TORCH_CHECK(out.dim() == 2 && out.size(0) == M, "gemm_tc: out rows");
-    TORCH_CHECK(out.size(1) == (swiglu ? N / 2 : N), "gemm_tc: out columns");
+    TORCH_CHECK(out.size(1) == (swiglu ? N / 2 : (swiglu_bwd ? 2 * N : N)), "gemm_tc: out columns");
     TORCH_CHECK((epi == EPI_F32 || epi == EPI_ADD_F32) == (out.scalar_type() == at::kFloat),
                 "gemm_tc: fp32 output for F32/ADD_F32 epilogues, bf16 otherwise");
     to = epi_map(out);

@@ -51,6 +51,7 @@ enum GemmEpi : int {
   EPI_ADD_F32 = 2,
   EPI_SWIGLU = 3,
   EPI_ROPE = 4,
+  EPI_SWIGLU_BWD = 5,
   EPI_CE_FWD = 7,
   EPI_CE_BWD = 8,
 };
@@ -60,7 +61,8 @@ struct GemmArgs {
   int m_tiles, n_tiles, splits, kb_per_split, k_blocks;
   int epi;
   float alpha;
-  int F;  // SWIGLU: width of h (gate|up matrices have 2F rows)
+  int F;  // SWIGLU: width of h (gate|up matrices have 2F rows); SWIGLU_BWD: N
+  const __nv_bfloat16* gu;  // SWIGLU_BWD: saved [g | u] pre-activations, bf16 [M, 2F]
   const int* pos;
   const float* cos_t;
   const float* sin_t;
@@ -235,6 +237,56 @@ __device__ __forceinline__ void run_epilogue(const GemmArgs& a, const CUtensorMa
         s = st.acquire();
         stage_bf16(s, v, 1.f);
         issue_store(tm_out, s, col, row0, ST_STORE);
+        st.release();
+      }
+      break;
+    }
+    case EPI_SWIGLU_BWD: {
+      // The accumulator is dh = dL/dh for h columns [nb*BN, ...); with the saved gate
+      // and up pre-activations of this row it becomes dg = dh u s (1 + g (1 - s)) and
+      // du = dh g s (s = sigmoid(g)), stored into [dg | du] (bf16 [M, 2F]), so dh never
+      // reaches HBM.
+      const __nv_bfloat16* gr = a.gu + static_cast<long>(row_ok ? row : 0) * 2 * a.F;
+      float u[32];
+#pragma unroll 1
+      for (int c = 0; c < BN; c += 32) {
+        const int col = nb * BN + c;
+        if (col >= a.N) break;  // uniform across the warp
+        uint4 gv[4], uv[4];
+        if (row_ok) {
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            gv[j] = __ldg(reinterpret_cast<const uint4*>(gr + col) + j);
+            uv[j] = __ldg(reinterpret_cast<const uint4*>(gr + a.F + col) + j);
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < 4; ++j) gv[j] = uv[j] = make_uint4(0, 0, 0, 0);
+        }
+        tmem_load_f32(tacc + c, v);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const uint32_t* gp = &gv[j].x;
+          const uint32_t* up = &uv[j].x;
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const float2 g2 = unpack_bf16x2(gp[k]), u2 = unpack_bf16x2(up[k]);
+            const int i = 8 * j + 2 * k;
+            const float s0 = sigmoidf_(g2.x), s1 = sigmoidf_(g2.y);
+            const float d0 = v[i], d1 = v[i + 1];
+            v[i] = d0 * u2.x * s0 * (1.f + g2.x * (1.f - s0));
+            v[i + 1] = d1 * u2.y * s1 * (1.f + g2.y * (1.f - s1));
+            u[i] = d0 * g2.x * s0;
+            u[i + 1] = d1 * g2.y * s1;
+          }
+        }
+        uint8_t* s = st.acquire();
+        stage_bf16(s, v, 1.f);
+        issue_store(tm_out, s, col, row0, ST_STORE);
+        st.release();
+        s = st.acquire();
+        stage_bf16(s, u, 1.f);
+        issue_store(tm_out, s, a.F + col, row0, ST_STORE);
         st.release();
       }
       break;

@@ -31,7 +31,7 @@ from packbalance_b200.models.llama import CausalLMOutput
 from packbalance_b200.ops import _native
 from packbalance_b200.ops.attention import attention_plan, attn_backward_packed, attn_forward_packed
 from packbalance_b200.ops.cross_entropy import lmhead_ce_backward, lmhead_ce_forward
-from packbalance_b200.ops.gemm import EPI_BF16, EPI_F32, EPI_ROPE, EPI_SWIGLU, gemm, linear_wgrad
+from packbalance_b200.ops.gemm import EPI_BF16, EPI_F32, EPI_ROPE, EPI_SWIGLU, EPI_SWIGLU_BWD, gemm, linear_wgrad
 from packbalance_b200.parallel.flat import FlatParameters
 
 
@@ -176,11 +176,10 @@ class _Decoder(torch.autograd.Function):
         dx2 = dx2.contiguous()
         dx2b = dx2b.contiguous() if dx2b is not None else dx2.to(torch.bfloat16)
         # MLP
-        dh = torch.empty(t, F, device=dev, dtype=torch.bfloat16)
-        gemm(dx2b, flat.shadow_of(wd), dh, t, F, d, b_mn=True, epi=EPI_BF16)
-        _wgrad(flat, (wd,), dx2b, hmid)
+        # down-projection dgrad with the SwiGLU backward in its epilogue: [dg | du]
         dgu = torch.empty(t, 2 * F, device=dev, dtype=torch.bfloat16)
-        C.swiglu_bwd_packed(dh, gu, dgu)
+        gemm(dx2b, flat.shadow_of(wd), dgu, t, F, d, b_mn=True, epi=EPI_SWIGLU_BWD, aux=gu)
+        _wgrad(flat, (wd,), dx2b, hmid)
         dxn2 = torch.empty(t, d, device=dev, dtype=torch.float32)
         gemm(dgu, flat.shadow_of(wg, wu), dxn2, t, d, 2 * F, b_mn=True, epi=EPI_F32)
         _wgrad(flat, (wg, wu), dgu, xn2)

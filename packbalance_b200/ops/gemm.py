@@ -16,7 +16,7 @@ import torch
 
 from packbalance_b200.ops import _native
 
-EPI_BF16, EPI_F32, EPI_ADD_F32, EPI_SWIGLU, EPI_ROPE = 0, 1, 2, 3, 4
+EPI_BF16, EPI_F32, EPI_ADD_F32, EPI_SWIGLU, EPI_ROPE, EPI_SWIGLU_BWD = 0, 1, 2, 3, 4, 5
 EPI_CE_FWD, EPI_CE_BWD = 7, 8
 
 _SM_COUNT: dict[int, int] = {}
@@ -100,7 +100,10 @@ def gemm(
 
     ``ag``: fused all-gather of a sharded K-major B (13 ints, built by
     :meth:`packbalance_b200.parallel.sharded.ShardedParameters.gather_spec`): copy warps
-    fetch the peer-owned rows of B into this GPU's gathered buffer during the GEMM."""
+    fetch the peer-owned rows of B into this GPU's gathered buffer during the GEMM.
+
+    ``EPI_SWIGLU_BWD``: ``n`` = F, the accumulator is dh; ``aux`` holds the saved
+    ``[g | u]`` (bf16 [m, 2F]) and ``out`` receives ``[dg | du]`` (bf16 [m, 2F])."""
     if bn is None:
         allowed = (256, 128, 64)
         if epi == EPI_ROPE:

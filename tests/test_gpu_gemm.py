@@ -4,7 +4,9 @@ import pytest
 import torch
 
 from packbalance_b200.ops import _native
-from packbalance_b200.ops.gemm import EPI_ADD_F32, EPI_BF16, EPI_F32, EPI_ROPE, EPI_SWIGLU, gemm, linear_wgrad
+from packbalance_b200.ops.gemm import (
+    EPI_ADD_F32, EPI_BF16, EPI_F32, EPI_ROPE, EPI_SWIGLU, EPI_SWIGLU_BWD, gemm, linear_wgrad,
+)
 
 pytestmark = pytest.mark.gpu
 dev = "cuda"
@@ -86,6 +88,24 @@ def test_gemm_swiglu(bn):
     _close(dgu[:, F:], dh.float() * g * s)
     _close(dgu[:, :F], dh.float() * u * s * (1 + g * (1 - s)))
     _native.check_status()
+
+
+@pytest.mark.parametrize("bn", [64, 128, 256])
+def test_gemm_swiglu_bwd_epilogue(bn):
+    """Down-projection dgrad with the SwiGLU backward fused: dh = dy @ Wd stays in
+    TMEM and [dg | du] is written, against the fp32 chain dy @ Wd -> SwiGLU'."""
+    torch.manual_seed(4)
+    m, d, F = 300, 256, 416
+    dy, wd = _bf(m, d), _bf(d, F)
+    gu = _bf(m, 2 * F) * 2
+    dgu = torch.full((m, 2 * F), float("nan"), device=dev, dtype=torch.bfloat16)
+    gemm(dy, wd, dgu, m, F, d, b_mn=True, epi=EPI_SWIGLU_BWD, aux=gu, bn=bn)
+    _native.check_status()
+    dh = dy.float() @ wd.float()
+    g, u = gu.float()[:, :F], gu.float()[:, F:]
+    s = torch.sigmoid(g)
+    _close(dgu[:, :F], dh * u * s * (1 + g * (1 - s)))
+    _close(dgu[:, F:], dh * g * s)
 
 
 @pytest.mark.parametrize("hd,bn", [(64, 128), (64, 256), (128, 256), (64, 64)])
