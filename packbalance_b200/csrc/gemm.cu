@@ -4,9 +4,25 @@
 #include <c10/cuda/CUDAGuard.h>
 
 #include "gemm_kernel.cuh"
+#include "gemm_pair.cuh"
 #include "host_utils.h"
 
 namespace pb {
+
+// BN=256 launches without a fused gather and with more than 128 rows run on CTA pairs
+// (gemm_pair.cuh): mode 1 with 6 pipeline stages and 4 store-staging slots per
+// epilogue warp, mode 2 (the default: measured faster with the store-heavy epilogues)
+// with 5 stages and 8 slots; mode 0: always the single-CTA kernel.
+static int g_pair_mode = 2;
+
+int64_t gemm_pair_mode(int64_t mode) {
+  const int prev = g_pair_mode;
+  if (mode >= 0) {
+    TORCH_CHECK(mode <= 2, "gemm_pair_mode: 0, 1 or 2");
+    g_pair_mode = (int)mode;
+  }
+  return prev;
+}
 
 // ------------------------------------ host ----------------------------------------
 template <int BN, bool A_MN, bool B_MN>
@@ -24,6 +40,56 @@ static void launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const CUte
   }
   kern<<<grid, threads, C::SMEM_BYTES, stream>>>(ta, tb, to, tx, args);
   PB_CUDA_CHECK(cudaGetLastError());
+}
+
+template <bool A_MN, bool B_MN, int STAGES, int NSLOT>
+static void launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& to, const CUtensorMap& tx,
+                        const GemmArgs& args, int max_ctas, cudaStream_t stream) {
+  using PC = PairCfg<STAGES, NSLOT>;
+  auto kern = gemm_pair_kernel<A_MN, B_MN, STAGES, NSLOT>;
+  static int max_clusters[64] = {0};
+  int dev = 0;
+  PB_CUDA_CHECK(cudaGetDevice(&dev));
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cudaLaunchConfig_t cfg{};
+  cfg.blockDim = dim3(192, 1, 1);
+  cfg.dynamicSmemBytes = PC::SMEM_BYTES;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (max_clusters[dev] == 0) {
+    PB_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, PC::SMEM_BYTES));
+    cfg.gridDim = dim3(2 * (num_sms(dev) / 2), 1, 1);
+    int n = 0;
+    PB_CUDA_CHECK(cudaOccupancyMaxActiveClusters(&n, kern, &cfg));
+    max_clusters[dev] = std::max(1, n);
+  }
+  const int tiles = args.m_tiles * args.n_tiles * args.splits;
+  int clusters = std::min(tiles, max_clusters[dev]);
+  if (max_ctas > 0) clusters = std::min(clusters, std::max(1, max_ctas / 2));
+  cfg.gridDim = dim3(2 * std::max(clusters, 1), 1, 1);
+  PB_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kern, ta, tb, to, tx, args));
+}
+
+template <int STAGES, int NSLOT>
+static void dispatch_pair_cfg(bool a_mn, bool b_mn, const CUtensorMap& ta, const CUtensorMap& tb,
+                              const CUtensorMap& to, const CUtensorMap& tx, const GemmArgs& args, int max_ctas,
+                              cudaStream_t s) {
+  if (!a_mn && !b_mn) launch_pair<false, false, STAGES, NSLOT>(ta, tb, to, tx, args, max_ctas, s);
+  else if (!a_mn && b_mn) launch_pair<false, true, STAGES, NSLOT>(ta, tb, to, tx, args, max_ctas, s);
+  else if (a_mn && b_mn) launch_pair<true, true, STAGES, NSLOT>(ta, tb, to, tx, args, max_ctas, s);
+  else launch_pair<true, false, STAGES, NSLOT>(ta, tb, to, tx, args, max_ctas, s);
+}
+
+static void dispatch_pair(int mode, bool a_mn, bool b_mn, const CUtensorMap& ta, const CUtensorMap& tb,
+                          const CUtensorMap& to, const CUtensorMap& tx, const GemmArgs& args, int max_ctas,
+                          cudaStream_t s) {
+  if (mode == 2) dispatch_pair_cfg<5, 8>(a_mn, b_mn, ta, tb, to, tx, args, max_ctas, s);
+  else dispatch_pair_cfg<6, 4>(a_mn, b_mn, ta, tb, to, tx, args, max_ctas, s);
 }
 
 template <int BN>
@@ -109,7 +175,8 @@ void gemm_tc(at::Tensor a, at::Tensor b, at::Tensor out, int64_t M, int64_t N, i
   g.N = (int)N;
   g.K = (int)K;
   g.F = swiglu ? (int)(N / 2) : (swiglu_bwd ? (int)N : 0);
-  g.m_tiles = (int)((M + 127) / 128);
+  const bool pair = g_pair_mode && bn == 256 && M > 128 && ag.empty();
+  g.m_tiles = pair ? (int)((M + 255) / 256) : (int)((M + 127) / 128);
   g.n_tiles = swiglu ? (int)((N / 2 + bn / 2 - 1) / (bn / 2)) : (int)((N + bn - 1) / bn);
   g.k_blocks = (int)((K + 63) / 64);
   g.splits = (int)std::max<int64_t>(1, std::min<int64_t>(splits, g.k_blocks));
@@ -165,7 +232,7 @@ void gemm_tc(at::Tensor a, at::Tensor b, at::Tensor out, int64_t M, int64_t N, i
                         : make_tmap_bf16_2d(a.data_ptr(), K, M, a.stride(0) * 2, 64, 128);
   CUtensorMap tb;
   if (b_mn) tb = make_tmap_bf16_2d(b.data_ptr(), N, K, b.stride(0) * 2, 64, 64);
-  else tb = make_tmap_bf16_2d(b.data_ptr(), K, N, b.stride(0) * 2, 64, swiglu ? bn / 2 : bn);
+  else tb = make_tmap_bf16_2d(b.data_ptr(), K, N, b.stride(0) * 2, 64, (swiglu || pair) ? bn / 2 : bn);
 
   cudaStream_t stream0 = at::cuda::getCurrentCUDAStream();
   if (!ag.empty()) {
@@ -198,6 +265,10 @@ void gemm_tc(at::Tensor a, at::Tensor b, at::Tensor out, int64_t M, int64_t N, i
     }
     const long nblocks = (s.hi - s.lo + (1L << s.block_shift) - 1) >> s.block_shift;
     PB_CUDA_CHECK(cudaMemsetAsync(s.counters, 0, sizeof(uint32_t) * (1 + nblocks), stream0));
+  }
+  if (pair) {
+    dispatch_pair(g_pair_mode, a_mn, b_mn, ta, tb, to, tx, g, (int)max_ctas, at::cuda::getCurrentCUDAStream());
+    return;
   }
   const int tiles = g.m_tiles * g.n_tiles * g.splits;
   int grid = std::min<int>(tiles, num_sms(a.device().index()));

@@ -81,7 +81,7 @@ struct GemmArgs {
   int n_rot;  // n-blocks are visited starting at this one (wrapping)
 };
 
-constexpr int kEpiWarpBytes = 8192;  // two 4 KB staging slots per epilogue warp
+constexpr int kEpiWarpBytes = 8192;  // staging ring of one epilogue warp (Stager)
 
 template <int BN>
 struct GemmCfg {
@@ -106,24 +106,27 @@ __device__ __forceinline__ void tile_coords(const GemmArgs& a, int tile, int& mb
 }
 
 // ------------------------------- epilogue helpers ---------------------------------
-// Per-warp staging ring in shared memory for the epilogue's TMA stores: 4 slots of
-// 2 KB (a 32 x 32 bf16 box) or 2 slots of 4 KB (a 32 x 32 fp32 box), so up to 3 (or 1)
-// stores are in flight while the next box is staged.
-struct Stager {
-  uint8_t* base;  // this warp's 8 KB
+// Per-warp staging ring in shared memory for the epilogue's TMA stores: NSLOT slots of
+// 2 KB (a 32 x 32 bf16 box) or NSLOT / 2 slots of 4 KB (a 32 x 32 fp32 box), so up to
+// NSLOT - 1 (or NSLOT / 2 - 1) stores are in flight while the next box is staged.
+template <int NSLOT>
+struct StagerT {
+  static constexpr int kBytes = NSLOT * 2048;
+  uint8_t* base;  // this warp's kBytes
   int slot;
   bool wide;  // fp32 boxes
   __device__ __forceinline__ uint8_t* acquire() {
     // The store that last used this slot must have finished reading it.
     if ((threadIdx.x & 31) == 0) {
-      if (wide) bulk_wait_read<1>();
-      else bulk_wait_read<3>();
+      if (wide) bulk_wait_read<NSLOT / 2 - 1>();
+      else bulk_wait_read<NSLOT - 1>();
     }
     __syncwarp();
     return base + slot * (wide ? 4096 : 2048);
   }
-  __device__ __forceinline__ void release() { slot = (slot + 1) & (wide ? 1 : 3); }
+  __device__ __forceinline__ void release() { slot = (slot + 1) & (wide ? NSLOT / 2 - 1 : NSLOT - 1); }
 };
+using Stager = StagerT<4>;
 
 // 32 fp32 of this lane's row -> 128-byte row of a 128B-swizzled [32 x 32] fp32 box.
 __device__ __forceinline__ void stage_f32(uint8_t* s, const float (&v)[32], float scale) {
@@ -183,10 +186,26 @@ __device__ __forceinline__ void tmem_load_f32x2(uint32_t ta, float (&v)[32], uin
 
 __device__ __forceinline__ float bf16_round(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
 
-// Epilogue of one 128 x BN tile for the 32 rows [row0, row0 + 32) owned by this warp.
+// Called by an epilogue warp before it waits for the tile's accumulator: inputs of the
+// epilogue that do not depend on the MMAs start moving towards the SM (into L2) while
+// the MMAs run.
 template <int BN>
+__device__ __forceinline__ void prefetch_epilogue(const GemmArgs& a, int row0, int nb) {
+  if (a.epi != EPI_SWIGLU_BWD) return;
+  const int row = row0 + (threadIdx.x & 31);
+  if (row >= a.M) return;
+  const int c0 = nb * BN, c1 = min(c0 + BN, a.N);
+  const __nv_bfloat16* gr = a.gu + static_cast<long>(row) * 2 * a.F;
+  for (int c = c0; c < c1; c += 64) {  // 128-byte lines of g and of u
+    asm volatile("prefetch.global.L2 [%0];" ::"l"(gr + c));
+    asm volatile("prefetch.global.L2 [%0];" ::"l"(gr + a.F + c));
+  }
+}
+
+// Epilogue of one 128 x BN tile for the 32 rows [row0, row0 + 32) owned by this warp.
+template <int BN, class Stg>
 __device__ __forceinline__ void run_epilogue(const GemmArgs& a, const CUtensorMap* tm_out, const CUtensorMap* tm_aux,
-                                             Stager& st, uint32_t tacc, int row0, int nb) {
+                                             Stg& st, uint32_t tacc, int row0, int nb) {
   const int lane = threadIdx.x & 31;
   const int row = row0 + lane;
   const bool row_ok = row < a.M;
@@ -245,24 +264,25 @@ __device__ __forceinline__ void run_epilogue(const GemmArgs& a, const CUtensorMa
       // The accumulator is dh = dL/dh for h columns [nb*BN, ...); with the saved gate
       // and up pre-activations of this row it becomes dg = dh u s (1 + g (1 - s)) and
       // du = dh g s (s = sigmoid(g)), stored into [dg | du] (bf16 [M, 2F]), so dh never
-      // reaches HBM.
+      // reaches HBM.  The row's g / u segments were prefetched into L2 before the
+      // accumulator was ready (prefetch_epilogue); here the loads of the next 32 columns
+      // are in flight while the current ones are processed.
       const __nv_bfloat16* gr = a.gu + static_cast<long>(row_ok ? row : 0) * 2 * a.F;
       float u[32];
+      uint4 gv[4], uv[4], gn[4], un[4];
+      auto load = [&](int col, uint4 (&g4)[4], uint4 (&u4)[4]) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          g4[j] = row_ok && col < a.N ? __ldg(reinterpret_cast<const uint4*>(gr + col) + j) : make_uint4(0, 0, 0, 0);
+          u4[j] = row_ok && col < a.N ? __ldg(reinterpret_cast<const uint4*>(gr + a.F + col) + j) : make_uint4(0, 0, 0, 0);
+        }
+      };
+      load(nb * BN, gv, uv);
 #pragma unroll 1
       for (int c = 0; c < BN; c += 32) {
         const int col = nb * BN + c;
         if (col >= a.N) break;  // uniform across the warp
-        uint4 gv[4], uv[4];
-        if (row_ok) {
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            gv[j] = __ldg(reinterpret_cast<const uint4*>(gr + col) + j);
-            uv[j] = __ldg(reinterpret_cast<const uint4*>(gr + a.F + col) + j);
-          }
-        } else {
-#pragma unroll
-          for (int j = 0; j < 4; ++j) gv[j] = uv[j] = make_uint4(0, 0, 0, 0);
-        }
+        if (c + 32 < BN) load(col + 32, gn, un);
         tmem_load_f32(tacc + c, v);
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
@@ -288,6 +308,11 @@ __device__ __forceinline__ void run_epilogue(const GemmArgs& a, const CUtensorMa
         stage_bf16(s, u, 1.f);
         issue_store(tm_out, s, a.F + col, row0, ST_STORE);
         st.release();
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          gv[j] = gn[j];
+          uv[j] = un[j];
+        }
       }
       break;
     }
@@ -598,6 +623,7 @@ __global__ void __launch_bounds__(256, 1)
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
       int mb, nb, sp;
       tile_coords(args, tile, mb, nb, sp);
+      prefetch_epilogue<BN>(args, mb * C::BM + q * 32, nb);
       if (!mbar_wait_warp(&accf_bar[acc], acc_phase, args.status, 106, &abort_sh)) break;
       tc_fence_after();
       const uint32_t tacc = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN;

@@ -73,7 +73,7 @@ def run(args) -> list[dict]:
     from packbalance_b200.ops import _native
     from packbalance_b200.ops.attention import attention_plan, attn_backward_packed, attn_forward_packed
     from packbalance_b200.ops.cross_entropy import linear_cross_entropy
-    from packbalance_b200.ops.gemm import EPI_BF16, EPI_ROPE, EPI_SWIGLU, gemm, linear_wgrad
+    from packbalance_b200.ops.gemm import EPI_BF16, EPI_ROPE, EPI_SWIGLU, EPI_SWIGLU_BWD, gemm, linear_wgrad
     from packbalance_b200.ops.reference import rmsnorm_reference, swiglu_reference
     from packbalance_b200.ops.rmsnorm import rmsnorm
     from packbalance_b200.ops.swiglu import swiglu
@@ -140,6 +140,12 @@ def run(args) -> list[dict]:
         gu = torch.empty(m, 4096, device=dev, dtype=torch.bfloat16)
         add("gemm_fwd_gateup_swiglu", timeit(lambda: gemm(a, wgu, h, m, 4096, k, epi=EPI_SWIGLU, aux=gu), args.iters,
                                              args.warmup), flops=2.0 * m * 4096 * k, shape=[m, 4096, k])
+        dy = torch.randn(m, k, device=dev).to(torch.bfloat16)
+        wd = torch.randn(k, 2048, device=dev).to(torch.bfloat16)
+        dgu = torch.empty(m, 4096, device=dev, dtype=torch.bfloat16)
+        add("gemm_dgrad_down_swiglu_bwd", timeit(lambda: gemm(dy, wd, dgu, m, 2048, k, b_mn=True, epi=EPI_SWIGLU_BWD,
+                                                               aux=gu), args.iters, args.warmup),
+            flops=2.0 * m * 2048 * k, shape=[m, 2048, k])
         wqkv = torch.randn(1280, k, device=dev).to(torch.bfloat16)
         qkv = torch.empty(m, 1280, device=dev, dtype=torch.bfloat16)
         pos = (torch.arange(m, device=dev) % 2048).to(torch.int32)
@@ -193,7 +199,13 @@ def main() -> None:
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--output", default=None)
+    ap.add_argument("--pair", type=int, default=-1,
+                    help="GEMMs with 256-wide tiles on CTA pairs (1) or single CTAs (0); default: the library default")
     args = ap.parse_args()
+    if args.pair >= 0:
+        from packbalance_b200.ops import _native
+
+        _native.module().gemm_pair_mode(args.pair)
     res = run(args)
     if args.output:
         Path(args.output).parent.mkdir(parents=True, exist_ok=True)

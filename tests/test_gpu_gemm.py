@@ -40,6 +40,53 @@ def test_gemm_majors(bn, a_mn, b_mn, mnk):
     _close(out16, ref)
 
 
+@pytest.mark.parametrize("mode", [1, 2])
+@pytest.mark.parametrize("a_mn,b_mn", [(False, False), (False, True), (True, True), (True, False)])
+def test_gemm_cta_pair_matches_single_cta(a_mn, b_mn, mode):
+    """The 2-SM kernel (256 x 256 tiles on CTA pairs, cta_group::2 MMAs) accumulates
+    every output element over K in the same order as the single-CTA kernel: the two
+    must agree bit for bit, also with the SwiGLU epilogue (B halves split across the
+    pair) and with split-K reduce-adds of exactly representable values."""
+    torch.manual_seed(5)
+    C = _native.module()
+    m, n, k = 1000, 768, 520
+    a = _bf(k, m) if a_mn else _bf(m, k)
+    b = _bf(k, n) if b_mn else _bf(n, k)
+    outs = []
+    prev = C.gemm_pair_mode(-1)
+    try:
+        for md in (mode, 0):
+            C.gemm_pair_mode(md)
+            out = torch.empty(m, n, device=dev, dtype=torch.float32)
+            gemm(a, b, out, m, n, k, a_mn=a_mn, b_mn=b_mn, epi=EPI_F32, bn=256)
+            outs.append(out)
+            if not a_mn and not b_mn:
+                F = n // 2
+                h = torch.empty(m, F, device=dev, dtype=torch.bfloat16)
+                gu = torch.empty(m, n, device=dev, dtype=torch.bfloat16)
+                gemm(a, b, h, m, n, k, epi=EPI_SWIGLU, aux=gu, bn=256)
+                outs += [h, gu]
+        _native.check_status()
+    finally:
+        C.gemm_pair_mode(prev)
+    half = len(outs) // 2
+    for x, y in zip(outs[:half], outs[half:]):
+        assert torch.equal(x, y)
+    A = a.float().t() if a_mn else a.float()
+    B = b.float() if b_mn else b.float().t()
+    _close(outs[0], A @ B, 1e-2)
+    ints = torch.randint(-2, 3, (m, k), device=dev).to(torch.bfloat16)
+    intw = torch.randint(-2, 3, (n, k), device=dev).to(torch.bfloat16)
+    acc = torch.zeros(m, n, device=dev)
+    prev = C.gemm_pair_mode(mode)
+    try:
+        gemm(ints, intw, acc, m, n, k, epi=EPI_ADD_F32, splits=3, bn=256)
+    finally:
+        C.gemm_pair_mode(prev)
+    _native.check_status()
+    assert torch.equal(acc, ints.float() @ intw.float().t())
+
+
 def test_gemm_accumulate_and_splitk():
     torch.manual_seed(1)
     m, n, k = 384, 256, 4096
