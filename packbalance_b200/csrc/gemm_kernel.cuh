@@ -184,6 +184,34 @@ __device__ __forceinline__ void tmem_load_f32x2(uint32_t ta, float (&v)[32], uin
   }
 }
 
+// Visits the 32-column chunks [0, ncols) of this warp's accumulator lanes in order,
+// fn(c, v) with v the chunk's 32 fp32 values; the TMEM load of chunk c + 32 is in
+// flight while fn processes chunk c.
+template <class Fn>
+__device__ __forceinline__ void tmem_walk(uint32_t tacc, int ncols, Fn&& fn) {
+  uint32_t ra[32], rb[32];
+  float v[32];
+  tmem_ld32(tacc, ra);
+  tmem_wait_ld_regs(ra);
+#pragma unroll 1
+  for (int c = 0; c < ncols; c += 64) {
+    const bool has_b = c + 32 < ncols;
+    if (has_b) tmem_ld32(tacc + c + 32, rb);
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(ra[i]);
+    fn(c, v);
+    if (has_b) {
+      tmem_wait_ld_regs(rb);
+      const bool has_a = c + 64 < ncols;
+      if (has_a) tmem_ld32(tacc + c + 64, ra);
+#pragma unroll
+      for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(rb[i]);
+      fn(c + 32, v);
+      if (has_a) tmem_wait_ld_regs(ra);
+    }
+  }
+}
+
 __device__ __forceinline__ float bf16_round(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
 
 // Called by an epilogue warp before it waits for the tile's accumulator: inputs of the
@@ -214,17 +242,15 @@ __device__ __forceinline__ void run_epilogue(const GemmArgs& a, const CUtensorMa
     case EPI_BF16:
     case EPI_F32:
     case EPI_ADD_F32: {
-#pragma unroll 1
-      for (int c = 0; c < BN; c += 32) {
-        tmem_load_f32(tacc + c, v);
+      tmem_walk(tacc, BN, [&](int c, float (&x)[32]) {
         const int col = nb * BN + c;
-        if (col >= a.N) continue;  // uniform across the warp
+        if (col >= a.N) return;  // uniform across the warp
         uint8_t* s = st.acquire();
-        if (a.epi == EPI_BF16) stage_bf16(s, v, a.alpha);
-        else stage_f32(s, v, a.alpha);
+        if (a.epi == EPI_BF16) stage_bf16(s, x, a.alpha);
+        else stage_f32(s, x, a.alpha);
         issue_store(tm_out, s, col, row0, a.epi == EPI_ADD_F32 ? ST_ADD : ST_STORE);
         st.release();
-      }
+      });
       break;
     }
     case EPI_SWIGLU: {
@@ -395,28 +421,26 @@ __device__ __forceinline__ void run_epilogue(const GemmArgs& a, const CUtensorMa
     case EPI_CE_FWD: {
       float mx = -INFINITY, se = 0.f;
       const int64_t tgt = row_ok ? a.targets[row] : -1;
-#pragma unroll 1
-      for (int c = 0; c < BN; c += 32) {
-        tmem_load_f32(tacc + c, v);
+      tmem_walk(tacc, BN, [&](int c, float (&x)[32]) {
         const int col = nb * BN + c;
         const int valid = min(32, a.N - col);
-        if (valid <= 0) continue;
+        if (valid <= 0) return;
         float cm = -INFINITY;
 #pragma unroll
-        for (int i = 0; i < 32; ++i) cm = fmaxf(cm, i < valid ? v[i] : -INFINITY);
+        for (int i = 0; i < 32; ++i) cm = fmaxf(cm, i < valid ? x[i] : -INFINITY);
         const float nm = fmaxf(mx, cm);
         float s = 0.f;
 #pragma unroll
-        for (int i = 0; i < 32; ++i) s += i < valid ? __expf(v[i] - nm) : 0.f;
+        for (int i = 0; i < 32; ++i) s += i < valid ? __expf(x[i] - nm) : 0.f;
         se = se * __expf(mx - nm) + s;
         mx = nm;
         if (tgt >= col && tgt < col + valid) {
           float t = 0.f;
 #pragma unroll
-          for (int i = 0; i < 32; ++i) t = (tgt == col + i) ? v[i] : t;
+          for (int i = 0; i < 32; ++i) t = (tgt == col + i) ? x[i] : t;
           a.tlogit[row] = t;
         }
-      }
+      });
       if (row_ok) {
         a.pmax[static_cast<long>(nb) * a.M + row] = mx;
         a.psum[static_cast<long>(nb) * a.M + row] = se;
@@ -432,22 +456,20 @@ __device__ __forceinline__ void run_epilogue(const GemmArgs& a, const CUtensorMa
         tgt = a.targets[row];
         zf = 1.f + 2.f * a.z_coeff * l;
       }
-#pragma unroll 1
-      for (int c = 0; c < BN; c += 32) {
-        tmem_load_f32(tacc + c, v);
+      tmem_walk(tacc, BN, [&](int c, float (&x)[32]) {
         const int col = nb * BN + c;
-        if (col >= a.N) continue;
+        if (col >= a.N) return;
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
-          float g = __expf(v[i] - l) * zf;
+          float g = __expf(x[i] - l) * zf;
           g -= (tgt == col + i) ? 1.f : 0.f;
-          v[i] = g * scale;
+          x[i] = g * scale;
         }
         uint8_t* s = st.acquire();
-        stage_bf16(s, v, 1.f);
+        stage_bf16(s, x, 1.f);
         issue_store(tm_out, s, col, row0, ST_STORE);
         st.release();
-      }
+      });
       break;
     }
     default:
