@@ -306,10 +306,20 @@ def run_ours(args, rank, world, dev) -> None:
     h2d = batch_tensor_bytes(engine.prepare_batch(host[0]))
     d2h = 4
     if not args.no_e2e:
+        from packbalance_b200.train.engine import HostScalars
+
+        # Every step: H2D of its inputs from pinned memory (inside engine.step) and a
+        # D2H read of its global loss; the read of step i completes after step i+1 has
+        # been launched (HostScalars, lag 1), so host work overlaps the device.
+        reader = HostScalars(lag=1)
+        losses: list[float] = []
+
         def e2e_step(i):
             j = timed[i]
-            out = engine.step([host[j]], plans[j].step_tokens)  # H2D from pinned memory inside
-            float(engine.global_loss(out["loss_sum"], plans[j].step_tokens).item())  # D2H read
+            out = engine.step([host[j]], plans[j].step_tokens)
+            v = reader.push(engine.global_loss(out["loss_sum"], plans[j].step_tokens))
+            if v is not None:
+                losses.append(v)
 
         barrier()
         t0 = time.perf_counter()
@@ -317,8 +327,10 @@ def run_ours(args, rank, world, dev) -> None:
         ev0.record()
         for i in range(args.steps):
             e2e_step(i)
+        losses += reader.drain()
         ev1.record()
         torch.cuda.synchronize()
+        assert len(losses) == args.steps and all(math.isfinite(x) for x in losses), losses
         e2e_ms = max_over_ranks(ev0.elapsed_time(ev1), dev)
         barrier()
         _ = time.perf_counter() - t0

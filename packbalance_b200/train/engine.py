@@ -77,6 +77,49 @@ def _copy_into(dst: dict[str, Any], src: dict[str, Any]) -> None:
             _copy_into(v, src[k])
 
 
+def _pin(tree: dict[str, Any]) -> dict[str, Any]:
+    return {k: (_pin(v) if isinstance(v, dict) else v.pin_memory() if isinstance(v, torch.Tensor) else v)
+            for k, v in tree.items()}
+
+
+class HostScalars:
+    """Device scalars (losses, norms) read back to the host without stalling the launch
+    queue: :meth:`push` starts a non-blocking copy into pinned memory and returns the
+    value pushed ``lag`` calls earlier (``None`` until there is one), so the host
+    prepares and launches step i+1 while step i runs; :meth:`drain` returns the rest.
+    Every pushed value reaches the host."""
+
+    def __init__(self, lag: int = 1) -> None:
+        self.lag = lag
+        self._pending: list[tuple[torch.Tensor, Any]] = []
+
+    def push(self, value: torch.Tensor) -> float | None:
+        value = value.detach().reshape(())
+        if value.is_cuda:
+            buf = torch.empty((), dtype=value.dtype, pin_memory=True)
+            buf.copy_(value, non_blocking=True)
+            ev = torch.cuda.Event()
+            ev.record()
+        else:
+            buf, ev = value.clone(), None
+        self._pending.append((buf, ev))
+        if len(self._pending) > self.lag:
+            return self._pop()
+        return None
+
+    def _pop(self) -> float:
+        buf, ev = self._pending.pop(0)
+        if ev is not None:
+            ev.synchronize()
+        return float(buf)
+
+    def drain(self) -> list[float]:
+        out = []
+        while self._pending:
+            out.append(self._pop())
+        return out
+
+
 def _clone_tensors(batch: dict[str, Any]) -> dict[str, Any]:
     out: dict[str, Any] = {}
     for k, v in batch.items():
@@ -90,12 +133,18 @@ def _clone_tensors(batch: dict[str, Any]) -> dict[str, Any]:
 class _GraphedStep:
     """One captured native step with static input buffers (see the module docstring)."""
 
+    HP_RING = 4
+
     def __init__(self, engine: "TrainEngine", batch: dict[str, Any]) -> None:
         dev = engine.device
         self.static = _clone_tensors(batch)
         self.loss_scale = torch.ones((), device=dev, dtype=torch.float32)
         self.hp = torch.zeros(3, device=dev, dtype=torch.float32)  # lr, bias corrections 1 and 2
-        self.hp_host = torch.zeros(3, dtype=torch.float32).pin_memory()
+        # A ring of pinned staging buffers for ``hp``: the host may run several steps
+        # ahead of the device, and a buffer is rewritten only after its copy ran.
+        self.hp_host = [torch.zeros(3, dtype=torch.float32).pin_memory() for _ in range(self.HP_RING)]
+        self.hp_done = [torch.cuda.Event() for _ in range(self.HP_RING)]
+        self.hp_next = 0
         engine.flat.refresh_shadow()
         torch.cuda.synchronize(dev)
         from packbalance_b200.models import fused
@@ -111,8 +160,13 @@ class _GraphedStep:
     def run(self, batch: dict[str, Any], loss_scale: float, hp: tuple[float, float, float]) -> dict[str, torch.Tensor]:
         _copy_into(self.static, batch)
         self.loss_scale.fill_(loss_scale)
-        self.hp_host[0], self.hp_host[1], self.hp_host[2] = hp
-        self.hp.copy_(self.hp_host, non_blocking=True)
+        k = self.hp_next
+        self.hp_next = (k + 1) % self.HP_RING
+        self.hp_done[k].synchronize()  # the copy that last used this buffer has run
+        buf = self.hp_host[k]
+        buf[0], buf[1], buf[2] = hp
+        self.hp.copy_(buf, non_blocking=True)
+        self.hp_done[k].record()
         self.graph.replay()
         return {k: v.clone() for k, v in self.out.items()}
 
@@ -225,7 +279,12 @@ class TrainEngine:
         if self.native and "attn_plan" not in batch and isinstance(batch.get("doc_start"), torch.Tensor) \
                 and not batch["doc_start"].is_cuda:
             batch = dict(batch)
-            batch["attn_plan"] = attention_plan_host(batch["doc_start"], self.cfg.model.n_heads)
+            plan = attention_plan_host(batch["doc_start"], self.cfg.model.n_heads)
+            if self.device.type == "cuda":
+                # pinned (torch's caching host allocator), so the copy to the device is
+                # asynchronous and the host can prepare the next step meanwhile
+                plan = _pin(plan)
+            batch["attn_plan"] = plan
         return batch
 
     def _forward_backward(self, batch: dict[str, Any], loss_scale: float) -> torch.Tensor:

@@ -27,3 +27,13 @@ def test_fused_microbatches_match_loop(store, data_cfg, model_cfg, flop_model) -
         torch.testing.assert_close(o1["loss_sum"], o2["loss_sum"], atol=1e-4, rtol=1e-5)
         torch.testing.assert_close(o1["grad_norm"], o2["grad_norm"], atol=1e-5, rtol=1e-4)
     torch.testing.assert_close(e1.flat.data, e2.flat.data, atol=2e-5, rtol=1e-3)
+
+
+def test_host_scalars_lagged_reads():
+    from packbalance_b200.train.engine import HostScalars
+
+    r = HostScalars(lag=2)
+    got = [r.push(torch.tensor(float(i))) for i in range(5)]
+    assert got == [None, None, 0.0, 1.0, 2.0]
+    assert r.drain() == [3.0, 4.0]
+    assert r.drain() == []
