@@ -29,6 +29,7 @@ void embedding_bwd(at::Tensor ids, at::Tensor dx, at::Tensor grad, bool accumula
 void ce_finalize(at::Tensor pmax, at::Tensor psum, at::Tensor tlogit, at::Tensor targets, int64_t ignore_index,
                  double z, at::Tensor lse, at::Tensor loss);
 void ce_row_scale(at::Tensor targets, int64_t ignore_index, at::Tensor grad_out, at::Tensor scale);
+void ce_dlogits(at::Tensor logits, at::Tensor lse, at::Tensor targets, at::Tensor scale, double z);
 void adamw_step(at::Tensor p, at::Tensor g, at::Tensor m, at::Tensor v, at::Tensor shadow, at::Tensor norm,
                 at::Tensor skipped, double lr, double b1, double b2, double eps, double wd, double bc1, double bc2,
                 double max_norm, bool write_shadow, c10::optional<at::Tensor> hparams);
@@ -66,6 +67,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("embedding_bwd", &pb::embedding_bwd);
   m.def("ce_finalize", &pb::ce_finalize);
   m.def("ce_row_scale", &pb::ce_row_scale);
+  m.def("ce_dlogits", &pb::ce_dlogits, "in-place dlogits over kept bf16 logits");
   m.def("adamw_step", &pb::adamw_step);
   m.def("l2_norm", &pb::l2_norm);
   m.def("status_read", &pb::status_read, pybind11::arg("dev"), pybind11::arg("clear") = true);

@@ -569,6 +569,49 @@ void ce_row_scale(at::Tensor targets, int64_t ignore_index, at::Tensor grad_out,
   PB_CUDA_CHECK(cudaGetLastError());
 }
 
+// dlogits = (softmax * (1 + 2 z lse) - onehot(target)) * scale[row], in place over the
+// bf16 logits kept by the forward GEMM; 8 columns per thread, blockIdx.y = row.
+__global__ void ce_dlogits_kernel(__nv_bfloat16* __restrict__ lg, const float* __restrict__ lse,
+                                  const int64_t* __restrict__ targets, const float* __restrict__ scale, float z, int V) {
+  const long r = blockIdx.y;
+  const int c = (blockIdx.x * blockDim.x + threadIdx.x) * 8;
+  if (c >= V) return;
+  const float sc = scale[r];
+  uint4* p = reinterpret_cast<uint4*>(lg + r * V + c);
+  if (sc == 0.f) {
+    *p = make_uint4(0, 0, 0, 0);
+    return;
+  }
+  const float l = lse[r];
+  const float zf = 1.f + 2.f * z * l;
+  const int64_t t = targets[r] - c;
+  uint4 v = *p;
+  uint32_t* w = &v.x;
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const float2 x = unpack_bf16x2(w[k]);
+    const float g0 = (__expf(x.x - l) * zf - (t == 2 * k ? 1.f : 0.f)) * sc;
+    const float g1 = (__expf(x.y - l) * zf - (t == 2 * k + 1 ? 1.f : 0.f)) * sc;
+    w[k] = pack_bf16x2(g0, g1);
+  }
+  *p = v;
+}
+
+void ce_dlogits(at::Tensor logits, at::Tensor lse, at::Tensor targets, at::Tensor scale, double z) {
+  TORCH_CHECK(logits.is_contiguous() && logits.scalar_type() == at::kBFloat16 && logits.dim() == 2);
+  const int rows = logits.size(0), V = logits.size(1);
+  TORCH_CHECK(V % 8 == 0, "ce_dlogits: vocabulary must be a multiple of 8");
+  TORCH_CHECK(lse.numel() == rows && targets.numel() == rows && scale.numel() == rows);
+  TORCH_CHECK(targets.scalar_type() == at::kLong && lse.scalar_type() == at::kFloat && scale.scalar_type() == at::kFloat);
+  const c10::cuda::CUDAGuard guard(logits.device());
+  if (rows == 0) return;
+  const dim3 grid((V / 8 + 255) / 256, rows);
+  ce_dlogits_kernel<<<grid, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      reinterpret_cast<__nv_bfloat16*>(logits.data_ptr()), lse.data_ptr<float>(), targets.data_ptr<int64_t>(),
+      scale.data_ptr<float>(), (float)z, V);
+  PB_CUDA_CHECK(cudaGetLastError());
+}
+
 // ------------------------------- optimizer ----------------------------------------
 // AdamW over flat fp32 buffers; the gradient is scaled by min(1, max_norm/(norm+1e-6))
 // when max_norm > 0, and nothing changes when the norm is not finite.

@@ -226,6 +226,12 @@ void gemm_tc(at::Tensor a, at::Tensor b, at::Tensor out, int64_t M, int64_t N, i
     to = epi_map(out);
   }
   if (swiglu) tx = epi_map(*aux);
+  if (epi == EPI_CE_FWD && aux.has_value()) {
+    TORCH_CHECK(aux->scalar_type() == at::kBFloat16 && aux->size(0) == M && aux->size(1) == N,
+                "gemm_tc: CE_FWD keeps the logits in aux (bf16 [M, N])");
+    tx = epi_map(*aux);
+    g.keep_logits = 1;
+  }
 
   // Operand TMA descriptors: 128-byte swizzle, 64-element (128 B) inner box.
   CUtensorMap ta = a_mn ? make_tmap_bf16_2d(a.data_ptr(), M, K, a.stride(0) * 2, 64, 64)

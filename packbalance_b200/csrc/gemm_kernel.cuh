@@ -77,6 +77,7 @@ struct GemmArgs {
   const float* row_scale;
   float z_coeff;
   int* status;
+  int keep_logits;  // CE_FWD: also store the bf16 logits through tm_aux
   AgSpec ag;  // ag.world == 0: B is already local
   int n_rot;  // n-blocks are visited starting at this one (wrapping)
 };
@@ -425,6 +426,16 @@ __device__ __forceinline__ void run_epilogue(const GemmArgs& a, const CUtensorMa
         const int col = nb * BN + c;
         const int valid = min(32, a.N - col);
         if (valid <= 0) return;
+        if (a.keep_logits) {
+          // the statistics are taken from the stored (bf16-rounded) logits, so the
+          // backward's softmax from them is normalised against this lse
+#pragma unroll
+          for (int i = 0; i < 32; ++i) x[i] = bf16_round(x[i]);
+          uint8_t* s = st.acquire();
+          stage_bf16(s, x, 1.f);
+          issue_store(tm_aux, s, col, row0, ST_STORE);
+          st.release();
+        }
         float cm = -INFINITY;
 #pragma unroll
         for (int i = 0; i < 32; ++i) cm = fmaxf(cm, i < valid ? x[i] : -INFINITY);

@@ -200,6 +200,12 @@ class _Decoder(torch.autograd.Function):
         return (dx, dxb if ctx.has_delta else None) + (None,) * 10
 
 
+# The LM head keeps its bf16 logits for the backward (one elementwise pass instead of
+# recomputing the logits GEMM) while they take at most this many bytes; larger heads
+# recompute the logits chunk by chunk.
+LOGITS_KEEP_BYTES = 1 << 30
+
+
 class _Head(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x_prev, delta_prev, w_norm, w_lm, labels, sc: StepContext):
@@ -207,9 +213,14 @@ class _Head(torch.autograd.Function):
         C = _native.module()
         x, xf, rstd = C.add_rmsnorm_fwd(x_prev, delta_prev, w_norm, cfg.norm_eps, True)
         ag = sc.flat.gather_spec(w_lm)
-        loss, lse = lmhead_ce_forward(xf, sc.flat.shadow_of(w_lm), labels, -100, cfg.z_loss_coeff, ag=ag)
+        t = xf.shape[0]
+        keep = t * cfg.vocab_size * 2 <= LOGITS_KEEP_BYTES and cfg.vocab_size % 8 == 0
+        logits = torch.empty(t, cfg.vocab_size, device=xf.device, dtype=torch.bfloat16) if keep else None
+        loss, lse = lmhead_ce_forward(xf, sc.flat.shadow_of(w_lm), labels, -100, cfg.z_loss_coeff, ag=ag,
+                                      logits_out=logits)
         ctx.sc = sc
         ctx.has_delta = delta_prev is not None
+        ctx.logits = logits
         ctx.saved = (x, xf, rstd, lse, labels)
         ctx.params = (w_norm, w_lm)
         return loss
@@ -223,8 +234,10 @@ class _Head(torch.autograd.Function):
         ctx.saved = None
         w_norm, w_lm = ctx.params
         dxf = lmhead_ce_backward(
-            xf, flat.shadow_of(w_lm), labels, lse, grad, flat.grad_of(w_lm), flat.claim(w_lm), -100, cfg.z_loss_coeff
+            xf, flat.shadow_of(w_lm), labels, lse, grad, flat.grad_of(w_lm), flat.claim(w_lm), -100, cfg.z_loss_coeff,
+            logits=ctx.logits,
         )
+        ctx.logits = None
         dxb = torch.empty(x.shape, device=x.device, dtype=torch.bfloat16)
         dx = _native.module().rmsnorm_bwd(dxf, x, w_norm, rstd, None, dxb, flat.grad_of(w_norm).view(-1),
                                           flat.claim(w_norm))

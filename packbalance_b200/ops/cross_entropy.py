@@ -11,6 +11,12 @@ fp32 backward GEMMs).  Here:
   ``dlogits = (softmax * (1 + 2 z lse) - onehot) * dloss`` in bf16 (the only
   materialised chunk), then two GEMMs give ``dx = dlogits @ W`` and
   ``dW (+)= dlogits.T @ x`` with fp32 accumulation.
+* optionally (``logits_out`` in the forward, ``logits`` in the backward), the forward
+  GEMM also stores the bf16 logits (its statistics are then taken from the rounded
+  values) and the backward turns them into dlogits in place with one elementwise pass
+  instead of recomputing them: T x V x 2 bytes of HBM for one GEMM of 2 T d V FLOPs,
+  the trade the training step makes when the logits are small (the reference's own
+  bf16 path also takes the softmax of bf16 logits).
 
 The loss is the *sum* over labelled tokens, like the reference.  CPU tensors run the
 chunked PyTorch reference.
@@ -35,9 +41,11 @@ def lmhead_ce_forward(
     ignore_index: int = -100,
     z_coeff: float = 0.0,
     ag: list[int] | None = None,
+    logits_out: torch.Tensor | None = None,
 ) -> tuple[torch.Tensor, torch.Tensor]:
     """Returns (summed loss, lse[T]).  ``x`` [T, d] bf16, ``w`` [V, d] bf16.  ``ag``: the
-    sharded LM head is fetched inside the GEMM (see :func:`~packbalance_b200.ops.gemm.gemm`)."""
+    sharded LM head is fetched inside the GEMM (see :func:`~packbalance_b200.ops.gemm.gemm`).
+    ``logits_out`` (bf16 [T, V]): also keep the logits, for :func:`lmhead_ce_backward`."""
     t, d = x.shape
     v = w.shape[0]
     nt = -(-v // CE_TILE)
@@ -47,7 +55,8 @@ def lmhead_ce_forward(
     lse = torch.empty(t, device=x.device, dtype=torch.float32)
     loss = torch.zeros((), device=x.device, dtype=torch.float32)
     tgt = targets.reshape(-1).to(torch.int64).contiguous()
-    gemm(x, w, pmax, t, v, d, epi=EPI_CE_FWD, bn=CE_TILE, targets=tgt, pmax=pmax, psum=psum, tlogit=tlogit, ag=ag)
+    gemm(x, w, pmax, t, v, d, epi=EPI_CE_FWD, bn=CE_TILE, targets=tgt, pmax=pmax, psum=psum, tlogit=tlogit, ag=ag,
+         aux=logits_out)
     _native.module().ce_finalize(pmax, psum, tlogit, tgt, ignore_index, float(z_coeff), lse, loss)
     return loss, lse
 
@@ -63,19 +72,32 @@ def lmhead_ce_backward(
     ignore_index: int = -100,
     z_coeff: float = 0.0,
     chunk_rows: int | None = None,
+    logits: torch.Tensor | None = None,
 ) -> torch.Tensor:
-    """Returns dx [T, d] fp32; writes (or adds) dW into ``dw_out`` [V, d] fp32."""
+    """Returns dx [T, d] fp32; writes (or adds) dW into ``dw_out`` [V, d] fp32.
+    ``logits``: the forward's kept bf16 logits (overwritten with dlogits)."""
     t, d = x.shape
     v = w.shape[0]
     tgt = targets.reshape(-1).to(torch.int64).contiguous()
     scale = torch.empty(t, device=x.device, dtype=torch.float32)
     _native.module().ce_row_scale(tgt, ignore_index, grad_loss.reshape(()).float().contiguous(), scale)
+    sms = sm_count(x.device)
+    if logits is not None:
+        _native.module().ce_dlogits(logits, lse, tgt, scale, float(z_coeff))
+        dx = torch.empty(t, d, device=x.device, dtype=torch.float32)
+        bn, splits = pick_tiling(t, d, v, sms)
+        if splits > 1:
+            dx.zero_()
+            gemm(logits, w, dx, t, d, v, b_mn=True, epi=EPI_ADD_F32, bn=bn, splits=splits)
+        else:
+            gemm(logits, w, dx, t, d, v, b_mn=True, epi=EPI_F32, bn=bn)
+        linear_wgrad(logits, x, dw_out, accumulate=accumulate_dw)
+        return dx
     if chunk_rows is None:
         chunk_rows = max(128, (DLOGIT_CHUNK_BYTES // (2 * v)) // 128 * 128)
     chunk_rows = min(chunk_rows, t)
     dx = torch.empty(t, d, device=x.device, dtype=torch.float32)
     dlog = torch.empty(chunk_rows, v, device=x.device, dtype=torch.bfloat16)
-    sms = sm_count(x.device)
     for i, r0 in enumerate(range(0, t, chunk_rows)):
         r1 = min(t, r0 + chunk_rows)
         rows = r1 - r0

@@ -29,8 +29,13 @@ def _batch(t, vocab, lengths, device="cuda"):
     return ids, labels, pos, doc
 
 
+@pytest.mark.parametrize("keep_logits", [True, False])
 @pytest.mark.parametrize("tied", [True, False])
-def test_native_model_matches_reference(tied):
+def test_native_model_matches_reference(tied, keep_logits, monkeypatch):
+    from packbalance_b200.models import fused
+
+    if not keep_logits:  # the LM head recomputes its logits in the backward
+        monkeypatch.setattr(fused, "LOGITS_KEEP_BYTES", 0)
     torch.manual_seed(0)
     cfg = _cfg(tie_embeddings=tied)
     lengths = [100, 300, 57, 555]

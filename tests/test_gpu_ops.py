@@ -144,6 +144,35 @@ def test_fused_linear_ce(z, shape):
     torch.testing.assert_close(w2.grad, w1.grad, atol=2e-2, rtol=2e-2)
 
 
+@pytest.mark.parametrize("z", [0.0, 0.01])
+@pytest.mark.parametrize("t,d,v", [(700, 256, 1000), (2048, 768, 32000)])
+def test_lmhead_ce_kept_logits(z, t, d, v):
+    """Forward keeping the bf16 logits, backward from them (in-place dlogits): loss,
+    dx and dW against the chunked fp32 reference, and the kept logits against x @ W.T."""
+    from packbalance_b200.ops.cross_entropy import lmhead_ce_backward, lmhead_ce_forward
+
+    torch.manual_seed(1)
+    x = (torch.randn(t, d, device=dev) * 0.5).to(torch.bfloat16)
+    w = (torch.randn(v, d, device=dev) * 0.05).to(torch.bfloat16)
+    tgt = torch.randint(0, v, (t,), device=dev)
+    tgt[::7] = -100
+    logits = torch.empty(t, v, device=dev, dtype=torch.bfloat16)
+    loss, lse = lmhead_ce_forward(x, w, tgt, -100, z, logits_out=logits)
+    _native.check_status()
+    ref_logits = x.float() @ w.float().t()
+    torch.testing.assert_close(logits.float(), ref_logits, atol=2e-2, rtol=2e-2)
+    g = torch.tensor(0.5, device=dev)
+    dw = torch.empty(v, d, device=dev)
+    dx = lmhead_ce_backward(x, w, tgt, lse, g, dw, False, -100, z, logits=logits)
+    _native.check_status()
+    x1, w1 = x.float().requires_grad_(), w.float().requires_grad_()
+    loss1 = chunked_linear_cross_entropy(x1, w1, tgt, chunk_size=1024, z_loss_coeff=z)
+    (loss1 * 0.5).backward()
+    torch.testing.assert_close(loss, loss1.detach(), atol=2e-2 * max(1.0, abs(loss1.item()) * 1e-3), rtol=1e-3)
+    torch.testing.assert_close(dx, x1.grad, atol=2e-2, rtol=2e-2)
+    torch.testing.assert_close(dw, w1.grad, atol=2e-2, rtol=2e-2)
+
+
 def _attn_ref(qkv, doc_start, h, hk, d):
     t = qkv.shape[0]
     q = qkv[:, : h * d].float().view(t, h, d)
