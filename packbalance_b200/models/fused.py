@@ -200,10 +200,12 @@ class _Decoder(torch.autograd.Function):
         return (dx, dxb if ctx.has_delta else None) + (None,) * 10
 
 
-# The LM head keeps its bf16 logits for the backward (one elementwise pass instead of
-# recomputing the logits GEMM) while they take at most this many bytes; larger heads
-# recompute the logits chunk by chunk.
-LOGITS_KEEP_BYTES = 1 << 30
+# The LM head can keep its bf16 logits for the backward (one elementwise pass instead
+# of recomputing the logits GEMM) while they take at most this many bytes.  Off by
+# default: on B200 at 8192 x 768 x 32000 the forward GEMM becomes store-bound
+# (396 -> 607 us) and the backward gains only 132 us (1104 -> 972 us), so recomputing
+# is faster (bench_kernels --cases lmhead).
+LOGITS_KEEP_BYTES = 0
 
 
 class _Head(torch.autograd.Function):

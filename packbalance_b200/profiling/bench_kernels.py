@@ -119,6 +119,34 @@ def run(args) -> list[dict]:
             w.grad = None
 
         add("linear_ce_fused_fwd_bwd", timeit(ce, args.iters, args.warmup), flops=6.0 * t * d * v, shape=[t, d, v])
+    if "lmhead" in cases:
+        # the training step's LM head (T = 4 packs of 2048): logits recomputed in the
+        # backward vs kept from the forward, forward and backward timed separately
+        from packbalance_b200.ops.cross_entropy import lmhead_ce_backward, lmhead_ce_forward
+
+        t, d, v = args.tokens * 4, args.ce_dim, args.vocab
+        x = (torch.randn(t, d, device=dev) * 0.5).to(torch.bfloat16)
+        w = (torch.randn(v, d, device=dev) * 0.02).to(torch.bfloat16)
+        tgt = torch.randint(0, v, (t,), device=dev)
+        g = torch.tensor(1.0 / t, device=dev)
+        dw = torch.empty(v, d, device=dev)
+        logits = torch.empty(t, v, device=dev, dtype=torch.bfloat16)
+        for keep in (False, True):
+            lo = logits if keep else None
+            tag = "kept" if keep else "recomputed"
+            add(f"lmhead_fwd_{tag}", timeit(lambda: lmhead_ce_forward(x, w, tgt, logits_out=lo), args.iters,
+                                           args.warmup), flops=2.0 * t * d * v, shape=[t, d, v])
+            _, lse = lmhead_ce_forward(x, w, tgt, logits_out=lo)
+
+            def bwd():
+                if keep:
+                    lmhead_ce_forward(x, w, tgt, logits_out=lo)  # refill: the backward overwrites them
+                lmhead_ce_backward(x, w, tgt, lse, g, dw, False, logits=lo)
+
+            ms = timeit(bwd, args.iters, args.warmup)
+            if keep:
+                ms -= res[-1]["ms"]  # minus the forward that refilled the logits (timed just above)
+            add(f"lmhead_bwd_{tag}", ms, flops=(4.0 if keep else 6.0) * t * d * v, shape=[t, d, v])
     if "gemm" in cases:
         t = args.tokens * 4
         for name, (m, n, k) in {"qkv": (t, 1280, 768), "o": (t, 768, 768), "gateup": (t, 4096, 768),

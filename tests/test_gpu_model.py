@@ -34,8 +34,8 @@ def _batch(t, vocab, lengths, device="cuda"):
 def test_native_model_matches_reference(tied, keep_logits, monkeypatch):
     from packbalance_b200.models import fused
 
-    if not keep_logits:  # the LM head recomputes its logits in the backward
-        monkeypatch.setattr(fused, "LOGITS_KEEP_BYTES", 0)
+    # the LM head keeps its logits for the backward, or recomputes them
+    monkeypatch.setattr(fused, "LOGITS_KEEP_BYTES", (1 << 30) if keep_logits else 0)
     torch.manual_seed(0)
     cfg = _cfg(tie_embeddings=tied)
     lengths = [100, 300, 57, 555]
