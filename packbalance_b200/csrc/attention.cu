@@ -849,11 +849,24 @@ __global__ void __launch_bounds__(448, 1)
 }
 
 // delta[h, t] = sum_d O[t, h, d] * dO[t, h, d]; one thread per (t, h), 16-byte loads.
+// The same thread zeroes its head's D columns of the fp32 dQ accumulator row t, and
+// the dK|dV accumulator columns of heads h, h + H, ... < 2 Hkv (both receive TMA
+// reduce-adds from the backward kernel).
 __global__ void attn_delta_kernel(const __nv_bfloat16* __restrict__ o, const __nv_bfloat16* __restrict__ dout,
-                                  float* __restrict__ delta, int T, int H, int D) {
+                                  float* __restrict__ delta, int T, int H, int D, float* __restrict__ dq_acc,
+                                  float* __restrict__ dkv_acc, int Hkv) {
   const long idx = blockIdx.x * (long)blockDim.x + threadIdx.x;
   if (idx >= static_cast<long>(T) * H) return;
   const int t = static_cast<int>(idx / H), h = static_cast<int>(idx % H);
+  {
+    const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
+    float4* q4 = reinterpret_cast<float4*>(dq_acc + (static_cast<long>(t) * H + h) * D);
+    for (int i = 0; i < D / 4; ++i) q4[i] = z;
+    for (int j = h; j < 2 * Hkv; j += H) {
+      float4* k4 = reinterpret_cast<float4*>(dkv_acc + (static_cast<long>(t) * 2 * Hkv + j) * D);
+      for (int i = 0; i < D / 4; ++i) k4[i] = z;
+    }
+  }
   const uint4* a = reinterpret_cast<const uint4*>(o + static_cast<long>(t) * H * D + h * D);
   const uint4* b = reinterpret_cast<const uint4*>(dout + static_cast<long>(t) * H * D + h * D);
   // all loads of the row (D <= 128: at most 16 + 16 of 16 bytes) before any use
@@ -978,14 +991,15 @@ void attn_bwd(at::Tensor qkv, at::Tensor out, at::Tensor dout, at::Tensor lse, a
   TORCH_CHECK(doc_end.scalar_type() == at::kInt && doc_end.numel() == qkv.size(0), "attention: doc_end");
   const c10::cuda::CUDAGuard guard(qkv.device());
   const int T = qkv.size(0);
+  TORCH_CHECK(dq_acc.size(0) == T && dkv_acc.size(0) == T && delta.numel() == static_cast<long>(T) * H,
+              "attention: accumulator rows");
   if (T == 0) return;
   auto s = at::cuda::getCurrentCUDAStream();
-  PB_CUDA_CHECK(cudaMemsetAsync(dq_acc.data_ptr(), 0, dq_acc.numel() * sizeof(float), s));
-  PB_CUDA_CHECK(cudaMemsetAsync(dkv_acc.data_ptr(), 0, dkv_acc.numel() * sizeof(float), s));
   const long pairs = static_cast<long>(T) * H;
   attn_delta_kernel<<<(pairs + 255) / 256, 256, 0, s>>>(reinterpret_cast<const __nv_bfloat16*>(out.data_ptr()),
                                                       reinterpret_cast<const __nv_bfloat16*>(dout.data_ptr()),
-                                                      delta.data_ptr<float>(), T, (int)H, (int)D);
+                                                      delta.data_ptr<float>(), T, (int)H, (int)D,
+                                                      dq_acc.data_ptr<float>(), dkv_acc.data_ptr<float>(), (int)Hkv);
   PB_CUDA_CHECK(cudaGetLastError());
   CUtensorMap tq = make_tmap_bf16_2d(qkv.data_ptr(), qkv.size(1), T, qkv.stride(0) * 2, 64, 128);
   CUtensorMap td = make_tmap_bf16_2d(dout.data_ptr(), dout.size(1), T, dout.stride(0) * 2, 64, 128);
