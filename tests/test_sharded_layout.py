@@ -44,3 +44,26 @@ def test_layer_segments_follow_the_fused_gemms(model_cfg: ModelConfig) -> None:
     (qlo, qhi), (glo, ghi) = layer.segments
     assert qlo == layer.slots[0].offset and qhi == layer.slots[3].offset + layer.slots[3].numel
     assert glo == layer.slots[4].offset and ghi == layer.slots[6].offset + layer.slots[6].numel
+
+
+def test_8b_config_fits_on_b200_at_8_ranks() -> None:
+    """BASELINE config #5 (Llama-3-8B shape) on 8 ranks: the sharded engine's persistent
+    buffers per rank (bf16 gathered weights, fp32 gradient, fp32 master + moments +
+    reduced-gradient shards) leave most of a B200's 180 GB for activations.  Built on
+    the meta device: no memory is allocated."""
+    from pathlib import Path
+
+    import torch
+
+    from packbalance_b200.config import load_config
+
+    cfg = load_config(Path(__file__).resolve().parents[1] / "configs" / "b5_8b_fsdp.yaml")
+    with torch.device("meta"):
+        model = LlamaForCausalLM(cfg.model)
+    n = sum(p.numel() for p in model.parameters())
+    assert 7.9e9 < n < 8.1e9
+    lay = plan_layout(model, 8)
+    assert lay.numel >= n and lay.numel - n < 0.001 * n  # padding stays small
+    assert lay.shard_numel * 8 >= n - lay.rep_n
+    per_rank = 2 * lay.numel + 4 * lay.numel + 16 * lay.shard_numel
+    assert per_rank < 70e9, per_rank / 1e9
