@@ -9,8 +9,8 @@
 
 namespace pb {
 
-// BN=256 launches without a fused gather and with more than 128 rows run on CTA pairs
-// (gemm_pair.cuh): mode 1 with 6 pipeline stages and 4 store-staging slots per
+// BN=256 launches (and, in mode 2, BN=192 launches with a K-major B) without a fused
+// gather and with more than 128 rows run on CTA pairs (gemm_pair.cuh): mode 1 with 6 pipeline stages and 4 store-staging slots per
 // epilogue warp, mode 2 (the default: measured faster with the store-heavy epilogues)
 // with 5 stages and 8 slots; mode 0: always the single-CTA kernel.
 static int g_pair_mode = 2;
@@ -42,11 +42,11 @@ static void launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const CUte
   PB_CUDA_CHECK(cudaGetLastError());
 }
 
-template <bool A_MN, bool B_MN, int STAGES, int NSLOT>
+template <int BN, bool A_MN, bool B_MN, int STAGES, int NSLOT>
 static void launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& to, const CUtensorMap& tx,
                         const GemmArgs& args, int max_ctas, cudaStream_t stream) {
-  using PC = PairCfg<STAGES, NSLOT>;
-  auto kern = gemm_pair_kernel<A_MN, B_MN, STAGES, NSLOT>;
+  using PC = PairCfg<BN, STAGES, NSLOT>;
+  auto kern = gemm_pair_kernel<BN, A_MN, B_MN, STAGES, NSLOT>;
   static int max_clusters[64] = {0};
   int dev = 0;
   PB_CUDA_CHECK(cudaGetDevice(&dev));
@@ -79,17 +79,23 @@ template <int STAGES, int NSLOT>
 static void dispatch_pair_cfg(bool a_mn, bool b_mn, const CUtensorMap& ta, const CUtensorMap& tb,
                               const CUtensorMap& to, const CUtensorMap& tx, const GemmArgs& args, int max_ctas,
                               cudaStream_t s) {
-  if (!a_mn && !b_mn) launch_pair<false, false, STAGES, NSLOT>(ta, tb, to, tx, args, max_ctas, s);
-  else if (!a_mn && b_mn) launch_pair<false, true, STAGES, NSLOT>(ta, tb, to, tx, args, max_ctas, s);
-  else if (a_mn && b_mn) launch_pair<true, true, STAGES, NSLOT>(ta, tb, to, tx, args, max_ctas, s);
-  else launch_pair<true, false, STAGES, NSLOT>(ta, tb, to, tx, args, max_ctas, s);
+  if (!a_mn && !b_mn) launch_pair<256, false, false, STAGES, NSLOT>(ta, tb, to, tx, args, max_ctas, s);
+  else if (!a_mn && b_mn) launch_pair<256, false, true, STAGES, NSLOT>(ta, tb, to, tx, args, max_ctas, s);
+  else if (a_mn && b_mn) launch_pair<256, true, true, STAGES, NSLOT>(ta, tb, to, tx, args, max_ctas, s);
+  else launch_pair<256, true, false, STAGES, NSLOT>(ta, tb, to, tx, args, max_ctas, s);
 }
 
-static void dispatch_pair(int mode, bool a_mn, bool b_mn, const CUtensorMap& ta, const CUtensorMap& tb,
+static void dispatch_pair(int mode, int bn, bool a_mn, bool b_mn, const CUtensorMap& ta, const CUtensorMap& tb,
                           const CUtensorMap& to, const CUtensorMap& tx, const GemmArgs& args, int max_ctas,
                           cudaStream_t s) {
-  if (mode == 2) dispatch_pair_cfg<5, 8>(a_mn, b_mn, ta, tb, to, tx, args, max_ctas, s);
-  else dispatch_pair_cfg<6, 4>(a_mn, b_mn, ta, tb, to, tx, args, max_ctas, s);
+  if (bn == 192) {  // K-major B only (pair_ok)
+    if (!a_mn) launch_pair<192, false, false, 5, 8>(ta, tb, to, tx, args, max_ctas, s);
+    else launch_pair<192, true, false, 5, 8>(ta, tb, to, tx, args, max_ctas, s);
+  } else if (mode == 2) {
+    dispatch_pair_cfg<5, 8>(a_mn, b_mn, ta, tb, to, tx, args, max_ctas, s);
+  } else {
+    dispatch_pair_cfg<6, 4>(a_mn, b_mn, ta, tb, to, tx, args, max_ctas, s);
+  }
 }
 
 template <int BN>
@@ -151,7 +157,7 @@ void gemm_tc(at::Tensor a, at::Tensor b, at::Tensor out, int64_t M, int64_t N, i
   TORCH_CHECK(a.is_cuda() && b.is_cuda(), "gemm_tc: CUDA tensors required");
   TORCH_CHECK(a.scalar_type() == at::kBFloat16 && b.scalar_type() == at::kBFloat16, "gemm_tc: bf16 operands");
   TORCH_CHECK(a.dim() == 2 && b.dim() == 2 && a.stride(1) == 1 && b.stride(1) == 1, "gemm_tc: 2-D row-major");
-  TORCH_CHECK(bn == 64 || bn == 128 || bn == 256, "gemm_tc: bn must be 64/128/256");
+  TORCH_CHECK(bn == 64 || bn == 128 || bn == 192 || bn == 256, "gemm_tc: bn must be 64/128/192/256");
   const c10::cuda::CUDAGuard guard(a.device());
   const bool swiglu = epi == EPI_SWIGLU;
   if (!a_mn) {
@@ -175,7 +181,7 @@ void gemm_tc(at::Tensor a, at::Tensor b, at::Tensor out, int64_t M, int64_t N, i
   g.N = (int)N;
   g.K = (int)K;
   g.F = swiglu ? (int)(N / 2) : (swiglu_bwd ? (int)N : 0);
-  const bool pair = g_pair_mode && bn == 256 && M > 128 && ag.empty();
+  const bool pair = g_pair_mode && M > 128 && ag.empty() && (bn == 256 || (bn == 192 && !b_mn && g_pair_mode == 2));
   g.m_tiles = pair ? (int)((M + 255) / 256) : (int)((M + 127) / 128);
   g.n_tiles = swiglu ? (int)((N / 2 + bn / 2 - 1) / (bn / 2)) : (int)((N + bn - 1) / bn);
   g.k_blocks = (int)((K + 63) / 64);
@@ -273,7 +279,7 @@ void gemm_tc(at::Tensor a, at::Tensor b, at::Tensor out, int64_t M, int64_t N, i
     PB_CUDA_CHECK(cudaMemsetAsync(s.counters, 0, sizeof(uint32_t) * (1 + nblocks), stream0));
   }
   if (pair) {
-    dispatch_pair(g_pair_mode, a_mn, b_mn, ta, tb, to, tx, g, (int)max_ctas, at::cuda::getCurrentCUDAStream());
+    dispatch_pair(g_pair_mode, (int)bn, a_mn, b_mn, ta, tb, to, tx, g, (int)max_ctas, at::cuda::getCurrentCUDAStream());
     return;
   }
   const int tiles = g.m_tiles * g.n_tiles * g.splits;
@@ -282,6 +288,7 @@ void gemm_tc(at::Tensor a, at::Tensor b, at::Tensor out, int64_t M, int64_t N, i
   grid = std::max(grid, 1);
   cudaStream_t stream = at::cuda::getCurrentCUDAStream();
   if (bn == 256) dispatch_major<256>(a_mn, b_mn, ta, tb, to, tx, g, grid, stream);
+  else if (bn == 192) dispatch_major<192>(a_mn, b_mn, ta, tb, to, tx, g, grid, stream);
   else if (bn == 128) dispatch_major<128>(a_mn, b_mn, ta, tb, to, tx, g, grid, stream);
   else dispatch_major<64>(a_mn, b_mn, ta, tb, to, tx, g, grid, stream);
 }

@@ -91,9 +91,9 @@ struct GemmCfg {
   static constexpr int A_BYTES = BM * BK * 2;
   static constexpr int B_BYTES = BN * BK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int STAGES = BN == 256 ? 4 : (BN == 128 ? 6 : 8);
+  static constexpr int STAGES = BN >= 192 ? 4 : (BN == 128 ? 6 : 8);
   static constexpr int EPI_OFF = STAGES * STAGE_BYTES;
-  static constexpr uint32_t TMEM_COLS = 2 * BN;
+  static constexpr uint32_t TMEM_COLS = BN == 192 ? 512 : 2 * BN;  // allocations are powers of two
   static constexpr int SMEM_BYTES = EPI_OFF + 4 * kEpiWarpBytes + 1024;
   static_assert(SMEM_BYTES <= 232448, "shared memory budget");
 };

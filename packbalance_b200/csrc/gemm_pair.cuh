@@ -1,5 +1,5 @@
 // Pair (2-SM) variant of the tcgen05 GEMM: a cluster of two CTAs on neighbouring SMs
-// computes one 256 x 256 tile with tcgen05.mma.cta_group::2.
+// computes one 256 x BN tile (BN = 256 or 192) with tcgen05.mma.cta_group::2.
 //
 // Each CTA stages its own 128 rows of A and one half (128 rows) of the tile's B; the
 // MMA, issued by one thread of the even CTA, reads both CTAs' shared memory at the same
@@ -29,12 +29,12 @@
 
 namespace pb {
 
-// STAGES pipeline stages of 32 KB and NSLOT 2 KB store-staging slots per epilogue warp
-// share the shared memory: (6, 4) or (5, 8).
-template <int STAGES_, int NSLOT_>
+// STAGES pipeline stages and NSLOT 2 KB store-staging slots per epilogue warp share the
+// shared memory: (6, 4) or (5, 8) for BN = 256 (32 KB stages), (5, 8) for BN = 192.
+template <int BN_, int STAGES_, int NSLOT_>
 struct PairCfg {
   static constexpr int BM = 128;  // rows per CTA; the pair's tile has 2 * BM rows
-  static constexpr int BN = 256;  // columns of the pair's tile; each CTA stages BN / 2 rows of B
+  static constexpr int BN = BN_;  // columns of the pair's tile; each CTA stages BN / 2 rows of B
   static constexpr int BK = 64;
   static constexpr int A_BYTES = BM * BK * 2;
   static constexpr int B_BYTES = (BN / 2) * BK * 2;
@@ -43,7 +43,7 @@ struct PairCfg {
   static constexpr int NSLOT = NSLOT_;
   using Stg = StagerT<NSLOT>;
   static constexpr int EPI_OFF = STAGES * STAGE_BYTES;
-  static constexpr uint32_t TMEM_COLS = 2 * BN;
+  static constexpr uint32_t TMEM_COLS = BN == 192 ? 512 : 2 * BN;  // allocations are powers of two
   static constexpr int SMEM_BYTES = EPI_OFF + 4 * Stg::kBytes + 1024;
   static_assert(SMEM_BYTES <= 232448, "shared memory budget");
 };
@@ -108,15 +108,18 @@ __device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols
   asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
 }
 
+// BN is 256, or 192 with a K-major B.
 // Launched with cluster dimension (2, 1, 1) and 192 threads: warp 0 TMA producer (both
 // CTAs), warp 1 TMEM allocation (both) and MMA issuer (even CTA), warps 2-5 epilogue.
 // ``args.m_tiles`` counts 256-row tiles.
-template <bool A_MN, bool B_MN, int STAGES, int NSLOT>
+template <int BN, bool A_MN, bool B_MN, int STAGES, int NSLOT>
 __global__ void __launch_bounds__(192, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
                      const __grid_constant__ CUtensorMap tm_out, const __grid_constant__ CUtensorMap tm_aux,
                      const GemmArgs args) {
-  using C = PairCfg<STAGES, NSLOT>;
+  using C = PairCfg<BN, STAGES, NSLOT>;
+  // an MN-major B half is staged as 64-column chunks
+  static_assert(!B_MN || (BN / 2) % 64 == 0, "MN-major B needs BN / 2 to be a multiple of 64");
   constexpr uint32_t IDESC = idesc_bf16_f32(2 * C::BM, C::BN, A_MN, B_MN);
   __shared__ __align__(8) uint64_t full_bar[C::STAGES];
   __shared__ __align__(8) uint64_t empty_bar[C::STAGES];
@@ -200,8 +203,8 @@ __global__ void __launch_bounds__(192, 1)
           if (!B_MN) {
             tma_load_2d_pair(sb, &tma_b, bar, k0, row_b);
           } else {
-            tma_load_2d_pair(sb, &tma_b, bar, row_b, k0);
-            tma_load_2d_pair(sb + 8192, &tma_b, bar, row_b + 64, k0);
+#pragma unroll
+            for (int j = 0; j < C::BN / 128; ++j) tma_load_2d_pair(sb + j * 8192, &tma_b, bar, row_b + j * 64, k0);
           }
           if (++stage == C::STAGES) {
             stage = 0;

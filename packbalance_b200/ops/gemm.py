@@ -31,10 +31,10 @@ def sm_count(device: torch.device) -> int:
 
 # Relative tensor-pipe efficiency of a 128 x BN tile (narrow tiles reload the A tile
 # more often per FLOP and issue more, smaller MMAs), measured on the bench shapes.
-_TILE_EFF = {256: 1.0, 128: 0.75, 64: 0.45}
+_TILE_EFF = {256: 1.0, 192: 0.9, 128: 0.75, 64: 0.45}
 
 
-def pick_bn(m: int, n: int, sms: int, allowed=(256, 128, 64)) -> int:
+def pick_bn(m: int, n: int, sms: int, allowed=(256, 192, 128, 64)) -> int:
     """Tile width minimising waves x per-tile time, per-tile time ~ (BN + 64) / eff(BN)."""
     best, best_cost = allowed[0], math.inf
     m_tiles = -(-m // 128)
@@ -105,7 +105,7 @@ def gemm(
     ``EPI_SWIGLU_BWD``: ``n`` = F, the accumulator is dh; ``aux`` holds the saved
     ``[g | u]`` (bf16 [m, 2F]) and ``out`` receives ``[dg | du]`` (bf16 [m, 2F])."""
     if bn is None:
-        allowed = (256, 128, 64)
+        allowed = (256, 192, 128, 64)
         if epi == EPI_ROPE:
             allowed = tuple(x for x in allowed if x % head_dim == 0)
         bn = pick_bn(m, n, sm_count(a.device), allowed)

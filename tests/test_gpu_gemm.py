@@ -20,7 +20,7 @@ def _close(a, b, tol=2e-2):
     torch.testing.assert_close(a.float(), b.float(), atol=tol * max(1.0, b.abs().max().item() * 0.05), rtol=tol)
 
 
-@pytest.mark.parametrize("bn", [64, 128, 256])
+@pytest.mark.parametrize("bn", [64, 128, 192, 256])
 @pytest.mark.parametrize("a_mn,b_mn", [(False, False), (False, True), (True, True), (True, False)])
 @pytest.mark.parametrize("mnk", [(256, 512, 256), (200, 136, 72), (1024, 768, 2048)])
 def test_gemm_majors(bn, a_mn, b_mn, mnk):
@@ -40,9 +40,9 @@ def test_gemm_majors(bn, a_mn, b_mn, mnk):
     _close(out16, ref)
 
 
-@pytest.mark.parametrize("mode", [1, 2])
+@pytest.mark.parametrize("mode,bn", [(1, 256), (2, 256), (2, 192)])
 @pytest.mark.parametrize("a_mn,b_mn", [(False, False), (False, True), (True, True), (True, False)])
-def test_gemm_cta_pair_matches_single_cta(a_mn, b_mn, mode):
+def test_gemm_cta_pair_matches_single_cta(a_mn, b_mn, mode, bn):
     """The 2-SM kernel (256 x 256 tiles on CTA pairs, cta_group::2 MMAs) accumulates
     every output element over K in the same order as the single-CTA kernel: the two
     must agree bit for bit, also with the SwiGLU epilogue (B halves split across the
@@ -58,13 +58,13 @@ def test_gemm_cta_pair_matches_single_cta(a_mn, b_mn, mode):
         for md in (mode, 0):
             C.gemm_pair_mode(md)
             out = torch.empty(m, n, device=dev, dtype=torch.float32)
-            gemm(a, b, out, m, n, k, a_mn=a_mn, b_mn=b_mn, epi=EPI_F32, bn=256)
+            gemm(a, b, out, m, n, k, a_mn=a_mn, b_mn=b_mn, epi=EPI_F32, bn=bn)
             outs.append(out)
             if not a_mn and not b_mn:
                 F = n // 2
                 h = torch.empty(m, F, device=dev, dtype=torch.bfloat16)
                 gu = torch.empty(m, n, device=dev, dtype=torch.bfloat16)
-                gemm(a, b, h, m, n, k, epi=EPI_SWIGLU, aux=gu, bn=256)
+                gemm(a, b, h, m, n, k, epi=EPI_SWIGLU, aux=gu, bn=bn)
                 outs += [h, gu]
         _native.check_status()
     finally:
@@ -80,7 +80,7 @@ def test_gemm_cta_pair_matches_single_cta(a_mn, b_mn, mode):
     acc = torch.zeros(m, n, device=dev)
     prev = C.gemm_pair_mode(mode)
     try:
-        gemm(ints, intw, acc, m, n, k, epi=EPI_ADD_F32, splits=3, bn=256)
+        gemm(ints, intw, acc, m, n, k, epi=EPI_ADD_F32, splits=3, bn=bn)
     finally:
         C.gemm_pair_mode(prev)
     _native.check_status()
@@ -116,7 +116,7 @@ def test_linear_wgrad_splitk(shape, accumulate):
     _close(out, ref + (base if accumulate else 0), 1e-2)
 
 
-@pytest.mark.parametrize("bn", [64, 128, 256])
+@pytest.mark.parametrize("bn", [64, 128, 192, 256])
 def test_gemm_swiglu(bn):
     torch.manual_seed(2)
     m, d, F = 320, 256, 384
@@ -137,7 +137,7 @@ def test_gemm_swiglu(bn):
     _native.check_status()
 
 
-@pytest.mark.parametrize("bn", [64, 128, 256])
+@pytest.mark.parametrize("bn", [64, 128, 192, 256])
 def test_gemm_swiglu_bwd_epilogue(bn):
     """Down-projection dgrad with the SwiGLU backward fused: dh = dy @ Wd stays in
     TMEM and [dg | du] is written, against the fp32 chain dy @ Wd -> SwiGLU'."""
@@ -155,7 +155,7 @@ def test_gemm_swiglu_bwd_epilogue(bn):
     _close(dgu[:, F:], dh * g * s)
 
 
-@pytest.mark.parametrize("hd,bn", [(64, 128), (64, 256), (128, 256), (64, 64)])
+@pytest.mark.parametrize("hd,bn", [(64, 128), (64, 192), (64, 256), (128, 256), (64, 64)])
 def test_gemm_rope_epilogue(hd, bn):
     torch.manual_seed(3)
     t, d, h, hk = 300, 256, 4, 2
