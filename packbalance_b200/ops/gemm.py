@@ -105,7 +105,9 @@ def gemm(
     ``EPI_SWIGLU_BWD``: ``n`` = F, the accumulator is dh; ``aux`` holds the saved
     ``[g | u]`` (bf16 [m, 2F]) and ``out`` receives ``[dg | du]`` (bf16 [m, 2F])."""
     if bn is None:
-        allowed = (256, 192, 128, 64)
+        # 192-wide tiles only where they run on CTA pairs (K-major B); with an MN-major
+        # B they fall back to single CTAs, measured slower than 256-wide pairs
+        allowed = (256, 128, 64) if b_mn else (256, 192, 128, 64)
         if epi == EPI_ROPE:
             allowed = tuple(x for x in allowed if x % head_dim == 0)
         bn = pick_bn(m, n, sm_count(a.device), allowed)
