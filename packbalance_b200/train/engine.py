@@ -36,7 +36,7 @@ from torch.profiler import record_function
 from packbalance_b200.config import PackBalanceConfig
 from packbalance_b200.data.dataset import concat_packs
 from packbalance_b200.models.llama import LlamaForCausalLM
-from packbalance_b200.ops.attention import attention_plan_host, plan_to_device
+from packbalance_b200.ops.attention import PLAN_CTAS, attention_plan_host, plan_to_device
 from packbalance_b200.parallel.distributed import DataParallel
 from packbalance_b200.parallel.flat import FlatParameters
 from packbalance_b200.parallel.optim import FlatAdamW, global_grad_norm
@@ -279,7 +279,12 @@ class TrainEngine:
         if self.native and "attn_plan" not in batch and isinstance(batch.get("doc_start"), torch.Tensor) \
                 and not batch["doc_start"].is_cuda:
             batch = dict(batch)
-            plan = attention_plan_host(batch["doc_start"], self.cfg.model.n_heads)
+            ctas = PLAN_CTAS
+            if self.device.type == "cuda":
+                from packbalance_b200.ops.gemm import sm_count
+
+                ctas = sm_count(self.device)
+            plan = attention_plan_host(batch["doc_start"], self.cfg.model.n_heads, ctas)
             if self.device.type == "cuda":
                 # pinned (torch's caching host allocator), so the copy to the device is
                 # asynchronous and the host can prepare the next step meanwhile

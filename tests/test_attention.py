@@ -59,7 +59,8 @@ def test_doc_start_and_end() -> None:
 
 def test_attention_plan_orders_by_cost() -> None:
     ds = torch.cat([torch.zeros(1024, dtype=torch.int32), torch.arange(1024, 1024 + 256, dtype=torch.int32)])
-    plan = attention_plan(ds, n_heads=2, n_kv_heads=1)
+    # one CTA: the dealt order is the cost order itself
+    plan = attention_plan(ds, n_heads=2, n_kv_heads=1, n_ctas=1)
     fwd = plan["fwd"]
     assert fwd.shape == (10 * 2, 3)
     # The last q tile of the 1024-token document sees 8 key tiles and comes first.
@@ -104,3 +105,24 @@ def test_host_plan_matches_device_plan() -> None:
             devp = attention_plan(torch.from_numpy(padded), 6, 2)
             for k in ("fwd", "bwd", "doc_start", "doc_end"):
                 assert torch.equal(devp[k], host["padded"][k]), (t, k)
+
+
+def test_plan_deals_every_item_once_and_balances() -> None:
+    """The dealt work lists are a permutation of the cost-sorted items, and the busiest
+    persistent CTA's cost stays near the mean on a skewed document mix."""
+    import numpy as np
+
+    from packbalance_b200.ops.attention import TILE, _deal_order, attention_plan_host
+
+    for n, g in ((768, 148), (100, 148), (1000, 37)):
+        d = _deal_order(n, g)
+        assert sorted(d.tolist()) == list(range(n))
+    rng = np.random.default_rng(0)
+    lens = np.clip(rng.lognormal(np.log(256), 1.2, 200).astype(int), 16, 2048)
+    ds = np.concatenate([np.full(n, s) for n, s in zip(lens, np.cumsum(np.r_[0, lens[:-1]]))])[:8192]
+    plan = attention_plan_host(ds, 12, 148)
+    fwd = plan["fwd"].numpy()
+    assert len({(int(a), int(b)) for a, b, _ in fwd}) == fwd.shape[0] == (8192 // TILE) * 12
+    cost = (fwd[:, 0] - fwd[:, 2] + 1).astype(float)
+    loads = np.bincount(np.arange(len(cost)) % 148, weights=cost, minlength=148)
+    assert loads.max() / loads.mean() < 1.12
