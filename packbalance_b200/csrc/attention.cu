@@ -849,24 +849,22 @@ __global__ void __launch_bounds__(448, 1)
 }
 
 // delta[h, t] = sum_d O[t, h, d] * dO[t, h, d]; one thread per (t, h), 16-byte loads.
-// The same thread zeroes its head's D columns of the fp32 dQ accumulator row t, and
-// the dK|dV accumulator columns of heads h, h + H, ... < 2 Hkv (both receive TMA
-// reduce-adds from the backward kernel).
+// The kernel also zeroes the fp32 dQ and dK|dV accumulators (both receive TMA
+// reduce-adds from the backward kernel), consecutive threads writing consecutive
+// 16-byte words.
 __global__ void attn_delta_kernel(const __nv_bfloat16* __restrict__ o, const __nv_bfloat16* __restrict__ dout,
                                   float* __restrict__ delta, int T, int H, int D, float* __restrict__ dq_acc,
                                   float* __restrict__ dkv_acc, int Hkv) {
   const long idx = blockIdx.x * (long)blockDim.x + threadIdx.x;
-  if (idx >= static_cast<long>(T) * H) return;
-  const int t = static_cast<int>(idx / H), h = static_cast<int>(idx % H);
+  const long nthreads = static_cast<long>(gridDim.x) * blockDim.x;
   {
     const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
-    float4* q4 = reinterpret_cast<float4*>(dq_acc + (static_cast<long>(t) * H + h) * D);
-    for (int i = 0; i < D / 4; ++i) q4[i] = z;
-    for (int j = h; j < 2 * Hkv; j += H) {
-      float4* k4 = reinterpret_cast<float4*>(dkv_acc + (static_cast<long>(t) * 2 * Hkv + j) * D);
-      for (int i = 0; i < D / 4; ++i) k4[i] = z;
-    }
+    const long nq = static_cast<long>(T) * H * D / 4, nk = static_cast<long>(T) * 2 * Hkv * D / 4;
+    for (long i = idx; i < nq; i += nthreads) reinterpret_cast<float4*>(dq_acc)[i] = z;
+    for (long i = idx; i < nk; i += nthreads) reinterpret_cast<float4*>(dkv_acc)[i] = z;
   }
+  if (idx >= static_cast<long>(T) * H) return;
+  const int t = static_cast<int>(idx / H), h = static_cast<int>(idx % H);
   const uint4* a = reinterpret_cast<const uint4*>(o + static_cast<long>(t) * H * D + h * D);
   const uint4* b = reinterpret_cast<const uint4*>(dout + static_cast<long>(t) * H * D + h * D);
   // all loads of the row (D <= 128: at most 16 + 16 of 16 bytes) before any use
