@@ -1,6 +1,9 @@
 // Allocation-free C entry point: fused LM-head cross-entropy forward.
 //
-// This entry point has no counterpart in the reference implementation.
+// This entry point has no counterpart in the reference implementation.  Its interface,
+// the callers it is for, its scratch limit and its sharing rules are declared in
+// noalloc.h, which this file includes so that the compiler checks the definitions
+// against those declarations.
 //
 // Who it is for.  Some callers of this library are not allowed to allocate device
 // memory at the time they run a step: code that lives inside another runtime which
@@ -10,16 +13,6 @@
 // (which can synchronize the device) are not acceptable.  The regular extension op
 // (``gemm_tc`` + ``ce_finalize`` from Python) gets its partial-sum buffers from
 // PyTorch's allocator; this variant keeps them in a fixed static array instead.
-//
-//   int pb_lmhead_ce_forward_noalloc(x, w, targets, T, d, V, ignore_index, z_coeff,
-//                                    loss_out, lse_out, stream)
-//
-// computes, for x [T, d] bf16, w [V, d] bf16 (both row-major, 16-byte aligned rows) and
-// int64 targets [T]:  lse_out[t] = logsumexp_v(x_t . w_v)  and
-// loss_out[0] = sum over t with targets[t] != ignore_index of
-//               lse_out[t] - x_t . w_{targets[t]} + z_coeff * lse_out[t]^2,
-// the same values as the extension's fused LM-head CE forward.  The caller passes all
-// inputs and outputs; nothing is allocated.
 //
 // Scratch.  One file-scope __device__ array of kScratchFloats fp32 (16 MiB) holds the
 // per-tile row partials (2 * ceil(V / 256) * T floats) and the target logits (T floats).
@@ -36,7 +29,8 @@
 // host code must never pass the array's host-side symbol to a kernel.  That first call
 // should come before any stream capture.
 //
-// Return codes: 0 ok, 1 CUDA error, 2 size beyond the scratch limit, 3 bad argument.
+// Return codes: 0 ok, 1 CUDA error, 2 size beyond the scratch limit, 3 bad argument
+// (including a device ordinal at or above PB_NOALLOC_MAX_DEVICES).
 #include <cuda.h>
 #include <cuda_runtime.h>
 #include <cudaTypedefs.h>
@@ -48,11 +42,12 @@
 
 #include "ce_kernels.cuh"
 #include "gemm_kernel.cuh"
+#include "noalloc.h"
 
 namespace pb {
 namespace noalloc {
 
-constexpr long kScratchFloats = 4L * 1024 * 1024;  // 16 MiB
+constexpr long kScratchFloats = PB_NOALLOC_SCRATCH_FLOATS;  // 16 MiB
 constexpr int kTile = 256;                         // logits columns per CE tile
 
 __device__ __align__(256) float g_scratch[kScratchFloats];
@@ -65,7 +60,7 @@ struct DeviceState {
   int sms = 0;
 };
 
-DeviceState g_state[64];
+DeviceState g_state[PB_NOALLOC_MAX_DEVICES];
 std::mutex g_mu;
 thread_local char g_msg[512] = "";
 
@@ -102,6 +97,8 @@ bool bf16_map(CUtensorMap* m, const void* ptr, int64_t inner, int64_t outer, uin
 
 // Once per device, with the device current: device addresses of the static arrays.
 int setup(int dev, DeviceState** out) {
+  if (dev < 0 || dev >= PB_NOALLOC_MAX_DEVICES)
+    return fail(3, "device ordinal %d is outside the supported range [0, %d)", dev, PB_NOALLOC_MAX_DEVICES);
   std::lock_guard<std::mutex> lock(g_mu);
   DeviceState& s = g_state[dev];
   if (!s.ready) {
@@ -150,7 +147,7 @@ extern "C" int pb_lmhead_ce_forward_noalloc(const void* x, const void* w, const 
                                             cudaStream_t stream) {
   g_msg[0] = '\0';
   if (T <= 0 || d <= 0 || V <= 0) return fail(3, "T, d and V must be positive (got %d, %d, %d)", T, d, V);
-  const long ntiles = (V + kTile - 1) / kTile;
+  const long ntiles = (static_cast<long>(V) + kTile - 1) / kTile;
   const long need = (2 * ntiles + 1) * static_cast<long>(T);
   if (need > kScratchFloats)
     return fail(2,
@@ -169,16 +166,16 @@ extern "C" int pb_lmhead_ce_forward_noalloc(const void* x, const void* w, const 
   DeviceState* st = nullptr;
   if (int rc = setup(dev, &st)) return rc;
 
+  CUtensorMap ta, tb, unused;
+  memset(&unused, 0, sizeof(unused));
+  if (!bf16_map(&ta, x, d, T, 128) || !bf16_map(&tb, w, d, V, kTile)) return fail(1, "tensor map encoding failed");
+
   float* pmax = st->scratch;
   float* psum = pmax + ntiles * T;
   float* tlogit = psum + ntiles * T;
   if ((e = cudaMemsetAsync(tlogit, 0, sizeof(float) * T, stream)) != cudaSuccess ||
       (e = cudaMemsetAsync(loss_out, 0, sizeof(float), stream)) != cudaSuccess)
     return fail(1, "cudaMemsetAsync: %s", cudaGetErrorString(e));
-
-  CUtensorMap ta, tb, unused;
-  memset(&unused, 0, sizeof(unused));
-  if (!bf16_map(&ta, x, d, T, 128) || !bf16_map(&tb, w, d, V, kTile)) return fail(1, "tensor map encoding failed");
   GemmArgs g{};
   g.M = T;
   g.N = V;

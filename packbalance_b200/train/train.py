@@ -12,8 +12,11 @@ names follow the reference (``train/train.py:175-507``).  Differences:
 * step time is device-timed (CUDA events) and the logged throughput uses the max
   over ranks; each log record also carries the measured rank imbalance
   (max rank time / mean rank time - 1) next to the analytical one;
-* the host synchronises only at ``log_interval`` (the reference calls ``.item()`` every
-  step, ``train/train.py:380``);
+* the host never waits for the step it has just launched: step i's device time and
+  scalars are read after step i+1 is enqueued (:class:`LaggedSteps`), the loss
+  all-reduce and the cross-rank gather of step times run only at log / save steps,
+  and the run's average loss is one all-reduce at the end (the reference calls
+  ``.item()`` and synchronises every step, ``train/train.py:364-380``);
 * checkpoints carry a commit marker and RNG state, and ``keep_last`` prunes.
 """
 
@@ -61,6 +64,74 @@ def _all_reduce_sum(value: torch.Tensor) -> torch.Tensor:
     if dist.is_available() and dist.is_initialized():
         dist.all_reduce(value, op=dist.ReduceOp.SUM)
     return value
+
+
+class LaggedSteps:
+    """Step records resolved one step late, so the host never waits for the step it
+    has just launched.
+
+    :meth:`launched` is called right after step i's kernels are enqueued; it records
+    step i's end event, starts non-blocking copies of the step's device scalars into
+    pinned memory (only for records that need them), and returns the records of the
+    steps before i, now complete: waiting on step i-1's end event while step i is
+    queued behind it keeps the device busy.  :meth:`drain` returns the rest.  Every
+    record is returned exactly once, in step order, so ranks that call the
+    collectives of a returned record do so at the same steps."""
+
+    def __init__(self, cuda: bool, lag: int = 1) -> None:
+        self.cuda = cuda
+        self.lag = lag
+        self._pending: list[dict] = []
+        self._ev0 = None
+        self._t0 = 0.0
+
+    def begin(self) -> None:
+        """Mark the start of a step (before its kernels are enqueued)."""
+        self._t0 = time.perf_counter()
+        if self.cuda:
+            self._ev0 = torch.cuda.Event(enable_timing=True)
+            self._ev0.record()
+
+    def launched(self, record: dict, scalars: dict[str, torch.Tensor] | None = None) -> list[dict]:
+        """Attach timing (and, if given, host copies of ``scalars``) to ``record``."""
+        entry = {"record": record, "ev0": self._ev0, "t0": self._t0, "names": [], "host": None}
+        if self.cuda:
+            ev1 = torch.cuda.Event(enable_timing=True)
+            ev1.record()
+            entry["ev1"] = ev1
+        else:
+            entry["ms"] = (time.perf_counter() - self._t0) * 1e3
+        if scalars:
+            names = list(scalars)
+            vals = torch.stack([scalars[n].detach().reshape(()).float() for n in names])
+            if vals.is_cuda:
+                host = torch.empty(vals.shape, dtype=vals.dtype, pin_memory=True)
+                host.copy_(vals, non_blocking=True)
+            else:
+                host = vals.clone()
+            entry["names"], entry["host"] = names, host
+        self._pending.append(entry)
+        out = []
+        while len(self._pending) > self.lag:
+            out.append(self._resolve(self._pending.pop(0)))
+        return out
+
+    def drain(self) -> list[dict]:
+        out = [self._resolve(e) for e in self._pending]
+        self._pending = []
+        return out
+
+    @staticmethod
+    def _resolve(entry: dict) -> dict:
+        rec = dict(entry["record"])
+        if "ev1" in entry:
+            entry["ev1"].synchronize()
+            rec["step_ms"] = entry["ev0"].elapsed_time(entry["ev1"])
+        else:
+            rec["step_ms"] = entry["ms"]
+        if entry["host"] is not None:
+            rec.update({n: float(v) for n, v in zip(entry["names"], entry["host"].tolist())})
+        return rec
 
 
 @torch.no_grad()
@@ -171,10 +242,50 @@ def train(cfg: PackBalanceConfig, device: torch.device, resume: bool = False) ->
     loader_iter = iter(build_dataloader(store, train_packs, cfg.data, schedule.rank_indices(rank)[epoch_step * A :]))
     step = start
     run_t0 = time.perf_counter()
-    tokens_done, loss_tok_sum, data_ms_sum, logged_tokens = 0, 0.0, 0.0, 0
+    tokens_done, data_ms_sum = 0, 0.0
     window_ms: list[float] = []
     cuda = device.type == "cuda"
     ckpt_root = out_dir / "checkpoints"
+    lagged = LaggedSteps(cuda)
+    # this rank's summed token loss over the run, reduced once at the end
+    loss_acc = torch.zeros((), device=device, dtype=torch.float32)
+
+    def _log(rec: dict) -> None:
+        # Runs on every rank for every step, one step late (LaggedSteps); the
+        # collective below runs at the same log steps on every rank.
+        nonlocal window_ms
+        window_ms.append(rec["step_ms"])
+        if not rec["log"]:
+            return
+        per_rank = all_gather_floats([rec["step_ms"]], device)
+        times = [r[0] for r in per_rank]
+        t_max = max(times)
+        tps = rec["tokens"] / max(t_max / 1e3, 1e-9)
+        mfu = None
+        if cfg.train.peak_tflops > 0:
+            mfu = 3.0 * rec["cost"] / (t_max / 1e3) / (world * cfg.train.peak_tflops * 1e12)
+        logger.log(
+            {
+                "step": rec["step"],
+                "loss": rec["loss"],
+                "lr": rec["lr"],
+                "grad_norm": rec["grad_norm"],
+                "tokens_per_sec": tps,
+                "step_ms": t_max,
+                "step_ms_p99_window": float(np.percentile(window_ms, 99)),
+                "data_ms": rec["data_ms"],
+                "gpu_mem_gb": torch.cuda.max_memory_allocated() / 1e9 if cuda else None,
+                "mfu": mfu,
+                "usd_per_b_tokens": (1e9 / tps) * (world * cfg.train.gpu_hourly_cost / 3600.0) if tps > 0 else None,
+                "tokens": rec["tokens"],
+                "cost_cv": sched_stats["step_cost_cv"],
+                "rank_imbalance_measured": t_max / (sum(times) / len(times)) - 1.0,
+                "skipped": int(rec.get("skipped", 0)),
+            }
+        )
+        window_ms = []
+        if cuda:
+            torch.cuda.reset_peak_memory_stats()
 
     def _save(at: int, extra: dict) -> None:
         save_checkpoint(
@@ -193,63 +304,34 @@ def train(cfg: PackBalanceConfig, device: torch.device, resume: bool = False) ->
             with record_function("packbalance/data"):
                 packs = [next(loader_iter) for _ in range(A)]
             data_ms = (time.perf_counter() - d0) * 1e3
-            if cuda:
-                ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-                ev0.record()
-            t0 = time.perf_counter()
+            lagged.begin()
             out = engine.step(packs, plan.step_tokens)
-            if cuda:
-                ev1.record()
-            global_loss = engine.global_loss(out["loss_sum"], plan.step_tokens)
-            if cuda:
-                ev1.synchronize()
-                step_ms = ev0.elapsed_time(ev1)
-            else:
-                step_ms = (time.perf_counter() - t0) * 1e3
-            window_ms.append(step_ms)
+            lr = engine.scheduler.get_last_lr()[0]
+            loss_acc += out["loss_sum"].detach().float()
+            log_now = step % cfg.train.log_interval == 0
+            save_now = bool(cfg.train.save_interval) and (step + 1) % cfg.train.save_interval == 0
+            scalars = None
+            if log_now or save_now:
+                # the loss all-reduce runs only where a value is read, at the same
+                # steps on every rank
+                scalars = {"loss": engine.global_loss(out["loss_sum"], plan.step_tokens), "grad_norm": out["grad_norm"]}
+                if not engine.fsdp:
+                    scalars["skipped"] = engine.optimizer.last_skipped
+            record = {"step": step, "log": log_now, "tokens": plan.step_tokens, "cost": plan.step_cost,
+                      "data_ms": data_ms, "lr": lr}
+            for rec in lagged.launched(record, scalars):
+                _log(rec)
             tokens_done += plan.step_tokens
             data_ms_sum += data_ms
-
-            if step % cfg.train.log_interval == 0:
-                loss_v = float(global_loss.item())
-                loss_tok_sum += loss_v * plan.step_tokens
-                logged_tokens += plan.step_tokens
-                per_rank = all_gather_floats([step_ms], device)
-                times = [r[0] for r in per_rank]
-                t_max = max(times)
-                tps = plan.step_tokens / max(t_max / 1e3, 1e-9)
-                mfu = None
-                if cfg.train.peak_tflops > 0:
-                    mfu = 3.0 * plan.step_cost / (t_max / 1e3) / (world * cfg.train.peak_tflops * 1e12)
-                logger.log(
-                    {
-                        "step": step,
-                        "loss": loss_v,
-                        "lr": engine.scheduler.get_last_lr()[0],
-                        "grad_norm": float(out["grad_norm"].item()),
-                        "tokens_per_sec": tps,
-                        "step_ms": t_max,
-                        "step_ms_p99_window": float(np.percentile(window_ms, 99)),
-                        "data_ms": data_ms,
-                        "gpu_mem_gb": torch.cuda.max_memory_allocated() / 1e9 if cuda else None,
-                        "mfu": mfu,
-                        "usd_per_b_tokens": (1e9 / tps) * (world * cfg.train.gpu_hourly_cost / 3600.0) if tps > 0 else None,
-                        "tokens": plan.step_tokens,
-                        "cost_cv": sched_stats["step_cost_cv"],
-                        "rank_imbalance_measured": t_max / (sum(times) / len(times)) - 1.0,
-                        "skipped": int(engine.optimizer.last_skipped.item()) if not engine.fsdp else 0,
-                    }
-                )
-                window_ms = []
-                if cuda:
-                    torch.cuda.reset_peak_memory_stats()
 
             if cfg.train.eval_interval and val_packs and (step + 1) % cfg.train.eval_interval == 0:
                 metrics = evaluate(engine, store, val_packs, cfg, rank, world)
                 if is_main_process():
                     logger.log({"step": step, **metrics})
-            if cfg.train.save_interval and (step + 1) % cfg.train.save_interval == 0:
-                _save(step + 1, {"loss": float(global_loss.item()), "tokens": plan.step_tokens})
+            if save_now:
+                for rec in lagged.drain():
+                    _log(rec)
+                _save(step + 1, {"loss": float(scalars["loss"]), "tokens": plan.step_tokens})
             if prof is not None:
                 prof.step()
             step += 1
@@ -259,15 +341,18 @@ def train(cfg: PackBalanceConfig, device: torch.device, resume: bool = False) ->
             print("[train] interrupted; saving checkpoint", flush=True)
         _save(step, {"interrupted": True})
     finally:
+        for rec in lagged.drain():
+            _log(rec)
         if prof is not None:
             prof.stop()
         writer.wait()
+        total_loss = float(_all_reduce_sum(loss_acc).item())
         if step > start and is_main_process():
             logger.log(
                 {
                     "event": "finish",
                     "step": step,
-                    "avg_loss": loss_tok_sum / max(1, logged_tokens),
+                    "avg_loss": total_loss / max(1, tokens_done),
                     "tokens": tokens_done,
                     "elapsed_s": time.perf_counter() - run_t0,
                     "avg_data_ms": data_ms_sum / max(1, step - start),

@@ -1,14 +1,35 @@
+"""Shared pytest set-up.
+
+Markers: ``gpu`` (needs a B200 and the native extension; skipped where CUDA is
+absent) and ``slow``.
+
+Fixtures build a small model and corpus that keep the CPU suite fast but still
+exercise what the packer, scheduler and kernels care about:
+
+* GQA with a head dimension of 8 (3 query heads per KV head) and an odd vocabulary,
+  so no size is a power of two by accident;
+* a lognormal corpus whose tail is longer than ``max_doc_len`` (documents get split)
+  and whose head reaches below the split length;
+* ``edge_store``: a hand-written corpus with a 1-token document, documents of exactly
+  ``seq_len`` and ``seq_len + 1`` tokens and a run of very short documents, for the
+  boundary cases of packing, labels and the document-start table.
+"""
+
 from __future__ import annotations
 
 from pathlib import Path
 
+import numpy as np
 import pytest
 import torch
 
 from packbalance_b200.config import DataConfig, ModelConfig
 from packbalance_b200.data.cost import FlopModel
-from packbalance_b200.data.prepare import prepare_synthetic
+from packbalance_b200.data.prepare import prepare_synthetic, write_corpus
 from packbalance_b200.data.store import TokenStore
+
+SEQ = 80        # pack length of the fixtures
+VOCAB = 203     # odd on purpose
 
 
 def pytest_configure(config):
@@ -19,28 +40,52 @@ def pytest_configure(config):
 def pytest_collection_modifyitems(config, items):
     if torch.cuda.is_available():
         return
-    skip = pytest.mark.skip(reason="no CUDA device")
+    no_gpu = pytest.mark.skip(reason="no CUDA device")
     for item in items:
         if "gpu" in item.keywords:
-            item.add_marker(skip)
+            item.add_marker(no_gpu)
 
 
 @pytest.fixture
 def model_cfg() -> ModelConfig:
+    """2-layer GQA decoder: d 48, 6 query heads over 2 KV heads (head_dim 8)."""
     return ModelConfig(
-        vocab_size=128, d_model=32, n_layers=2, n_heads=4, n_kv_heads=2, d_ff=64, max_seq_len=64,
-        tie_embeddings=True, attention_backend="eager", compile_attention=False, use_fused_rmsnorm=True,
-        use_fused_swiglu=True, use_fused_ce=False, ce_chunk_size=16,
+        vocab_size=VOCAB,
+        d_model=48,
+        n_layers=2,
+        n_heads=6,
+        n_kv_heads=2,
+        d_ff=88,
+        max_seq_len=SEQ,
+        tie_embeddings=True,
+        attention_backend="eager",
+        compile_attention=False,
+        use_fused_ce=False,
+        ce_chunk_size=24,
     )
 
 
 @pytest.fixture
 def data_cfg(tmp_path: Path) -> DataConfig:
+    """Lognormal corpus (median ~e^3.4 = 30 tokens) with a tail past ``max_doc_len``."""
     return DataConfig(
-        dataset="synthetic", data_dir=str(tmp_path / "data"), seq_len=64, mode="isoflop", pad_batch_size=4,
-        max_doc_len=64, min_doc_len=4, synthetic_num_docs=240, synthetic_mu=3.5, synthetic_sigma=0.8,
-        synthetic_min_len=8, synthetic_max_len=120, synthetic_vocab_size=128, num_workers=0, prefetch_factor=1,
-        val_fraction=0.2, seed=7,
+        dataset="synthetic",
+        data_dir=str(tmp_path / "corpus"),
+        seq_len=SEQ,
+        mode="isoflop",
+        pad_batch_size=3,
+        max_doc_len=SEQ,
+        min_doc_len=3,
+        synthetic_num_docs=260,
+        synthetic_mu=3.4,
+        synthetic_sigma=0.9,
+        synthetic_min_len=5,
+        synthetic_max_len=170,
+        synthetic_vocab_size=VOCAB,
+        num_workers=0,
+        prefetch_factor=1,
+        val_fraction=0.15,
+        seed=11,
     )
 
 
@@ -48,6 +93,17 @@ def data_cfg(tmp_path: Path) -> DataConfig:
 def store(data_cfg: DataConfig) -> TokenStore:
     prepare_synthetic(data_cfg, Path(data_cfg.data_dir))
     return TokenStore.open(data_cfg.data_dir)
+
+
+@pytest.fixture
+def edge_store(tmp_path: Path) -> TokenStore:
+    """Corpus with the boundary lengths: 1, SEQ, SEQ + 1, and a run of 2-token docs."""
+    rng = np.random.default_rng(5)
+    lengths = [1, SEQ, SEQ + 1, 17] + [2] * 9 + [SEQ // 2, 3 * SEQ]
+    docs = [rng.integers(1, VOCAB, size=n, dtype=np.int64) for n in lengths]
+    root = tmp_path / "edge_corpus"
+    write_corpus(root, docs, {"source": "edge-fixture", "vocab_size": VOCAB})
+    return TokenStore.open(root)
 
 
 @pytest.fixture

@@ -62,3 +62,26 @@ def test_concat_packs_keeps_documents_apart(store: TokenStore, data_cfg: DataCon
     real = cat["doc_ids"][cat["doc_ids"] >= 0]
     n_docs = sum(len(p.segments) for p in packs)
     assert len(torch.unique(real)) == n_docs
+
+
+def test_one_token_documents_have_no_label(edge_store: TokenStore, data_cfg: DataConfig,
+                                           flop_model: FlopModel) -> None:
+    """A 1-token document contributes an input but no target, sits in its own
+    document (its own doc_start), and does not leak attention into its neighbours."""
+    cfg = DataConfig(**{**data_cfg.__dict__, "mode": "pack_ffd", "min_doc_len": 1, "val_fraction": 0.0})
+    packs = build_packs(edge_store, cfg, flop_model)
+    ds = PackedDataset(edge_store, packs, cfg)
+    singles = 0
+    for i, p in enumerate(packs):
+        item = ds[i]
+        starts, labels = item["doc_start"].numpy(), item["labels"].numpy()
+        off = 0
+        for seg in p.segments:
+            if seg.length == 1:
+                singles += 1
+                assert labels[off] == -100 and starts[off] == off
+                if off + 1 < cfg.seq_len:
+                    assert starts[off + 1] == off + 1
+            off += seg.length
+        assert item["useful_tokens"] == p.tokens
+    assert singles >= 2

@@ -51,5 +51,5 @@ def test_untied_head(model_cfg: ModelConfig) -> None:
 
     model = LlamaForCausalLM(replace(model_cfg, tie_embeddings=False))
     assert "lm_head.weight" in model.state_dict()
-    out = model(torch.randint(0, 128, (1, 8)))
-    assert out.logits.shape == (1, 8, 128)
+    out = model(torch.randint(0, model_cfg.vocab_size, (1, 8)))
+    assert out.logits.shape == (1, 8, model_cfg.vocab_size)

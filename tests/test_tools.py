@@ -73,3 +73,22 @@ def test_plot_metrics_writes_svg(tmp_path: Path) -> None:
     out = plot_metrics.main(["--metrics", str(log), "--output", str(tmp_path / "curve.png")])
     text = out.read_text()
     assert out.suffix == ".svg" and text.startswith("<svg") and text.count("<polyline") == 3
+
+
+def test_step_profiler_writes_window_trace_and_summary(tmp_path: Path) -> None:
+    import torch
+    from torch.profiler import record_function
+
+    from packbalance_b200.profiling.profiler import make_profiler
+
+    prof = make_profiler(tmp_path / "prof", wait=1, warmup=1, active=2)
+    with prof:
+        for _ in range(5):
+            with record_function("packbalance/forward"):
+                torch.randn(64, 64) @ torch.randn(64, 64)
+            prof.step()
+    names = sorted(p.name for p in prof.written)
+    assert names == ["summary_steps2-3.json", "trace_steps2-3.json"]
+    summary = json.loads((tmp_path / "prof" / "summary_steps2-3.json").read_text())
+    assert summary["profiled_steps"] == 2
+    assert summary["phases_ms"]["packbalance/forward"] > 0

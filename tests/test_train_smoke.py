@@ -18,12 +18,14 @@ ROOT = Path(__file__).resolve().parents[1]
 
 def _config(out: Path, data_dir: str, **train) -> PackBalanceConfig:
     return PackBalanceConfig(
-        model=ModelConfig(vocab_size=128, d_model=32, n_layers=2, n_heads=4, n_kv_heads=2, d_ff=64, max_seq_len=64,
-                          attention_backend="eager", use_fused_ce=False, ce_chunk_size=16),
-        data=DataConfig(dataset="synthetic", data_dir=data_dir, seq_len=64, mode="isoflop", pad_batch_size=4,
-                        max_doc_len=64, min_doc_len=4, synthetic_num_docs=240, synthetic_mu=3.5, synthetic_sigma=0.8,
-                        synthetic_min_len=8, synthetic_max_len=120, synthetic_vocab_size=128, num_workers=0,
-                        prefetch_factor=1, val_fraction=0.2, seed=7, schedule="balanced"),
+        # 3 layers, GQA 4/2 at head_dim 10, the odd vocabulary of the shared corpus
+        # fixture; a corpus tail past the 72-token pack length, so documents are split
+        model=ModelConfig(vocab_size=203, d_model=40, n_layers=3, n_heads=4, n_kv_heads=2, d_ff=72, max_seq_len=72,
+                          attention_backend="eager", use_fused_ce=False, ce_chunk_size=20),
+        data=DataConfig(dataset="synthetic", data_dir=data_dir, seq_len=72, mode="isoflop", pad_batch_size=3,
+                        max_doc_len=72, min_doc_len=2, synthetic_num_docs=210, synthetic_mu=3.2, synthetic_sigma=1.0,
+                        synthetic_min_len=4, synthetic_max_len=150, synthetic_vocab_size=203, num_workers=0,
+                        prefetch_factor=1, val_fraction=0.2, seed=23, schedule="balanced"),
         train=TrainConfig(**{**dict(output_dir=str(out), max_steps=2, grad_accum=1, lr=1e-3, min_lr=1e-4,
                                     warmup_steps=1, dtype="fp32", log_interval=1, save_interval=1, eval_interval=0,
                                     gpu_hourly_cost=0.0, peak_tflops=0.0), **train}),

@@ -54,9 +54,10 @@ def test_noalloc_matches_extension_op(shape, z):
         lse = torch.full((t,), float("nan"), device="cuda")
         rc = _call(f, x, w, tgt, z, loss, lse)
         assert rc == 0, lib.pb_noalloc_last_error().decode()
-        ref_loss, ref_lse = lmhead_ce_forward(x, w, tgt, -100, z)
         torch.cuda.synchronize()
         assert lib.pb_noalloc_status(1) == 0
+        ref_loss, ref_lse = lmhead_ce_forward(x, w, tgt, -100, z)
+        torch.cuda.synchronize()
         torch.testing.assert_close(lse, ref_lse, atol=1e-4, rtol=1e-5)
         torch.testing.assert_close(loss, ref_loss, atol=1e-2, rtol=1e-5)
 
@@ -75,3 +76,24 @@ def test_noalloc_rejects_sizes_beyond_scratch():
            lse.data_ptr(), stream)
     assert rc == 2
     assert "scratch" in lib.pb_noalloc_last_error().decode()
+
+
+@pytest.mark.parametrize("case", ["d_not_multiple_of_8", "x_misaligned"])
+def test_noalloc_rejects_bad_arguments_and_leaves_outputs(case):
+    """Return code 3 for a row width that is not a whole number of 16-byte pieces and
+    for an x pointer that is not 16-byte aligned; the outputs keep their contents."""
+    lib, f = _lib()
+    d = 60 if case == "d_not_multiple_of_8" else 64
+    buf = torch.zeros(8 * d + 8, device="cuda", dtype=torch.bfloat16)
+    x_ptr = buf.data_ptr() + (2 if case == "x_misaligned" else 0)
+    w = torch.zeros(256, d, device="cuda", dtype=torch.bfloat16)
+    tgt = torch.zeros(8, device="cuda", dtype=torch.long)
+    loss = torch.full((), 123.0, device="cuda")
+    lse = torch.full((8,), -7.0, device="cuda")
+    stream = torch.cuda.current_stream().cuda_stream
+    rc = f(x_ptr, w.data_ptr(), tgt.data_ptr(), 8, d, 256, -100, 0.0, loss.data_ptr(), lse.data_ptr(), stream)
+    assert rc == 3, lib.pb_noalloc_last_error().decode()
+    assert lib.pb_noalloc_last_error().decode()
+    torch.cuda.synchronize()
+    assert float(loss) == 123.0
+    assert torch.equal(lse, torch.full((8,), -7.0, device="cuda"))
