@@ -28,10 +28,11 @@ from torch import nn
 
 from packbalance_b200.config import ModelConfig
 from packbalance_b200.models.attention import attention_forward, doc_start_from_doc_ids
-from packbalance_b200.models.rope import RotaryEmbedding, apply_rotary_pos_emb
+from packbalance_b200.models.rope import RotaryEmbedding
 from packbalance_b200.ops.reference import (
     chunked_linear_cross_entropy,
     rmsnorm_reference,
+    rope_reference,
     swiglu_reference,
 )
 
@@ -77,6 +78,36 @@ class LlamaMLP(nn.Module):
         return self.down_proj(hidden)
 
 
+class KVCache:
+    """Keys and values of every layer for incremental decoding.
+
+    ``k`` / ``v``: ``[n_layers, B, capacity, n_kv_heads, head_dim]`` (keys stored after
+    RoPE); ``length`` tokens of each row are valid.  A decode pass appends the new
+    tokens of every layer at ``length`` and then advances ``length`` once.
+    """
+
+    def __init__(self, cfg: ModelConfig, batch: int, capacity: int, dtype: torch.dtype,
+                 device: torch.device) -> None:
+        shape = (cfg.n_layers, batch, capacity, cfg.n_kv_heads, cfg.head_dim)
+        self.k = torch.zeros(shape, dtype=dtype, device=device)
+        self.v = torch.zeros(shape, dtype=dtype, device=device)
+        self.length = 0
+
+    @property
+    def capacity(self) -> int:
+        return self.k.shape[2]
+
+    def extend(self, layer: int, k_new: torch.Tensor, v_new: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+        """Store ``[B, n, KV, D]`` keys/values of ``layer`` after the valid prefix and
+        return that layer's keys and values up to and including them."""
+        end = self.length + k_new.shape[1]
+        if end > self.capacity:
+            raise ValueError(f"KV cache full: {end} > {self.capacity} tokens")
+        self.k[layer, :, self.length:end] = k_new
+        self.v[layer, :, self.length:end] = v_new
+        return self.k[layer, :, :end], self.v[layer, :, :end]
+
+
 class LlamaAttention(nn.Module):
     def __init__(self, cfg: ModelConfig) -> None:
         super().__init__()
@@ -90,20 +121,39 @@ class LlamaAttention(nn.Module):
         self.attention_backend = cfg.attention_backend
         self.compile_attention = cfg.compile_attention
 
-    def forward(self, hidden, cos, sin, doc_ids, block_mask=None) -> torch.Tensor:
-        b, s, _ = hidden.shape
-        q = self.q_proj(hidden).view(b, s, self.n_heads, self.head_dim).transpose(1, 2)
-        k = self.k_proj(hidden).view(b, s, self.n_kv_heads, self.head_dim).transpose(1, 2)
-        v = self.v_proj(hidden).view(b, s, self.n_kv_heads, self.head_dim).transpose(1, 2)
-        q, k = apply_rotary_pos_emb(q, k, cos, sin)
-        out = attention_forward(
-            q, k, v, doc_ids, block_mask=block_mask, backend=self.attention_backend,
-            compile_attention=self.compile_attention,
-        )
-        return self.o_proj(out.transpose(1, 2).reshape(b, s, -1))
+    def _rotated_heads(self, hidden: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor):
+        """q | k | v from one projection (the three weights stacked, as the native QKV
+        GEMM stores them), RoPE applied to the q and k heads together.  Token-major
+        ``[B, S, heads, D]`` results; ``cos`` / ``sin`` are ``[B, S, D/2]``."""
+        h, kv = self.n_heads, self.n_kv_heads
+        w = torch.cat((self.q_proj.weight, self.k_proj.weight, self.v_proj.weight))
+        heads = F.linear(hidden, w).unflatten(-1, (h + 2 * kv, self.head_dim))
+        qk = rope_reference(heads[:, :, : h + kv], cos.unsqueeze(2), sin.unsqueeze(2))
+        return qk[:, :, :h], qk[:, :, h:], heads[:, :, h + kv:]
+
+    def forward(self, hidden, cos, sin, doc_ids, block_mask=None, cache: tuple[KVCache, int] | None = None):
+        """Packed-sequence attention (``doc_ids`` separate the documents), or, with
+        ``cache=(kv_cache, layer)``, the next tokens of each row attending to the
+        cached prefix and causally to each other."""
+        q, k, v = self._rotated_heads(hidden, cos, sin)
+        if cache is None:
+            out = attention_forward(q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2), doc_ids,
+                                    block_mask=block_mask, backend=self.attention_backend,
+                                    compile_attention=self.compile_attention).transpose(1, 2)
+        else:
+            kv_cache, layer = cache
+            past = kv_cache.length
+            k_all, v_all = kv_cache.extend(layer, k, v)
+            n, total = q.shape[1], k_all.shape[1]
+            visible = torch.arange(total, device=q.device)[None, :] <= past + torch.arange(n, device=q.device)[:, None]
+            out = F.scaled_dot_product_attention(q.transpose(1, 2), k_all.transpose(1, 2), v_all.transpose(1, 2),
+                                                 attn_mask=visible, enable_gqa=True).transpose(1, 2)
+        return self.o_proj(out.flatten(2))
 
 
 class LlamaDecoderLayer(nn.Module):
+    """Pre-norm block: ``x + attn(norm(x))`` then ``+ mlp(norm(.))``."""
+
     def __init__(self, cfg: ModelConfig) -> None:
         super().__init__()
         self.input_layernorm = RMSNorm(cfg.d_model, cfg.norm_eps, cfg.use_fused_rmsnorm)
@@ -111,9 +161,10 @@ class LlamaDecoderLayer(nn.Module):
         self.post_attention_layernorm = RMSNorm(cfg.d_model, cfg.norm_eps, cfg.use_fused_rmsnorm)
         self.mlp = LlamaMLP(cfg)
 
-    def forward(self, hidden, cos, sin, doc_ids, block_mask=None) -> torch.Tensor:
-        hidden = hidden + self.self_attn(self.input_layernorm(hidden), cos, sin, doc_ids, block_mask)
-        return hidden + self.mlp(self.post_attention_layernorm(hidden))
+    def forward(self, hidden, cos, sin, doc_ids, block_mask=None, cache: tuple[KVCache, int] | None = None):
+        mixed = self.self_attn(self.input_layernorm(hidden), cos, sin, doc_ids, block_mask, cache)
+        residual = hidden + mixed
+        return residual + self.mlp(self.post_attention_layernorm(residual))
 
 
 class LlamaModel(nn.Module):
@@ -126,17 +177,25 @@ class LlamaModel(nn.Module):
         self.rotary = RotaryEmbedding(cfg.head_dim, cfg.max_seq_len, cfg.rope_theta)
         self.gradient_checkpointing = False
 
-    def forward(self, input_ids, position_ids, doc_ids, block_mask=None) -> torch.Tensor:
-        """Reference-path decoder stack (final norm applied)."""
-        hidden = self.embed_tokens(input_ids)
+    def forward(self, input_ids, position_ids, doc_ids, block_mask=None, kv_cache: KVCache | None = None):
+        """Decoder stack on the module path (final norm applied).  With ``kv_cache``
+        the tokens continue the cached rows: their positions start at the cache
+        length, and the cache grows by their count."""
+        if kv_cache is not None:
+            position_ids = kv_cache.length + torch.arange(input_ids.shape[1], device=input_ids.device)
+            position_ids = position_ids.expand_as(input_ids)
         cos, sin = self.rotary(position_ids)
-        for layer in self.layers:
-            if self.gradient_checkpointing and self.training:
-                hidden = torch.utils.checkpoint.checkpoint(
-                    layer, hidden, cos, sin, doc_ids, block_mask, use_reentrant=False
-                )
+        hidden = self.embed_tokens(input_ids)
+        recompute = self.gradient_checkpointing and self.training and kv_cache is None
+        for i, layer in enumerate(self.layers):
+            if recompute:
+                hidden = torch.utils.checkpoint.checkpoint(layer, hidden, cos, sin, doc_ids, block_mask,
+                                                           use_reentrant=False)
             else:
-                hidden = layer(hidden, cos, sin, doc_ids, block_mask)
+                hidden = layer(hidden, cos, sin, doc_ids, block_mask,
+                               None if kv_cache is None else (kv_cache, i))
+        if kv_cache is not None:
+            kv_cache.length += input_ids.shape[1]
         return self.norm(hidden)
 
 
@@ -209,17 +268,32 @@ class LlamaForCausalLM(nn.Module):
                 )
             return fused_causal_lm_forward(self, input_ids, labels, position_ids, doc_start, attn_plan)
         hidden = self.model(input_ids, position_ids, doc_ids, block_mask)
-        if labels is None:
-            return CausalLMOutput(logits=hidden @ self.lm_head_weight.t(), hidden_states=hidden)
-        loss = chunked_linear_cross_entropy(
-            hidden,
-            self.lm_head_weight,
-            labels,
-            chunk_size=self.cfg.ce_chunk_size,
-            ignore_index=-100,
-            z_loss_coeff=self.cfg.z_loss_coeff,
-        )
-        return CausalLMOutput(loss=loss, hidden_states=hidden)
+        return self._head(hidden, labels)
+
+    def _head(self, hidden: torch.Tensor, labels: torch.Tensor | None) -> CausalLMOutput:
+        """Module-path head: the summed chunked cross-entropy (+ z-loss) against
+        ``labels``, or the logits when there are none."""
+        out = CausalLMOutput(hidden_states=hidden)
+        if labels is not None:
+            out.loss = chunked_linear_cross_entropy(hidden, self.lm_head_weight, labels,
+                                                    chunk_size=self.cfg.ce_chunk_size, ignore_index=-100,
+                                                    z_loss_coeff=self.cfg.z_loss_coeff)
+        else:
+            out.logits = F.linear(hidden, self.lm_head_weight)
+        return out
+
+    @staticmethod
+    def _pick_next(logits: torch.Tensor, temperature: float, top_k: int | None) -> torch.Tensor:
+        """``[B, V]`` fp32 logits -> ``[B, 1]`` token ids: argmax when ``temperature <=
+        0``, else a draw from softmax(logits / temperature), restricted to the
+        ``top_k`` largest logits when given."""
+        if temperature <= 0:
+            return logits.argmax(dim=-1, keepdim=True)
+        scaled = logits / temperature
+        if top_k is None:
+            return torch.multinomial(scaled.softmax(dim=-1), 1)
+        best, where = scaled.topk(min(top_k, scaled.shape[-1]), dim=-1)
+        return where.gather(-1, torch.multinomial(best.softmax(dim=-1), 1))
 
     @torch.no_grad()
     def generate(
@@ -229,27 +303,29 @@ class LlamaForCausalLM(nn.Module):
         temperature: float = 0.0,
         top_k: int | None = None,
     ) -> torch.Tensor:
-        """Greedy or temperature/top-k sampling; recomputes the prefix each token."""
+        """Continue every row of ``input_ids`` ``[B, S]`` by up to ``max_new_tokens``
+        tokens, never past ``max_seq_len`` in total.
+
+        The prompt runs through the decoder once and fills a :class:`KVCache`; each
+        further token is a one-token pass that attends to the cache, so a sequence
+        of n new tokens costs O(n) token passes instead of re-running the prefix
+        every step.  Runs on the module path (any device)."""
+        budget = min(max_new_tokens, self.cfg.max_seq_len - input_ids.shape[1])
+        if budget <= 0:
+            return input_ids
         was_training = self.training
         self.eval()
-        ids = input_ids
         try:
-            for _ in range(max_new_tokens):
-                if ids.shape[1] >= self.cfg.max_seq_len:
-                    break
-                pos = torch.arange(ids.shape[1], device=ids.device).expand_as(ids)
-                logits = self.forward(ids, position_ids=pos, doc_ids=torch.zeros_like(ids)).logits
-                last = logits[:, -1, :].float()
-                if temperature <= 0:
-                    nxt = last.argmax(dim=-1, keepdim=True)
-                else:
-                    last = last / temperature
-                    if top_k is not None:
-                        kth = torch.topk(last, min(top_k, last.shape[-1])).values[:, -1:]
-                        last = last.masked_fill(last < kth, float("-inf"))
-                    nxt = torch.multinomial(F.softmax(last, dim=-1), num_samples=1)
-                ids = torch.cat([ids, nxt.to(ids.dtype)], dim=1)
-            return ids
+            w = self.lm_head_weight
+            cache = KVCache(self.cfg, input_ids.shape[0], input_ids.shape[1] + budget, w.dtype, w.device)
+            pieces = [input_ids]
+            step_ids = input_ids
+            for i in range(budget):
+                hidden = self.model(step_ids, None, None, kv_cache=cache)
+                logits = F.linear(hidden[:, -1], w).float()
+                step_ids = self._pick_next(logits, temperature, top_k).to(input_ids.dtype)
+                pieces.append(step_ids)
+            return torch.cat(pieces, dim=1)
         finally:
             self.train(was_training)
 

@@ -53,3 +53,30 @@ def test_untied_head(model_cfg: ModelConfig) -> None:
     assert "lm_head.weight" in model.state_dict()
     out = model(torch.randint(0, model_cfg.vocab_size, (1, 8)))
     assert out.logits.shape == (1, 8, model_cfg.vocab_size)
+
+
+def test_kv_cache_generate_matches_full_recompute(model_cfg: ModelConfig) -> None:
+    """Greedy decoding with the KV cache gives the tokens that re-running the whole
+    prefix through the module path gives, for a batch of two prompts."""
+    torch.manual_seed(3)
+    model = LlamaForCausalLM(model_cfg).eval()
+    prompt = torch.randint(0, model_cfg.vocab_size, (2, 5))
+    out = model.generate(prompt, max_new_tokens=9, temperature=0.0)
+    ref = prompt
+    with torch.no_grad():
+        for _ in range(9):
+            nxt = model(ref).logits[:, -1].argmax(-1, keepdim=True)
+            ref = torch.cat([ref, nxt], dim=1)
+    assert torch.equal(out, ref)
+
+
+def test_generate_sampling_and_length_cap(model_cfg: ModelConfig) -> None:
+    torch.manual_seed(4)
+    model = LlamaForCausalLM(model_cfg)
+    prompt = torch.randint(0, model_cfg.vocab_size, (1, model_cfg.max_seq_len - 3))
+    out = model.generate(prompt, max_new_tokens=10, temperature=0.7, top_k=5)
+    assert out.shape == (1, model_cfg.max_seq_len) and torch.equal(out[:, : prompt.shape[1]], prompt)
+    assert model.training  # mode restored
+    # top_k = 1 at any temperature is greedy
+    greedy = model.generate(prompt[:, :6], max_new_tokens=4, temperature=0.0)
+    assert torch.equal(model.generate(prompt[:, :6], max_new_tokens=4, temperature=1.3, top_k=1), greedy)
