@@ -382,40 +382,11 @@ def describe_model(m) -> str:
             f"V{m.vocab_size} {tie})")
 
 
-def locate_reference() -> tuple[str | None, list[str]]:
-    """Directory to put on ``sys.path`` so that ``import packbalance`` loads the
-    unmodified reference, and a note for every place that was tried.
-
-    Tried in order: the offline install ``baseline/_ref`` (``pip install --target``);
-    ``$PB_REFERENCE_PATH``; the ``reference_path`` of ``BASELINE.json`` (a source tree
-    whose ``packbalance/`` package is pure Python and imports as it is); a
-    ``packbalance`` distribution that the interpreter already finds on its path."""
-    tried: list[str] = []
-    cands: list[tuple[str, Path]] = [("baseline/_ref", ROOT / "baseline" / "_ref")]
-    if os.environ.get("PB_REFERENCE_PATH"):
-        cands.append(("$PB_REFERENCE_PATH", Path(os.environ["PB_REFERENCE_PATH"])))
-    with contextlib.suppress(OSError, ValueError, KeyError):
-        ref = json.loads((ROOT / "BASELINE.json").read_text())["reference_path"]
-        cands.append(("BASELINE.json reference_path", Path(ref)))
-    for label, path in cands:
-        pkg = path / "packbalance"
-        if not path.exists():
-            tried.append(f"{label} ({path}): missing")
-        elif not (pkg / "train" / "train.py").exists():
-            tried.append(f"{label} ({path}): no packbalance/train/train.py")
-        else:
-            return str(path), tried
-    import importlib.util
-
-    spec = importlib.util.find_spec("packbalance")
-    if spec is not None and spec.origin and "packbalance_b200" not in spec.origin:
-        return str(Path(spec.origin).parent.parent), tried
-    tried.append("importable packbalance distribution: none")
-    return None, tried
-
-
 def run_reference(args, rank, world, dev) -> None:
-    ref_root, tried = locate_reference()
+    sys.path.insert(0, str(ROOT))
+    from packbalance_b200.utils.reference import locate_reference
+
+    ref_root, tried = locate_reference(ROOT)
     if ref_root is None:
         if rank == 0:
             print(json.dumps({"impl": "reference",

@@ -156,9 +156,19 @@ def load_checkpoint(
         import torch.distributed.checkpoint as dcp
 
         state = {"model": model.state_dict(), "optimizer": optimizer.state_dict() if optimizer is not None else {}}
+        current_groups = [dict(g) for g in state["optimizer"].get("param_groups", [])]
+        # param-group fields the writer did not have (a run without an LR scheduler has
+        # no ``initial_lr``) are not requested; they keep this run's values
+        saved = dcp.FileSystemReader(str(ckpt / "dcp")).read_metadata().state_dict_metadata
+        for i, g in enumerate(state["optimizer"].get("param_groups", [])):
+            for k in [k for k in g if k != "params" and f"optimizer.param_groups.{i}.{k}" not in saved]:
+                del g[k]
         dcp.load(state, checkpoint_id=str(ckpt / "dcp"))
         model.load_state_dict(state["model"])
         if optimizer is not None:
+            for g, cur in zip(state["optimizer"].get("param_groups", []), current_groups):
+                for k, v in cur.items():
+                    g.setdefault(k, v)
             optimizer.load_state_dict(state["optimizer"])
         meta_file = ckpt / META
         return json.loads(meta_file.read_text(encoding="utf-8")) if meta_file.exists() else {}

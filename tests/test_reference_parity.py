@@ -4,8 +4,8 @@ Both frameworks read the same corpus; the test checks that the packs and the bal
 schedule are identical, starts both models from the same weights (the reference's
 initial state dict, loaded through the shared parameter names) and compares the global
 loss of 10 training steps: the reference's step body (DDP + AdamW + clipping, its own
-modules) against ``TrainEngine.step``.  Skipped when the reference is not installed in
-``baseline/_ref``.
+modules) against ``TrainEngine.step``.  Skipped when the reference cannot be found
+(``packbalance_b200.utils.reference.locate_reference``).
 """
 
 import json
@@ -18,10 +18,12 @@ from pathlib import Path
 
 import pytest
 
-ROOT = Path(__file__).resolve().parents[1]
-REF = ROOT / "baseline" / "_ref"
+from packbalance_b200.utils.reference import locate_reference
 
-pytestmark = pytest.mark.skipif(not (REF / "packbalance").exists(), reason="reference not installed in baseline/_ref")
+ROOT = Path(__file__).resolve().parents[1]
+REF, _TRIED = locate_reference(ROOT)
+
+pytestmark = pytest.mark.skipif(REF is None, reason="reference not found: " + "; ".join(_TRIED))
 
 
 def _free_port() -> int:
