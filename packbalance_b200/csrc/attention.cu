@@ -290,33 +290,39 @@ __global__ void __launch_bounds__(320, 1)
         }
         tc_fence_after();
         const int kv0 = (kt0 + j) * 128 + grp * 64;
-        float s[64];
-#pragma unroll
-        for (int c = 0; c < 2; ++c) {
-          uint32_t v[32];
-          tmem_ld32(tmem + lane_off + C::S_COL + (g % C::S_BUFS) * 128 + grp * 64 + c * 32, v);
-          tmem_wait_ld();
-#pragma unroll
-          for (int i = 0; i < 32; ++i) s[c * 32 + i] = __uint_as_float(v[i]) * args.scale_log2;
-        }
+        // Both 32-column halves of this group's raw scores, one wait for the two loads.
+        uint32_t sv[2][32];
+        tmem_ld32(tmem + lane_off + C::S_COL + (g % C::S_BUFS) * 128 + grp * 64, sv[0]);
+        tmem_ld32(tmem + lane_off + C::S_COL + (g % C::S_BUFS) * 128 + grp * 64 + 32, sv[1]);
+        tmem_wait_ld_regs(sv[0]);
+        reg_fence(sv[1]);
         if (C::S_BUFS == 1) {
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(&s_free);
         }
-        const bool full = kv0 >= lo && kv0 + 63 <= q;
-        float mx = -INFINITY;
-        if (full) {
-#pragma unroll
-          for (int i = 0; i < 64; ++i) mx = fmaxf(mx, s[i]);
-        } else {
+        // raw score i of this thread's row (masked to -inf below)
+#define PB_S(i) __uint_as_float(sv[(i) >> 5][(i) & 31])
+        // Tiles inside every row's window (most tiles of long documents) skip the mask;
+        // the test is warp-uniform so the warp never splits over it.
+        const bool inside = kv0 >= lo && kv0 + 63 <= q;
+        if (!__all_sync(0xffffffff, inside)) {
+          const int hi = qok ? q : -1;
 #pragma unroll
           for (int i = 0; i < 64; ++i) {
             const int k = kv0 + i;
-            if (k < lo || k > q) s[i] = -INFINITY;
-            mx = fmaxf(mx, s[i]);
+            if (!(k >= lo && k <= hi)) sv[i >> 5][i & 31] = __float_as_uint(-INFINITY);
           }
         }
+        // Row max of the raw scores with eight independent chains (the scale is positive,
+        // so it is applied once to the max).
+        float mx8[8];
+#pragma unroll
+        for (int c = 0; c < 8; ++c) mx8[c] = PB_S(c);
+#pragma unroll
+        for (int i = 8; i < 64; ++i) mx8[i & 7] = fmaxf(mx8[i & 7], PB_S(i));
+        const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                               fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7]))) * args.scale_log2;
         // Lazy rescaling: the exponent base only moves when the running max grows by more
         // than 2^8 (or on the first finite max), so most tiles neither touch O nor wait
         // for the previous P V product.  Exact: O and l always share the base, and
@@ -326,15 +332,19 @@ __global__ void __launch_bounds__(320, 1)
         const bool rescale = __any_sync(0xffffffff, need);  // warp-uniform: TMEM ops below
         const float base = (rescale || m == -INFINITY) ? (m_new == -INFINITY ? 0.f : m_new) : m;
         const float corr = m == -INFINITY ? 0.f : fast_exp2(m - base);  // 1 when the base stays
-        float sum = 0.f;
+        // p = 2^(raw * scale - base): one FFMA and one ex2 per score; four partial sums.
+        const float sl2 = args.scale_log2, nb = -base;
+        float sum4[4] = {0.f, 0.f, 0.f, 0.f};
         uint32_t pk[32];
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
-          const float p0 = fast_exp2(s[2 * i] - base);
-          const float p1 = fast_exp2(s[2 * i + 1] - base);
-          sum += p0 + p1;
+          const float p0 = fast_exp2(fmaf(PB_S(2 * i), sl2, nb));
+          const float p1 = fast_exp2(fmaf(PB_S(2 * i + 1), sl2, nb));
+          sum4[i & 3] += p0 + p1;
           pk[i] = pack_bf16x2(p0, p1);
         }
+#undef PB_S
+        const float sum = (sum4[0] + sum4[1]) + (sum4[2] + sum4[3]);
         l = l * corr + sum;
         // P V products of this item that must be complete: tiles <= j - 2 (their P slot is
         // reused now) and, to rescale O, tile j - 1 too, waited tile by tile in order.
@@ -967,10 +977,10 @@ std::vector<at::Tensor> attn_fwd(at::Tensor qkv, at::Tensor doc_start, at::Tenso
   auto s = at::cuda::getCurrentCUDAStream();
   if (D == 64) {
     set_smem(attn_fwd_kernel<64>, FwdCfg<64>::SMEM);
-    attn_fwd_kernel<64><<<grid, 320, FwdCfg<64>::SMEM, s>>>(tm, a);
+    attn_fwd_kernel<64><<<pb::smem_max(attn_fwd_kernel<64>, grid), 320, FwdCfg<64>::SMEM, s>>>(tm, a);
   } else {
     set_smem(attn_fwd_kernel<128>, FwdCfg<128>::SMEM);
-    attn_fwd_kernel<128><<<grid, 320, FwdCfg<128>::SMEM, s>>>(tm, a);
+    attn_fwd_kernel<128><<<pb::smem_max(attn_fwd_kernel<128>, grid), 320, FwdCfg<128>::SMEM, s>>>(tm, a);
   }
   PB_CUDA_CHECK(cudaGetLastError());
   return {out, lse};
@@ -1022,10 +1032,10 @@ void attn_bwd(at::Tensor qkv, at::Tensor out, at::Tensor dout, at::Tensor lse, a
   const int grid = std::min<int>(a.n_items, num_sms(qkv.device().index()));
   if (D == 64) {
     set_smem(attn_bwd_kernel<64>, BwdCfg<64>::SMEM);
-    attn_bwd_kernel<64><<<grid, 448, BwdCfg<64>::SMEM, s>>>(tq, td, tdq, tdkv, a);
+    attn_bwd_kernel<64><<<pb::smem_max(attn_bwd_kernel<64>, grid), 448, BwdCfg<64>::SMEM, s>>>(tq, td, tdq, tdkv, a);
   } else {
     set_smem(attn_bwd_kernel<128>, BwdCfg<128>::SMEM);
-    attn_bwd_kernel<128><<<grid, 448, BwdCfg<128>::SMEM, s>>>(tq, td, tdq, tdkv, a);
+    attn_bwd_kernel<128><<<pb::smem_max(attn_bwd_kernel<128>, grid), 448, BwdCfg<128>::SMEM, s>>>(tq, td, tdq, tdkv, a);
   }
   PB_CUDA_CHECK(cudaGetLastError());
   const long n4 = static_cast<long>(T) * (H + 2 * Hkv) * (D / 8);

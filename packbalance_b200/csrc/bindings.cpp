@@ -7,6 +7,7 @@
 
 namespace pb {
 int64_t gemm_pair_mode(int64_t mode);
+int64_t gemm_pair_test_arm_limit(int64_t n);
 void gemm_tc(at::Tensor a, at::Tensor b, at::Tensor out, int64_t M, int64_t N, int64_t K, bool a_mn, bool b_mn,
              int64_t epi, int64_t bn, int64_t splits, int64_t max_ctas, double alpha,
              c10::optional<at::Tensor> aux, c10::optional<at::Tensor> pos, c10::optional<at::Tensor> cos_t,
@@ -56,6 +57,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "packbalance_b200 native sm_100a kernels";
   m.def("gemm_tc", &pb::gemm_tc);
   m.def("gemm_pair_mode", &pb::gemm_pair_mode, "set (0/1) or read (-1) the CTA-pair GEMM mode; returns the previous");
+  m.def("gemm_pair_test_arm_limit", &pb::gemm_pair_test_arm_limit,
+        "tests only: the even CTA of pair GEMMs stalls after arming n k-blocks (0 = off); returns the previous");
   m.def("rmsnorm_fwd", &pb::rmsnorm_fwd);
   m.def("add_rmsnorm_fwd", &pb::add_rmsnorm_fwd);
   m.def("swiglu_bwd_packed", &pb::swiglu_bwd_packed);

@@ -155,17 +155,20 @@ __global__ void __launch_bounds__(kCommThreads, kCommMinBlocks) nvls_allreduce_k
   if (!cta_barrier(a, 0, &abort_sh)) return;
   long s0, s1;
   sub_range(a, cs, sub, a.rank, s0, s1);
+  // Eight 16-byte multimem loads in flight per thread: a narrow launch (a few CTAs beside
+  // the backward pass's kernels) still keeps enough bytes in flight over NVLink.
+  constexpr int U = 8;
   float ss = 0.f;
-  const long step = static_cast<long>(blockDim.x) * 16;
+  const long step = static_cast<long>(blockDim.x) * 4 * U;
   for (long i = s0 + threadIdx.x * 4; i < s1; i += step) {
-    float4 v[4];
+    float4 v[U];
 #pragma unroll
-    for (int u = 0; u < 4; ++u) {
+    for (int u = 0; u < U; ++u) {
       const long j = i + u * blockDim.x * 4;
       if (j + 3 < s1) v[u] = mm_ld_reduce(mc + j);
     }
 #pragma unroll
-    for (int u = 0; u < 4; ++u) {
+    for (int u = 0; u < U; ++u) {
       const long j = i + u * blockDim.x * 4;
       if (j + 3 < s1) {
         float4 x = v[u];
@@ -213,7 +216,7 @@ void nvls_allreduce(int64_t ptrs_dev, int64_t pads_dev, int64_t pad_words, int64
   a.scale = (float)scale;
   a.sumsq = local_sumsq.data_ptr<float>();
   a.status = status_ptr(local_sumsq.device().index());
-  nvls_allreduce_kernel<<<(int)ctas, kCommThreads, 0, at::cuda::getCurrentCUDAStream()>>>(
+  nvls_allreduce_kernel<<<pb::smem_max(nvls_allreduce_kernel, (int)ctas), kCommThreads, 0, at::cuda::getCurrentCUDAStream()>>>(
       a, reinterpret_cast<float*>(mc_ptr), reinterpret_cast<float*>(mc_sumsq));
   PB_CUDA_CHECK(cudaGetLastError());
 }
@@ -240,13 +243,13 @@ void fused_allreduce(int64_t ptrs_dev, int64_t pads_dev, int64_t pad_words, int6
   a.status = status_ptr(sumsq.device().index());
   auto st = at::cuda::getCurrentCUDAStream();
   switch (world) {
-    case 2: fused_allreduce_kernel<2><<<(int)ctas, kCommThreads, 0, st>>>(a); break;
-    case 3: fused_allreduce_kernel<3><<<(int)ctas, kCommThreads, 0, st>>>(a); break;
-    case 4: fused_allreduce_kernel<4><<<(int)ctas, kCommThreads, 0, st>>>(a); break;
-    case 5: fused_allreduce_kernel<5><<<(int)ctas, kCommThreads, 0, st>>>(a); break;
-    case 6: fused_allreduce_kernel<6><<<(int)ctas, kCommThreads, 0, st>>>(a); break;
-    case 7: fused_allreduce_kernel<7><<<(int)ctas, kCommThreads, 0, st>>>(a); break;
-    case 8: fused_allreduce_kernel<8><<<(int)ctas, kCommThreads, 0, st>>>(a); break;
+    case 2: fused_allreduce_kernel<2><<<pb::smem_max(fused_allreduce_kernel<2>, (int)ctas), kCommThreads, 0, st>>>(a); break;
+    case 3: fused_allreduce_kernel<3><<<pb::smem_max(fused_allreduce_kernel<3>, (int)ctas), kCommThreads, 0, st>>>(a); break;
+    case 4: fused_allreduce_kernel<4><<<pb::smem_max(fused_allreduce_kernel<4>, (int)ctas), kCommThreads, 0, st>>>(a); break;
+    case 5: fused_allreduce_kernel<5><<<pb::smem_max(fused_allreduce_kernel<5>, (int)ctas), kCommThreads, 0, st>>>(a); break;
+    case 6: fused_allreduce_kernel<6><<<pb::smem_max(fused_allreduce_kernel<6>, (int)ctas), kCommThreads, 0, st>>>(a); break;
+    case 7: fused_allreduce_kernel<7><<<pb::smem_max(fused_allreduce_kernel<7>, (int)ctas), kCommThreads, 0, st>>>(a); break;
+    case 8: fused_allreduce_kernel<8><<<pb::smem_max(fused_allreduce_kernel<8>, (int)ctas), kCommThreads, 0, st>>>(a); break;
     default: TORCH_CHECK(false, "fused_allreduce: world size 2..8 on one node");
   }
   PB_CUDA_CHECK(cudaGetLastError());
@@ -258,7 +261,7 @@ __global__ void epoch_bump_kernel(uint32_t* base, uint32_t inc) { *base += inc; 
 void epoch_bump(at::Tensor base, int64_t inc) {
   TORCH_CHECK(base.is_cuda() && base.scalar_type() == at::kInt && base.numel() >= 1, "epoch_bump: int32 CUDA tensor");
   const c10::cuda::CUDAGuard guard(base.device());
-  epoch_bump_kernel<<<1, 1, 0, at::cuda::getCurrentCUDAStream()>>>(reinterpret_cast<uint32_t*>(base.data_ptr()),
+  epoch_bump_kernel<<<pb::smem_max(epoch_bump_kernel, 1), 1, 0, at::cuda::getCurrentCUDAStream()>>>(reinterpret_cast<uint32_t*>(base.data_ptr()),
                                                                      static_cast<uint32_t>(inc));
   PB_CUDA_CHECK(cudaGetLastError());
 }

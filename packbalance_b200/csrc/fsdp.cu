@@ -103,15 +103,17 @@ __device__ __forceinline__ float rs_chunk_mc(const float* mc, long c0, long c1, 
   const long sub = ((n + gridDim.x - 1) / gridDim.x + 3) / 4 * 4;
   const long s0 = min(c0 + static_cast<long>(blockIdx.x) * sub, c1);
   const long s1 = min(s0 + sub, c1);
+  // eight 16-byte multimem loads in flight per thread (narrow launches beside compute)
+  constexpr int U = 8;
   float ss = 0.f;
   const long stride = static_cast<long>(blockDim.x) * 4;
-  for (long i = s0 + threadIdx.x * 4; i < s1; i += 4 * stride) {
-    float4 v[4];
+  for (long i = s0 + threadIdx.x * 4; i < s1; i += U * stride) {
+    float4 v[U];
 #pragma unroll
-    for (int u = 0; u < 4; ++u)
+    for (int u = 0; u < U; ++u)
       if (i + u * stride < s1) v[u] = mm_ld_reduce(mc + i + u * stride);
 #pragma unroll
-    for (int u = 0; u < 4; ++u) {
+    for (int u = 0; u < U; ++u) {
       const long j = i + u * stride;
       if (j < s1) {
         float4 acc = v[u];
@@ -314,13 +316,13 @@ void fsdp_reduce_scatter(int64_t gptrs_dev, int64_t pads_dev, int64_t pad_words,
   const float* m = reinterpret_cast<const float*>(mc);
   auto st = at::cuda::getCurrentCUDAStream();
   switch (world) {
-    case 2: fsdp_reduce_scatter_kernel<2><<<(int)ctas, kCommThreads, 0, st>>>(a, o, m); break;
-    case 3: fsdp_reduce_scatter_kernel<3><<<(int)ctas, kCommThreads, 0, st>>>(a, o, m); break;
-    case 4: fsdp_reduce_scatter_kernel<4><<<(int)ctas, kCommThreads, 0, st>>>(a, o, m); break;
-    case 5: fsdp_reduce_scatter_kernel<5><<<(int)ctas, kCommThreads, 0, st>>>(a, o, m); break;
-    case 6: fsdp_reduce_scatter_kernel<6><<<(int)ctas, kCommThreads, 0, st>>>(a, o, m); break;
-    case 7: fsdp_reduce_scatter_kernel<7><<<(int)ctas, kCommThreads, 0, st>>>(a, o, m); break;
-    case 8: fsdp_reduce_scatter_kernel<8><<<(int)ctas, kCommThreads, 0, st>>>(a, o, m); break;
+    case 2: fsdp_reduce_scatter_kernel<2><<<pb::smem_max(fsdp_reduce_scatter_kernel<2>, (int)ctas), kCommThreads, 0, st>>>(a, o, m); break;
+    case 3: fsdp_reduce_scatter_kernel<3><<<pb::smem_max(fsdp_reduce_scatter_kernel<3>, (int)ctas), kCommThreads, 0, st>>>(a, o, m); break;
+    case 4: fsdp_reduce_scatter_kernel<4><<<pb::smem_max(fsdp_reduce_scatter_kernel<4>, (int)ctas), kCommThreads, 0, st>>>(a, o, m); break;
+    case 5: fsdp_reduce_scatter_kernel<5><<<pb::smem_max(fsdp_reduce_scatter_kernel<5>, (int)ctas), kCommThreads, 0, st>>>(a, o, m); break;
+    case 6: fsdp_reduce_scatter_kernel<6><<<pb::smem_max(fsdp_reduce_scatter_kernel<6>, (int)ctas), kCommThreads, 0, st>>>(a, o, m); break;
+    case 7: fsdp_reduce_scatter_kernel<7><<<pb::smem_max(fsdp_reduce_scatter_kernel<7>, (int)ctas), kCommThreads, 0, st>>>(a, o, m); break;
+    case 8: fsdp_reduce_scatter_kernel<8><<<pb::smem_max(fsdp_reduce_scatter_kernel<8>, (int)ctas), kCommThreads, 0, st>>>(a, o, m); break;
     default: TORCH_CHECK(false, "fsdp_reduce_scatter: world size 2..8 on one node");
   }
   PB_CUDA_CHECK(cudaGetLastError());
@@ -330,7 +332,8 @@ template <int W>
 static void launch_final(FinalArgs& f, int ctas, cudaStream_t st) {
   auto kern = fsdp_adamw_kernel<W>;
   void* args[] = {&f};
-  PB_CUDA_CHECK(cudaLaunchCooperativeKernel(reinterpret_cast<void*>(kern), dim3(ctas), dim3(512), args, 0, st));
+  PB_CUDA_CHECK(cudaLaunchCooperativeKernel(reinterpret_cast<void*>(kern), pb::smem_max(kern, dim3(ctas)), dim3(512),
+                                            args, 0, st));
 }
 
 // Largest grid of the cooperative optimizer kernel on this device.
@@ -403,7 +406,7 @@ at::Tensor fsdp_embedding_fwd(at::Tensor ids, int64_t masters_dev, int64_t row0,
   const long T = ids.numel();
   auto out = at::empty({T, d}, ids.options().dtype(at::kFloat));
   if (T > 0) {
-    fsdp_embedding_kernel<<<(unsigned)((T + 7) / 8), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+    fsdp_embedding_kernel<<<pb::smem_max(fsdp_embedding_kernel, (unsigned)((T + 7) / 8)), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
         ids.data_ptr<int64_t>(), T, reinterpret_cast<float* const*>(masters_dev), row0, unit0, cs, soff, (int)d, vocab,
         out.data_ptr<float>(), status_ptr(ids.device().index()));
     PB_CUDA_CHECK(cudaGetLastError());
@@ -422,7 +425,7 @@ void fsdp_all_gather(std::vector<int64_t> ag, int64_t ctas) {
   auto st = at::cuda::getCurrentCUDAStream();
   const long nblocks = (s.hi - s.lo + (1L << s.block_shift) - 1) >> s.block_shift;
   PB_CUDA_CHECK(cudaMemsetAsync(s.counters, 0, sizeof(uint32_t) * (1 + nblocks), st));
-  fsdp_all_gather_kernel<<<(int)ctas, 128, 0, st>>>(s);
+  fsdp_all_gather_kernel<<<pb::smem_max(fsdp_all_gather_kernel, (int)ctas), 128, 0, st>>>(s);
   PB_CUDA_CHECK(cudaGetLastError());
 }
 

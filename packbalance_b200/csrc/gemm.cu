@@ -15,6 +15,16 @@ namespace pb {
 // with 5 stages and 8 slots; mode 0: always the single-CTA kernel.
 static int g_pair_mode = 2;
 
+// Tests of the pair kernel's abort path only: GemmArgs::test_arm_limit of the next
+// launches (0 = off).
+static int g_pair_test_arm_limit = 0;
+
+int64_t gemm_pair_test_arm_limit(int64_t n) {
+  const int prev = g_pair_test_arm_limit;
+  g_pair_test_arm_limit = static_cast<int>(std::max<int64_t>(0, n));
+  return prev;
+}
+
 int64_t gemm_pair_mode(int64_t mode) {
   const int prev = g_pair_mode;
   if (mode >= 0) {
@@ -38,7 +48,7 @@ static void launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const CUte
     PB_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES));
     configured[dev] = true;
   }
-  kern<<<grid, threads, C::SMEM_BYTES, stream>>>(ta, tb, to, tx, args);
+  kern<<<pb::smem_max(kern, grid), threads, C::SMEM_BYTES, stream>>>(ta, tb, to, tx, args);
   PB_CUDA_CHECK(cudaGetLastError());
 }
 
@@ -71,7 +81,7 @@ static void launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const CUte
   const int tiles = args.m_tiles * args.n_tiles * args.splits;
   int clusters = std::min(tiles, max_clusters[dev]);
   if (max_ctas > 0) clusters = std::min(clusters, std::max(1, max_ctas / 2));
-  cfg.gridDim = dim3(2 * std::max(clusters, 1), 1, 1);
+  cfg.gridDim = pb::smem_max(kern, dim3(2 * std::max(clusters, 1), 1, 1));
   PB_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kern, ta, tb, to, tx, args));
 }
 
@@ -190,6 +200,7 @@ void gemm_tc(at::Tensor a, at::Tensor b, at::Tensor out, int64_t M, int64_t N, i
   g.splits = (g.k_blocks + g.kb_per_split - 1) / g.kb_per_split;
   g.epi = (int)epi;
   g.alpha = (float)alpha;
+  g.test_arm_limit = pair ? g_pair_test_arm_limit : 0;
   g.pos = static_cast<const int*>(opt_ptr(pos));
   g.cos_t = static_cast<const float*>(opt_ptr(cos_t));
   g.sin_t = static_cast<const float*>(opt_ptr(sin_t));

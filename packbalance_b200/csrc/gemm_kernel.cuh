@@ -78,6 +78,10 @@ struct GemmArgs {
   float z_coeff;
   int* status;
   int keep_logits;  // CE_FWD: also store the bf16 logits through tm_aux
+  // Tests of the pair kernel's abort path only (0 = off): the even CTA's producer stops
+  // after arming this many k-blocks, as if it had stalled, without stopping the odd CTA,
+  // whose own bounded waits then run out.
+  int test_arm_limit;
   AgSpec ag;  // ag.world == 0: B is already local
   int n_rot;  // n-blocks are visited starting at this one (wrapping)
 };

@@ -21,6 +21,17 @@
 // set-up and another before TMEM release and exit keep either CTA from touching the
 // other's barriers before they exist or after it has left.
 //
+// Abort without loads in flight: the odd CTA's loads complete on the even CTA's full
+// barrier, which the odd CTA cannot wait on, and the even CTA may stop (a bounded wait ran
+// out) before it has armed a stage the odd CTA already loads into.  When the odd producer
+// leaves its loop, normally or not, it stores its count of issued k-blocks with a done bit
+// into ``odd_done`` in the even CTA's shared memory (release, cluster scope).  An aborting
+// even producer first sets the odd CTA's abort flag (so its waits end at once), waits
+// (bounded) for that count, arms the stages of the k-blocks the odd CTA issued beyond its
+// own arming with the odd CTA's bytes only, and then waits (bounded) for every armed
+// stage.  So no load is in flight when the final cluster barrier lets either CTA exit.
+// The normal path exchanges nothing per k-block.
+//
 // Only TMA loads from this GPU's own memory are issued (no all-gather role, no cluster
 // multicast of loads); the launch that gathers B from peers uses the single-CTA kernel.
 #pragma once
@@ -63,6 +74,15 @@ __device__ __forceinline__ uint32_t cluster_addr(uint32_t saddr, uint32_t rank) 
 __device__ __forceinline__ void cluster_sync() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
+__device__ __forceinline__ void st_release_cluster(uint32_t cluster_saddr, uint32_t v) {
+  asm volatile("st.release.cluster.shared::cluster.u32 [%0], %1;" ::"r"(cluster_saddr), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_cluster(const volatile uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.cluster.shared::cta.u32 %0, [%1];" : "=r"(v) : "r"(smem_u32((const void*)p)) : "memory");
+  return v;
+}
+constexpr uint32_t kOddDone = 0x80000000u;
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar_cluster_addr) {
   asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar_cluster_addr) : "memory");
 }
@@ -128,6 +148,7 @@ __global__ void __launch_bounds__(192, 1)
   __shared__ __align__(8) uint64_t drain_bar;
   __shared__ uint32_t tmem_base_sh;
   __shared__ volatile int abort_sh;
+  __shared__ volatile uint32_t odd_done_sh;  // even CTA: the odd producer's issued k-blocks | kOddDone
   extern __shared__ uint8_t dyn_smem[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(dyn_smem) + 1023) & ~uintptr_t(1023));
 
@@ -137,6 +158,7 @@ __global__ void __launch_bounds__(192, 1)
   const int pair = blockIdx.x >> 1;
   const int npairs = gridDim.x >> 1;
   if (threadIdx.x == 0) {
+    odd_done_sh = 0;
     for (int s = 0; s < C::STAGES; ++s) {
       mbar_init(&full_bar[s], 1);
       mbar_init(&empty_bar[s], 1);
@@ -171,6 +193,7 @@ __global__ void __launch_bounds__(192, 1)
       int stage = 0;
       uint32_t phase = 0;
       uint32_t armed_mask = 0, armed_phase = 0;  // even CTA: per stage, armed and its phase
+      uint32_t n_kb = 0;                         // k-blocks armed (even) / issued (odd)
       bool ok = true;
       for (int tile = pair; tile < num_tiles && ok; tile += npairs) {
         int mb, nb, sp;
@@ -186,10 +209,15 @@ __global__ void __launch_bounds__(192, 1)
             break;
           }
           if (cta == 0) {
+            if (args.test_arm_limit > 0 && n_kb >= static_cast<uint32_t>(args.test_arm_limit)) {
+              ok = false;  // test of the abort path: stop arming as if stalled
+              break;
+            }
             mbar_arrive_expect_tx(&full_bar[stage], 2 * C::STAGE_BYTES);
             armed_mask |= 1u << stage;
             armed_phase = (armed_phase & ~(1u << stage)) | (phase << stage);
           }
+          ++n_kb;
           const uint32_t bar = full0 + stage * 8;
           uint8_t* sa = smem + stage * C::STAGE_BYTES;
           uint8_t* sb = sa + C::A_BYTES;
@@ -212,8 +240,38 @@ __global__ void __launch_bounds__(192, 1)
           }
         }
       }
-      if (!ok && cta == 0) {
-        // Drain: wait (bounded, once more) for the stages this CTA armed.
+      if (cta == 1) {
+        // issued count for the even CTA's abort path (read only there)
+        st_release_cluster(cluster_addr(smem_u32((const void*)&odd_done_sh), 0), n_kb | kOddDone);
+      } else if (!ok) {
+        // Stop the odd producer (its waits check this flag), except in the abort-path test,
+        // where its own bounded wait has to run out.
+        if (args.test_arm_limit <= 0) st_release_cluster(cluster_addr(smem_u32((const void*)&abort_sh), 1), 1u);
+        // The odd CTA's count of issued k-blocks (bounded: its waits end within one
+        // timeout); k-blocks it issued beyond this CTA's arming get armed with its bytes
+        // only (at most STAGES of them, each on its own stage), so their phases complete.
+        uint32_t done = 0;
+        const uint64_t t0 = globaltimer();
+        while (!((done = ld_acquire_cluster(&odd_done_sh)) & kOddDone)) {
+          if (globaltimer() - t0 > 2 * PB_WAIT_TIMEOUT_NS) {
+            report_error(args.status, 127);
+            break;
+          }
+        }
+        if (done & kOddDone) {
+          const uint32_t n_odd = done & ~kOddDone;
+          for (uint32_t kb = n_kb; kb < n_odd && kb < n_kb + C::STAGES; ++kb) {
+            mbar_arrive_expect_tx(&full_bar[stage], C::STAGE_BYTES);
+            armed_mask |= 1u << stage;
+            armed_phase = (armed_phase & ~(1u << stage)) | (phase << stage);
+            if (++stage == C::STAGES) {
+              stage = 0;
+              phase ^= 1;
+            }
+          }
+        }
+        // Drain: wait (bounded, once more) for every armed stage; the odd CTA's loads of
+        // those stages complete on the same barriers.
         for (int s = 0; s < C::STAGES; ++s)
           if (armed_mask & (1u << s)) mbar_wait(&full_bar[s], (armed_phase >> s) & 1u, args.status, 122, nullptr);
       }

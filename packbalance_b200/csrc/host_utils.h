@@ -10,6 +10,8 @@
 #include <c10/util/Exception.h>
 
 #include <mutex>
+#include <set>
+#include <utility>
 
 #define PB_CUDA_CHECK(expr)                                                              \
   do {                                                                                   \
@@ -87,6 +89,28 @@ inline int* status_ptr(int dev) {
     PB_CUDA_CHECK(cudaSetDevice(prev));
   }
   return ptrs[dev];
+}
+
+// Kernels whose shared-memory carveouts differ cannot be resident on one SM at the same
+// time.  The collectives that run beside the tensor-core kernels (and those kernels,
+// which need ~225 KB anyway) ask for the largest carveout, so a collective CTA never
+// switches an SM to a configuration a GEMM or attention CTA cannot share.  (What keeps a
+// collective from holding back the compute kernels in practice is its width: see
+// parallel/comm.py.)  Returns ``value``, used as the first launch argument:
+// ``k<<<pb::smem_max(k, grid), ...>>>``; one attribute call per (device, kernel).
+template <typename K, typename V>
+inline V smem_max(K* kernel, V value) {
+  static std::mutex mu;
+  static std::set<std::pair<int, const void*>> done;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return value;
+  const auto key = std::make_pair(dev, reinterpret_cast<const void*>(kernel));
+  std::lock_guard<std::mutex> lock(mu);
+  if (done.insert(key).second)
+    PB_CUDA_CHECK(cudaFuncSetAttribute(reinterpret_cast<const void*>(kernel),
+                                       cudaFuncAttributePreferredSharedMemoryCarveout,
+                                       cudaSharedmemCarveoutMaxShared));
+  return value;
 }
 
 }  // namespace pb

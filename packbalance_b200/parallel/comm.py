@@ -36,7 +36,15 @@ class FusedAllReduce:
     """``mode``: "nvls" (multimem through the NVSwitch; default when the multicast
     object is available), "p2p" (two-shot over peer loads) or "auto"."""
 
-    CTAS = 148  # small CTAs (csrc/comm_common.cuh: 128 threads), about one per SM
+    # Launch widths (CTAs of 128 threads, csrc/comm_common.cuh).  A bucket reduced while
+    # the backward pass still runs gets a narrow launch: a collective with a CTA on every
+    # SM keeps the ~225 KB GEMM and attention CTAs from being scheduled until it ends
+    # (measured: a GEMM beside 148 resident collective CTAs waits for them, beside 16 it
+    # runs at full speed), and a few CTAs with eight loads in flight per thread move a
+    # bucket well within one layer's backward.  A bucket with nothing left to overlap
+    # (the last one of the step) gets the whole GPU.
+    CTAS_OVERLAP = 24
+    CTAS_TAIL = 4 * 148
     SYNC_WORDS = 16384
 
     def __init__(self, grad: torch.Tensor, group: dist.ProcessGroup | None = None, flat=None, mode: str | None = None) -> None:
@@ -66,7 +74,9 @@ class FusedAllReduce:
         if not 2 <= self.world <= 8:
             raise RuntimeError("fused all-reduce covers 2..8 ranks of one node")
         self.pad_words = self.SYNC_WORDS
-        self.ctas = min(self.CTAS, self.pad_words // (3 * self.world))
+        cap = self.pad_words // (3 * self.world)
+        self.ctas = min(self.CTAS_OVERLAP, cap)
+        self.ctas_tail = min(self.CTAS_TAIL, cap)
         if self.ctas < 1:
             raise RuntimeError("signal pad too small for the fused all-reduce")
         # Barrier epochs: a device base bumped by EPOCH_STRIDE at every step start plus the
@@ -94,8 +104,11 @@ class FusedAllReduce:
         _native.module().epoch_bump(self.epoch_base, self.EPOCH_STRIDE)
         self._k = 0
 
-    def all_reduce_mean(self, lo: int, hi: int) -> torch.Tensor:
-        """Average elements [lo, hi) of the gradient over all ranks (current stream)."""
+    def all_reduce_mean(self, lo: int, hi: int, tail: bool = False) -> torch.Tensor:
+        """Average elements [lo, hi) of the gradient over all ranks (current stream).
+        ``tail``: nothing else runs meanwhile, launch over the whole GPU (every rank must
+        pass the same value for the same bucket)."""
+        ctas = self.ctas_tail if tail else self.ctas
         self._k += 1
         if self._k >= self.EPOCH_STRIDE:
             raise RuntimeError("more all-reduce launches in one step than the epoch stride allows")
@@ -105,12 +118,12 @@ class FusedAllReduce:
             n = self.buf.numel()
             C.nvls_allreduce(
                 self.handle.buffer_ptrs_dev, self.h_sync.buffer_ptrs_dev, self.pad_words, self.mc,
-                self.mc + 4 * n, lo, hi, self.rank, self.world, self._k, 1.0 / self.world, self.sumsq, self.ctas, base,
+                self.mc + 4 * n, lo, hi, self.rank, self.world, self._k, 1.0 / self.world, self.sumsq, ctas, base,
             )
         else:
             C.fused_allreduce(
                 self.handle.buffer_ptrs_dev, self.h_sync.buffer_ptrs_dev, self.pad_words, lo, hi, self.rank,
-                self.world, self._k, 1.0 / self.world, self.sumsq, self.ctas, base,
+                self.world, self._k, 1.0 / self.world, self.sumsq, ctas, base,
             )
         return self.sumsq
 

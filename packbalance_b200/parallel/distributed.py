@@ -141,8 +141,11 @@ class DataParallel:
             if not self._issued[i] and lo >= offset:
                 self._issue(i)
 
-    def _issue(self, i: int) -> None:
+    def _issue(self, i: int, tail: bool = False) -> None:
         lo, hi = self.buckets[i]
+        # The bucket at offset 0 (the embedding, written by the last kernel of the
+        # backward pass) and buckets issued after the backward have nothing to overlap.
+        tail = tail or lo == 0
         self._issued[i] = True
         view = self.flat.grad[lo:hi]
         if self.stream is not None:
@@ -152,7 +155,7 @@ class DataParallel:
             ctx = contextlib.nullcontext()
         with ctx:
             if self.fused is not None:
-                self.fused.all_reduce_mean(lo, hi)
+                self.fused.all_reduce_mean(lo, hi, tail=tail)
             else:
                 dist.all_reduce(view, op=dist.ReduceOp.SUM, group=self.group)
                 view.mul_(1.0 / self.world)
@@ -165,7 +168,7 @@ class DataParallel:
             return None
         for i in range(len(self.buckets)):
             if not self._issued[i]:
-                self._issue(i)
+                self._issue(i, tail=True)
         if self.stream is not None:
             torch.cuda.current_stream().wait_stream(self.stream)
         if self.fused is not None:

@@ -130,7 +130,13 @@ def plan_layout(model, world: int) -> Layout:
 class ShardedParameters(GradWindow):
     """Sharded parameter/gradient/optimizer-state buffers of one model (CUDA, W >= 2)."""
 
-    def __init__(self, model, group: dist.ProcessGroup | None = None, rs_ctas: int = 148) -> None:
+    # Reduce-scatter launch widths: narrow while the backward pass still runs beside it
+    # (a collective with a CTA on every SM keeps the GEMM / attention CTAs from being
+    # scheduled until it ends), the whole GPU once nothing is left to overlap.
+    RS_CTAS_OVERLAP = 24
+    RS_CTAS_TAIL = 4 * 148
+
+    def __init__(self, model, group: dist.ProcessGroup | None = None, rs_ctas: int | None = None) -> None:
         import torch.distributed._symmetric_memory as symm_mem
 
         self.group = group if group is not None else dist.group.WORLD
@@ -199,7 +205,9 @@ class ShardedParameters(GradWindow):
         self.ag_counters = torch.zeros(max_blocks + 1, dtype=torch.int32, device=dev)
         self._epoch = 0  # barrier epochs (sync pads), one per collective launch
         self._arrive_total = 0
-        self.rs_ctas = min(rs_ctas, SYNC_WORDS // (3 * W))
+        cap = SYNC_WORDS // (3 * W)
+        self.rs_ctas = min(rs_ctas or self.RS_CTAS_OVERLAP, cap)
+        self.rs_ctas_tail = min(rs_ctas or self.RS_CTAS_TAIL, cap)
         C = _native.module()
         self.final_ctas = int(min(C.fsdp_adamw_max_ctas(W), SYNC_WORDS // (3 * W)))
         self.comm = torch.cuda.Stream(device=dev, priority=-1)
@@ -350,7 +358,7 @@ class ShardedParameters(GradWindow):
                 self.grad[s.offset : s.offset + s.numel].zero_()
                 self._fresh.add(id(s.param))
 
-    def _issue_rs(self, u: Unit) -> None:
+    def _issue_rs(self, u: Unit, tail: bool = False) -> None:
         self._issued.add(u.order)
         self._finish_unit(u)
         self.comm.wait_stream(torch.cuda.current_stream(self.device))
@@ -360,7 +368,7 @@ class ShardedParameters(GradWindow):
             _native.module().fsdp_reduce_scatter(
                 int(self.h_grad.buffer_ptrs_dev), int(self.h_sync.buffer_ptrs_dev), SYNC_WORDS, lo, lo + u.cs,
                 self.shard_grad.data_ptr() + 4 * u.soff, self.rank, self.world, self._epoch, 1.0 / self.world,
-                self.sumsq, self.rs_ctas, self.grad_mc,
+                self.sumsq, self.rs_ctas_tail if tail else self.rs_ctas, self.grad_mc,
             )
 
     # ---- optimizer step -----------------------------------------------------------------
@@ -372,7 +380,7 @@ class ShardedParameters(GradWindow):
         self.finish_window()
         for u in self.units:
             if u.order not in self._issued and u is not self.embed_unit:
-                self._issue_rs(u)
+                self._issue_rs(u, tail=True)
         self.comm.wait_stream(torch.cuda.current_stream(self.device))
         with torch.cuda.stream(self.comm):
             self.rep_sumsq.zero_()

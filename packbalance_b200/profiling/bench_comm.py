@@ -44,14 +44,14 @@ def main() -> None:
     for m in args.modes.split(","):
         f = FusedAllReduce(grad, mode=m)
         if args.ctas:
-            f.ctas = args.ctas
+            f.ctas = f.ctas_tail = args.ctas
         fused_by_mode[f"fused_{f.mode}"] = f
 
-    def runner(f):
+    def runner(f, tail):
         def run():
             f.start_step()
             for lo, hi in zip(cuts[:-1], cuts[1:]):
-                f.all_reduce_mean(lo, hi)
+                f.all_reduce_mean(lo, hi, tail=tail)
 
         return run
 
@@ -60,7 +60,9 @@ def main() -> None:
             dist.all_reduce(grad[lo:hi])
 
     res = {}
-    for name, fn in [*((k, runner(f)) for k, f in fused_by_mode.items()), ("nccl", run_nccl)]:
+    # narrow: the launch width used beside the backward pass; tail: the whole GPU
+    cases = [(f"{k}_{w}", runner(f, w == "tail")) for k, f in fused_by_mode.items() for w in ("narrow", "tail")]
+    for name, fn in [*cases, ("nccl", run_nccl)]:
         for _ in range(3):
             fn()
         torch.cuda.synchronize()
@@ -78,9 +80,10 @@ def main() -> None:
         res[name] = {"ms": t, "busbw_gbs": need / t / 1e6, "frac_of_nvlink_770": need / t / 1e6 / NVLINK_GBS}
     for f in fused_by_mode.values():
         f.check()
-    ctas = next(iter(fused_by_mode.values())).ctas
+    f0 = next(iter(fused_by_mode.values()))
     if rank == 0:
-        print(json.dumps({"world": world, "mb": args.mb, "buckets": args.buckets, "ctas": ctas, **res}), flush=True)
+        print(json.dumps({"world": world, "mb": args.mb, "buckets": args.buckets, "ctas_narrow": f0.ctas,
+                          "ctas_tail": f0.ctas_tail, **res}), flush=True)
     for f in fused_by_mode.values():
         f.close()
     dist.barrier()

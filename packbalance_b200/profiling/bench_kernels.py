@@ -156,6 +156,9 @@ def run(args) -> list[dict]:
             o = torch.empty(m, n, device=dev, dtype=torch.bfloat16)
             add(f"gemm_fwd_{name}", timeit(lambda: gemm(a, b, o, m, n, k, epi=EPI_BF16), args.iters, args.warmup),
                 flops=2.0 * m * n * k, shape=[m, n, k])
+            # the library's bf16 GEMM on the same shape (baseline for the tile-count effects)
+            add(f"gemm_fwd_{name}_cublas", timeit(lambda: torch.matmul(a, b.t(), out=o), args.iters, args.warmup),
+                flops=2.0 * m * n * k, shape=[m, n, k])
             dy = torch.randn(m, n, device=dev).to(torch.bfloat16)
             gw = torch.empty(n, k, device=dev)
             add(f"gemm_wgrad_{name}", timeit(lambda: linear_wgrad(dy, a, gw), args.iters, args.warmup),

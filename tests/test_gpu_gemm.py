@@ -174,3 +174,32 @@ def test_gemm_rope_epilogue(hd, bn):
     ref = torch.cat([rot[:, : h + hk], y[:, h + hk :]], 1).reshape(t, n)
     _close(out, ref)
     _native.check_status()
+
+
+def test_pair_gemm_abort_path_reports_status():
+    """The even CTA of every pair stops arming after two of sixteen k-blocks without
+    stopping the odd CTA (a test knob, no fault).  The odd CTA loads five stages ahead and
+    its bounded wait for the next free stage runs out; it reports the k-blocks it issued,
+    the even CTA arms those stages with the odd CTA's bytes and drains them, the MMA
+    issuer's wait for the next stage runs out, and the kernel records a status code and
+    returns with no load in flight.  The GPU keeps working."""
+    C = _native.module()
+    torch.manual_seed(1)
+    m, n, k = 512, 512, 1024  # 256-wide tiles on CTA pairs, sixteen 64-deep k-blocks
+    a, b = _bf(m, k), _bf(n, k)
+    out = torch.empty(m, n, device=dev, dtype=torch.bfloat16)
+    d = torch.cuda.current_device()
+    C.status_read(d, True)
+    prev_mode = C.gemm_pair_mode(2)
+    prev = C.gemm_pair_test_arm_limit(2)
+    try:
+        gemm(a, b, out, m, n, k, epi=EPI_BF16, bn=256)
+        torch.cuda.synchronize()
+    finally:
+        C.gemm_pair_test_arm_limit(prev)
+    code = C.status_read(d, True)
+    assert code in (121, 124, 126, 127), code
+    gemm(a, b, out, m, n, k, epi=EPI_BF16, bn=256)
+    C.gemm_pair_mode(prev_mode)
+    _native.check_status()
+    _close(out, a.float() @ b.float().t())
