@@ -51,7 +51,9 @@ def lmhead_ce_forward(
     nt = -(-v // CE_TILE)
     pmax = torch.empty(nt, t, device=x.device, dtype=torch.float32)
     psum = torch.empty(nt, t, device=x.device, dtype=torch.float32)
-    tlogit = torch.zeros(t, device=x.device, dtype=torch.float32)
+    # written by the one logits tile that holds each row's target column; read only for
+    # labelled rows, so it needs no zero fill
+    tlogit = torch.empty(t, device=x.device, dtype=torch.float32)
     lse = torch.empty(t, device=x.device, dtype=torch.float32)
     loss = torch.zeros((), device=x.device, dtype=torch.float32)
     tgt = targets.reshape(-1).to(torch.int64).contiguous()

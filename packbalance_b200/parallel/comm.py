@@ -75,7 +75,7 @@ class FusedAllReduce:
             raise RuntimeError("fused all-reduce covers 2..8 ranks of one node")
         self.pad_words = self.SYNC_WORDS
         cap = self.pad_words // (3 * self.world)
-        self.ctas = min(self.CTAS_OVERLAP, cap)
+        self.ctas = min(int(os.environ.get("PB_COMM_CTAS", self.CTAS_OVERLAP)), cap)
         self.ctas_tail = min(self.CTAS_TAIL, cap)
         if self.ctas < 1:
             raise RuntimeError("signal pad too small for the fused all-reduce")
@@ -91,7 +91,17 @@ class FusedAllReduce:
         if mode == "nvls" and self.mode != "nvls":
             raise RuntimeError("NVLink multicast is not available for this group")
         self.mc = mc
-        self.sumsq = full[n] if self.mode == "nvls" else torch.zeros((), device=grad.device, dtype=torch.float32)
+        # Tail buckets (nothing left to overlap) take the faster kernel for the width: at two
+        # ranks the two-shot peer-load kernel moves less over NVLink than multimem (each GPU
+        # also reads its own copy through the switch) and measured faster (98 MB: 0.24 vs
+        # 0.31 ms); from four ranks on, the in-switch reduction moves less.
+        tail_env = os.environ.get("PB_ALLREDUCE_TAIL")
+        self.tail_mode = tail_env if tail_env in ("p2p", "nvls") else ("p2p" if self.world == 2 else self.mode)
+        if self.tail_mode == "nvls" and not mc:
+            self.tail_mode = "p2p"
+        # one norm accumulator for both kernels: in the symmetric buffer, where the multimem
+        # kernel adds every rank's part and the peer-load kernel adds the whole bucket's
+        self.sumsq = full[n]
         if flat is not None:
             flat.rebind_grad(buf)
         _native.module().fused_allreduce  # fail loudly if the extension lacks the kernel
@@ -109,12 +119,13 @@ class FusedAllReduce:
         ``tail``: nothing else runs meanwhile, launch over the whole GPU (every rank must
         pass the same value for the same bucket)."""
         ctas = self.ctas_tail if tail else self.ctas
+        mode = self.tail_mode if tail else self.mode
         self._k += 1
         if self._k >= self.EPOCH_STRIDE:
             raise RuntimeError("more all-reduce launches in one step than the epoch stride allows")
         C = _native.module()
         base = self.epoch_base.data_ptr()
-        if self.mode == "nvls":
+        if mode == "nvls":
             n = self.buf.numel()
             C.nvls_allreduce(
                 self.handle.buffer_ptrs_dev, self.h_sync.buffer_ptrs_dev, self.pad_words, self.mc,

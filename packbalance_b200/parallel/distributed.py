@@ -111,10 +111,28 @@ class DataParallel:
         self._issued: list[bool] = [False] * len(self.buckets)
         self._norm_parts: list[torch.Tensor] = []
         self.hold = False  # set while a non-final microbatch runs its backward pass
+        # Buckets below this offset are reduced once the backward pass has (almost) ended:
+        # those of the first decoder layer (only the embedding's backward follows them) and
+        # the embedding's.  They take the wide launch.
+        self.tail_offset = self._tail_offset()
+
+    def _tail_offset(self) -> int:
+        for name in ("model.layers.0.post_attention_layernorm.weight", "model.layers.1.input_layernorm.weight"):
+            for s in self.flat.slots:
+                if s.name == name:
+                    return s.offset
+        return 1  # no decoder layers found: only the bucket at offset 0
+
+    # A decoder layer's backward finishes its MLP weights (and the norm before the MLP)
+    # half way through: buckets start at these parameters, so the MLP half of a layer's
+    # gradient goes out while the layer's attention backward still runs.
+    READY_POINTS = ("post_attention_layernorm.weight", "input_layernorm.weight")
 
     def _make_buckets(self) -> list[tuple[int, int]]:
-        """Contiguous ranges of whole parameters, last parameters first (backward order).
-        Bucket starts are 16-byte aligned (cuts only at offsets that are multiples of 4)."""
+        """Contiguous ranges of whole parameters, last parameters first (backward order):
+        a new bucket starts at every ready point (the norm weight in front of a layer's MLP
+        and of its attention) and wherever a bucket would exceed the size cap.  Bucket
+        starts are 16-byte aligned (cuts only at offsets that are multiples of 4)."""
         buckets: list[tuple[int, int]] = []
         hi = self.flat.numel
         lo = hi
@@ -123,7 +141,11 @@ class DataParallel:
                 buckets.append((lo, hi))
                 hi = lo
             lo = s.offset
-        buckets.append((lo, hi))
+            if s.name.endswith(self.READY_POINTS) and lo % 4 == 0 and lo < hi:
+                buckets.append((lo, hi))
+                hi = lo
+        if lo < hi:
+            buckets.append((lo, hi))
         return buckets
 
     def start_step(self) -> None:
@@ -132,24 +154,27 @@ class DataParallel:
         if self.fused is not None:
             self.fused.start_step()
 
-    def notify_ready(self, offset: int) -> None:
-        """Every gradient at flat offset >= ``offset`` is final for this step: issue
-        the buckets that lie entirely above it."""
+    def notify_ready(self, offset: int, streams: tuple = ()) -> None:
+        """Every gradient at flat offset >= ``offset`` is final for this step once the
+        current stream and ``streams`` (e.g. the weight-gradient stream) reach this point:
+        issue the buckets that lie entirely above it."""
         if self.world <= 1 or not self.overlap or self.hold:
             return
         for i, (lo, hi) in enumerate(self.buckets):
             if not self._issued[i] and lo >= offset:
-                self._issue(i)
+                self._issue(i, streams=streams)
 
-    def _issue(self, i: int, tail: bool = False) -> None:
+    def _issue(self, i: int, tail: bool = False, streams: tuple = ()) -> None:
         lo, hi = self.buckets[i]
-        # The bucket at offset 0 (the embedding, written by the last kernel of the
-        # backward pass) and buckets issued after the backward have nothing to overlap.
-        tail = tail or lo == 0
+        # Buckets of the first decoder layer and the embedding (written by the last kernels
+        # of the backward pass) and buckets issued after the backward have nothing to overlap.
+        tail = tail or lo < self.tail_offset
         self._issued[i] = True
         view = self.flat.grad[lo:hi]
         if self.stream is not None:
             self.stream.wait_stream(torch.cuda.current_stream())
+            for st in streams:
+                self.stream.wait_stream(st)
             ctx = torch.cuda.stream(self.stream)
         else:
             ctx = contextlib.nullcontext()

@@ -59,6 +59,23 @@ class GradWindow:
             self._fresh.add(id(p))
         return False
 
+    def prezero(self, *params: nn.Parameter) -> None:
+        """Zero the gradients of ``params`` that no writer has claimed yet this window, with
+        one fill per contiguous run of them, and claim them: their writers then add into
+        zeros.  A layer's split-K weight-gradient GEMMs (which add partial products) need
+        zeroed memory; one fill per layer replaces one per GEMM."""
+        slots = sorted((self.by_param[id(p)] for p in params if id(p) not in self._fresh), key=lambda s: s.offset)
+        runs: list[list[int]] = []
+        for s in slots:
+            if runs and runs[-1][1] == s.offset:
+                runs[-1][1] = s.offset + s.numel
+            else:
+                runs.append([s.offset, s.offset + s.numel])
+        for lo, hi in runs:
+            self.grad[lo:hi].zero_()
+        for s in slots:
+            self._fresh.add(id(s.param))
+
 
 class FlatParameters(GradWindow):
     def __init__(self, module: nn.Module, *, with_shadow: bool | None = None) -> None:
@@ -152,18 +169,19 @@ class FlatParameters(GradWindow):
                 self.grad[s.offset : s.offset + s.numel].zero_()
                 self._fresh.add(id(s.param))
 
-    def ready(self, offset: int) -> None:
-        """Gradients at flat offsets >= ``offset`` are final for this step."""
+    def ready(self, offset: int, streams: tuple = ()) -> None:
+        """Gradients at flat offsets >= ``offset`` are final for this step once the
+        current stream and ``streams`` reach this point."""
         if self.ready_hook is not None:
-            self.ready_hook(offset)
+            self.ready_hook(offset, streams)
 
     def ready_all(self) -> None:
         self.ready(0)
 
-    def ready_after(self, p: nn.Parameter) -> None:
+    def ready_after(self, p: nn.Parameter, streams: tuple = ()) -> None:
         """The gradients of ``p`` and of every parameter registered after it are final
         (the backward pass runs in reverse registration order)."""
-        self.ready(self.slot(p).offset)
+        self.ready(self.slot(p).offset, streams)
 
     # ---- hooks the sharded layout overrides ------------------------------------
     def gather_spec(self, *params: nn.Parameter) -> list[int] | None:

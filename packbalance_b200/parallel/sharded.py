@@ -161,9 +161,13 @@ class ShardedParameters(GradWindow):
         self.unit_of = {id(s.param): u for u in units for s in u.slots}
         # norms (and, for the ready protocol, their layer's unit order)
         self.rep_order = {}
+        # a layer's unit is only final at its input norm: the half-way point (the norm in
+        # front of the MLP) releases nothing here
+        self.mid_layer: set[int] = set()
         for i, layer in enumerate(model.model.layers):
             self.rep_order[id(layer.input_layernorm.weight)] = i + 1
             self.rep_order[id(layer.post_attention_layernorm.weight)] = i + 1
+            self.mid_layer.add(id(layer.post_attention_layernorm.weight))
         self.rep_order[id(model.model.norm.weight)] = len(model.model.layers) + 1
 
         # ---- buffers -------------------------------------------------------------------
@@ -339,13 +343,14 @@ class ShardedParameters(GradWindow):
         self._issued.clear()
         self.sumsq.zero_()
 
-    def ready(self, offset: int) -> None:  # FlatParameters-compatible entry (unused)
+    def ready(self, offset: int, streams: tuple = ()) -> None:  # FlatParameters-compatible entry (unused)
         pass
 
-    def ready_after(self, p: nn.Parameter) -> None:
+    def ready_after(self, p: nn.Parameter, streams: tuple = ()) -> None:
         """``p``'s unit and every later unit (model order) have final gradients: reduce-
-        scatter them now, except the embedding unit, which the optimizer kernel reduces."""
-        if self.hold_ready:
+        scatter them now, except the embedding unit, which the optimizer kernel reduces.
+        (The callers join the weight-gradient stream before a unit's last ready point.)"""
+        if self.hold_ready or id(p) in self.mid_layer:
             return
         order = self.unit_of[id(p)].order if id(p) in self.unit_of else self.rep_order[id(p)]
         for u in self.units:

@@ -147,6 +147,12 @@ def run(args) -> list[dict]:
             if keep:
                 ms -= res[-1]["ms"]  # minus the forward that refilled the logits (timed just above)
             add(f"lmhead_bwd_{tag}", ms, flops=(4.0 if keep else 6.0) * t * d * v, shape=[t, d, v])
+        # recomputing backward with smaller dlogits chunks (a chunk of 1024 rows x 32000 is
+        # 65 MB of bf16 and stays in the 126 MB L2 between its GEMMs)
+        for rows in (1024, 2048, 4096):
+            add(f"lmhead_bwd_recomputed_chunk{rows}",
+                timeit(lambda: lmhead_ce_backward(x, w, tgt, lse, g, dw, False, chunk_rows=rows), args.iters,
+                       args.warmup), flops=6.0 * t * d * v, shape=[t, d, v])
     if "gemm" in cases:
         t = args.tokens * 4
         for name, (m, n, k) in {"qkv": (t, 1280, 768), "o": (t, 768, 768), "gateup": (t, 4096, 768),

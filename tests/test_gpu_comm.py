@@ -30,7 +30,7 @@ WORKER = textwrap.dedent(
     rank = int(os.environ["RANK"]); world = int(os.environ["WORLD_SIZE"])
     torch.cuda.set_device(rank)
     dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=60), device_id=torch.device("cuda", rank))
-    n = 3 * 1000 * 1000 + 12
+    n = 3 * 1000 * 1000 + 13  # ragged end: the last bucket is not a multiple of 16 bytes
     g = torch.Generator(device="cuda").manual_seed(1234 + rank)
     grad = torch.randn(n, device="cuda", generator=g)
     ref = grad.clone()
@@ -38,13 +38,15 @@ WORKER = textwrap.dedent(
     ref /= world
     ar = FusedAllReduce(grad, mode=os.environ["PB_ALLREDUCE"])
     if rank == 0:
-        print("mode", ar.mode)
+        print("mode", ar.mode, "tail", ar.tail_mode)
     for step in range(3):
         ar.buf.copy_(grad)
         ar.start_step()
-        cuts = [0, 1000, 2_000_000, n]
-        for lo, hi in zip(cuts[:-1], cuts[1:]):
-            ar.all_reduce_mean(lo, hi)
+        # a 4-element bucket, a bucket smaller than one CTA's share, large ones; narrow
+        # (beside-compute) and wide (tail) launches, both kernels when the tail kernel differs
+        cuts = [0, 4, 1000, 2_000_000, n]
+        for i, (lo, hi) in enumerate(zip(cuts[:-1], cuts[1:])):
+            ar.all_reduce_mean(lo, hi, tail=(i + step) % 2 == 1)
         torch.cuda.synchronize()
         _native.check_status()
         err = (ar.buf - ref).abs().max().item()
@@ -54,7 +56,7 @@ WORKER = textwrap.dedent(
     ar.close()
     dist.barrier()
     dist.destroy_process_group()
-    print("rank", rank, "ok")
+    print(f"rank {rank} ok", flush=True)  # one write: ranks do not interleave
     """
 )
 

@@ -103,7 +103,7 @@ WORKER = textwrap.dedent(
     shd.close(); ddp.close()
     dist.barrier()
     dist.destroy_process_group()
-    print("rank", rank, "ok", worst, frac)
+    print(f"rank {rank} ok {worst} {frac}", flush=True)  # one write: ranks do not interleave
     """
 )
 
