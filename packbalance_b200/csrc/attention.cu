@@ -80,10 +80,15 @@ constexpr float kLazyRescaleLog2 = 8.f;  // forward: rescale O only when the max
 template <int D>
 struct FwdCfg {
   static constexpr int TILE_BYTES = 128 * D * 2;  // one 128-row tile of Q, K or V
-  static constexpr int Q_OFF = 0;
-  static constexpr int K_OFF = TILE_BYTES;             // 2 stages
-  static constexpr int V_OFF = K_OFF + 2 * TILE_BYTES;  // 2 stages
-  static constexpr int STAT_OFF = V_OFF + 2 * TILE_BYTES;  // group-1 (max, sum) per row
+  // Two Q buffers: the producer loads the next item's Q while the current item's last
+  // key tiles are still in flight, so an item boundary costs no Q-load latency.
+  static constexpr int Q_OFF = 0;                      // 2 buffers
+  // K/V ring: four stages at head_dim 64, so the producer runs into the next item's key
+  // tiles while the current item's last ones are in use; two at 128 (shared memory).
+  static constexpr int KV_STAGES = D == 64 ? 4 : 2;
+  static constexpr int K_OFF = 2 * TILE_BYTES;
+  static constexpr int V_OFF = K_OFF + KV_STAGES * TILE_BYTES;
+  static constexpr int STAT_OFF = V_OFF + KV_STAGES * TILE_BYTES;  // group-1 (max, sum) per row
   // At least 120 KB so that a second CTA (which would block in tcgen05.alloc on
   // the fully allocated TMEM) is never co-scheduled on the same SM.
   static constexpr int SMEM_USED = STAT_OFF + 1024 + 1024;
@@ -123,7 +128,8 @@ __global__ void __launch_bounds__(320, 1)
   // p_ready / o_done [group][P slot] (tile g uses slot g & 1): one barrier per slot, so
   // with the softmax groups running up to two tiles ahead of the P V products no
   // barrier ever completes a second phase before its first has been waited for.
-  __shared__ __align__(8) uint64_t q_full, q_empty, kv_full[2], kv_empty[2], s_full[2], s_free, p_ready[2][2],
+  __shared__ __align__(8) uint64_t q_full[2], q_empty[2], kv_full[FwdCfg<D>::KV_STAGES], kv_empty[FwdCfg<D>::KV_STAGES],
+      s_full[2], s_free, p_ready[2][2],
       o_done[2][2], o_free, stats_ready, drain_bar;
   __shared__ uint32_t tmem_sh;
   __shared__ volatile int abort_sh;
@@ -131,11 +137,15 @@ __global__ void __launch_bounds__(320, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(dyn) + 1023) & ~uintptr_t(1023));
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   if (threadIdx.x == 0) {
-    mbar_init(&q_full, 1);
-    mbar_init(&q_empty, 1);
     for (int i = 0; i < 2; ++i) {
+      mbar_init(&q_full[i], 1);
+      mbar_init(&q_empty[i], 1);
+    }
+    for (int i = 0; i < C::KV_STAGES; ++i) {
       mbar_init(&kv_full[i], 1);
       mbar_init(&kv_empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
       mbar_init(&p_ready[i][0], 4);
       mbar_init(&p_ready[i][1], 4);
@@ -171,13 +181,14 @@ __global__ void __launch_bounds__(320, 1)
         if (it + (int)gridDim.x < args.n_items) nx = checked_item(ld_item(args.items, it + gridDim.x), args.T, args.H, args.status);
         const int hk = h / group;
         const int q0 = qt * 128;
-        if (!mbar_wait(&q_empty, (q_it & 1) ^ 1, args.status, 201, &abort_sh)) break;
-        mbar_arrive_expect_tx(&q_full, C::TILE_BYTES);
-        load_tile_rows(smem + C::Q_OFF, &tmap, &q_full, h * D, q0, D);
+        const int qb = q_it & 1;
+        if (!mbar_wait(&q_empty[qb], ((q_it >> 1) & 1) ^ 1, args.status, 201, &abort_sh)) break;
+        mbar_arrive_expect_tx(&q_full[qb], C::TILE_BYTES);
+        load_tile_rows(smem + C::Q_OFF + qb * C::TILE_BYTES, &tmap, &q_full[qb], h * D, q0, D);
         ++q_it;
         for (int kt = kt0; kt <= qt; ++kt, ++kv_it) {
-          const int s = kv_it & 1;
-          if (!mbar_wait(&kv_empty[s], ((kv_it >> 1) & 1) ^ 1, args.status, 202, &abort_sh)) {
+          const int s = kv_it % C::KV_STAGES;
+          if (!mbar_wait(&kv_empty[s], ((kv_it / C::KV_STAGES) & 1) ^ 1, args.status, 202, &abort_sh)) {
             ok = false;
             break;
           }
@@ -189,71 +200,89 @@ __global__ void __launch_bounds__(320, 1)
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      uint32_t kv_it = 0, q_it = 0, item_n = 0;
+      // The key tiles of all this CTA's items form one stream g = 0, 1, ...: S_g is issued
+      // before P_{g-1} V_{g-1}, across item boundaries too, so when the softmax warps
+      // finish an item the next item's first scores are already in TMEM.
       bool ok = true;
-      const uint32_t qa = smem_u32(smem + C::Q_OFF);
-      int3 nx = blockIdx.x < args.n_items ? checked_item(ld_item(args.items, blockIdx.x), args.T, args.H, args.status) : make_int3(0, 0, 0);
-      for (int it = blockIdx.x; it < args.n_items && ok; it += gridDim.x, ++item_n) {
-        const int qt = nx.x, kt0 = nx.z;
-        if (it + (int)gridDim.x < args.n_items) nx = checked_item(ld_item(args.items, it + gridDim.x), args.T, args.H, args.status);
-        const int nkv = qt - kt0 + 1;
-        if (!mbar_wait(&q_full, q_it & 1, args.status, 203, &abort_sh)) break;
-        ++q_it;
-        tc_fence_after();
-        for (int j = 0; j <= nkv && ok; ++j) {
-          if (j < nkv) {
-            const uint32_t g = kv_it + j;
-            const int s = g & 1;
-            if (!mbar_wait(&kv_full[s], (g >> 1) & 1, args.status, 205, &abort_sh)) {
-              ok = false;
-              break;
+      uint32_t q_it = 0;                                    // items whose Q the S side used
+      int it_s = blockIdx.x, j_s = 0;                      // S side: item, tile within it
+      int3 cur_s = it_s < args.n_items ? checked_item(ld_item(args.items, it_s), args.T, args.H, args.status)
+                                       : make_int3(0, 0, 0);
+      int nkv_s = cur_s.x - cur_s.z + 1;
+      int qb_s = 0;
+      uint32_t qa_s = smem_u32(smem + C::Q_OFF);
+      int it_p = blockIdx.x, j_p = 0;                      // P V side, one tile behind
+      int nkv_p = nkv_s;
+      uint32_t item_p = 0;                                  // items the P V side has started
+      uint32_t g = 0, gp = 0;                               // global tile index of each side
+      while (ok && (it_s < args.n_items || gp < g)) {
+        if (it_s < args.n_items) {
+          if (j_s == 0) {
+            qb_s = q_it & 1;
+            qa_s = smem_u32(smem + C::Q_OFF + qb_s * C::TILE_BYTES);
+            if (!mbar_wait(&q_full[qb_s], (q_it >> 1) & 1, args.status, 203, &abort_sh)) break;
+            ++q_it;
+          }
+          const int s = g % C::KV_STAGES;
+          if (!mbar_wait(&kv_full[s], (g / C::KV_STAGES) & 1, args.status, 205, &abort_sh)) break;
+          // With one S buffer, both groups must have read S_{g-1}.
+          if (C::S_BUFS == 1 && g > 0 && !mbar_wait(&s_free, (g - 1) & 1, args.status, 211, &abort_sh)) break;
+          tc_fence_after();
+          const uint32_t ka = smem_u32(smem + C::K_OFF + s * C::TILE_BYTES);
+          const uint32_t sb = tmem + C::S_COL + (g % C::S_BUFS) * 128;
+#pragma unroll
+          for (int kk = 0; kk < D / 16; ++kk) {
+            const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
+            umma_ss(sb, sdesc_sw128(qa_s + off, 16, 1024), sdesc_sw128(ka + off, 16, 1024), C::IDESC_S,
+                    kk > 0 ? 1u : 0u);
+          }
+          umma_commit(&s_full[g % C::S_BUFS]);
+          ++g;
+          if (++j_s == nkv_s) {
+            umma_commit(&q_empty[qb_s]);
+            j_s = 0;
+            it_s += gridDim.x;
+            if (it_s < args.n_items) {
+              cur_s = checked_item(ld_item(args.items, it_s), args.T, args.H, args.status);
+              nkv_s = cur_s.x - cur_s.z + 1;
             }
-            // With one S buffer, both groups must have read S_{g-1}.
-            if (C::S_BUFS == 1 && g > 0 && !mbar_wait(&s_free, (g - 1) & 1, args.status, 211, &abort_sh)) {
+          }
+        }
+        // P V of the previous tile of the stream (all of them once the S side is done)
+        if (gp + 1 < g || (it_s >= args.n_items && gp < g)) {
+          const int s = gp % C::KV_STAGES;
+          const uint32_t va = smem_u32(smem + C::V_OFF + s * C::TILE_BYTES);
+          if (j_p == 0) {
+            // The first PV of an item overwrites O: the previous item's O must be read out.
+            if (!mbar_wait(&o_free, (item_p & 1) ^ 1, args.status, 204, &abort_sh)) break;
+            ++item_p;
+          }
+#pragma unroll
+          for (int grp = 0; grp < 2; ++grp) {
+            if (!mbar_wait(&p_ready[grp][gp & 1], (gp >> 1) & 1, args.status, 206, &abort_sh)) {
               ok = false;
               break;
             }
             tc_fence_after();
-            const uint32_t ka = smem_u32(smem + C::K_OFF + s * C::TILE_BYTES);
-            const uint32_t sb = tmem + C::S_COL + (g % C::S_BUFS) * 128;
+            const uint32_t pa = tmem + C::P_COL + (grp * 2 + (gp & 1)) * 32;
 #pragma unroll
-            for (int kk = 0; kk < D / 16; ++kk) {
-              const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
-              umma_ss(sb, sdesc_sw128(qa + off, 16, 1024), sdesc_sw128(ka + off, 16, 1024), C::IDESC_S,
-                      kk > 0 ? 1u : 0u);
-            }
-            umma_commit(&s_full[g % C::S_BUFS]);
-            if (j == nkv - 1) umma_commit(&q_empty);
+            for (int kk = 0; kk < 4; ++kk)
+              umma_ts(tmem + C::O_COL + grp * D, pa + kk * 8, sdesc_sw128(va + grp * 8192 + kk * 2048, 16384, 1024),
+                      C::IDESC_O, (j_p > 0 || kk > 0) ? 1u : 0u);
+            umma_commit(&o_done[grp][gp & 1]);
           }
-          if (j > 0) {
-            const uint32_t g = kv_it + j - 1;
-            const int s = g & 1;
-            const uint32_t va = smem_u32(smem + C::V_OFF + s * C::TILE_BYTES);
-            // The first PV overwrites O: the previous item's O must have been read out.
-            if (j == 1 && !mbar_wait(&o_free, (item_n & 1) ^ 1, args.status, 204, &abort_sh)) {
-              ok = false;
-              break;
+          if (!ok) break;
+          umma_commit(&kv_empty[s]);
+          ++gp;
+          if (++j_p == nkv_p) {
+            j_p = 0;
+            it_p += gridDim.x;
+            if (it_p < args.n_items) {
+              const int3 c = checked_item(ld_item(args.items, it_p), args.T, args.H, args.status);
+              nkv_p = c.x - c.z + 1;
             }
-#pragma unroll
-            for (int grp = 0; grp < 2; ++grp) {
-              if (!mbar_wait(&p_ready[grp][g & 1], (g >> 1) & 1, args.status, 206, &abort_sh)) {
-                ok = false;
-                break;
-              }
-              tc_fence_after();
-              const uint32_t pa = tmem + C::P_COL + (grp * 2 + (g & 1)) * 32;
-#pragma unroll
-              for (int kk = 0; kk < 4; ++kk)
-                umma_ts(tmem + C::O_COL + grp * D, pa + kk * 8,
-                        sdesc_sw128(va + grp * 8192 + kk * 2048, 16384, 1024), C::IDESC_O,
-                        (j > 1 || kk > 0) ? 1u : 0u);
-              umma_commit(&o_done[grp][g & 1]);
-            }
-            if (!ok) break;
-            umma_commit(&kv_empty[s]);
           }
         }
-        kv_it += nkv;
       }
       umma_commit(&drain_bar);
       mbar_wait(&drain_bar, 0, args.status, 207, nullptr);

@@ -27,6 +27,7 @@ void rope_apply(at::Tensor x, at::Tensor pos, at::Tensor cos_t, at::Tensor sin_t
                 int64_t head_dim, bool inverse);
 at::Tensor embedding_fwd(at::Tensor ids, at::Tensor w);
 void embedding_bwd(at::Tensor ids, at::Tensor dx, at::Tensor grad, bool accumulate);
+bool set_deterministic(bool on);
 void ce_finalize(at::Tensor pmax, at::Tensor psum, at::Tensor tlogit, at::Tensor targets, int64_t ignore_index,
                  double z, at::Tensor lse, at::Tensor loss);
 void ce_row_scale(at::Tensor targets, int64_t ignore_index, at::Tensor grad_out, at::Tensor scale);
@@ -68,6 +69,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("rope_apply", &pb::rope_apply);
   m.def("embedding_fwd", &pb::embedding_fwd);
   m.def("embedding_bwd", &pb::embedding_bwd);
+  m.def("set_deterministic", &pb::set_deterministic,
+        "fixed-order reductions for RMSNorm dw and the embedding gradient; returns the previous setting");
   m.def("ce_finalize", &pb::ce_finalize);
   m.def("ce_row_scale", &pb::ce_row_scale);
   m.def("ce_dlogits", &pb::ce_dlogits, "in-place dlogits over kept bf16 logits");

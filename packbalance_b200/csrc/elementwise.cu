@@ -78,7 +78,7 @@ template <typename TI, typename TD>
 __global__ void rmsnorm_bwd_kernel(const TD* __restrict__ dy, const TI* __restrict__ x, const float* __restrict__ w,
                                    const float* __restrict__ rstd, const float* __restrict__ dres,
                                    float* __restrict__ dx, __nv_bfloat16* __restrict__ dx_bf16,
-                                   float* __restrict__ dw_out, int rows, int n) {
+                                   float* __restrict__ dw_out, int rows, int n, float* __restrict__ dw_part) {
   extern __shared__ float sdw[];  // [warps][n]
   const int warps = blockDim.x / 32;
   const int wid = threadIdx.x / 32, lane = threadIdx.x % 32;
@@ -112,7 +112,8 @@ __global__ void rmsnorm_bwd_kernel(const TD* __restrict__ dy, const TI* __restri
   for (int c = threadIdx.x; c < n; c += blockDim.x) {
     float t = 0.f;
     for (int k = 0; k < warps; ++k) t += sdw[static_cast<long>(k) * n + c];
-    atomicAdd(dw_out + c, t);
+    if (dw_part != nullptr) dw_part[static_cast<long>(blockIdx.x) * n + c] = t;  // summed in block order later
+    else atomicAdd(dw_out + c, t);
   }
 }
 
@@ -163,7 +164,8 @@ __global__ void __launch_bounds__(256) rmsnorm_bwd_reg_kernel(const TD* __restri
                                                                const float* __restrict__ rstd,
                                                                const float* __restrict__ dres, float* __restrict__ dx,
                                                                __nv_bfloat16* __restrict__ dx_bf16,
-                                                               float* __restrict__ dw_out, int rows) {
+                                                               float* __restrict__ dw_out, int rows,
+                                                               float* __restrict__ dw_part) {
   constexpr int n = 128 * CH;
   __shared__ float sdw[8][n];
   const int lane = threadIdx.x & 31, wid = threadIdx.x / 32;
@@ -213,8 +215,30 @@ __global__ void __launch_bounds__(256) rmsnorm_bwd_reg_kernel(const TD* __restri
   for (int c = threadIdx.x; c < n; c += blockDim.x) {
     float t = 0.f;
     for (int q = 0; q < warps; ++q) t += sdw[q][c];
-    atomicAdd(dw_out + c, t);
+    if (dw_part != nullptr) dw_part[static_cast<long>(blockIdx.x) * n + c] = t;  // summed in block order later
+    else atomicAdd(dw_out + c, t);
   }
+}
+
+// Deterministic mode: dw_out[c] (+)= sum over blocks b = 0, 1, ... of part[b, c], always in
+// that order.
+__global__ void dw_reduce_kernel(const float* __restrict__ part, int blocks, int n, float* __restrict__ dw_out) {
+  for (int c = blockIdx.x * blockDim.x + threadIdx.x; c < n; c += gridDim.x * blockDim.x) {
+    float t = 0.f;
+    for (int b = 0; b < blocks; ++b) t += part[static_cast<long>(b) * n + c];
+    dw_out[c] += t;
+  }
+}
+
+// Reductions whose order depends on scheduling (fp32 atomics) are replaced, while this is
+// set, by ones with a fixed order: RMSNorm dw through per-block partials summed in block
+// order, the embedding gradient through a stable sort of the token ids.
+static bool g_deterministic = false;
+
+bool set_deterministic(bool on) {
+  const bool prev = g_deterministic;
+  g_deterministic = on;
+  return prev;
 }
 
 std::vector<at::Tensor> add_rmsnorm_fwd(at::Tensor x, c10::optional<at::Tensor> delta, at::Tensor w, double eps,
@@ -293,20 +317,28 @@ at::Tensor rmsnorm_bwd(at::Tensor dy, at::Tensor x, at::Tensor w, at::Tensor rst
   auto s = at::cuda::getCurrentCUDAStream();
   if (!accumulate_dw) PB_CUDA_CHECK(cudaMemsetAsync(dw_out.data_ptr(), 0, n * sizeof(float), s));
   if (rows == 0) return dx;
+  // deterministic mode: per-block dw partials, then one ordered sum (dw_reduce_kernel)
+  auto reduce_parts = [&](const at::Tensor& part, int blocks) {
+    dw_reduce_kernel<<<(n + 255) / 256, 256, 0, s>>>(part.data_ptr<float>(), blocks, n, dw_out.data_ptr<float>());
+  };
   if (x.scalar_type() == at::kFloat && dy.scalar_type() == at::kFloat && n % 128 == 0 && n / 128 <= 8) {
     // one persistent wave: 1 CTA of 8 warps per SM for CH >= 6 (register-bound), else 2
     const int g2 = std::min<int>((rows + 7) / 8, (n / 128 >= 6 ? 1 : 2) * num_sms(x.device().index()));
     const float* dres_q = dres.has_value() ? dres->data_ptr<float>() : nullptr;
     __nv_bfloat16* dxq = dx_bf16.has_value() ? reinterpret_cast<__nv_bfloat16*>(dx_bf16->data_ptr()) : nullptr;
+    at::Tensor part;
+    if (g_deterministic) part = at::empty({g2, n}, x.options().dtype(at::kFloat));
+    float* pp = g_deterministic ? part.data_ptr<float>() : nullptr;
     bool done = true;
     switch (n / 128) {
 #define PB_BWD_CH(C) \
-  case C: rmsnorm_bwd_reg_kernel<C, float, float><<<g2, 256, 0, s>>>(dy.data_ptr<float>(), x.data_ptr<float>(), w.data_ptr<float>(), rstd.data_ptr<float>(), dres_q, dx.data_ptr<float>(), dxq, dw_out.data_ptr<float>(), rows); break;
+  case C: rmsnorm_bwd_reg_kernel<C, float, float><<<g2, 256, 0, s>>>(dy.data_ptr<float>(), x.data_ptr<float>(), w.data_ptr<float>(), rstd.data_ptr<float>(), dres_q, dx.data_ptr<float>(), dxq, dw_out.data_ptr<float>(), rows, pp); break;
       PB_BWD_CH(2) PB_BWD_CH(4) PB_BWD_CH(6) PB_BWD_CH(8)
 #undef PB_BWD_CH
       default: done = false;
     }
     if (done) {
+      if (g_deterministic) reduce_parts(part, g2);
       PB_CUDA_CHECK(cudaGetLastError());
       return dx;
     }
@@ -317,13 +349,16 @@ at::Tensor rmsnorm_bwd(at::Tensor dy, at::Tensor x, at::Tensor w, at::Tensor rst
   __nv_bfloat16* dxb = dx_bf16.has_value() ? reinterpret_cast<__nv_bfloat16*>(dx_bf16->data_ptr()) : nullptr;
   const size_t smem = static_cast<size_t>(warps) * n * sizeof(float);
   TORCH_CHECK(smem <= 200 * 1024, "rmsnorm_bwd: feature dim too large");
+  at::Tensor part;
+  if (g_deterministic) part = at::empty({nb, n}, x.options().dtype(at::kFloat));
+  float* pp = g_deterministic ? part.data_ptr<float>() : nullptr;
 #define PB_RMS_BWD(TI, TD)                                                                                    \
   do {                                                                                                        \
     auto k = rmsnorm_bwd_kernel<TI, TD>;                                                                      \
     if (smem > 48 * 1024) PB_CUDA_CHECK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)); \
     k<<<nb, warps * 32, smem, s>>>(reinterpret_cast<const TD*>(dy.data_ptr()), reinterpret_cast<const TI*>(x.data_ptr()), \
                                    w.data_ptr<float>(), rstd.data_ptr<float>(), dres_p, dx.data_ptr<float>(), dxb,      \
-                                   dw_out.data_ptr<float>(), rows, n);                                        \
+                                   dw_out.data_ptr<float>(), rows, n, pp);                                    \
   } while (0)
   const bool xf = x.scalar_type() == at::kFloat, df = dy.scalar_type() == at::kFloat;
   if (xf && df) PB_RMS_BWD(float, float);
@@ -331,6 +366,7 @@ at::Tensor rmsnorm_bwd(at::Tensor dy, at::Tensor x, at::Tensor w, at::Tensor rst
   else if (!xf && df) PB_RMS_BWD(__nv_bfloat16, float);
   else PB_RMS_BWD(__nv_bfloat16, __nv_bfloat16);
 #undef PB_RMS_BWD
+  if (g_deterministic) reduce_parts(part, nb);
   PB_CUDA_CHECK(cudaGetLastError());
   return dx;
 }
@@ -513,6 +549,29 @@ __global__ void embedding_bwd_kernel(const int64_t* __restrict__ ids, const floa
   }
 }
 
+// Deterministic embedding gradient: token positions sorted stably by id; one thread per
+// (run of equal ids, 4 columns) sums the run's rows in position order and adds the sum to
+// the row of the table.  ``starts``: first sorted position of every run, then the total.
+__global__ void embedding_bwd_sorted_kernel(const int64_t* __restrict__ sorted_ids, const int64_t* __restrict__ pos,
+                                            const int64_t* __restrict__ starts, int runs, const float* __restrict__ dx,
+                                            float* __restrict__ grad, int d, int64_t vocab, int* status) {
+  const int d4 = d / 4;
+  const long total = static_cast<long>(runs) * d4;
+  for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
+    const int run = static_cast<int>(i / d4), c = static_cast<int>(i % d4);
+    const long a = starts[run], b = starts[run + 1];
+    float4 t = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (long k = a; k < b; ++k) {
+      const float4 v = reinterpret_cast<const float4*>(dx + pos[k] * d)[c];
+      t.x += v.x; t.y += v.y; t.z += v.z; t.w += v.w;
+    }
+    float4* g = reinterpret_cast<float4*>(grad + checked_id(sorted_ids[a], vocab, status) * d) + c;
+    float4 o = *g;
+    o.x += t.x; o.y += t.y; o.z += t.z; o.w += t.w;
+    *g = o;
+  }
+}
+
 at::Tensor embedding_fwd(at::Tensor ids, at::Tensor w) {
   TORCH_CHECK(ids.scalar_type() == at::kLong && w.scalar_type() == at::kFloat && w.size(1) % 4 == 0);
   const c10::cuda::CUDAGuard guard(w.device());
@@ -536,6 +595,22 @@ void embedding_bwd(at::Tensor ids, at::Tensor dx, at::Tensor grad, bool accumula
   if (!accumulate) grad.zero_();
   const int rows = ids.numel(), d = grad.size(1);
   if (rows == 0) return;
+  if (g_deterministic) {
+    auto flat_ids = ids.reshape(-1);
+    auto sorted = at::sort(flat_ids, /*stable=*/true, /*dim=*/0, /*descending=*/false);
+    auto sid = std::get<0>(sorted), pos = std::get<1>(sorted);
+    auto uc = at::unique_consecutive(sid, /*return_inverse=*/false, /*return_counts=*/true);
+    auto counts = std::get<2>(uc);
+    auto starts = at::cat({at::zeros({1}, counts.options()), at::cumsum(counts, 0)});
+    const int runs = static_cast<int>(counts.numel());
+    const long total = (long)runs * d / 4;
+    embedding_bwd_sorted_kernel<<<ew_grid(total, grad.device().index()), 256, 0,
+                                  at::cuda::getCurrentCUDAStream()>>>(
+        sid.data_ptr<int64_t>(), pos.data_ptr<int64_t>(), starts.data_ptr<int64_t>(), runs, dx.data_ptr<float>(),
+        grad.data_ptr<float>(), d, grad.size(0), status_ptr(grad.device().index()));
+    PB_CUDA_CHECK(cudaGetLastError());
+    return;
+  }
   const long total = (long)rows * d / 4;
   embedding_bwd_kernel<<<ew_grid(total, grad.device().index()), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
       ids.data_ptr<int64_t>(), dx.data_ptr<float>(), grad.data_ptr<float>(), rows, d, grad.size(0),
@@ -683,7 +758,7 @@ void adamw_step(at::Tensor p, at::Tensor g, at::Tensor m, at::Tensor v, at::Tens
   PB_CUDA_CHECK(cudaGetLastError());
 }
 
-__global__ void sumsq_kernel(const float* __restrict__ x, long n, float* __restrict__ out) {
+__global__ void sumsq_kernel(const float* __restrict__ x, long n, float* __restrict__ out, float* __restrict__ part) {
   float s = 0.f;
   const long n4 = n / 4;
   for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < n4; i += (long)gridDim.x * blockDim.x) {
@@ -699,7 +774,10 @@ __global__ void sumsq_kernel(const float* __restrict__ x, long n, float* __restr
   if (threadIdx.x < 32) {
     float t = threadIdx.x < blockDim.x / 32 ? red[threadIdx.x] : 0.f;
     t = warp_sum(t);
-    if (threadIdx.x == 0) atomicAdd(out, t);
+    if (threadIdx.x == 0) {
+      if (part != nullptr) part[blockIdx.x] = t;  // deterministic mode: summed in block order
+      else atomicAdd(out, t);
+    }
   }
 }
 
@@ -707,9 +785,16 @@ at::Tensor l2_norm(at::Tensor x) {
   const c10::cuda::CUDAGuard guard(x.device());
   auto acc = at::zeros({}, x.options().dtype(at::kFloat));
   const long n = x.numel();
-  if (n > 0)
-    sumsq_kernel<<<2 * num_sms(x.device().index()), 512, 0, at::cuda::getCurrentCUDAStream()>>>(
-        x.data_ptr<float>(), n, acc.data_ptr<float>());
+  const int blocks = 2 * num_sms(x.device().index());
+  at::Tensor part;
+  if (g_deterministic) part = at::empty({blocks}, x.options().dtype(at::kFloat));
+  if (n > 0) {
+    sumsq_kernel<<<blocks, 512, 0, at::cuda::getCurrentCUDAStream()>>>(
+        x.data_ptr<float>(), n, acc.data_ptr<float>(), g_deterministic ? part.data_ptr<float>() : nullptr);
+    if (g_deterministic)
+      dw_reduce_kernel<<<1, 32, 0, at::cuda::getCurrentCUDAStream()>>>(part.data_ptr<float>(), blocks, 1,
+                                                                         acc.data_ptr<float>());
+  }
   PB_CUDA_CHECK(cudaGetLastError());
   return acc.sqrt();
 }

@@ -188,10 +188,6 @@ class _Decoder(torch.autograd.Function):
         _wgrad(flat, (wg, wu), dgu, xn2)
         dx1b = torch.empty(t, d, device=dev, dtype=torch.bfloat16)
         dx1 = C.rmsnorm_bwd(dxn2, x1, w_post, rstd2, dx2, dx1b, flat.grad_of(w_post).view(-1), flat.claim(w_post))
-        # the MLP half of the layer's gradient (and the norm in front of it) is final once
-        # its weight-gradient GEMMs are done: it can be reduced while the attention runs
-        ws = _WGRAD_STREAMS.get(_dev_index(dev)) if ASYNC_WGRAD and dev.type == "cuda" else None
-        flat.ready_after(w_post, (ws,) if ws is not None else ())
         # attention
         do = torch.empty(t, h * hd, device=dev, dtype=torch.bfloat16)
         gemm(dx1b, flat.shadow_of(wo), do, t, h * hd, d, b_mn=True, epi=EPI_BF16)

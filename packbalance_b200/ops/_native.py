@@ -31,6 +31,30 @@ def available() -> bool:
     return True
 
 
+_DETERMINISTIC = False
+
+
+def set_deterministic(on: bool) -> bool:
+    """Fixed-order reductions in the native step (the reference's ``train.deterministic``).
+
+    While on: weight-gradient and CE-backward GEMMs run without split-K (one writer per
+    output tile, no reduce-adds); RMSNorm dw, the gradient norm and the embedding
+    gradient are summed in a fixed order instead of with fp32 atomics; the attention
+    backward runs as an fp32 per-document recomputation (no reduce-adds across key tiles or
+    heads).  Two runs on the same inputs then give bitwise identical weights, at the cost
+    of speed (a debugging mode).  Returns the previous setting."""
+    global _DETERMINISTIC
+    prev = _DETERMINISTIC
+    _DETERMINISTIC = bool(on)
+    if available():
+        module().set_deterministic(_DETERMINISTIC)
+    return prev
+
+
+def deterministic() -> bool:
+    return _DETERMINISTIC
+
+
 class KernelTimeout(RuntimeError):
     """A device-side bounded wait gave up (see the status code for which one)."""
 

@@ -190,6 +190,8 @@ def attn_backward_packed(
     and k gradients are rotated back to the pre-RoPE frame (the gradient w.r.t. the QKV
     GEMM output); without it they are w.r.t. the rotated q/k."""
     t = qkv.shape[0]
+    if _native.deterministic():
+        return _attn_backward_fixed_order(qkv, dout, plan["doc_start"][:t], n_heads, n_kv_heads, head_dim, rope)
     pl = _padded(plan, n_heads, n_kv_heads, t)
     tp = pl["doc_start"].numel()
     if tp != t:
@@ -207,6 +209,41 @@ def attn_backward_packed(
         *(rope if rope is not None else (None, None, None)),
     )
     return dqkv[:t] if tp != t else dqkv
+
+
+def _attn_backward_fixed_order(qkv, dout, doc_start, n_heads, n_kv_heads, head_dim, rope) -> torch.Tensor:
+    """Deterministic-mode attention backward: per document, the fp32 causal attention is
+    recomputed with PyTorch and differentiated, so no gradient is summed by reduce-adds
+    whose order depends on scheduling (the native kernel reduce-adds dQ over key tiles
+    and dK/dV over the query heads of a group).  Slow; for the deterministic mode only."""
+    t, h, hk, d = qkv.shape[0], n_heads, n_kv_heads, head_dim
+    q = qkv[:, : h * d].float().view(t, h, d)
+    k = qkv[:, h * d : (h + hk) * d].float().view(t, hk, d)
+    v = qkv[:, (h + hk) * d :].float().view(t, hk, d)
+    do = dout.float().view(t, h, d)
+    dq, dk, dv = torch.zeros_like(q), torch.zeros_like(k), torch.zeros_like(v)
+    ds = doc_start.long()
+    starts = (ds == torch.arange(t, device=ds.device)).nonzero().flatten().tolist() + [t]
+    scale = 1.0 / math.sqrt(d)
+    with torch.enable_grad():
+        for a, b in zip(starts[:-1], starts[1:]):
+            qd = q[a:b].transpose(0, 1).detach().requires_grad_()
+            kd = k[a:b].transpose(0, 1).detach().requires_grad_()
+            vd = v[a:b].transpose(0, 1).detach().requires_grad_()
+            kr, vr = kd.repeat_interleave(h // hk, 0), vd.repeat_interleave(h // hk, 0)
+            s = (qd @ kr.transpose(-1, -2)) * scale
+            n = b - a
+            s = s.masked_fill(torch.ones(n, n, dtype=torch.bool, device=s.device).triu(1), float("-inf"))
+            o = s.softmax(-1) @ vr
+            gq, gk, gv = torch.autograd.grad(o, (qd, kd, vd), do[a:b].transpose(0, 1))
+            dq[a:b], dk[a:b], dv[a:b] = gq.transpose(0, 1), gk.transpose(0, 1), gv.transpose(0, 1)
+    if rope is not None:
+        from packbalance_b200.ops.reference import rope_reference
+
+        pos, cos, sin = rope
+        c, sn = cos[pos.long()][:, None, :], sin[pos.long()][:, None, :]
+        dq, dk = rope_reference(dq, c, -sn), rope_reference(dk, c, -sn)  # rotate back: R^T = R(-theta)
+    return torch.cat([dq.reshape(t, h * d), dk.reshape(t, hk * d), dv.reshape(t, hk * d)], 1).to(qkv.dtype)
 
 
 class _VarlenAttention(torch.autograd.Function):

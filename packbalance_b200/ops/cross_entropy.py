@@ -88,6 +88,8 @@ def lmhead_ce_backward(
         _native.module().ce_dlogits(logits, lse, tgt, scale, float(z_coeff))
         dx = torch.empty(t, d, device=x.device, dtype=torch.float32)
         bn, splits = pick_tiling(t, d, v, sms)
+        if _native.deterministic():
+            splits = 1
         if splits > 1:
             dx.zero_()
             gemm(logits, w, dx, t, d, v, b_mn=True, epi=EPI_ADD_F32, bn=bn, splits=splits)
@@ -107,6 +109,8 @@ def lmhead_ce_backward(
         gemm(x[r0:r1], w, dl, rows, v, d, epi=EPI_CE_BWD, bn=CE_TILE, targets=tgt[r0:r1], lse=lse[r0:r1],
              row_scale=scale[r0:r1], z_coeff=z_coeff)
         bn, splits = pick_tiling(rows, d, v, sms)
+        if _native.deterministic():
+            splits = 1
         if splits > 1:
             dx[r0:r1].zero_()
             gemm(dl, w, dx[r0:r1], rows, d, v, b_mn=True, epi=EPI_ADD_F32, bn=bn, splits=splits)

@@ -141,6 +141,8 @@ def linear_wgrad(dy: torch.Tensor, x: torch.Tensor, out: torch.Tensor | None = N
     if out is None:
         out = torch.empty(n, k, device=dy.device, dtype=torch.float32)
     bn, splits = pick_tiling(n, k, m, sm_count(dy.device))
+    if _native.deterministic():
+        splits = 1  # one writer per output tile: no order-dependent reduce-adds
     if splits == 1 and not accumulate:
         return gemm(dy, x, out, n, k, m, a_mn=True, b_mn=True, epi=EPI_F32, bn=bn)
     if not accumulate:

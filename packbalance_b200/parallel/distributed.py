@@ -86,8 +86,12 @@ class DataParallel:
         backend: str = "auto",
         group: dist.ProcessGroup | None = None,
         overlap: bool | None = None,
+        deterministic: bool = False,
     ) -> None:
         self.flat = flat
+        # deterministic mode: the peer-load kernel (sums in rank order) and a norm taken
+        # afterwards in a fixed order (the fused partial norms are added atomically)
+        self.deterministic = deterministic
         # Issue buckets during the backward pass (overlap) or all at once after it.
         env = os.environ.get("PB_COMM_OVERLAP")
         self.overlap = (env != "0") if overlap is None and env is not None else (True if overlap is None else overlap)
@@ -101,7 +105,10 @@ class DataParallel:
             from packbalance_b200.parallel.comm import FusedAllReduce
 
             try:
-                self.fused = FusedAllReduce(flat.grad, group=group, flat=flat)
+                self.fused = FusedAllReduce(flat.grad, group=group, flat=flat,
+                                            mode="p2p" if deterministic else None)
+                if deterministic:
+                    self.fused.tail_mode = "p2p"
             except Exception as exc:  # peer memory unavailable
                 if backend == "fused":
                     raise
@@ -123,16 +130,18 @@ class DataParallel:
                     return s.offset
         return 1  # no decoder layers found: only the bucket at offset 0
 
-    # A decoder layer's backward finishes its MLP weights (and the norm before the MLP)
-    # half way through: buckets start at these parameters, so the MLP half of a layer's
-    # gradient goes out while the layer's attention backward still runs.
-    READY_POINTS = ("post_attention_layernorm.weight", "input_layernorm.weight")
+    # Buckets start at a decoder layer's first parameter, so a layer's gradient goes out as
+    # one bucket when its backward ends and is reduced beside the next layer's MLP GEMMs.
+    # (Measured at W = 2: splitting a layer at its MLP half, reduced beside the attention
+    # backward, made the step slower, 11.74 against 10.61 ms: the attention backward's
+    # CTAs fill the register file and the collective's share of it.)
+    READY_POINTS = ("input_layernorm.weight",)
 
     def _make_buckets(self) -> list[tuple[int, int]]:
         """Contiguous ranges of whole parameters, last parameters first (backward order):
-        a new bucket starts at every ready point (the norm weight in front of a layer's MLP
-        and of its attention) and wherever a bucket would exceed the size cap.  Bucket
-        starts are 16-byte aligned (cuts only at offsets that are multiples of 4)."""
+        a new bucket starts at every ready point (a decoder layer's first parameter) and
+        wherever a bucket would exceed the size cap.  Bucket starts are 16-byte aligned
+        (cuts only at offsets that are multiples of 4)."""
         buckets: list[tuple[int, int]] = []
         hi = self.flat.numel
         lo = hi
@@ -196,7 +205,7 @@ class DataParallel:
                 self._issue(i, tail=True)
         if self.stream is not None:
             torch.cuda.current_stream().wait_stream(self.stream)
-        if self.fused is not None:
+        if self.fused is not None and not self.deterministic:
             return self.fused.sumsq
         return None
 

@@ -203,7 +203,10 @@ def run(args) -> list[dict]:
             flops=2.0 * n ** 3, shape=[n, n, n])
     if "attn_fwd" in cases or "attn_bwd" in cases:
         h, hk, d = 12, 4, 64
-        lengths = bench_doc_lengths(args.tokens * 4)
+        # --doc-len L: every document L tokens long (per-item overheads amortised over
+        # more key/query tiles); default: the bench corpus's length law
+        lengths = bench_doc_lengths(args.tokens * 4) if args.doc_len <= 0 else \
+            [args.doc_len] * -(-(args.tokens * 4) // args.doc_len)
         ds = doc_starts(lengths, dev)[: args.tokens * 4]
         t = ds.numel()
         qkv = torch.randn(t, (h + 2 * hk) * d, device=dev).to(torch.bfloat16)
@@ -233,6 +236,7 @@ def main() -> None:
     ap.add_argument("--tokens", type=int, default=2048)
     ap.add_argument("--ce-dim", type=int, default=768)
     ap.add_argument("--vocab", type=int, default=32000)
+    ap.add_argument("--doc-len", type=int, default=0, help="attention cases: fixed document length (0: bench law)")
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--output", default=None)

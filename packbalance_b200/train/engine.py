@@ -206,6 +206,14 @@ class TrainEngine:
         self.fsdp = bool(cfg.train.fsdp) and self.world > 1
         self.sharded = None
         native_ok = device.type == "cuda" and self.model.uses_native_path(torch.empty(0, device=device))
+        # the reference's train.deterministic: fixed-order reductions in the native kernels
+        # (ops/_native.set_deterministic), eager steps (no CUDA graphs), peer-load
+        # all-reduce summed in rank order
+        self.deterministic = bool(cfg.train.deterministic) and native_ok
+        if self.deterministic:
+            from packbalance_b200.ops import _native
+
+            _native.set_deterministic(True)
         if self.fsdp and native_ok:
             # Native sharded path: per-unit shards in symmetric memory, all-gather fused
             # into the consuming GEMMs, reduce-scatter fused with the sharded AdamW.
@@ -242,7 +250,8 @@ class TrainEngine:
         else:
             self.flat = FlatParameters(self.model)
             self.model.flat = self.flat
-            self.dp = DataParallel(self.flat, cfg.train.bucket_cap_mb, cfg.train.comm_backend)
+            self.dp = DataParallel(self.flat, cfg.train.bucket_cap_mb, cfg.train.comm_backend,
+                                   deterministic=self.deterministic)
             self.flat.ready_hook = self.dp.notify_ready
             self.optimizer = FlatAdamW(
                 self.flat,
@@ -257,6 +266,7 @@ class TrainEngine:
         env = os.environ.get("PB_CUDA_GRAPHS")
         self.use_graphs = (
             cfg.train.cuda_graphs and (env != "0") and self.native and self.sharded is None and not self.fsdp
+            and not self.deterministic
             and device.type == "cuda" and (self.world == 1 or (self.dp is not None and self.dp.fused is not None))
         )
         amp = get_autocast_dtype(cfg.train.dtype) if device.type == "cuda" and not self.native else None
@@ -410,3 +420,7 @@ class TrainEngine:
     def close(self) -> None:
         if self.dp is not None:
             self.dp.close()
+        if self.deterministic:
+            from packbalance_b200.ops import _native
+
+            _native.set_deterministic(False)
