@@ -233,7 +233,7 @@ def report(args, world, dev, rank, impl, step_ms_ranks, e2e_ms, tokens_steps, la
         "scaling": "weak",
         "vs_baseline": None,
         "dtype": "bf16",
-        "data": "synthetic (lognormal median 256 sigma 1.2 clipped [16,2048], Zipf(1.1) ids; random-init weights)",
+        "data": extra_cfg.pop("data_desc", "synthetic; random-init weights"),
         "config": extra_cfg,
         "clocks": clocks,
         "gpu_launches": launches,
@@ -301,6 +301,8 @@ def run_ours(args, rank, world, dev) -> None:
     clocks = sampler.stop(clocks_gpus(world))
     _native.check_status(dev)
     step_ms_ranks = gather(ms, dev)
+    free, total_mem = torch.cuda.mem_get_info(dev)
+    mem_used_gb = max_over_ranks((total_mem - free) / 1e9, dev)  # everything on the device, max over ranks
 
     e2e_ms = None
     h2d = batch_tensor_bytes(engine.prepare_batch(host[0]))
@@ -366,10 +368,21 @@ def run_ours(args, rank, world, dev) -> None:
         "analytical_rank_imbalance": sched.stats()["rank_cost_imbalance"],
         "l2": "no flush; per-step working set (weights+Adam state+activations) >> 126 MB L2",
         "comm": comm,
+        "device_mem_used_gb": round(mem_used_gb, 2),
+        "data_desc": describe_data(cfg.data),
     }
     report(args, world, dev, rank, "ours", step_ms_ranks, e2e_ms, [p.step_tokens for p in plans[args.warmup:]],
            launches, clocks, extra, h2d, d2h)
     engine.close()
+
+
+def describe_data(d) -> str:
+    """The ``data`` field of the JSON line, from the config actually run."""
+    med = d.synthetic_median if d.synthetic_median is not None else math.exp(d.synthetic_mu)
+    ids = f"Zipf({d.synthetic_zipf_s:g}) ids" if d.synthetic_token_dist == "zipf" else "uniform ids"
+    long_docs = f", {d.synthetic_long_doc_frac:g} of documents {d.seq_len} tokens" if d.synthetic_long_doc_frac else ""
+    return (f"synthetic (lognormal median {med:g} sigma {d.synthetic_sigma:g} clipped [{d.synthetic_min_len},"
+            f"{d.synthetic_max_len}]{long_docs}, {ids}; random-init weights)")
 
 
 def describe_model(m) -> str:
@@ -493,6 +506,7 @@ def run_reference(args, rank, world, dev) -> None:
         "padding_waste": pack_stats(packs, fm)["padding_waste"],
         "l2": "no flush; per-step working set >> 126 MB L2",
         "comm": "torch FSDP2 (NCCL)" if rcfg.train.fsdp and world > 1 else "torch DDP (NCCL)",
+        "data_desc": describe_data(ours.data),
     }
     report(args, world, dev, rank, "reference", step_ms_ranks, e2e_ms, [p.step_tokens for p in plans[args.warmup:]],
            None, clocks, extra, h2d, 4)

@@ -60,6 +60,10 @@ class Unit:
     order: int = 0  # position in model order (embedding 0, layers 1..L, head L+1)
     span: int = 0  # elements of parameters (the rest up to W * cs is padding)
     segments: list[tuple[int, int]] = field(default_factory=list)  # gather ranges (element lo, hi)
+    # where this unit's gradient lives: in the fixed buffer (norms, embedding, head) or in
+    # a rotating window (decoder layers), at element ``goff`` of that buffer
+    gwin: int = -1  # window index, -1: fixed buffer
+    goff: int = 0
 
 
 def _units_of(model) -> tuple[list[Slot], list[Unit]]:
@@ -127,6 +131,40 @@ def plan_layout(model, world: int) -> Layout:
     return Layout(rep, units, rep_n, off, soff)
 
 
+@dataclass
+class GradStorage:
+    fixed_numel: int  # norms (at their layout offsets), then the non-layer units
+    win_numel: int  # one window (the largest layer unit, W * cs elements)
+    windows: int  # 0: every unit in the fixed buffer (no rotation)
+
+
+def plan_grad_storage(layout: Layout, world: int, windows: int) -> GradStorage:
+    """Physical placement of the gradients.  With ``windows`` = K > 0 the decoder layers'
+    gradients rotate through K windows of the largest layer's size, in backward order
+    (the last layer takes window 0): a layer's window is written again K layers later,
+    after its reduce-scatter has finished on every rank.  The norms, the embedding and an
+    untied head keep their own storage (the embedding is reduced by the optimizer kernel
+    at the end of the step).  With K = 0 every unit keeps its own storage, as a full
+    gradient buffer."""
+    off = layout.rep_n
+    layers = [u for u in layout.units if u.name.startswith("layer")]
+    if windows == 1:
+        raise ValueError("gradient windows: 0 (no rotation) or at least 2")
+    rotate = windows > 0 and len(layers) > 0
+    for u in layout.units:
+        if rotate and u.name.startswith("layer"):
+            continue
+        u.gwin, u.goff = -1, off
+        off += world * u.cs
+    win_numel = 0
+    if rotate:
+        win_numel = max(world * u.cs for u in layers)
+        for pos, u in enumerate(reversed(layers)):
+            u.gwin = pos % windows
+            u.goff = u.gwin * win_numel
+    return GradStorage(off, win_numel, windows if rotate else 0)
+
+
 class ShardedParameters(GradWindow):
     """Sharded parameter/gradient/optimizer-state buffers of one model (CUDA, W >= 2)."""
 
@@ -136,7 +174,11 @@ class ShardedParameters(GradWindow):
     RS_CTAS_OVERLAP = 24
     RS_CTAS_TAIL = 4 * 148
 
-    def __init__(self, model, group: dist.ProcessGroup | None = None, rs_ctas: int | None = None) -> None:
+    # Decoder-layer gradients rotate through this many windows (0: a full gradient buffer).
+    GRAD_WINDOWS = 3
+
+    def __init__(self, model, group: dist.ProcessGroup | None = None, rs_ctas: int | None = None,
+                 grad_windows: int | None = None) -> None:
         import torch.distributed._symmetric_memory as symm_mem
 
         self.group = group if group is not None else dist.group.WORLD
@@ -153,6 +195,7 @@ class ShardedParameters(GradWindow):
         layout = plan_layout(model, W)
         self.rep_n, self.numel, self.shard_numel = layout.rep_n, layout.numel, layout.shard_numel
         rep, units = layout.rep, layout.units
+        self.gstore = plan_grad_storage(layout, W, self.GRAD_WINDOWS if grad_windows is None else grad_windows)
         self.rep_slots = rep
         self.units = units
         self.embed_unit = units[0]
@@ -173,24 +216,38 @@ class ShardedParameters(GradWindow):
         # ---- buffers -------------------------------------------------------------------
         dev = self.device
         self.gathered = symm_mem.empty(self.numel, dtype=torch.bfloat16, device=dev)
-        self.grad = symm_mem.empty(self.numel, dtype=torch.float32, device=dev)
+        # gradients: norms and non-layer units in ``grad``; decoder layers in the rotating
+        # windows of ``grad_win`` (plan_grad_storage)
+        self.grad = symm_mem.empty(self.gstore.fixed_numel, dtype=torch.float32, device=dev)
+        K = self.gstore.windows
+        self.grad_win = symm_mem.empty(max(K * self.gstore.win_numel, 4), dtype=torch.float32, device=dev)
         self.master = symm_mem.empty(max(self.shard_numel, 4), dtype=torch.float32, device=dev)
         self.sync = symm_mem.empty(SYNC_WORDS + 64, dtype=torch.int32, device=dev)
         self.grad.zero_()
+        self.grad_win.zero_()
         self.master.zero_()
         self.sync.zero_()
         self.h_gath = symm_mem.rendezvous(self.gathered, self.group)
         self.h_grad = symm_mem.rendezvous(self.grad, self.group)
+        self.h_win = symm_mem.rendezvous(self.grad_win, self.group)
         self.h_master = symm_mem.rendezvous(self.master, self.group)
         self.h_sync = symm_mem.rendezvous(self.sync, self.group)
-        for h in (self.h_gath, self.h_grad, self.h_master, self.h_sync):
+        for h in (self.h_gath, self.h_grad, self.h_win, self.h_master, self.h_sync):
             if int(getattr(h, "offset", 0)) != 0:
                 raise RuntimeError("symmetric buffers must start at their allocation base")
         # NVLS: reduce-scatter with multimem.ld_reduce when the driver bound a multicast
         # object over the gradient buffers (PB_ALLREDUCE=p2p forces peer loads)
         use_mc = os.environ.get("PB_ALLREDUCE", "auto") in ("auto", "nvls")
         self.grad_mc = int(self.h_grad.multicast_ptr or 0) if use_mc else 0
+        self.win_mc = int(self.h_win.multicast_ptr or 0) if use_mc else 0
+        if not (self.grad_mc and self.win_mc):
+            self.grad_mc = self.win_mc = 0  # one kernel kind for every unit
         self.mode = "nvls" if self.grad_mc else "p2p"
+        # window w may be written again once this event (recorded on the communication
+        # stream after a later reduce-scatter, whose first barrier every rank passes only
+        # after finishing the reduce-scatter that read window w) has completed
+        self._win_free = [torch.cuda.Event() for _ in range(K)]
+        self._last_win_unit: Unit | None = None
         self.xchg_ptrs = torch.tensor([int(p) + 4 * SYNC_WORDS for p in self.h_sync.buffer_ptrs], dtype=torch.int64,
                                       device=dev)
         self.exp_avg = torch.zeros(max(self.shard_numel, 4), dtype=torch.float32, device=dev)
@@ -314,8 +371,57 @@ class ShardedParameters(GradWindow):
         self._ensure_gathered(params)
         return self._span(self.gathered, params)
 
+    def _unit_grad(self, u: Unit) -> torch.Tensor:
+        """The unit's gradient (its W * cs elements, unit layout) where it lives now."""
+        buf = self.grad_win if u.gwin >= 0 else self.grad
+        return buf[u.goff : u.goff + self.world * u.cs]
+
+    def _slot_grad(self, s: Slot) -> torch.Tensor:
+        u = self.unit_of.get(id(s.param))
+        if u is None:  # replicated norm: fixed buffer at its layout offset
+            return self.grad[s.offset : s.offset + s.numel]
+        return self._unit_grad(u)[s.offset - u.unit0 : s.offset - u.unit0 + s.numel]
+
     def grad_of(self, *params: nn.Parameter) -> torch.Tensor:
-        return self._span(self.grad, params)
+        slots = [self.by_param[id(p)] for p in params]
+        for a, b in zip(slots, slots[1:], strict=False):
+            if a.offset + a.numel != b.offset:
+                raise ValueError(f"parameters {a.name} and {b.name} are not adjacent")
+        cols = slots[0].shape[-1]
+        rows = sum(x.numel for x in slots) // cols
+        u = self.unit_of.get(id(params[0]))
+        if u is None:
+            return self.grad[slots[0].offset : slots[0].offset + rows * cols].view(rows, cols)
+        lo = slots[0].offset - u.unit0
+        return self._unit_grad(u)[lo : lo + rows * cols].view(rows, cols)
+
+    def prezero(self, *params: nn.Parameter) -> None:
+        """GradWindow.prezero over this layout: a decoder layer's window is zeroed (once
+        the window is free on every rank) in one fill of its claimed range."""
+        fresh = [p for p in params if id(p) not in self._fresh]
+        by_unit: dict[int, list[Slot]] = {}
+        for p in fresh:
+            u = self.unit_of.get(id(p))
+            by_unit.setdefault(id(u) if u is not None else 0, []).append(self.by_param[id(p)])
+        for key, slots in by_unit.items():
+            u = self.unit_of.get(id(slots[0].param))
+            if u is not None and u.gwin >= 0:
+                torch.cuda.current_stream(self.device).wait_event(self._win_free[u.gwin])
+            slots.sort(key=lambda x: x.offset)
+            runs: list[list[Slot]] = []
+            for x in slots:
+                if runs and runs[-1][-1].offset + runs[-1][-1].numel == x.offset:
+                    runs[-1].append(x)
+                else:
+                    runs.append([x])
+            for run in runs:
+                first, last = run[0], run[-1]
+                if u is None:
+                    self.grad[first.offset : last.offset + last.numel].zero_()
+                else:
+                    self._unit_grad(u)[first.offset - u.unit0 : last.offset - u.unit0 + last.numel].zero_()
+            for x in slots:
+                self._fresh.add(id(x.param))
 
     def embedding(self, ids: torch.Tensor, weight: nn.Parameter) -> torch.Tensor:
         u = self.unit_of[id(weight)]
@@ -329,14 +435,20 @@ class ShardedParameters(GradWindow):
 
     # ---- gradient protocol -------------------------------------------------------------
     def finish_window(self) -> None:
-        for s in self.slots:
+        """Zero the gradients no writer claimed this window: the norms, and the units whose
+        reduce-scatter has not been issued yet (issued ones were finished just before)."""
+        for s in self.rep_slots:
             if id(s.param) not in self._fresh:
                 self.grad[s.offset : s.offset + s.numel].zero_()
                 self._fresh.add(id(s.param))
+        for u in self.units:
+            if u.order not in self._issued:
+                self._finish_unit(u)
 
     def zero_grad(self) -> None:
         self._fresh.clear()
         self.grad.zero_()
+        self.grad_win.zero_()
 
     def start_step(self) -> None:
         """Called before the step's first backward: clears the norm accumulator."""
@@ -360,21 +472,31 @@ class ShardedParameters(GradWindow):
     def _finish_unit(self, u: Unit) -> None:
         for s in u.slots:
             if id(s.param) not in self._fresh:
-                self.grad[s.offset : s.offset + s.numel].zero_()
+                if u.gwin >= 0:
+                    torch.cuda.current_stream(self.device).wait_event(self._win_free[u.gwin])
+                self._slot_grad(s).zero_()
                 self._fresh.add(id(s.param))
 
     def _issue_rs(self, u: Unit, tail: bool = False) -> None:
         self._issued.add(u.order)
         self._finish_unit(u)
         self.comm.wait_stream(torch.cuda.current_stream(self.device))
+        win = u.gwin >= 0
         with torch.cuda.stream(self.comm):
             self._epoch += 1
-            lo = u.unit0 + self.rank * u.cs
+            lo = u.goff + self.rank * u.cs
+            h = self.h_win if win else self.h_grad
             _native.module().fsdp_reduce_scatter(
-                int(self.h_grad.buffer_ptrs_dev), int(self.h_sync.buffer_ptrs_dev), SYNC_WORDS, lo, lo + u.cs,
+                int(h.buffer_ptrs_dev), int(self.h_sync.buffer_ptrs_dev), SYNC_WORDS, lo, lo + u.cs,
                 self.shard_grad.data_ptr() + 4 * u.soff, self.rank, self.world, self._epoch, 1.0 / self.world,
-                self.sumsq, self.rs_ctas_tail if tail else self.rs_ctas, self.grad_mc,
+                self.sumsq, self.rs_ctas_tail if tail else self.rs_ctas, self.win_mc if win else self.grad_mc,
             )
+            # this launch's first barrier means every rank finished the reduce-scatter of
+            # the previous windowed unit: that window is free once this launch completes
+            if win:
+                if self._last_win_unit is not None:
+                    self._win_free[self._last_win_unit.gwin].record(self.comm)
+                self._last_win_unit = u
 
     # ---- optimizer step -----------------------------------------------------------------
     def optimizer_step(self, lr: float, b1: float, b2: float, eps: float, wd: float, bc1: float, bc2: float,
@@ -397,7 +519,7 @@ class ShardedParameters(GradWindow):
             self._epoch += 1
             self._arrive_total += self.final_ctas
             e = self.embed_unit
-            lo = e.unit0 + self.rank * e.cs
+            lo = e.goff + self.rank * e.cs
             C.fsdp_adamw(
                 [int(self.h_grad.buffer_ptrs_dev), int(self.h_sync.buffer_ptrs_dev), SYNC_WORDS, self.rank,
                  self.world, self._epoch, lo, lo + e.cs, self.shard_grad.data_ptr() + 4 * e.soff,
@@ -407,6 +529,11 @@ class ShardedParameters(GradWindow):
                 [1.0 / self.world, lr, b1, b2, eps, wd, bc1, bc2, max_norm],
                 self.sumsq, self.norm_out, self.skipped,
             )
+            # the optimizer kernel's barriers follow every reduce-scatter of the step:
+            # after it, every window is free on every rank
+            for ev in self._win_free:
+                ev.record(self.comm)
+        self._last_win_unit = None
         torch.cuda.current_stream(self.device).wait_stream(self.comm)
         self._issued.add(e.order)
         self._gathered_segs.clear()

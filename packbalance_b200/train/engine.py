@@ -219,7 +219,9 @@ class TrainEngine:
             # into the consuming GEMMs, reduce-scatter fused with the sharded AdamW.
             from packbalance_b200.parallel.sharded import ShardedAdamW, ShardedParameters
 
-            self.sharded = ShardedParameters(self.model)
+            # rotating gradient windows need one backward per step (the microbatch loop
+            # keeps every unit's gradient until the optimizer step)
+            self.sharded = ShardedParameters(self.model, grad_windows=None if cfg.train.fuse_microbatches else 0)
             self.model.flat = self.sharded
             self.flat = self.sharded
             self.dp = None

@@ -67,3 +67,52 @@ def test_8b_config_fits_on_b200_at_8_ranks() -> None:
     assert lay.shard_numel * 8 >= n - lay.rep_n
     per_rank = 2 * lay.numel + 4 * lay.numel + 16 * lay.shard_numel
     assert per_rank < 70e9, per_rank / 1e9
+
+
+@pytest.mark.parametrize("windows", [0, 2, 3])
+def test_gradient_windows_rotate_in_backward_order(model_cfg: ModelConfig, windows: int) -> None:
+    from packbalance_b200.parallel.sharded import plan_grad_storage
+
+    cfg = replace(model_cfg, n_layers=5, tie_embeddings=False)
+    lay = plan_layout(LlamaForCausalLM(cfg), 4)
+    st = plan_grad_storage(lay, 4, windows)
+    layers = [u for u in lay.units if u.name.startswith("layer")]
+    fixed = [u for u in lay.units if not u.name.startswith("layer")]
+    if windows == 0:
+        assert st.windows == 0 and all(u.gwin == -1 for u in lay.units)
+        assert st.fixed_numel == lay.numel  # every unit keeps its own storage
+    else:
+        assert st.windows == windows and st.win_numel == max(4 * u.cs for u in layers)
+        # backward order (last layer first) cycles through the windows
+        assert [u.gwin for u in reversed(layers)] == [i % windows for i in range(len(layers))]
+        assert all(u.goff == u.gwin * st.win_numel for u in layers)
+    if windows == 0:
+        assert all(u.goff == u.unit0 for u in lay.units)  # the layout itself
+    else:
+        # fixed-buffer units: after the norms, disjoint, in order
+        off = lay.rep_n
+        for u in fixed:
+            assert u.gwin == -1 and u.goff == off
+            off += 4 * u.cs
+        assert st.fixed_numel == off
+
+
+def test_8b_gradient_windows_shrink_the_per_rank_footprint() -> None:
+    """Config #5 on 8 ranks: three rotating windows instead of a model-size fp32
+    gradient buffer."""
+    from pathlib import Path
+
+    import torch
+
+    from packbalance_b200.config import load_config
+    from packbalance_b200.parallel.sharded import ShardedParameters, plan_grad_storage
+
+    cfg = load_config(Path(__file__).resolve().parents[1] / "configs" / "b5_8b_fsdp.yaml")
+    with torch.device("meta"):
+        model = LlamaForCausalLM(cfg.model)
+    lay = plan_layout(model, 8)
+    st = plan_grad_storage(lay, 8, ShardedParameters.GRAD_WINDOWS)
+    grad_bytes = 4 * (st.fixed_numel + st.windows * st.win_numel)
+    assert grad_bytes < 0.25 * 4 * lay.numel, grad_bytes / 1e9  # vs a full fp32 gradient
+    per_rank = 2 * lay.numel + grad_bytes + 16 * lay.shard_numel
+    assert per_rank < 40e9, per_rank / 1e9
