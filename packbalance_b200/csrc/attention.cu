@@ -153,8 +153,8 @@ __global__ void __launch_bounds__(320, 1)
       mbar_init(&o_done[i][1], 1);
     }
     mbar_init(&s_free, 8);
-    mbar_init(&o_free, 4);
-    mbar_init(&stats_ready, 4);
+    mbar_init(&o_free, 8);
+    mbar_init(&stats_ready, 8);
     mbar_init(&drain_bar, 1);
     abort_sh = 0;
     fence_mbar_init();
@@ -423,42 +423,51 @@ __global__ void __launch_bounds__(320, 1)
       }
       if (!ok) break;
       tc_fence_after();
-      if (grp == 1) {
-        stats[2 * r] = m;
-        stats[2 * r + 1] = l;
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&stats_ready);
-      } else {
-        if (!mbar_wait_warp(&stats_ready, item_n & 1, args.status, 212, &abort_sh)) break;
-        const float mb = stats[2 * r], lb = stats[2 * r + 1];
-        const float mm = fmaxf(m, mb);
+      // Both groups finish the item together: each publishes its (max, sum) per row, then
+      // group g merges the two partial O accumulators for head-dim columns
+      // [g D/2, (g + 1) D/2) and group 0 writes the log-sum-exp.
+      stats[grp * 256 + 2 * r] = m;
+      stats[grp * 256 + 2 * r + 1] = l;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&stats_ready);
+      if (!mbar_wait_warp(&stats_ready, item_n & 1, args.status, 212, &abort_sh)) break;
+      {
+        const float ma = stats[2 * r], la = stats[2 * r + 1];
+        const float mb = stats[256 + 2 * r], lb = stats[256 + 2 * r + 1];
+        const float mm = fmaxf(ma, mb);
         const float base = mm == -INFINITY ? 0.f : mm;
-        const float fa = fast_exp2(m - base), fb = fast_exp2(mb - base);
-        const float lt = l * fa + lb * fb;
+        const float fa = fast_exp2(ma - base), fb = fast_exp2(mb - base);
+        const float lt = la * fa + lb * fb;
         const float inv = lt > 0.f ? 1.f / lt : 0.f;
         const float sa = fa * inv, sbb = fb * inv;
 #pragma unroll
-        for (int c = 0; c < D; c += 16) {
-          uint32_t oa[16], ob[16];
-          tmem_ld16(tmem + lane_off + C::O_COL + c, oa);
-          tmem_ld16(tmem + lane_off + C::O_COL + D + c, ob);
-          tmem_wait_ld();
+        for (int c = grp * (D / 2); c < (grp + 1) * (D / 2); c += 32) {
+          uint32_t oa[32], ob[32];
+          tmem_ld32(tmem + lane_off + C::O_COL + c, oa);
+          tmem_ld32(tmem + lane_off + C::O_COL + D + c, ob);
+          tmem_wait_ld_regs(oa);
+          reg_fence(ob);
           if (qok) {
-            uint32_t pk[8];
-#pragma unroll
-            for (int i = 0; i < 8; ++i)
-              pk[i] = pack_bf16x2(__uint_as_float(oa[2 * i]) * sa + __uint_as_float(ob[2 * i]) * sbb,
-                                  __uint_as_float(oa[2 * i + 1]) * sa + __uint_as_float(ob[2 * i + 1]) * sbb);
             uint4* dst = reinterpret_cast<uint4*>(args.out + static_cast<long>(q) * H * D + h * D + c);
-            dst[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-            dst[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              uint32_t pk[4];
+#pragma unroll
+              for (int i = 0; i < 4; ++i) {
+                const int e = 8 * k + 2 * i;
+                pk[i] = pack_bf16x2(__uint_as_float(oa[e]) * sa + __uint_as_float(ob[e]) * sbb,
+                                    __uint_as_float(oa[e + 1]) * sa + __uint_as_float(ob[e + 1]) * sbb);
+              }
+              dst[k] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+            }
           }
         }
-        if (qok) args.lse[static_cast<long>(h) * T + q] = lt > 0.f ? (base + __log2f(lt)) * kLn2 : -INFINITY;
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&o_free);
+        if (grp == 0 && qok)
+          args.lse[static_cast<long>(h) * T + q] = lt > 0.f ? (base + __log2f(lt)) * kLn2 : -INFINITY;
       }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&o_free);
       kv_it += nkv;
     }
   }

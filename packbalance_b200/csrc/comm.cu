@@ -255,6 +255,169 @@ void fused_allreduce(int64_t ptrs_dev, int64_t pads_dev, int64_t pad_words, int6
   PB_CUDA_CHECK(cudaGetLastError());
 }
 
+// ------------------------------ bf16 wire (two-shot) ---------------------------------
+// The bucket crosses NVLink as bf16, half the bytes of the fp32 kernel; every sum is fp32.
+//   phase 0   each CTA casts its sub-range of every chunk of this rank's bucket to bf16
+//             into this rank's wire buffer (symmetric, same element indexing)
+//   barrier 0
+//   phase 1   rank r sums its chunk over the ranks' wires in rank order (fp32), scales,
+//             rounds to bf16, and writes the rounded value to its wire (for the peers)
+//             and, as fp32, to its gradient
+//   barrier 1
+//   phase 2   rank r copies the other ranks' reduced chunks from their wires (bf16 -> fp32)
+//   barrier 2
+// Every rank ends with the same (bf16-rounded) average, so the replicas stay identical.
+// Chunk and sub-range sizes are multiples of 8 elements (16-byte bf16 vectors).
+__device__ __forceinline__ void bf16x8_to_f32(uint4 v, float (&f)[8]) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 t = unpack_bf16x2(w[i]);
+    f[2 * i] = t.x;
+    f[2 * i + 1] = t.y;
+  }
+}
+
+template <int W>
+__global__ void __launch_bounds__(kCommThreads, kCommMinBlocks)
+    fused_allreduce_bf16_kernel(const ArArgs a, __nv_bfloat16* const* wires) {
+  __shared__ volatile int abort_sh;
+  __shared__ float red[32];
+  if (threadIdx.x == 0) abort_sh = 0;
+  __syncthreads();
+  const long n = a.hi - a.lo;
+  const long cs = ((n + W - 1) / W + 7) / 8 * 8;
+  const long sub = ((cs + gridDim.x - 1) / gridDim.x + 7) / 8 * 8;
+  float* mine = a.ptrs[a.rank];
+  __nv_bfloat16* wmine = wires[a.rank];
+  const long step = static_cast<long>(blockDim.x) * 8;
+  // phase 0: cast this CTA's sub-range of every chunk
+#pragma unroll 1
+  for (int c = 0; c < W; ++c) {
+    long s0, s1;
+    sub_range(a, cs, sub, c, s0, s1);
+    for (long i = s0 + threadIdx.x * 8; i < s1; i += step) {
+      if (i + 7 < s1) {
+        const float4 x0 = *reinterpret_cast<const float4*>(mine + i);
+        const float4 x1 = *reinterpret_cast<const float4*>(mine + i + 4);
+        *reinterpret_cast<uint4*>(wmine + i) = make_uint4(pack_bf16x2(x0.x, x0.y), pack_bf16x2(x0.z, x0.w),
+                                                          pack_bf16x2(x1.x, x1.y), pack_bf16x2(x1.z, x1.w));
+      } else {
+        for (long e = i; e < s1; ++e) wmine[e] = __float2bfloat16(mine[e]);
+      }
+    }
+  }
+  if (!cta_barrier(a, 0, &abort_sh)) return;
+  // phase 1: reduce this rank's chunk (fp32 sums in rank order)
+  float ss = 0.f;
+  {
+    long s0, s1;
+    sub_range(a, cs, sub, a.rank, s0, s1);
+    for (long i = s0 + threadIdx.x * 8; i < s1; i += step) {
+      if (i + 7 < s1) {
+        uint4 v[W];
+#pragma unroll
+        for (int p = 0; p < W; ++p) v[p] = __ldcg(reinterpret_cast<const uint4*>(wires[p] + i));
+        float acc[8], t[8];
+        bf16x8_to_f32(v[0], acc);
+#pragma unroll
+        for (int p = 1; p < W; ++p) {
+          bf16x8_to_f32(v[p], t);
+#pragma unroll
+          for (int k = 0; k < 8; ++k) acc[k] += t[k];
+        }
+        uint32_t pk[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) pk[k] = pack_bf16x2(acc[2 * k] * a.scale, acc[2 * k + 1] * a.scale);
+        const uint4 out = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+        *reinterpret_cast<uint4*>(wmine + i) = out;
+        float r[8];
+        bf16x8_to_f32(out, r);
+        *reinterpret_cast<float4*>(mine + i) = make_float4(r[0], r[1], r[2], r[3]);
+        *reinterpret_cast<float4*>(mine + i + 4) = make_float4(r[4], r[5], r[6], r[7]);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) ss += r[k] * r[k];
+      } else {
+        for (long e = i; e < s1; ++e) {
+          float acc = 0.f;
+          for (int p = 0; p < W; ++p) acc += __bfloat162float(__ldcg(wires[p] + e));
+          const __nv_bfloat16 b = __float2bfloat16(acc * a.scale);
+          wmine[e] = b;
+          const float r = __bfloat162float(b);
+          mine[e] = r;
+          ss += r * r;
+        }
+      }
+    }
+  }
+  if (!cta_barrier(a, 1, &abort_sh)) return;
+  // phase 2: the other ranks' reduced chunks
+#pragma unroll 1
+  for (int p = 0; p < W; ++p) {
+    if (p == a.rank) continue;
+    long s0, s1;
+    sub_range(a, cs, sub, p, s0, s1);
+    for (long i = s0 + threadIdx.x * 8; i < s1; i += step) {
+      if (i + 7 < s1) {
+        float r[8];
+        bf16x8_to_f32(__ldcg(reinterpret_cast<const uint4*>(wires[p] + i)), r);
+        *reinterpret_cast<float4*>(mine + i) = make_float4(r[0], r[1], r[2], r[3]);
+        *reinterpret_cast<float4*>(mine + i + 4) = make_float4(r[4], r[5], r[6], r[7]);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) ss += r[k] * r[k];
+      } else {
+        for (long e = i; e < s1; ++e) {
+          const float r = __bfloat162float(__ldcg(wires[p] + e));
+          mine[e] = r;
+          ss += r * r;
+        }
+      }
+    }
+  }
+  if (!cta_barrier(a, 2, &abort_sh)) return;
+  ss = warp_sum(ss);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x / 32] = ss;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float v = threadIdx.x < blockDim.x / 32 ? red[threadIdx.x] : 0.f;
+    v = warp_sum(v);
+    if (threadIdx.x == 0) atomicAdd(a.sumsq, v);
+  }
+}
+
+// wires_dev: device array of W bf16 wire buffers (symmetric; same indexing as the fp32
+// gradient buffers).  ``lo`` must be a multiple of 8 elements.
+void fused_allreduce_bf16(int64_t ptrs_dev, int64_t wires_dev, int64_t pads_dev, int64_t pad_words, int64_t lo,
+                          int64_t hi, int64_t rank, int64_t world, int64_t epoch, double scale, at::Tensor sumsq,
+                          int64_t ctas, int64_t epoch_base) {
+  TORCH_CHECK(sumsq.is_cuda() && sumsq.scalar_type() == at::kFloat);
+  TORCH_CHECK(lo % 8 == 0, "fused_allreduce_bf16: bucket start must be a multiple of 8 elements");
+  TORCH_CHECK(3 * ctas * world <= pad_words, "fused_allreduce_bf16: signal pad too small for ", ctas, " CTAs");
+  const c10::cuda::CUDAGuard guard(sumsq.device());
+  ArArgs a{};
+  a.ptrs = reinterpret_cast<float* const*>(ptrs_dev);
+  a.pads = reinterpret_cast<uint32_t* const*>(pads_dev);
+  a.lo = lo;
+  a.hi = hi;
+  a.rank = (int)rank;
+  a.world = (int)world;
+  a.epoch = static_cast<uint32_t>(epoch);
+  a.epoch_base = reinterpret_cast<const uint32_t*>(epoch_base);
+  a.scale = (float)scale;
+  a.sumsq = sumsq.data_ptr<float>();
+  a.status = status_ptr(sumsq.device().index());
+  auto wires = reinterpret_cast<__nv_bfloat16* const*>(wires_dev);
+  auto st = at::cuda::getCurrentCUDAStream();
+  switch (world) {
+#define PB_AR16(w) \
+  case w: fused_allreduce_bf16_kernel<w><<<pb::smem_max(fused_allreduce_bf16_kernel<w>, (int)ctas), kCommThreads, 0, st>>>(a, wires); break;
+    PB_AR16(2) PB_AR16(3) PB_AR16(4) PB_AR16(5) PB_AR16(6) PB_AR16(7) PB_AR16(8)
+#undef PB_AR16
+    default: TORCH_CHECK(false, "fused_allreduce_bf16: world size 2..8 on one node");
+  }
+  PB_CUDA_CHECK(cudaGetLastError());
+}
+
 __global__ void epoch_bump_kernel(uint32_t* base, uint32_t inc) { *base += inc; }
 
 // Adds ``inc`` to the device epoch base (stream-ordered, capturable in a CUDA graph).
@@ -269,6 +432,7 @@ void epoch_bump(at::Tensor base, int64_t inc) {
 void comm_bindings(pybind11::module& m) {
   m.def("epoch_bump", &epoch_bump);
   m.def("fused_allreduce", &fused_allreduce);
+  m.def("fused_allreduce_bf16", &fused_allreduce_bf16);
   m.def("nvls_allreduce", &nvls_allreduce);
 }
 
