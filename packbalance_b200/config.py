@@ -183,6 +183,10 @@ class TrainConfig:
     cuda_graphs: bool = True
     # Skip the optimizer step when the gradient norm is not finite.
     skip_nonfinite_steps: bool = True
+    # Data type on the wire of the fused gradient all-reduce: "fp32" (the reference's
+    # precision), or "bf16" (half the NVLink bytes; every sum in fp32, each rank's input
+    # and the average rounded to bf16, identical on every rank).
+    grad_reduce_dtype: str = "fp32"
 
     def __post_init__(self) -> None:
         if self.dtype not in DTYPES:
@@ -195,6 +199,8 @@ class TrainConfig:
             raise ValueError(f"comm_backend must be one of {COMM_BACKENDS}")
         if self.keep_last < 0:
             raise ValueError("keep_last must be >= 0")
+        if self.grad_reduce_dtype not in ("fp32", "bf16"):
+            raise ValueError("grad_reduce_dtype must be fp32 or bf16")
 
 
 @dataclass

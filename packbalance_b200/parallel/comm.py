@@ -47,7 +47,8 @@ class FusedAllReduce:
     CTAS_TAIL = 4 * 148
     SYNC_WORDS = 16384
 
-    def __init__(self, grad: torch.Tensor, group: dist.ProcessGroup | None = None, flat=None, mode: str | None = None) -> None:
+    def __init__(self, grad: torch.Tensor, group: dist.ProcessGroup | None = None, flat=None, mode: str | None = None,
+                 wire: str = "fp32") -> None:
         import os
 
         import torch.distributed._symmetric_memory as symm_mem
@@ -102,9 +103,25 @@ class FusedAllReduce:
         # one norm accumulator for both kernels: in the symmetric buffer, where the multimem
         # kernel adds every rank's part and the peer-load kernel adds the whole bucket's
         self.sumsq = full[n]
+        # bf16 wire: a symmetric bf16 copy of the gradient crosses NVLink instead of the
+        # fp32 values (the two-shot kernel; sums in fp32, result rounded to bf16 on every
+        # rank alike); bucket starts must then be multiples of 8 elements.
+        if wire not in ("fp32", "bf16"):
+            raise ValueError("wire must be fp32 or bf16")
+        self.wire = wire
+        self.h_wire = None
+        if wire == "bf16":
+            self.wire_buf = symm_mem.empty(n + 8, dtype=torch.bfloat16, device=grad.device)
+            self.h_wire = symm_mem.rendezvous(self.wire_buf, self.group)
+            self.mode = self.tail_mode = "p2p"
         if flat is not None:
             flat.rebind_grad(buf)
         _native.module().fused_allreduce  # fail loudly if the extension lacks the kernel
+
+    @property
+    def align(self) -> int:
+        """Required multiple (in elements) of a bucket's start."""
+        return 8 if self.wire == "bf16" else 4
 
     EPOCH_STRIDE = 64  # launches per step, at most
 
@@ -125,7 +142,12 @@ class FusedAllReduce:
             raise RuntimeError("more all-reduce launches in one step than the epoch stride allows")
         C = _native.module()
         base = self.epoch_base.data_ptr()
-        if mode == "nvls":
+        if self.wire == "bf16":
+            C.fused_allreduce_bf16(
+                self.handle.buffer_ptrs_dev, self.h_wire.buffer_ptrs_dev, self.h_sync.buffer_ptrs_dev, self.pad_words,
+                lo, hi, self.rank, self.world, self._k, 1.0 / self.world, self.sumsq, ctas, base,
+            )
+        elif mode == "nvls":
             n = self.buf.numel()
             C.nvls_allreduce(
                 self.handle.buffer_ptrs_dev, self.h_sync.buffer_ptrs_dev, self.pad_words, self.mc,
@@ -144,3 +166,4 @@ class FusedAllReduce:
     def close(self) -> None:
         self.handle = None
         self.h_sync = None
+        self.h_wire = None

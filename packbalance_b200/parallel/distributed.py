@@ -87,8 +87,11 @@ class DataParallel:
         group: dist.ProcessGroup | None = None,
         overlap: bool | None = None,
         deterministic: bool = False,
+        wire: str = "fp32",
     ) -> None:
         self.flat = flat
+        self.wire = wire
+        self.align = 8 if wire == "bf16" else 4  # bucket starts: 16-byte vectors of the wire type
         # deterministic mode: the peer-load kernel (sums in rank order) and a norm taken
         # afterwards in a fixed order (the fused partial norms are added atomically)
         self.deterministic = deterministic
@@ -106,7 +109,7 @@ class DataParallel:
 
             try:
                 self.fused = FusedAllReduce(flat.grad, group=group, flat=flat,
-                                            mode="p2p" if deterministic else None)
+                                            mode="p2p" if deterministic else None, wire=wire)
                 if deterministic:
                     self.fused.tail_mode = "p2p"
             except Exception as exc:  # peer memory unavailable
@@ -141,16 +144,16 @@ class DataParallel:
         """Contiguous ranges of whole parameters, last parameters first (backward order):
         a new bucket starts at every ready point (a decoder layer's first parameter) and
         wherever a bucket would exceed the size cap.  Bucket starts are 16-byte aligned
-        (cuts only at offsets that are multiples of 4)."""
+        in the wire type (cuts only at offsets that are multiples of ``align``)."""
         buckets: list[tuple[int, int]] = []
         hi = self.flat.numel
         lo = hi
         for s in reversed(self.flat.slots):
-            if hi - s.offset > self.cap and lo < hi and lo % 4 == 0:
+            if hi - s.offset > self.cap and lo < hi and lo % self.align == 0:
                 buckets.append((lo, hi))
                 hi = lo
             lo = s.offset
-            if s.name.endswith(self.READY_POINTS) and lo % 4 == 0 and lo < hi:
+            if s.name.endswith(self.READY_POINTS) and lo % self.align == 0 and lo < hi:
                 buckets.append((lo, hi))
                 hi = lo
         if lo < hi:
@@ -190,6 +193,12 @@ class DataParallel:
         with ctx:
             if self.fused is not None:
                 self.fused.all_reduce_mean(lo, hi, tail=tail)
+            elif self.wire == "bf16":
+                # library path of the bf16 wire: the same rounding of the inputs, the sum
+                # rounded once more by the library (identical on every rank)
+                w = view.to(torch.bfloat16)
+                dist.all_reduce(w, op=dist.ReduceOp.SUM, group=self.group)
+                view.copy_(w).mul_(1.0 / self.world)
             else:
                 dist.all_reduce(view, op=dist.ReduceOp.SUM, group=self.group)
                 view.mul_(1.0 / self.world)

@@ -253,7 +253,7 @@ class TrainEngine:
             self.flat = FlatParameters(self.model)
             self.model.flat = self.flat
             self.dp = DataParallel(self.flat, cfg.train.bucket_cap_mb, cfg.train.comm_backend,
-                                   deterministic=self.deterministic)
+                                   deterministic=self.deterministic, wire=cfg.train.grad_reduce_dtype)
             self.flat.ready_hook = self.dp.notify_ready
             self.optimizer = FlatAdamW(
                 self.flat,

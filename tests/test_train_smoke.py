@@ -67,9 +67,10 @@ def _free_port() -> int:
 
 
 @pytest.mark.slow
-@pytest.mark.parametrize("fsdp", [False, True])
-def test_two_rank_gloo_smoke(tmp_path: Path, store, data_cfg, fsdp: bool) -> None:
-    cfg = _write(_config(tmp_path / "ddp", data_cfg.data_dir, max_steps=2, save_interval=0, fsdp=fsdp), tmp_path / "c.yaml")
+@pytest.mark.parametrize("fsdp,wire", [(False, "fp32"), (True, "fp32"), (False, "bf16")])
+def test_two_rank_gloo_smoke(tmp_path: Path, store, data_cfg, fsdp: bool, wire: str) -> None:
+    cfg = _write(_config(tmp_path / "ddp", data_cfg.data_dir, max_steps=2, save_interval=0, fsdp=fsdp,
+                         grad_reduce_dtype=wire), tmp_path / "c.yaml")
     r = _run(["-m", "torch.distributed.run", "--standalone", "--nnodes=1", "--nproc_per_node=2",
               "-m", "packbalance_b200.train.train", "--config", str(cfg)],
              env={"MASTER_ADDR": "127.0.0.1", "MASTER_PORT": str(_free_port()), "OMP_NUM_THREADS": "1"})
