@@ -57,6 +57,8 @@ def parse_args():
     ap.add_argument("--mode", default="pack_ffd")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-count", action="store_true", help="skip the profiler pass that counts kernel launches")
+    ap.add_argument("--set", action="append", default=[], metavar="SECTION.KEY=VALUE",
+                    help="config override, e.g. train.fsdp_weight_windows=2 (repeatable)")
     return ap.parse_args()
 
 
@@ -234,7 +236,7 @@ def report(args, world, dev, rank, impl, step_ms_ranks, e2e_ms, tokens_steps, la
         "vs_baseline": None,
         "dtype": "bf16",
         "data": extra_cfg.pop("data_desc", "synthetic; random-init weights"),
-        "config": extra_cfg,
+        "config": {**extra_cfg, **({"overrides": list(args.set)} if args.set else {})},
         "clocks": clocks,
         "gpu_launches": launches,
     }
@@ -267,12 +269,12 @@ def time_steps(fn, steps: int, dev) -> list[float]:
 # ----------------------------------------------------------------------------------
 def run_ours(args, rank, world, dev) -> None:
     sys.path.insert(0, str(ROOT))
-    from packbalance_b200.config import load_config
+    from packbalance_b200.config import apply_overrides, load_config
     from packbalance_b200.data.dataset import PackedDataset, batch_tensor_bytes, concat_packs
     from packbalance_b200.ops import _native
     from packbalance_b200.train.engine import TrainEngine, to_device_batch
 
-    cfg = load_config(args.config)
+    cfg = apply_overrides(load_config(args.config), args.set)
     total = args.warmup + args.steps
     store, packs, sched, pstats = build_data(cfg, args.mode, world, rank, total)
     ds = PackedDataset(store, packs, cfg.data)
@@ -420,10 +422,10 @@ def run_reference(args, rank, world, dev) -> None:
     from packbalance.train.distributed import no_sync, wrap_model
 
     sys.path.insert(1, str(ROOT))
-    from packbalance_b200.config import load_config
+    from packbalance_b200.config import apply_overrides, load_config
     from packbalance_b200.data.prepare import prepare_synthetic
 
-    ours = load_config(args.config)
+    ours = apply_overrides(load_config(args.config), args.set)
     data_dir = ROOT / ours.data.data_dir
     if rank == 0 and not (data_dir / "meta.json").exists():
         prepare_synthetic(ours.data, data_dir)  # same corpus format; the reference reads it with its TokenStore

@@ -187,6 +187,11 @@ class TrainConfig:
     # precision), or "bf16" (half the NVLink bytes; every sum in fp32, each rank's input
     # and the average rounded to bf16, identical on every rank).
     grad_reduce_dtype: str = "fp32"
+    # Native sharded engine (fsdp on CUDA): 0 keeps every unit's gathered bf16 weights
+    # for the whole step (2 B/param per rank, no second all-gather); K >= 2 rotates the
+    # decoder layers' gathered weights through K windows of one layer, fetched again for
+    # the backward pass one layer ahead (the reference's FSDP2 resharding after forward).
+    fsdp_weight_windows: int = 0
 
     def __post_init__(self) -> None:
         if self.dtype not in DTYPES:
@@ -201,6 +206,8 @@ class TrainConfig:
             raise ValueError("keep_last must be >= 0")
         if self.grad_reduce_dtype not in ("fp32", "bf16"):
             raise ValueError("grad_reduce_dtype must be fp32 or bf16")
+        if self.fsdp_weight_windows < 0 or self.fsdp_weight_windows == 1:
+            raise ValueError("fsdp_weight_windows must be 0 or at least 2")
 
 
 @dataclass
@@ -240,6 +247,21 @@ def config_from_dict(raw: dict[str, Any]) -> PackBalanceConfig:
         raise ValueError(f"unknown config sections: {extra}")
     parts = {name: _section(cls, raw.get(name), name) for name, cls in _SECTIONS.items()}
     return PackBalanceConfig(**parts)
+
+
+def apply_overrides(config: PackBalanceConfig, items: list[str]) -> PackBalanceConfig:
+    """``section.key=value`` overrides (value parsed as YAML: ``2``, ``true``, ``bf16``),
+    validated like a config file."""
+    raw = asdict(config)
+    for item in items:
+        key, sep, value = item.partition("=")
+        section, dot, name = key.partition(".")
+        if not sep or not dot or section not in _SECTIONS:
+            raise ValueError(f"override {item!r}: expected section.key=value")
+        if name not in raw[section]:
+            raise ValueError(f"unknown {section} key in override: {name}")
+        raw[section][name] = yaml.safe_load(value)
+    return config_from_dict(raw)
 
 
 def save_config(config: PackBalanceConfig, path: str | Path) -> None:

@@ -1,10 +1,13 @@
 // Parameter all-gather over NVSwitch peer memory, as a role inside a consumer kernel.
 //
-// Sharded training keeps every sharded unit (a decoder layer's projection weights, the
-// embedding, the LM head) as one contiguous range of a bf16 "gathered" buffer that
-// every rank allocates in symmetric memory with the same layout.  Rank p owns elements
-// [unit0 + p * cs, unit0 + (p + 1) * cs) of a unit and writes them after its optimizer
-// step; the others fetch them before use.
+// Sharded training addresses every sharded unit (a decoder layer's projection weights,
+// the embedding, the LM head) in "gathered coordinates": elements [unit0, unit0 + W cs),
+// of which rank p owns [unit0 + p cs, unit0 + (p + 1) cs).  The owner writes the bf16
+// copy of its chunk into its symmetric "owned" buffer after its optimizer step; a fetch
+// copies the chunks into this rank's gathered storage (the unit's fixed place, or a
+// rotating window).  The spec carries per-owner source bases and a destination base
+// already offset by the unit's placement, so element e of owner p is read at src[p] + e
+// and written at dst + e.  ``copy_own`` also copies this rank's own chunk (local memory).
 //
 // A fetch of [lo, hi) is cut into pieces of 2^piece_shift elements (8 KB: one round of
 // 16-byte loads of a warp).  Copy warps of the consumer kernel (the GEMM that first reads
@@ -41,6 +44,7 @@ struct AgSpec {
   int rank, world;                  // world == 0: no gather in this launch
   int piece_shift, block_shift;
   int rot;                          // first piece handed out (no split)
+  int copy_own;                     // 1: copy this rank's chunk too (from src[rank])
   uint32_t* counters;               // [0]: tickets, [1 + b]: elements of block b made local
 };
 
@@ -132,7 +136,8 @@ __device__ __forceinline__ void ag_copy_warp(const AgSpec& s) {
     for (long e = e0; e < e1;) {
       const int p = static_cast<int>((e - s.unit0) / s.cs);
       const long seg_end = min(e1, s.unit0 + (p + 1) * s.cs);
-      if (p != s.rank && PB_BOUNDS_OK(p >= 0 && p < s.world, nullptr, 0)) ag_copy_span(s.src[p] + e, s.dst + e, seg_end - e);
+      if ((p != s.rank || s.copy_own) && PB_BOUNDS_OK(p >= 0 && p < s.world, nullptr, 0))
+        ag_copy_span(s.src[p] + e, s.dst + e, seg_end - e);
       e = seg_end;
     }
     fence_proxy_async_global();

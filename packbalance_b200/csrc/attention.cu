@@ -88,16 +88,20 @@ struct FwdCfg {
   static constexpr int KV_STAGES = D == 64 ? 4 : 2;
   static constexpr int K_OFF = 2 * TILE_BYTES;
   static constexpr int V_OFF = K_OFF + KV_STAGES * TILE_BYTES;
-  static constexpr int STAT_OFF = V_OFF + KV_STAGES * TILE_BYTES;  // group-1 (max, sum) per row
+  // (max, sum) per row of both softmax groups: 2 x 128 x 2 floats
+  static constexpr int STAT_OFF = V_OFF + KV_STAGES * TILE_BYTES;
+  static constexpr int STAT_BYTES = 2 * 128 * 2 * 4;
   // At least 120 KB so that a second CTA (which would block in tcgen05.alloc on
-  // the fully allocated TMEM) is never co-scheduled on the same SM.
-  static constexpr int SMEM_USED = STAT_OFF + 1024 + 1024;
+  // the fully allocated TMEM) is never co-scheduled on the same SM.  The last 1024 bytes
+  // are the slack of aligning the dynamic shared memory base to 1024.
+  static constexpr int SMEM_USED = STAT_OFF + STAT_BYTES + 1024;
   static constexpr int SMEM = SMEM_USED > 122880 ? SMEM_USED : 122880;
   static constexpr int S_BUFS = D == 64 ? 2 : 1;
   static constexpr uint32_t S_COL = 0;                 // S_BUFS x 128 columns
   static constexpr uint32_t P_COL = S_BUFS * 128;      // P[group][2] x 32 columns (64 bf16)
   static constexpr uint32_t O_COL = P_COL + 128;       // O[group] x D columns
   static_assert(O_COL + 2 * D <= 512, "TMEM budget");
+  static_assert(SMEM <= 232448, "shared memory budget");
   static constexpr uint32_t IDESC_S = idesc_bf16_f32(128, 128, false, false);
   static constexpr uint32_t IDESC_O = idesc_bf16_f32(128, D, false, true);
 };
@@ -423,7 +427,8 @@ __global__ void __launch_bounds__(320, 1)
       }
       if (!ok) break;
       tc_fence_after();
-      // Both groups finish the item together: each publishes its (max, sum) per row, then
+      // Both groups finish the item together: each publishes its (max, sum) per row (group
+      // g at stats[256 g ..], inside STAT_BYTES), then
       // group g merges the two partial O accumulators for head-dim columns
       // [g D/2, (g + 1) D/2) and group 0 writes the log-sum-exp.
       stats[grp * 256 + 2 * r] = m;

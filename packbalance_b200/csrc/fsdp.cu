@@ -1,12 +1,13 @@
 // Sharded data parallelism (FSDP) over NVSwitch peer memory (sm_100a).
 //
-// Layout (built by packbalance_b200/parallel/sharded.py).  Every rank allocates, in
-// symmetric memory and with the same layout, a bf16 "gathered" buffer holding all
-// weights, an fp32 gradient buffer of the same coordinates, and an fp32 master shard.
-// A sharded unit (one decoder layer's projections, the embedding, the LM head) covers
+// Layout (built by packbalance_b200/parallel/sharded.py).  A sharded unit (one decoder
+// layer's projections, the embedding, the LM head) covers gathered coordinates
 // [unit0, unit0 + W * cs); rank p owns [unit0 + p * cs, unit0 + (p + 1) * cs) and keeps
-// the fp32 master, Adam moments and reduced gradient of that chunk at offset
-// soff + (e - unit0 - p * cs) of its shard buffers (soff is the same on every rank).
+// the fp32 master, Adam moments, reduced gradient and bf16 copy ("owned") of that chunk
+// at offset soff + (e - unit0 - p * cs) of its shard buffers (soff is the same on every
+// rank; master and owned are symmetric memory).  Gradients live in symmetric fp32
+// buffers (fixed places and rotating per-layer windows); the gathered bf16 weights in
+// local storage that the fetches of ag_copy.cuh fill from the owners' bf16 chunks.
 // RMSNorm weights are few and small: they stay replicated in fp32 and their gradient
 // is averaged with the fused all-reduce (comm.cu).
 //
@@ -23,8 +24,8 @@
 //                         squared norms of all ranks' shards exchanged through peer
 //                         memory, clip coefficient, AdamW over the whole shard and the
 //                         replicated norms, bf16 copy of the updated shard written into
-//                         this rank's part of the gathered buffer, closing barrier (no
-//                         rank fetches a chunk before its owner has written it).
+//                         this rank's owned buffer, closing barrier (no rank fetches a
+//                         chunk before its owner has written it).
 //                         Cooperative launch: the CTAs wait for one another once.
 //   fsdp_embedding_fwd    the embedding lookup reads each token's row straight from
 //                         the owners' fp32 master shards, so the table is never gathered
@@ -414,11 +415,10 @@ at::Tensor fsdp_embedding_fwd(at::Tensor ids, int64_t masters_dev, int64_t row0,
   return out;
 }
 
-// ``ag``: the 13-field spec of gemm_tc's fused all-gather (b0 unused).
+// ``ag``: the spec of gemm_tc's fused all-gather (b0 unused).
 void parse_ag_spec(const std::vector<int64_t>& ag, AgSpec& s);
 
 void fsdp_all_gather(std::vector<int64_t> ag, int64_t ctas) {
-  TORCH_CHECK(ag.size() == 13, "fsdp_all_gather: 13 fields");
   AgSpec s{};
   parse_ag_spec(ag, s);
   if (s.hi <= s.lo) return;

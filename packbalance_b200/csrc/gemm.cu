@@ -117,8 +117,10 @@ static void dispatch_major(bool a_mn, bool b_mn, const CUtensorMap& ta, const CU
   else launch_gemm<BN, true, false>(ta, tb, to, tx, args, grid, s);
 }
 
-// 13-field all-gather spec shared by gemm_tc and fsdp_all_gather (ag_copy.cuh).
+// All-gather spec shared by gemm_tc and fsdp_all_gather (ag_copy.cuh): 13 fields, and an
+// optional 14th, copy_own.
 void parse_ag_spec(const std::vector<int64_t>& ag, AgSpec& s) {
+  TORCH_CHECK(ag.size() == 13 || ag.size() == 14, "ag spec: 13 or 14 fields");
   s.src = reinterpret_cast<const __nv_bfloat16* const*>(ag[0]);
   s.dst = reinterpret_cast<__nv_bfloat16*>(ag[1]);
   s.lo = ag[2];
@@ -132,6 +134,7 @@ void parse_ag_spec(const std::vector<int64_t>& ag, AgSpec& s) {
   s.piece_shift = (int)ag[10];
   s.block_shift = (int)ag[11];
   s.counters = reinterpret_cast<uint32_t*>(ag[12]);
+  s.copy_own = ag.size() > 13 ? (int)(ag[13] != 0) : 0;
   s.rot = 0;
   TORCH_CHECK(s.world >= 2 && s.world <= 8 && s.rank >= 0 && s.rank < s.world, "ag: rank/world");
   TORCH_CHECK(s.lo % 8 == 0 && s.hi % 8 == 0 && s.unit0 % 8 == 0 && s.cs % 8 == 0 && s.cs > 0 && s.split % 8 == 0,
@@ -260,8 +263,7 @@ void gemm_tc(at::Tensor a, at::Tensor b, at::Tensor out, int64_t M, int64_t N, i
   cudaStream_t stream0 = at::cuda::getCurrentCUDAStream();
   if (!ag.empty()) {
     // Fused all-gather of B: {src_ptrs_dev, dst, lo, hi, unit0, cs, b0, split, rank, world,
-    //                         piece_shift, block_shift, counters}
-    TORCH_CHECK(ag.size() == 13, "gemm_tc: ag spec has 13 fields");
+    //                         piece_shift, block_shift, counters[, copy_own]}
     TORCH_CHECK(!b_mn, "gemm_tc: the fused all-gather feeds a K-major B");
     AgSpec& s = g.ag;
     parse_ag_spec(ag, s);
@@ -274,11 +276,13 @@ void gemm_tc(at::Tensor a, at::Tensor b, at::Tensor out, int64_t M, int64_t N, i
     } else {
       // Copies start right after this rank's own range (or at lo when the range holds
       // none of it); tiles start with this rank's own rows (no wait), else with the
-      // rows of the first piece copied, so the MMAs follow the copies.
+      // rows of the first piece copied, so the MMAs follow the copies.  When the own
+      // chunk is copied too (from local memory, the fastest pieces), copies start at it.
       const long own0 = s.unit0 + s.rank * s.cs, own1 = own0 + s.cs;
       const bool mine = own0 < s.hi && own1 > s.lo;
       const long np = (s.hi - s.lo + (1L << s.piece_shift) - 1) >> s.piece_shift;
-      s.rot = (mine && own1 < s.hi) ? (int)((own1 - s.lo) >> s.piece_shift) : 0;
+      if (s.copy_own) s.rot = mine ? (int)((std::max(own0, s.lo) - s.lo) >> s.piece_shift) : 0;
+      else s.rot = (mine && own1 < s.hi) ? (int)((own1 - s.lo) >> s.piece_shift) : 0;
       if (s.rot >= np) s.rot = 0;
       const long first = mine ? std::max(own0, s.lo) : s.lo;
       const long row = std::max<long>(0, (first - s.b0) / K);

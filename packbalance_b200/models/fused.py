@@ -163,6 +163,7 @@ class _Decoder(torch.autograd.Function):
         flat = sc.flat
         C = _native.module()
         w_in, wq, wk, wv, wo, w_post, wg, wu, wd = ctx.params
+        flat.backward_begin(wq, wk, wv, wo, wg, wu, wd)
         if ctx.saved is None:  # checkpointed: recompute this layer's activations
             ctx.saved = _layer_forward(*ctx.inputs, ctx.params, sc)[2]
             ctx.inputs = None

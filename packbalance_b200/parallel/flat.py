@@ -59,6 +59,10 @@ class GradWindow:
             self._fresh.add(id(p))
         return False
 
+    def backward_begin(self, *params: nn.Parameter) -> None:
+        """A decoder layer's backward pass starts (``params``: its weights).  Replicated
+        weights need nothing; the sharded engine prefetches the previous layer here."""
+
     def prezero(self, *params: nn.Parameter) -> None:
         """Zero the gradients of ``params`` that no writer has claimed yet this window, with
         one fill per contiguous run of them, and claim them: their writers then add into

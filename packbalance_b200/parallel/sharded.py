@@ -5,13 +5,18 @@ per decoder layer, then the root) for the native CUDA path.  Same sharding units
 per decoder layer, one for the embedding, one for an untied LM head); the collectives
 are this framework's own kernels:
 
-* **all-gather fused into the consuming GEMM.**  Each unit lives in a bf16 "gathered"
-  buffer in symmetric memory (same layout on every rank; rank p owns the p-th of W
-  equal chunks of every unit).  The first GEMM that reads a unit's weights in a step
-  (the QKV GEMM for q|k|v|o, the gate|up GEMM for gate|up|down, the LM-head GEMM for
-  the head) carries copy warps that fetch the peer-owned chunks over NVLink while its
-  MMAs run on the tiles that are already local (``csrc/ag_copy.cuh``).  The embedding
-  lookup reads its rows straight from the owners' fp32 master shards.
+* **all-gather fused into the consuming GEMM.**  Rank p owns the p-th of W equal chunks
+  of every unit and keeps the bf16 copy of its chunks in a symmetric "owned" buffer
+  (written by its optimizer step).  A unit is used from this rank's bf16 gathered
+  storage: its own place (embedding, head, and every unit when the weights persist), or
+  one of ``weight_windows`` rotating windows (decoder layers).  The first GEMM that
+  reads a unit's weights (the QKV GEMM for q|k|v|o, the gate|up GEMM for gate|up|down,
+  the LM-head GEMM for the head) carries copy warps that fetch the chunks over NVLink
+  while its MMAs run on the tiles already copied (``csrc/ag_copy.cuh``).  With windows,
+  a layer's weights are fetched again for its backward pass: a narrow all-gather on a
+  side stream, issued when the next layer's backward starts (one layer ahead), like the
+  reference's FSDP2 resharding after forward with prefetch.  The embedding lookup reads
+  its rows straight from the owners' fp32 master shards.
 * **reduce-scatter as each unit's backward finishes**, on a communication stream: rank
   r sums chunk r of the unit's gradient over all ranks, scales by 1/W and keeps only
   that chunk (fp32), plus its squared norm.
@@ -21,11 +26,16 @@ are this framework's own kernels:
   the bf16 copy of its chunk into the gathered buffer for the next step's fetches
   (``csrc/fsdp.cu``).
 
-Memory per rank (B200 has 180 GB): bf16 weights 2 B/param (kept for the whole step,
-so the backward pass needs no second all-gather), fp32 gradient 4 B/param, and
-16 B/param / W of sharded fp32 master + moments + reduced gradient.  RMSNorm weights
-(a few KB per layer) stay replicated in fp32; their gradient is averaged with the
-fused all-reduce.
+Memory per rank (B200 has 180 GB), P parameters, W ranks, layer = the largest decoder
+layer's parameters, E = embedding + head parameters:
+
+* sharded state: 18 B/param / W (fp32 master, moments and reduced gradient, bf16 owned);
+* fp32 gradients: 4 B x E plus ``grad_windows`` (3) x 4 B x layer;
+* bf16 weights: 2 B x P persistent (``weight_windows`` = 0: the backward pass needs no
+  second all-gather), or 2 B x E plus ``weight_windows`` (2) x 2 B x layer.
+
+RMSNorm weights (a few KB per layer) stay replicated in fp32; their gradient is averaged
+with the fused all-reduce.
 
 Checkpoints use the reference's FSDP layout (``torch.distributed.checkpoint`` with
 ``model.<name>`` and AdamW ``optimizer.state.<i>.*`` keys, full tensors).
@@ -64,6 +74,9 @@ class Unit:
     # a rotating window (decoder layers), at element ``goff`` of that buffer
     gwin: int = -1  # window index, -1: fixed buffer
     goff: int = 0
+    # where its gathered bf16 weights live: own place or a rotating window, at ``woff``
+    wwin: int = -1
+    woff: int = 0
 
 
 def _units_of(model) -> tuple[list[Slot], list[Unit]]:
@@ -165,6 +178,41 @@ def plan_grad_storage(layout: Layout, world: int, windows: int) -> GradStorage:
     return GradStorage(off, win_numel, windows if rotate else 0)
 
 
+@dataclass
+class WeightStorage:
+    fixed_numel: int  # the non-layer units (all units without windows), then the windows
+    win_numel: int
+    windows: int
+    numel: int  # whole gathered storage
+
+
+def plan_weight_storage(layout: Layout, world: int, windows: int) -> WeightStorage:
+    """Physical placement of the gathered bf16 weights.  With ``windows`` = K > 0 the
+    decoder layers take K rotating windows of the largest layer's size (layer i in window
+    i % K): the forward pass gathers layer i while layers i-1 .. i-K+1 stay resident, the
+    backward pass gathers layer i-1 while layer i runs.  The embedding and an untied head
+    keep their own place.  With K = 0 every unit keeps its own place."""
+    layers = [u for u in layout.units if u.name.startswith("layer")]
+    if windows == 1:
+        raise ValueError("weight windows: 0 (persistent weights) or at least 2")
+    rotate = windows > 0 and len(layers) > 0
+    off = 0
+    for u in layout.units:
+        if rotate and u.name.startswith("layer"):
+            continue
+        u.wwin, u.woff = -1, off
+        off += world * u.cs
+    fixed = off
+    win_numel = 0
+    if rotate:
+        win_numel = max(world * u.cs for u in layers)
+        for i, u in enumerate(layers):
+            u.wwin = i % windows
+            u.woff = fixed + u.wwin * win_numel
+        off = fixed + windows * win_numel
+    return WeightStorage(fixed, win_numel, windows if rotate else 0, max(off, 8))
+
+
 class ShardedParameters(GradWindow):
     """Sharded parameter/gradient/optimizer-state buffers of one model (CUDA, W >= 2)."""
 
@@ -176,9 +224,11 @@ class ShardedParameters(GradWindow):
 
     # Decoder-layer gradients rotate through this many windows (0: a full gradient buffer).
     GRAD_WINDOWS = 3
+    # Width of the backward pass's weight prefetch (beside the running layer's kernels).
+    AG_CTAS_PREFETCH = 24
 
     def __init__(self, model, group: dist.ProcessGroup | None = None, rs_ctas: int | None = None,
-                 grad_windows: int | None = None) -> None:
+                 grad_windows: int | None = None, weight_windows: int = 0) -> None:
         import torch.distributed._symmetric_memory as symm_mem
 
         self.group = group if group is not None else dist.group.WORLD
@@ -196,6 +246,7 @@ class ShardedParameters(GradWindow):
         self.rep_n, self.numel, self.shard_numel = layout.rep_n, layout.numel, layout.shard_numel
         rep, units = layout.rep, layout.units
         self.gstore = plan_grad_storage(layout, W, self.GRAD_WINDOWS if grad_windows is None else grad_windows)
+        self.wstore = plan_weight_storage(layout, W, weight_windows)
         self.rep_slots = rep
         self.units = units
         self.embed_unit = units[0]
@@ -215,7 +266,10 @@ class ShardedParameters(GradWindow):
 
         # ---- buffers -------------------------------------------------------------------
         dev = self.device
-        self.gathered = symm_mem.empty(self.numel, dtype=torch.bfloat16, device=dev)
+        # bf16 weights: this rank's chunks (read by the peers' fetches) and the local
+        # gathered storage (plan_weight_storage)
+        self.owned = symm_mem.empty(max(self.shard_numel, 8), dtype=torch.bfloat16, device=dev)
+        self.gathered = torch.empty(self.wstore.numel, dtype=torch.bfloat16, device=dev)
         # gradients: norms and non-layer units in ``grad``; decoder layers in the rotating
         # windows of ``grad_win`` (plan_grad_storage)
         self.grad = symm_mem.empty(self.gstore.fixed_numel, dtype=torch.float32, device=dev)
@@ -227,12 +281,12 @@ class ShardedParameters(GradWindow):
         self.grad_win.zero_()
         self.master.zero_()
         self.sync.zero_()
-        self.h_gath = symm_mem.rendezvous(self.gathered, self.group)
+        self.h_owned = symm_mem.rendezvous(self.owned, self.group)
         self.h_grad = symm_mem.rendezvous(self.grad, self.group)
         self.h_win = symm_mem.rendezvous(self.grad_win, self.group)
         self.h_master = symm_mem.rendezvous(self.master, self.group)
         self.h_sync = symm_mem.rendezvous(self.sync, self.group)
-        for h in (self.h_gath, self.h_grad, self.h_win, self.h_master, self.h_sync):
+        for h in (self.h_owned, self.h_grad, self.h_win, self.h_master, self.h_sync):
             if int(getattr(h, "offset", 0)) != 0:
                 raise RuntimeError("symmetric buffers must start at their allocation base")
         # NVLS: reduce-scatter with multimem.ld_reduce when the driver bound a multicast
@@ -264,6 +318,18 @@ class ShardedParameters(GradWindow):
         self.go = torch.zeros(1, dtype=torch.int32, device=dev)
         max_blocks = max(((hi - lo) >> BLOCK_SHIFT) + 2 for u in units for lo, hi in u.segments)
         self.ag_counters = torch.zeros(max_blocks + 1, dtype=torch.int32, device=dev)
+        # fetch sources: owner p's element e of unit u sits at owned_p[soff + e - unit0 - p cs];
+        # row u holds the W bases that make that ``src[p] + e`` (bf16 elements)
+        src = [[int(self.h_owned.buffer_ptrs[p]) + 2 * (u.soff - u.unit0 - p * u.cs) for p in range(W)]
+               for u in units]
+        self.ag_src = torch.tensor(src, dtype=torch.int64, device=dev)
+        # backward-pass prefetch of the next layer's weights (side stream, own counters)
+        self.ag_stream = torch.cuda.Stream(device=dev, priority=-1)
+        self.ag_counters_pf = torch.zeros_like(self.ag_counters)
+        self.ag_ctas_prefetch = self.AG_CTAS_PREFETCH
+        Kw = self.wstore.windows
+        self._resident: list[Unit | None] = [None] * Kw  # unit gathered in each window
+        self._pending: list[torch.cuda.Event | None] = [None] * Kw  # prefetch not yet waited on
         self._epoch = 0  # barrier epochs (sync pads), one per collective launch
         self._arrive_total = 0
         cap = SYNC_WORDS // (3 * W)
@@ -279,23 +345,31 @@ class ShardedParameters(GradWindow):
                 self.rep_data[s.offset : s.offset + s.numel].copy_(s.param.detach().reshape(-1))
             for u in units:
                 full = self._unit_from_params(u)
-                self.gathered[u.unit0 : u.unit0 + W * u.cs].copy_(full)
                 lo = self.rank * u.cs
                 self.master[u.soff : u.soff + u.cs].copy_(full[lo : lo + u.cs])
-        # parameters become views: norms -> replicated fp32, sharded -> gathered bf16
+                self.owned[u.soff : u.soff + u.cs].copy_(full[lo : lo + u.cs])
+                if u.wwin < 0:
+                    self.gathered[u.woff : u.woff + W * u.cs].copy_(full)
+        # parameters become views: norms -> replicated fp32, sharded -> gathered bf16 (a
+        # windowed layer's view shows its weights only while the layer is resident)
         for s in rep:
             s.param.data = self.rep_data[s.offset : s.offset + s.numel].view(s.shape)
             s.param.grad = self.grad[s.offset : s.offset + s.numel].view(s.shape)
         for u in units:
             for s in u.slots:
                 s.param.grad = None
-                s.param.data = self.gathered[s.offset : s.offset + s.numel].view(s.shape)
+                o = u.woff + s.offset - u.unit0
+                s.param.data = self.gathered[o : o + s.numel].view(s.shape)
         self._segs = self._build_segments()
         self._fresh: set[int] = set()
-        self._gathered_segs: set[tuple[int, int]] = {seg for u in units for seg in u.segments}
+        self._gathered_segs: set[tuple[int, int]] = {seg for u in units if u.wwin < 0 for seg in u.segments}
         self._issued: set[int] = set()
         self.ready_hook = None
         self.hold_ready = False  # set while a non-final microbatch runs its backward pass
+        self.hold_prefetch = False  # tests: no backward-pass prefetch
+        # the first fetches read the peers' owned chunks written above
+        torch.cuda.synchronize(dev)
+        dist.barrier(group=self.group)
 
     # ---- construction helpers ---------------------------------------------------------
     def _unit_from_params(self, u: Unit) -> torch.Tensor:
@@ -307,12 +381,12 @@ class ShardedParameters(GradWindow):
 
     def _build_segments(self) -> torch.Tensor:
         rows = []
-        base = self.gathered.data_ptr()
+        base = self.owned.data_ptr()
         for u in self.units:
             rows.append([
                 self.master.data_ptr() + 4 * u.soff, self.exp_avg.data_ptr() + 4 * u.soff,
                 self.exp_avg_sq.data_ptr() + 4 * u.soff, self.shard_grad.data_ptr() + 4 * u.soff,
-                base + 2 * (u.unit0 + self.rank * u.cs), u.cs,
+                base + 2 * u.soff, u.cs,
             ])
         rows.append([self.rep_data.data_ptr(), self.rep_m.data_ptr(), self.rep_v.data_ptr(),
                      self.grad.data_ptr(), 0, self.rep_n])
@@ -322,14 +396,17 @@ class ShardedParameters(GradWindow):
     def slot(self, p: nn.Parameter) -> Slot:
         return self.by_param[id(p)]
 
-    def _span(self, buf: torch.Tensor, params) -> torch.Tensor:
+    def _span(self, params) -> torch.Tensor:
+        """[rows, cols] view of adjacent ``params`` in the gathered storage."""
         slots = [self.by_param[id(p)] for p in params]
         for a, b in zip(slots, slots[1:], strict=False):
             if a.offset + a.numel != b.offset:
                 raise ValueError(f"parameters {a.name} and {b.name} are not adjacent")
         cols = slots[0].shape[-1]
         rows = sum(s.numel for s in slots) // cols
-        return buf[slots[0].offset : slots[0].offset + rows * cols].view(rows, cols)
+        u = self.unit_of[id(params[0])]
+        o = u.woff + slots[0].offset - u.unit0
+        return self.gathered[o : o + rows * cols].view(rows, cols)
 
     def _segment(self, p: nn.Parameter) -> tuple[Unit, tuple[int, int]]:
         u = self.unit_of[id(p)]
@@ -339,11 +416,32 @@ class ShardedParameters(GradWindow):
                 return u, seg
         raise AssertionError("parameter outside its unit's segments")
 
-    def _ag_spec(self, u: Unit, seg: tuple[int, int], b0: int, split: int = 0) -> list[int]:
+    def _ag_spec(self, u: Unit, seg: tuple[int, int], b0: int, split: int = 0, counters: torch.Tensor | None = None
+                 ) -> list[int]:
+        # sources: the owners' ``owned`` buffers (row u of ag_src); destination: the unit's
+        # place in the gathered storage, both addressed by gathered-coordinate elements
         return [
-            int(self.h_gath.buffer_ptrs_dev), self.gathered.data_ptr(), seg[0], -(-seg[1] // 8) * 8, u.unit0, u.cs, b0,
-            split, self.rank, self.world, PIECE_SHIFT, BLOCK_SHIFT, self.ag_counters.data_ptr(),
+            self.ag_src[u.order].data_ptr(), self.gathered.data_ptr() + 2 * (u.woff - u.unit0), seg[0],
+            -(-seg[1] // 8) * 8, u.unit0, u.cs, b0, split, self.rank, self.world, PIECE_SHIFT, BLOCK_SHIFT,
+            (self.ag_counters if counters is None else counters).data_ptr(), 1,
         ]
+
+    def _make_resident(self, u: Unit) -> None:
+        """Bookkeeping before ``u`` is gathered: its window's previous unit is evicted."""
+        if u.wwin < 0:
+            return
+        prev = self._resident[u.wwin]
+        if prev is not None and prev is not u:
+            for seg in prev.segments:
+                self._gathered_segs.discard(seg)
+        self._resident[u.wwin] = u
+
+    def _use(self, u: Unit) -> None:
+        """The current stream is about to read ``u``'s gathered weights: wait for a
+        prefetch that filled its window."""
+        if u.wwin >= 0 and self._pending[u.wwin] is not None:
+            torch.cuda.current_stream(self.device).wait_event(self._pending[u.wwin])
+            self._pending[u.wwin] = None
 
     def gather_spec(self, *params: nn.Parameter) -> list[int] | None:
         """Spec of the fused all-gather for the GEMM that reads ``params`` as its B
@@ -352,7 +450,10 @@ class ShardedParameters(GradWindow):
             return None
         u, seg = self._segment(params[0])
         if seg in self._gathered_segs:
+            self._use(u)
             return None
+        self._make_resident(u)
+        self._use(u)
         self._gathered_segs.add(seg)
         # gate|up: the two matrices are copied interleaved, in the order SwiGLU tiles read them
         split = params[0].numel() if len(params) == 2 and params[0].shape == params[1].shape else 0
@@ -364,12 +465,40 @@ class ShardedParameters(GradWindow):
                 continue
             u, seg = self._segment(p)
             if seg not in self._gathered_segs:
+                self._make_resident(u)
+                self._use(u)
                 self._gathered_segs.add(seg)
                 _native.module().fsdp_all_gather(self._ag_spec(u, seg, seg[0]), 2 * _sms(self.device))
+            else:
+                self._use(u)
 
     def shadow_of(self, *params: nn.Parameter) -> torch.Tensor:
         self._ensure_gathered(params)
-        return self._span(self.gathered, params)
+        return self._span(params)
+
+    def backward_begin(self, *params: nn.Parameter) -> None:
+        """A decoder layer's backward pass starts (``params``: its weights).  With weight
+        windows, fetch the previous layer's weights into its window on the prefetch stream,
+        beside this layer's kernels; the window's last reader (the layer ``windows``
+        positions later) was enqueued on the current stream before this point."""
+        u = self.unit_of.get(id(params[0]))
+        if u is None or u.wwin < 0 or self.hold_prefetch:
+            return
+        prev = next((v for v in self.units if v.order == u.order - 1), None)
+        if prev is None or prev.wwin < 0 or all(seg in self._gathered_segs for seg in prev.segments):
+            return
+        cur = torch.cuda.current_stream(self.device)
+        self.ag_stream.wait_stream(cur)
+        self._make_resident(prev)
+        with torch.cuda.stream(self.ag_stream):
+            for seg in prev.segments:
+                if seg not in self._gathered_segs:
+                    self._gathered_segs.add(seg)
+                    _native.module().fsdp_all_gather(
+                        self._ag_spec(prev, seg, seg[0], counters=self.ag_counters_pf), self.ag_ctas_prefetch)
+            ev = torch.cuda.Event()
+            ev.record(self.ag_stream)
+        self._pending[prev.wwin] = ev
 
     def _unit_grad(self, u: Unit) -> torch.Tensor:
         """The unit's gradient (its W * cs elements, unit layout) where it lives now."""
@@ -505,6 +634,13 @@ class ShardedParameters(GradWindow):
         Leaves the global gradient norm in ``norm_out`` and the skip flag in ``skipped``."""
         C = _native.module()
         self.finish_window()
+        # every prefetch of this step has finished before the optimizer kernel's first
+        # barrier (after it the owners overwrite the chunks the prefetches read)
+        cur = torch.cuda.current_stream(self.device)
+        for w, ev in enumerate(self._pending):
+            if ev is not None:
+                cur.wait_event(ev)
+                self._pending[w] = None
         for u in self.units:
             if u.order not in self._issued and u is not self.embed_unit:
                 self._issue_rs(u, tail=True)
@@ -536,7 +672,17 @@ class ShardedParameters(GradWindow):
         self._last_win_unit = None
         torch.cuda.current_stream(self.device).wait_stream(self.comm)
         self._issued.add(e.order)
+        self._invalidate_gathered()
+
+    def _invalidate_gathered(self) -> None:
+        """The owned chunks changed: every unit is fetched again before its next use."""
         self._gathered_segs.clear()
+        self._resident = [None] * self.wstore.windows
+        cur = torch.cuda.current_stream(self.device)
+        for w, ev in enumerate(self._pending):
+            if ev is not None:
+                cur.wait_event(ev)
+                self._pending[w] = None
 
     def check(self) -> None:
         _native.check_status(self.device)
@@ -585,10 +731,15 @@ class ShardedParameters(GradWindow):
                     lo, hi = max(s.offset, c0), min(s.offset + s.numel, c1)
                     if lo < hi:
                         shard[u.soff + lo - c0 : u.soff + hi - c0].copy_(t[lo - s.offset : hi - s.offset])
-                    if which == "param":
-                        self.gathered[s.offset : s.offset + s.numel].copy_(t)
+            if which == "param":
+                for u in self.units:
+                    self.owned[u.soff : u.soff + u.cs].copy_(self.master[u.soff : u.soff + u.cs])
         if which == "param":
-            self._gathered_segs = {seg for u in self.units for seg in u.segments}
+            # the peers fetch these owned chunks in the next step: every rank has written its
+            # own before any rank reads
+            self._invalidate_gathered()
+            torch.cuda.synchronize(self.device)
+            dist.barrier(group=self.group)
 
     def model_order(self) -> list[Slot]:
         """Slots in ``model.named_parameters()`` order (the optimizer's param indices)."""

@@ -107,7 +107,7 @@ def main() -> None:
         def local_only():
             gemm(x, w_full, out, T, n, d, epi=epi, aux=aux)
 
-        shard = sp.gathered[u.unit0 + rank * u.cs: u.unit0 + (rank + 1) * u.cs].clone()
+        shard = sp.owned[u.soff: u.soff + u.cs].clone()
         full = torch.empty(world * u.cs, device=dev, dtype=torch.bfloat16)
 
         def nccl():

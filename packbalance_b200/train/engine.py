@@ -152,7 +152,9 @@ class _GraphedStep:
         self.graph = torch.cuda.CUDAGraph()
         fused.ASYNC_WGRAD = True  # weight gradients on a parallel branch of the graph
         try:
-            with torch.cuda.graph(self.graph):
+            # thread-local capture: a data-loader thread pinning host memory meanwhile
+            # (cudaHostAlloc) must not invalidate this thread's capture
+            with torch.cuda.graph(self.graph, capture_error_mode="thread_local"):
                 self.out = engine._native_body([self.static], self.loss_scale, self.hp)
         finally:
             fused.ASYNC_WGRAD = False
@@ -221,7 +223,8 @@ class TrainEngine:
 
             # rotating gradient windows need one backward per step (the microbatch loop
             # keeps every unit's gradient until the optimizer step)
-            self.sharded = ShardedParameters(self.model, grad_windows=None if cfg.train.fuse_microbatches else 0)
+            self.sharded = ShardedParameters(self.model, grad_windows=None if cfg.train.fuse_microbatches else 0,
+                                             weight_windows=cfg.train.fsdp_weight_windows)
             self.model.flat = self.sharded
             self.flat = self.sharded
             self.dp = None

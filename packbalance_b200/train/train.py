@@ -32,7 +32,7 @@ import torch
 import torch.distributed as dist
 from torch.profiler import record_function
 
-from packbalance_b200.config import PackBalanceConfig, load_config, save_config
+from packbalance_b200.config import PackBalanceConfig, apply_overrides, load_config, save_config
 from packbalance_b200.data.cost import FlopModel
 from packbalance_b200.data.dataset import build_dataloader, concat_packs, to_device
 from packbalance_b200.data.packer import build_packs, pack_stats
@@ -378,12 +378,14 @@ def parse_args(argv=None) -> argparse.Namespace:
     ap.add_argument("--compile", action="store_true")
     ap.add_argument("--profile", action="store_true")
     ap.add_argument("--no-fused-ce", action="store_true")
+    ap.add_argument("--set", action="append", default=[], metavar="SECTION.KEY=VALUE",
+                    help="config override, e.g. train.grad_reduce_dtype=bf16 (repeatable)")
     return ap.parse_args(argv)
 
 
 def main(argv=None) -> None:
     args = parse_args(argv)
-    cfg = load_config(args.config)
+    cfg = apply_overrides(load_config(args.config), args.set)
     if args.max_steps is not None:
         cfg.train.max_steps = args.max_steps
     if args.seed is not None:

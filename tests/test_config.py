@@ -43,3 +43,16 @@ def test_validation() -> None:
     with pytest.raises(ValueError):
         TrainConfig(dtype="fp8")
     assert abs(DataConfig(synthetic_median=256.0).lognormal_mu - 5.545) < 1e-3
+
+
+def test_overrides_parse_yaml_values_and_validate() -> None:
+    from packbalance_b200.config import PackBalanceConfig, apply_overrides
+
+    cfg = apply_overrides(PackBalanceConfig(), ["train.fsdp_weight_windows=2", "train.grad_reduce_dtype=bf16",
+                                                "model.tie_embeddings=false", "data.seq_len=1024"])
+    assert cfg.train.fsdp_weight_windows == 2 and cfg.train.grad_reduce_dtype == "bf16"
+    assert cfg.model.tie_embeddings is False and cfg.data.seq_len == 1024
+    for bad in ("train.nope=1", "train.fsdp_weight_windows", "nope.x=1", "train.fsdp_weight_windows=1",
+                "train.grad_reduce_dtype=fp16"):
+        with pytest.raises(ValueError):
+            apply_overrides(PackBalanceConfig(), [bad])

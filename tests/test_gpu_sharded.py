@@ -42,8 +42,12 @@ WORKER = textwrap.dedent(
     dev = torch.device("cuda", rank)
     dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=60), device_id=dev)
     tie = os.environ["PB_TIE"] == "1"
-    mcfg = ModelConfig(vocab_size=4096, d_model=256, n_layers=2, n_heads=4, n_kv_heads=2, d_ff=512, max_seq_len=512,
-                       tie_embeddings=tie, attention_backend="auto")
+    wwin = int(os.environ.get("PB_WWIN", "0"))
+    # with weight windows: more layers than windows, so layers are evicted and fetched
+    # again (backward prefetch); optionally with activation checkpointing (recompute)
+    mcfg = ModelConfig(vocab_size=4096, d_model=256, n_layers=5 if wwin else 2, n_heads=4, n_kv_heads=2, d_ff=512,
+                       max_seq_len=512, tie_embeddings=tie, attention_backend="auto",
+                       gradient_checkpointing=os.environ.get("PB_CKPT") == "1")
     dcfg = DataConfig(dataset="synthetic", data_dir=os.path.join(os.environ["PB_TMP"], f"d{rank}"), seq_len=512,
                       mode="pack_ffd", max_doc_len=512, min_doc_len=8, synthetic_num_docs=400, synthetic_mu=4.5,
                       synthetic_sigma=0.8, synthetic_min_len=16, synthetic_max_len=900, synthetic_vocab_size=4096,
@@ -56,13 +60,14 @@ WORKER = textwrap.dedent(
     mine = [ds[i] for i in range(rank * per, (rank + 1) * per)]
     tokens = sum(p.tokens for p in packs[: world * per])
     base = PackBalanceConfig(model=mcfg, data=dcfg, train=TrainConfig(lr=3e-3, warmup_steps=1, max_steps=10,
-                                                                     grad_clip=0.5, dtype="bf16"))
+                                                                     grad_clip=0.5, dtype="bf16",
+                                                                     fsdp_weight_windows=wwin))
     torch.manual_seed(0)
     ddp = TrainEngine(replace(base, train=replace(base.train, fsdp=False)), dev)
     init = {n: p.detach().float().cpu().clone() for n, p in ddp.model.named_parameters()}
     torch.manual_seed(0)
     shd = TrainEngine(replace(base, train=replace(base.train, fsdp=True)), dev)
-    assert shd.sharded is not None
+    assert shd.sharded is not None and shd.sharded.wstore.windows == wwin
     for step in range(3):
         a = ddp.step(mine, tokens)
         b = shd.step(mine, tokens)
@@ -109,14 +114,16 @@ WORKER = textwrap.dedent(
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-@pytest.mark.parametrize("tie,mode", [(True, "p2p"), (False, "p2p"), (True, "auto")])
-def test_sharded_engine_matches_ddp(tmp_path, tie, mode):
+@pytest.mark.parametrize("tie,mode,wwin,ckpt", [(True, "p2p", 0, 0), (False, "p2p", 0, 0), (True, "auto", 0, 0),
+                                               (False, "auto", 2, 0), (True, "p2p", 3, 1)])
+def test_sharded_engine_matches_ddp(tmp_path, tie, mode, wwin, ckpt):
     world = min(torch.cuda.device_count(), 4)
     script = tmp_path / "worker.py"
     script.write_text(WORKER)
     port = str(_free_port())
     env = {**os.environ, "PB_ROOT": str(ROOT), "PB_TMP": str(tmp_path), "PB_TIE": "1" if tie else "0",
-           "MASTER_ADDR": "127.0.0.1", "MASTER_PORT": port, "NCCL_NVLS_ENABLE": "0", "PB_ALLREDUCE": mode}
+           "MASTER_ADDR": "127.0.0.1", "MASTER_PORT": port, "NCCL_NVLS_ENABLE": "0", "PB_ALLREDUCE": mode,
+           "PB_WWIN": str(wwin), "PB_CKPT": str(ckpt)}
     r = subprocess.run(
         ["timeout", "-k", "30", "300", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
          f"--nproc-per-node={world}", "--master-addr=127.0.0.1", f"--master-port={port}", str(script)],

@@ -116,3 +116,54 @@ def test_8b_gradient_windows_shrink_the_per_rank_footprint() -> None:
     assert grad_bytes < 0.25 * 4 * lay.numel, grad_bytes / 1e9  # vs a full fp32 gradient
     per_rank = 2 * lay.numel + grad_bytes + 16 * lay.shard_numel
     assert per_rank < 40e9, per_rank / 1e9
+
+
+@pytest.mark.parametrize("windows", [0, 2, 3])
+def test_weight_windows_place_layers_in_forward_order(model_cfg: ModelConfig, windows: int) -> None:
+    from packbalance_b200.parallel.sharded import plan_weight_storage
+
+    cfg = replace(model_cfg, n_layers=5, tie_embeddings=False)
+    lay = plan_layout(LlamaForCausalLM(cfg), 4)
+    st = plan_weight_storage(lay, 4, windows)
+    layers = [u for u in lay.units if u.name.startswith("layer")]
+    fixed = [u for u in lay.units if not u.name.startswith("layer")]
+    # units with their own place: disjoint, in order, from 0
+    placed = lay.units if windows == 0 else fixed
+    off = 0
+    for u in placed:
+        assert u.wwin == -1 and u.woff == off
+        off += 4 * u.cs
+    assert st.fixed_numel == off
+    if windows == 0:
+        assert st.windows == 0 and st.numel == off
+    else:
+        assert st.windows == windows and st.win_numel == max(4 * u.cs for u in layers)
+        # forward order cycles through the windows; every window fits its largest layer
+        assert [u.wwin for u in layers] == [i % windows for i in range(len(layers))]
+        assert all(u.woff == st.fixed_numel + u.wwin * st.win_numel for u in layers)
+        assert st.numel == st.fixed_numel + windows * st.win_numel
+    with pytest.raises(ValueError):
+        plan_weight_storage(lay, 4, 1)
+
+
+def test_8b_weight_windows_shrink_the_per_rank_footprint() -> None:
+    """Config #5 on 8 ranks with two weight windows: the gathered bf16 weights are the
+    embedding, the head and two layers instead of the whole model."""
+    from pathlib import Path
+
+    import torch
+
+    from packbalance_b200.config import load_config
+    from packbalance_b200.parallel.sharded import ShardedParameters, plan_grad_storage, plan_weight_storage
+
+    cfg = load_config(Path(__file__).resolve().parents[1] / "configs" / "b5_8b_fsdp.yaml")
+    with torch.device("meta"):
+        model = LlamaForCausalLM(cfg.model)
+    lay = plan_layout(model, 8)
+    gs = plan_grad_storage(lay, 8, ShardedParameters.GRAD_WINDOWS)
+    ws = plan_weight_storage(lay, 8, 2)
+    weight_bytes = 2 * ws.numel
+    assert weight_bytes < 0.2 * 2 * lay.numel, weight_bytes / 1e9  # vs persistent bf16 weights
+    grad_bytes = 4 * (gs.fixed_numel + gs.windows * gs.win_numel)
+    per_rank = weight_bytes + grad_bytes + 18 * lay.shard_numel
+    assert per_rank < 30e9, per_rank / 1e9  # 41 GB with persistent weights
