@@ -3,14 +3,18 @@
 // Input is the fused QKV GEMM output qkv[T, (H + 2 Hkv) * D] (bf16, RoPE applied).
 // Query t attends to key k iff doc_start[t] <= k <= t.  Head dims 64 and 128.
 //
-// Forward (persistent; work items = (query tile of 128 rows, head), pre-sorted by
-// number of key tiles, most expensive first):
-//   warp 0      TMA: Q tile once per item, K/V tiles into a 2-deep ring
-//   warp 1      tcgen05.mma: S_j = Q K_j^T into one of two TMEM S buffers, then
-//               O += P_{j-1} V_{j-1} with P read from TMEM (A operand in tensor memory)
-//   warps 2..5  softmax, thread = query row: masking from doc_start, online max/sum in
-//               base 2, O rescale in TMEM when the max grows, P -> TMEM (bf16), final
-//               O / l and the log-sum-exp.
+// Forward (persistent; work items = (query tile of 128 rows, head), dealt to the CTAs
+// from a cost-ordered plan):
+//   warp 0        TMA: Q tile once per item (two buffers), K/V tiles into a ring
+//   warp 1        tcgen05.mma: S_j = Q K_j^T into TMEM, then O += P_{j-1} V_{j-1} with P
+//                 read from TMEM (A operand in tensor memory), one tile stream across items
+//   warps 2..9    softmax, thread = query row, two groups of four warps on the two key
+//                 column halves: masking from doc_start, online max/sum in base 2, lazy O
+//                 rescale in TMEM, P -> TMEM (bf16), then the row's (max, sum) to shared
+//                 memory, and on to the next item
+//   warps 10..13  epilogue, thread = query row: merges the groups' O accumulators,
+//                 O / l -> bf16 output, the log-sum-exp; frees the O buffer (two at
+//                 head_dim 64, so the next item's P V products do not wait for it).
 // Only key tiles from the first document start of the query tile up to the tile's
 // last row are visited; tiles entirely inside the causal/document window skip the
 // per-element mask.
@@ -88,19 +92,22 @@ struct FwdCfg {
   static constexpr int KV_STAGES = D == 64 ? 4 : 2;
   static constexpr int K_OFF = 2 * TILE_BYTES;
   static constexpr int V_OFF = K_OFF + KV_STAGES * TILE_BYTES;
-  // (max, sum) per row of both softmax groups: 2 x 128 x 2 floats
+  // (max, sum) per row of both softmax groups for two items: [item & 1][group][128][2]
   static constexpr int STAT_OFF = V_OFF + KV_STAGES * TILE_BYTES;
-  static constexpr int STAT_BYTES = 2 * 128 * 2 * 4;
+  static constexpr int STAT_BYTES = 2 * 2 * 128 * 2 * 4;
   // At least 120 KB so that a second CTA (which would block in tcgen05.alloc on
   // the fully allocated TMEM) is never co-scheduled on the same SM.  The last 1024 bytes
   // are the slack of aligning the dynamic shared memory base to 1024.
   static constexpr int SMEM_USED = STAT_OFF + STAT_BYTES + 1024;
   static constexpr int SMEM = SMEM_USED > 122880 ? SMEM_USED : 122880;
-  static constexpr int S_BUFS = D == 64 ? 2 : 1;
-  static constexpr uint32_t S_COL = 0;                 // S_BUFS x 128 columns
-  static constexpr uint32_t P_COL = S_BUFS * 128;      // P[group][2] x 32 columns (64 bf16)
-  static constexpr uint32_t O_COL = P_COL + 128;       // O[group] x D columns
-  static_assert(O_COL + 2 * D <= 512, "TMEM budget");
+  // TMEM columns: S (128), P[group][2 slots] x 32 (64 bf16 each), O[buffer][group] x D.
+  // Two O buffers at head_dim 64, so the next item's P V products run while the
+  // epilogue warps still read this item's O; one at 128 (512 columns in all).
+  static constexpr int O_BUFS = D == 64 ? 2 : 1;
+  static constexpr uint32_t S_COL = 0;
+  static constexpr uint32_t P_COL = 128;
+  static constexpr uint32_t O_COL = 256;
+  static_assert(O_COL + O_BUFS * 2 * D <= 512, "TMEM budget");
   static_assert(SMEM <= 232448, "shared memory budget");
   static constexpr uint32_t IDESC_S = idesc_bf16_f32(128, 128, false, false);
   static constexpr uint32_t IDESC_O = idesc_bf16_f32(128, D, false, true);
@@ -126,15 +133,16 @@ __device__ __forceinline__ int3 checked_item(int3 it, int T, int H, int* status)
 }
 
 template <int D>
-__global__ void __launch_bounds__(320, 1)
+__global__ void __launch_bounds__(448, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tmap, const AttnArgs args) {
   using C = FwdCfg<D>;
   // p_ready / o_done [group][P slot] (tile g uses slot g & 1): one barrier per slot, so
   // with the softmax groups running up to two tiles ahead of the P V products no
   // barrier ever completes a second phase before its first has been waited for.
+  // o_ready / o_free [O buffer] and stats_ready / stats_free [item & 1] hand an item's
+  // result from the softmax groups and the MMA warp to the epilogue warps and back.
   __shared__ __align__(8) uint64_t q_full[2], q_empty[2], kv_full[FwdCfg<D>::KV_STAGES], kv_empty[FwdCfg<D>::KV_STAGES],
-      s_full[2], s_free, p_ready[2][2],
-      o_done[2][2], o_free, stats_ready, drain_bar;
+      s_full, s_free, p_ready[2][2], o_done[2][2], o_ready[2], o_free[2], stats_ready[2], stats_free[2], drain_bar;
   __shared__ uint32_t tmem_sh;
   __shared__ volatile int abort_sh;
   extern __shared__ uint8_t dyn[];
@@ -149,16 +157,18 @@ __global__ void __launch_bounds__(320, 1)
       mbar_init(&kv_full[i], 1);
       mbar_init(&kv_empty[i], 1);
     }
+    mbar_init(&s_full, 1);
+    mbar_init(&s_free, 8);
     for (int i = 0; i < 2; ++i) {
-      mbar_init(&s_full[i], 1);
       mbar_init(&p_ready[i][0], 4);
       mbar_init(&p_ready[i][1], 4);
       mbar_init(&o_done[i][0], 1);
       mbar_init(&o_done[i][1], 1);
+      mbar_init(&o_ready[i], 1);
+      mbar_init(&o_free[i], 4);
+      mbar_init(&stats_ready[i], 8);
+      mbar_init(&stats_free[i], 4);
     }
-    mbar_init(&s_free, 8);
-    mbar_init(&o_free, 8);
-    mbar_init(&stats_ready, 8);
     mbar_init(&drain_bar, 1);
     abort_sh = 0;
     fence_mbar_init();
@@ -174,6 +184,7 @@ __global__ void __launch_bounds__(320, 1)
   const uint32_t tmem = tmem_sh;
   const int H = args.H, Hkv = args.Hkv, T = args.T;
   const int group = H / Hkv;
+  float* stats = reinterpret_cast<float*>(smem + C::STAT_OFF);
 
   if (warp == 0) {
     if (lane == 0) {
@@ -205,8 +216,9 @@ __global__ void __launch_bounds__(320, 1)
   } else if (warp == 1) {
     if (lane == 0) {
       // The key tiles of all this CTA's items form one stream g = 0, 1, ...: S_g is issued
-      // before P_{g-1} V_{g-1}, across item boundaries too, so when the softmax warps
-      // finish an item the next item's first scores are already in TMEM.
+      // (once both groups have read S_{g-1}) before P_{g-1} V_{g-1}, across item
+      // boundaries too, so when the softmax warps finish an item the next item's first
+      // scores are already in TMEM.
       bool ok = true;
       uint32_t q_it = 0;                                    // items whose Q the S side used
       int it_s = blockIdx.x, j_s = 0;                      // S side: item, tile within it
@@ -217,7 +229,8 @@ __global__ void __launch_bounds__(320, 1)
       uint32_t qa_s = smem_u32(smem + C::Q_OFF);
       int it_p = blockIdx.x, j_p = 0;                      // P V side, one tile behind
       int nkv_p = nkv_s;
-      uint32_t item_p = 0;                                  // items the P V side has started
+      uint32_t item_p = 0;                                  // items the P V side has finished
+      uint32_t ob = 0;                                      // O buffer of the P V side's item
       uint32_t g = 0, gp = 0;                               // global tile index of each side
       while (ok && (it_s < args.n_items || gp < g)) {
         if (it_s < args.n_items) {
@@ -229,18 +242,17 @@ __global__ void __launch_bounds__(320, 1)
           }
           const int s = g % C::KV_STAGES;
           if (!mbar_wait(&kv_full[s], (g / C::KV_STAGES) & 1, args.status, 205, &abort_sh)) break;
-          // With one S buffer, both groups must have read S_{g-1}.
-          if (C::S_BUFS == 1 && g > 0 && !mbar_wait(&s_free, (g - 1) & 1, args.status, 211, &abort_sh)) break;
+          // one S buffer: both groups must have read S_{g-1}
+          if (g > 0 && !mbar_wait(&s_free, (g - 1) & 1, args.status, 211, &abort_sh)) break;
           tc_fence_after();
           const uint32_t ka = smem_u32(smem + C::K_OFF + s * C::TILE_BYTES);
-          const uint32_t sb = tmem + C::S_COL + (g % C::S_BUFS) * 128;
 #pragma unroll
           for (int kk = 0; kk < D / 16; ++kk) {
             const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
-            umma_ss(sb, sdesc_sw128(qa_s + off, 16, 1024), sdesc_sw128(ka + off, 16, 1024), C::IDESC_S,
+            umma_ss(tmem + C::S_COL, sdesc_sw128(qa_s + off, 16, 1024), sdesc_sw128(ka + off, 16, 1024), C::IDESC_S,
                     kk > 0 ? 1u : 0u);
           }
-          umma_commit(&s_full[g % C::S_BUFS]);
+          umma_commit(&s_full);
           ++g;
           if (++j_s == nkv_s) {
             umma_commit(&q_empty[qb_s]);
@@ -257,9 +269,10 @@ __global__ void __launch_bounds__(320, 1)
           const int s = gp % C::KV_STAGES;
           const uint32_t va = smem_u32(smem + C::V_OFF + s * C::TILE_BYTES);
           if (j_p == 0) {
-            // The first PV of an item overwrites O: the previous item's O must be read out.
-            if (!mbar_wait(&o_free, (item_p & 1) ^ 1, args.status, 204, &abort_sh)) break;
-            ++item_p;
+            // The first P V of an item overwrites its O buffer: the epilogue must have
+            // read the item that used the buffer before.
+            ob = item_p % C::O_BUFS;
+            if (!mbar_wait(&o_free[ob], ((item_p / C::O_BUFS) & 1) ^ 1, args.status, 204, &abort_sh)) break;
           }
 #pragma unroll
           for (int grp = 0; grp < 2; ++grp) {
@@ -269,16 +282,19 @@ __global__ void __launch_bounds__(320, 1)
             }
             tc_fence_after();
             const uint32_t pa = tmem + C::P_COL + (grp * 2 + (gp & 1)) * 32;
+            const uint32_t oc = tmem + C::O_COL + (ob * 2 + grp) * D;
 #pragma unroll
             for (int kk = 0; kk < 4; ++kk)
-              umma_ts(tmem + C::O_COL + grp * D, pa + kk * 8, sdesc_sw128(va + grp * 8192 + kk * 2048, 16384, 1024),
-                      C::IDESC_O, (j_p > 0 || kk > 0) ? 1u : 0u);
+              umma_ts(oc, pa + kk * 8, sdesc_sw128(va + grp * 8192 + kk * 2048, 16384, 1024), C::IDESC_O,
+                      (j_p > 0 || kk > 0) ? 1u : 0u);
             umma_commit(&o_done[grp][gp & 1]);
           }
           if (!ok) break;
           umma_commit(&kv_empty[s]);
           ++gp;
           if (++j_p == nkv_p) {
+            umma_commit(&o_ready[ob]);  // every P V of the item: its O is final
+            ++item_p;
             j_p = 0;
             it_p += gridDim.x;
             if (it_p < args.n_items) {
@@ -291,33 +307,32 @@ __global__ void __launch_bounds__(320, 1)
       umma_commit(&drain_bar);
       mbar_wait(&drain_bar, 0, args.status, 207, nullptr);
     }
-  } else {
+  } else if (warp < 10) {
     // ---------------- softmax groups (thread = query row) ----------------
     const int grp = (warp - 2) / 4;  // 0: key columns 0-63, 1: key columns 64-127
     const int q4 = warp & 3;
     const int r = q4 * 32 + lane;
     const uint32_t lane_off = static_cast<uint32_t>(q4 * 32) << 16;
-    float* stats = reinterpret_cast<float*>(smem + C::STAT_OFF);
     uint32_t kv_it = 0, item_n = 0;
+    uint32_t pv_waited = 0;  // P V products (global tile index) whose completion this warp saw
     int3 nx = blockIdx.x < args.n_items ? checked_item(ld_item(args.items, blockIdx.x), args.T, args.H, args.status) : make_int3(0, 0, 0);
     int nlo = (blockIdx.x < args.n_items && nx.x * 128 + r < T) ? args.doc_start[nx.x * 128 + r] : 0x7fffffff;
     for (int it = blockIdx.x; it < args.n_items; it += gridDim.x, ++item_n) {
-      const int qt = nx.x, h = nx.y, kt0 = nx.z;
+      const int qt = nx.x, kt0 = nx.z;
       const int lo = nlo;
       if (it + (int)gridDim.x < args.n_items) {
         nx = checked_item(ld_item(args.items, it + gridDim.x), args.T, args.H, args.status);
         nlo = nx.x * 128 + r < T ? args.doc_start[nx.x * 128 + r] : 0x7fffffff;
       }
-      const int q0 = qt * 128;
+      const uint32_t ob = item_n % C::O_BUFS;
       const int nkv = qt - kt0 + 1;
-      const int q = q0 + r;
+      const int q = qt * 128 + r;
       const bool qok = q < T;
       float m = -INFINITY, l = 0.f;
       bool ok = true;
-      uint32_t pv_waited = 0;  // o_done phases of this item waited so far
       for (int j = 0; j < nkv; ++j) {
         const uint32_t g = kv_it + j;
-        if (!mbar_wait_warp(&s_full[g % C::S_BUFS], (g / C::S_BUFS) & 1, args.status, 208, &abort_sh)) {
+        if (!mbar_wait_warp(&s_full, g & 1, args.status, 208, &abort_sh)) {
           ok = false;
           break;
         }
@@ -325,15 +340,13 @@ __global__ void __launch_bounds__(320, 1)
         const int kv0 = (kt0 + j) * 128 + grp * 64;
         // Both 32-column halves of this group's raw scores, one wait for the two loads.
         uint32_t sv[2][32];
-        tmem_ld32(tmem + lane_off + C::S_COL + (g % C::S_BUFS) * 128 + grp * 64, sv[0]);
-        tmem_ld32(tmem + lane_off + C::S_COL + (g % C::S_BUFS) * 128 + grp * 64 + 32, sv[1]);
+        tmem_ld32(tmem + lane_off + C::S_COL + grp * 64, sv[0]);
+        tmem_ld32(tmem + lane_off + C::S_COL + grp * 64 + 32, sv[1]);
         tmem_wait_ld_regs(sv[0]);
         reg_fence(sv[1]);
-        if (C::S_BUFS == 1) {
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&s_free);
-        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&s_free);  // the next S may overwrite the buffer
         // raw score i of this thread's row (masked to -inf below)
 #define PB_S(i) __uint_as_float(sv[(i) >> 5][(i) & 31])
         // Tiles inside every row's window (most tiles of long documents) skip the mask;
@@ -379,11 +392,13 @@ __global__ void __launch_bounds__(320, 1)
 #undef PB_S
         const float sum = (sum4[0] + sum4[1]) + (sum4[2] + sum4[3]);
         l = l * corr + sum;
-        // P V products of this item that must be complete: tiles <= j - 2 (their P slot is
-        // reused now) and, to rescale O, tile j - 1 too, waited tile by tile in order.
-        const uint32_t need_done = rescale ? j : (j > 0 ? j - 1 : 0);
+        // P V products that must be complete, waited in stream order: tiles <= g - 2
+        // (their P slot is reused now; across item boundaries too) and, to rescale this
+        // item's O, tile g - 1.
+        const bool rs = rescale && j > 0;
+        const uint32_t need_done = rs ? g : (g >= 2 ? g - 1 : 0);
         while (pv_waited < need_done) {
-          const uint32_t t = kv_it + pv_waited;
+          const uint32_t t = pv_waited;
           if (!mbar_wait_warp(&o_done[grp][t & 1], (t >> 1) & 1, args.status, 209, &abort_sh)) {
             ok = false;
             break;
@@ -392,15 +407,16 @@ __global__ void __launch_bounds__(320, 1)
         }
         if (!ok) break;
         tc_fence_after();
-        if (rescale && j > 0) {
+        if (rs) {
+          const uint32_t oc = C::O_COL + (ob * 2 + grp) * D;
 #pragma unroll
           for (int c = 0; c < D; c += 16) {
             uint32_t ov[16];
-            tmem_ld16(tmem + lane_off + C::O_COL + grp * D + c, ov);
+            tmem_ld16(tmem + lane_off + oc + c, ov);
             tmem_wait_ld();
 #pragma unroll
             for (int i = 0; i < 16; ++i) ov[i] = __float_as_uint(__uint_as_float(ov[i]) * corr);
-            tmem_st16(tmem + lane_off + C::O_COL + grp * D + c, ov);
+            tmem_st16(tmem + lane_off + oc + c, ov);
           }
         }
         m = m_new == -INFINITY ? m : base;
@@ -417,63 +433,70 @@ __global__ void __launch_bounds__(320, 1)
         if (lane == 0) mbar_arrive(&p_ready[grp][g & 1]);
       }
       if (!ok) break;
-      while (pv_waited < static_cast<uint32_t>(nkv)) {  // every P V of the item
-        const uint32_t t = kv_it + pv_waited;
-        if (!mbar_wait_warp(&o_done[grp][t & 1], (t >> 1) & 1, args.status, 210, &abort_sh)) {
-          ok = false;
-          break;
-        }
-        ++pv_waited;
-      }
-      if (!ok) break;
-      tc_fence_after();
-      // Both groups finish the item together: each publishes its (max, sum) per row (group
-      // g at stats[256 g ..], inside STAT_BYTES), then
-      // group g merges the two partial O accumulators for head-dim columns
-      // [g D/2, (g + 1) D/2) and group 0 writes the log-sum-exp.
-      stats[grp * 256 + 2 * r] = m;
-      stats[grp * 256 + 2 * r + 1] = l;
+      // Publish this row's (max, sum) for the epilogue and go on with the next item.
+      const uint32_t sb = item_n & 1;
+      if (!mbar_wait_warp(&stats_free[sb], ((item_n >> 1) & 1) ^ 1, args.status, 212, &abort_sh)) break;
+      stats[((sb * 2 + grp) * 128 + r) * 2] = m;
+      stats[((sb * 2 + grp) * 128 + r) * 2 + 1] = l;
       __syncwarp();
-      if (lane == 0) mbar_arrive(&stats_ready);
-      if (!mbar_wait_warp(&stats_ready, item_n & 1, args.status, 212, &abort_sh)) break;
-      {
-        const float ma = stats[2 * r], la = stats[2 * r + 1];
-        const float mb = stats[256 + 2 * r], lb = stats[256 + 2 * r + 1];
-        const float mm = fmaxf(ma, mb);
-        const float base = mm == -INFINITY ? 0.f : mm;
-        const float fa = fast_exp2(ma - base), fb = fast_exp2(mb - base);
-        const float lt = la * fa + lb * fb;
-        const float inv = lt > 0.f ? 1.f / lt : 0.f;
-        const float sa = fa * inv, sbb = fb * inv;
+      if (lane == 0) mbar_arrive(&stats_ready[sb]);
+      kv_it += nkv;
+    }
+  } else {
+    // ---------------- epilogue (thread = query row) ----------------
+    // Merges the two groups' partial O accumulators of an item with their (max, sum),
+    // writes O / l as bf16 and the log-sum-exp, and frees the O buffer and the stats.
+    const int q4 = warp & 3;
+    const int r = q4 * 32 + lane;
+    const uint32_t lane_off = static_cast<uint32_t>(q4 * 32) << 16;
+    uint32_t item_n = 0;
+    for (int it = blockIdx.x; it < args.n_items; it += gridDim.x, ++item_n) {
+      const int3 c3 = checked_item(ld_item(args.items, it), args.T, args.H, args.status);
+      const int h = c3.y;
+      const int q = c3.x * 128 + r;
+      const bool qok = q < T;
+      const uint32_t sb = item_n & 1, ob = item_n % C::O_BUFS;
+      if (!mbar_wait_warp(&stats_ready[sb], (item_n >> 1) & 1, args.status, 213, &abort_sh)) break;
+      if (!mbar_wait_warp(&o_ready[ob], (item_n / C::O_BUFS) & 1, args.status, 210, &abort_sh)) break;
+      tc_fence_after();
+      const float ma = stats[((sb * 2) * 128 + r) * 2], la = stats[((sb * 2) * 128 + r) * 2 + 1];
+      const float mb = stats[((sb * 2 + 1) * 128 + r) * 2], lb = stats[((sb * 2 + 1) * 128 + r) * 2 + 1];
+      const float mm = fmaxf(ma, mb);
+      const float base = mm == -INFINITY ? 0.f : mm;
+      const float fa = fast_exp2(ma - base), fb = fast_exp2(mb - base);
+      const float lt = la * fa + lb * fb;
+      const float inv = lt > 0.f ? 1.f / lt : 0.f;
+      const float sa = fa * inv, sbb = fb * inv;
+      const uint32_t oc = C::O_COL + ob * 2 * D;
 #pragma unroll
-        for (int c = grp * (D / 2); c < (grp + 1) * (D / 2); c += 32) {
-          uint32_t oa[32], ob[32];
-          tmem_ld32(tmem + lane_off + C::O_COL + c, oa);
-          tmem_ld32(tmem + lane_off + C::O_COL + D + c, ob);
-          tmem_wait_ld_regs(oa);
-          reg_fence(ob);
-          if (qok) {
-            uint4* dst = reinterpret_cast<uint4*>(args.out + static_cast<long>(q) * H * D + h * D + c);
+      for (int c = 0; c < D; c += 32) {
+        uint32_t oa[32], obv[32];
+        tmem_ld32(tmem + lane_off + oc + c, oa);
+        tmem_ld32(tmem + lane_off + oc + D + c, obv);
+        tmem_wait_ld_regs(oa);
+        reg_fence(obv);
+        if (qok) {
+          uint4* dst = reinterpret_cast<uint4*>(args.out + static_cast<long>(q) * H * D + h * D + c);
 #pragma unroll
-            for (int k = 0; k < 4; ++k) {
-              uint32_t pk[4];
+          for (int k = 0; k < 4; ++k) {
+            uint32_t pk[4];
 #pragma unroll
-              for (int i = 0; i < 4; ++i) {
-                const int e = 8 * k + 2 * i;
-                pk[i] = pack_bf16x2(__uint_as_float(oa[e]) * sa + __uint_as_float(ob[e]) * sbb,
-                                    __uint_as_float(oa[e + 1]) * sa + __uint_as_float(ob[e + 1]) * sbb);
-              }
-              dst[k] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+            for (int i = 0; i < 4; ++i) {
+              const int e = 8 * k + 2 * i;
+              pk[i] = pack_bf16x2(__uint_as_float(oa[e]) * sa + __uint_as_float(obv[e]) * sbb,
+                                  __uint_as_float(oa[e + 1]) * sa + __uint_as_float(obv[e + 1]) * sbb);
             }
+            dst[k] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
           }
         }
-        if (grp == 0 && qok)
-          args.lse[static_cast<long>(h) * T + q] = lt > 0.f ? (base + __log2f(lt)) * kLn2 : -INFINITY;
       }
+      if (qok) args.lse[static_cast<long>(h) * T + q] = lt > 0.f ? (base + __log2f(lt)) * kLn2 : -INFINITY;
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&o_free);
-      kv_it += nkv;
+      if (lane == 0) {
+        mbar_arrive(&o_free[ob]);
+        mbar_arrive(&stats_free[sb]);
+      }
     }
   }
   tc_fence_before();
@@ -1020,10 +1043,10 @@ std::vector<at::Tensor> attn_fwd(at::Tensor qkv, at::Tensor doc_start, at::Tenso
   auto s = at::cuda::getCurrentCUDAStream();
   if (D == 64) {
     set_smem(attn_fwd_kernel<64>, FwdCfg<64>::SMEM);
-    attn_fwd_kernel<64><<<pb::smem_max(attn_fwd_kernel<64>, grid), 320, FwdCfg<64>::SMEM, s>>>(tm, a);
+    attn_fwd_kernel<64><<<pb::smem_max(attn_fwd_kernel<64>, grid), 448, FwdCfg<64>::SMEM, s>>>(tm, a);
   } else {
     set_smem(attn_fwd_kernel<128>, FwdCfg<128>::SMEM);
-    attn_fwd_kernel<128><<<pb::smem_max(attn_fwd_kernel<128>, grid), 320, FwdCfg<128>::SMEM, s>>>(tm, a);
+    attn_fwd_kernel<128><<<pb::smem_max(attn_fwd_kernel<128>, grid), 448, FwdCfg<128>::SMEM, s>>>(tm, a);
   }
   PB_CUDA_CHECK(cudaGetLastError());
   return {out, lse};
