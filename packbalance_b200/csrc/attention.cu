@@ -72,7 +72,18 @@ struct AttnArgs {
   // backward
   const float* delta;  // [H, T]
   int* status;
+  // Optional event trace (nullptr: off): [CTA][kTraceRoles][kTraceMax] SM clock stamps.
+  unsigned long long* trace;
 };
+
+// Event trace of the attention kernels, for finding where an item's time goes: each
+// role's lane 0 stamps clock64() at its steps (see the roles in each kernel).  Off
+// unless a buffer was set with attn_trace(); the test is one uniform branch.
+constexpr int kTraceRoles = 8, kTraceMax = 128;
+__device__ __forceinline__ void trace_ev(unsigned long long* tr, int role, uint32_t idx) {
+  if (tr != nullptr && idx < static_cast<uint32_t>(kTraceMax))
+    tr[(static_cast<size_t>(blockIdx.x) * kTraceRoles + role) * kTraceMax + idx] = clock64();
+}
 
 // =================================== forward ======================================
 // Two softmax warpgroups per query tile: group g owns key columns [64g, 64g + 64) of
@@ -185,6 +196,10 @@ __global__ void __launch_bounds__(448, 1)
   const int H = args.H, Hkv = args.Hkv, T = args.T;
   const int group = H / Hkv;
   float* stats = reinterpret_cast<float*>(smem + C::STAT_OFF);
+  // trace roles: 0 Q load issued (per item; slot 127: start), 1 K/V load issued, 2 S
+  // issued, 3 P V issued (per tile), 4 S read by softmax warp 2, 5 its P ready (per
+  // tile), 6 epilogue warp 10 starts an item, 7 ... ends it
+  if (threadIdx.x == 0) trace_ev(args.trace, 0, kTraceMax - 1);
 
   if (warp == 0) {
     if (lane == 0) {
@@ -200,6 +215,7 @@ __global__ void __launch_bounds__(448, 1)
         if (!mbar_wait(&q_empty[qb], ((q_it >> 1) & 1) ^ 1, args.status, 201, &abort_sh)) break;
         mbar_arrive_expect_tx(&q_full[qb], C::TILE_BYTES);
         load_tile_rows(smem + C::Q_OFF + qb * C::TILE_BYTES, &tmap, &q_full[qb], h * D, q0, D);
+        trace_ev(args.trace, 0, q_it);
         ++q_it;
         for (int kt = kt0; kt <= qt; ++kt, ++kv_it) {
           const int s = kv_it % C::KV_STAGES;
@@ -210,6 +226,7 @@ __global__ void __launch_bounds__(448, 1)
           mbar_arrive_expect_tx(&kv_full[s], 2 * C::TILE_BYTES);
           load_tile_rows(smem + C::K_OFF + s * C::TILE_BYTES, &tmap, &kv_full[s], (H + hk) * D, kt * 128, D);
           load_tile_rows(smem + C::V_OFF + s * C::TILE_BYTES, &tmap, &kv_full[s], (H + Hkv + hk) * D, kt * 128, D);
+          trace_ev(args.trace, 1, kv_it);
         }
       }
     }
@@ -253,6 +270,7 @@ __global__ void __launch_bounds__(448, 1)
                     kk > 0 ? 1u : 0u);
           }
           umma_commit(&s_full);
+          trace_ev(args.trace, 2, g);
           ++g;
           if (++j_s == nkv_s) {
             umma_commit(&q_empty[qb_s]);
@@ -291,6 +309,7 @@ __global__ void __launch_bounds__(448, 1)
           }
           if (!ok) break;
           umma_commit(&kv_empty[s]);
+          trace_ev(args.trace, 3, gp);
           ++gp;
           if (++j_p == nkv_p) {
             umma_commit(&o_ready[ob]);  // every P V of the item: its O is final
@@ -338,6 +357,7 @@ __global__ void __launch_bounds__(448, 1)
         }
         tc_fence_after();
         const int kv0 = (kt0 + j) * 128 + grp * 64;
+        if (warp == 2 && lane == 0) trace_ev(args.trace, 4, g);
         // Both 32-column halves of this group's raw scores, one wait for the two loads.
         uint32_t sv[2][32];
         tmem_ld32(tmem + lane_off + C::S_COL + grp * 64, sv[0]);
@@ -431,6 +451,7 @@ __global__ void __launch_bounds__(448, 1)
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&p_ready[grp][g & 1]);
+        if (warp == 2 && lane == 0) trace_ev(args.trace, 5, g);
       }
       if (!ok) break;
       // Publish this row's (max, sum) for the epilogue and go on with the next item.
@@ -458,6 +479,7 @@ __global__ void __launch_bounds__(448, 1)
       const uint32_t sb = item_n & 1, ob = item_n % C::O_BUFS;
       if (!mbar_wait_warp(&stats_ready[sb], (item_n >> 1) & 1, args.status, 213, &abort_sh)) break;
       if (!mbar_wait_warp(&o_ready[ob], (item_n / C::O_BUFS) & 1, args.status, 210, &abort_sh)) break;
+      if (warp == 10 && lane == 0) trace_ev(args.trace, 6, item_n);
       tc_fence_after();
       const float ma = stats[((sb * 2) * 128 + r) * 2], la = stats[((sb * 2) * 128 + r) * 2 + 1];
       const float mb = stats[((sb * 2 + 1) * 128 + r) * 2], lb = stats[((sb * 2 + 1) * 128 + r) * 2 + 1];
@@ -496,6 +518,7 @@ __global__ void __launch_bounds__(448, 1)
       if (lane == 0) {
         mbar_arrive(&o_free[ob]);
         mbar_arrive(&stats_free[sb]);
+        if (warp == 10) trace_ev(args.trace, 7, item_n);
       }
     }
   }
@@ -610,6 +633,10 @@ __global__ void __launch_bounds__(448, 1)
   const uint32_t tmem = tmem_sh;
   const int H = args.H, Hkv = args.Hkv, T = args.T;
   const int group = H / Hkv;
+  // trace roles: 0 K/V load issued (per item; slot 127: start), 1 Q/dO load issued, 2
+  // S^T / dP^T issued, 3 ds_ready seen by the MMA warp, 4 dV/dK/dQ issued (per tile), 5
+  // S^T read by gradient warp 2, 6 its dS^T ready (per tile), 7 its dK/dV written (item)
+  if (threadIdx.x == 0) trace_ev(args.trace, 0, kTraceMax - 1);
 
   if (warp == 0) {
     if (lane == 0) {
@@ -624,6 +651,7 @@ __global__ void __launch_bounds__(448, 1)
         mbar_arrive_expect_tx(&kv_full, 2 * C::TILE_BYTES);
         load_tile_rows(smem + C::K_OFF, &tm_qkv, &kv_full, (H + hk) * D, kt * 128, D);
         load_tile_rows(smem + C::V_OFF, &tm_qkv, &kv_full, (H + Hkv + hk) * D, kt * 128, D);
+        trace_ev(args.trace, 0, item_n);
         for (int qt = kt; qt <= qhi; ++qt, ++g) {
           const int s = g % C::QSTAGES;
           const uint32_t ph = (g / C::QSTAGES) & 1;
@@ -640,6 +668,7 @@ __global__ void __launch_bounds__(448, 1)
           uint8_t* vs = smem + C::VSTAGE_OFF + s * 1024;
           bulk_load(vs, args.lse + static_cast<long>(h) * T + qt * 128, vb, &qd_full[s]);
           bulk_load(vs + 512, args.delta + static_cast<long>(h) * T + qt * 128, vb, &qd_full[s]);
+          trace_ev(args.trace, 1, g);
         }
       }
     }
@@ -675,6 +704,7 @@ __global__ void __launch_bounds__(448, 1)
                   kk > 0 ? 1u : 0u);
         }
         umma_commit(&st_full);
+        trace_ev(args.trace, 2, gx);
         return true;
       };
       int3 nx = blockIdx.x < args.n_items ? checked_item(ld_item(args.items, blockIdx.x), args.T, args.H, args.status) : make_int3(0, 0, 0);
@@ -703,6 +733,7 @@ __global__ void __launch_bounds__(448, 1)
             break;
           }
           const bool first = qt == kt;
+          trace_ev(args.trace, 3, g);
           tc_fence_after();
 #pragma unroll
           for (int kk = 0; kk < 8; ++kk) {
@@ -727,6 +758,7 @@ __global__ void __launch_bounds__(448, 1)
           }
           umma_commit(&mma2_done);
           umma_commit(&qd_empty[s]);
+          trace_ev(args.trace, 4, g);
           if (!C::SPLIT_DQ && qt < qhi && !issue_st(g + 1)) {
             ok = false;
             break;
@@ -774,6 +806,7 @@ __global__ void __launch_bounds__(448, 1)
           ok = false;
           break;
         }
+        if (warp == 2 && lane == 0) trace_ev(args.trace, 5, g);
         const float* s_lse = reinterpret_cast<const float*>(smem + C::VSTAGE_OFF + s * 1024);
         const float* s_delta = s_lse + 128;
         tc_fence_after();
@@ -844,6 +877,7 @@ __global__ void __launch_bounds__(448, 1)
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&ds_ready);
+        if (warp == 2 && lane == 0) trace_ev(args.trace, 6, g);
       }
       if (!ok) break;
       // dK (scaled) and dV rows of this key tile -> fp32 accumulators (TMA reduce-add).
@@ -871,6 +905,7 @@ __global__ void __launch_bounds__(448, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_free);
+      if (warp == 2 && lane == 0) trace_ev(args.trace, 7, item_n);
     }
     if (lane == 0) bulk_wait_all<0>();
     __syncwarp();
@@ -1014,6 +1049,11 @@ static void set_smem(K kern, int bytes) {
   PB_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
 }
 
+// Event-trace buffer of the next attention launches (0: off), set by attn_trace().
+static unsigned long long* g_attn_trace = nullptr;
+
+void attn_trace(int64_t ptr) { g_attn_trace = reinterpret_cast<unsigned long long*>(ptr); }
+
 std::vector<at::Tensor> attn_fwd(at::Tensor qkv, at::Tensor doc_start, at::Tensor items, int64_t H, int64_t Hkv,
                                  int64_t D, double scale, at::Tensor out) {
   TORCH_CHECK(qkv.is_cuda() && qkv.scalar_type() == at::kBFloat16 && qkv.dim() == 2 && qkv.is_contiguous());
@@ -1027,6 +1067,7 @@ std::vector<at::Tensor> attn_fwd(at::Tensor qkv, at::Tensor doc_start, at::Tenso
   if (T == 0) return {out, lse};
   CUtensorMap tm = make_tmap_bf16_2d(qkv.data_ptr(), qkv.size(1), T, qkv.stride(0) * 2, 64, 128);
   AttnArgs a{};
+  a.trace = g_attn_trace;
   a.T = T;
   a.H = (int)H;
   a.Hkv = (int)Hkv;
@@ -1082,6 +1123,7 @@ void attn_bwd(at::Tensor qkv, at::Tensor out, at::Tensor dout, at::Tensor lse, a
   CUtensorMap tdkv = make_tmap_2d(dkv_acc.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_FLOAT32, dkv_acc.size(1), T,
                                   dkv_acc.stride(0) * 4, 32, 32, CU_TENSOR_MAP_SWIZZLE_128B);
   AttnArgs a{};
+  a.trace = g_attn_trace;
   a.T = T;
   a.H = (int)H;
   a.Hkv = (int)Hkv;

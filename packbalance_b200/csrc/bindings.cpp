@@ -38,6 +38,7 @@ void adamw_step(at::Tensor p, at::Tensor g, at::Tensor m, at::Tensor v, at::Tens
 at::Tensor l2_norm(at::Tensor x);
 std::vector<at::Tensor> attn_fwd(at::Tensor qkv, at::Tensor doc_start, at::Tensor tiles, int64_t n_heads,
                                  int64_t n_kv_heads, int64_t head_dim, double scale, at::Tensor out);
+void attn_trace(int64_t ptr);
 void attn_bwd(at::Tensor qkv, at::Tensor out, at::Tensor dout, at::Tensor lse, at::Tensor doc_start,
               at::Tensor doc_end, at::Tensor items, int64_t H, int64_t Hkv, int64_t D, double scale, at::Tensor dqkv,
               at::Tensor dq_acc, at::Tensor dkv_acc, at::Tensor delta, c10::optional<at::Tensor> pos,
@@ -79,6 +80,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("status_read", &pb::status_read, pybind11::arg("dev"), pybind11::arg("clear") = true);
   m.def("attn_fwd", &pb::attn_fwd);
   m.def("attn_bwd", &pb::attn_bwd);
+  m.def("attn_trace", &pb::attn_trace);
   pb::comm_bindings(m);
   pb::fsdp_bindings(m);
 }
