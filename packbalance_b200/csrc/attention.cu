@@ -547,17 +547,14 @@ struct BwdCfg {
   static constexpr int TILE_BYTES = 128 * D * 2;
   static constexpr bool SPLIT_DQ = 256 + 3 * D <= 512;  // dQ in its own TMEM columns
   static constexpr int QSTAGES = D == 64 ? 2 : 1;
-  // dS^T tiles: at head_dim 64 two, so the gradient warps write tile g + 1's while the
-  // dK / dQ MMAs of tile g still read tile g's (shared memory allows one at 128)
-  static constexpr int DS_BUFS = D == 64 ? 2 : 1;
-  static constexpr int DQ_SLOTS = 1;                    // 4 KB staging slot per dQ warp
+  static constexpr int DQ_SLOTS = D == 64 ? 2 : 1;      // 4 KB staging slots per dQ warp
   static constexpr int K_OFF = 0;
   static constexpr int V_OFF = TILE_BYTES;
   static constexpr int Q_OFF = 2 * TILE_BYTES;  // stage s: Q at Q_OFF + 2*s*TILE, dO right after
   static constexpr int VSTAGE_OFF = Q_OFF + QSTAGES * 2 * TILE_BYTES;  // stage s: lse[128], delta[128] fp32
   static constexpr int P_OFF = VSTAGE_OFF + 2048;                      // P^T  [128 kv x 128 q] bf16
-  static constexpr int DS_OFF = P_OFF + 32768;                   // dS^T [128 kv x 128 q] bf16, DS_BUFS
-  static constexpr int DQS_OFF = DS_OFF + DS_BUFS * 32768;       // dQ staging, 4 warps
+  static constexpr int DS_OFF = P_OFF + 32768;                   // dS^T [128 kv x 128 q] bf16
+  static constexpr int DQS_OFF = DS_OFF + 32768;                 // dQ staging, 4 warps
   static constexpr int SMEM = DQS_OFF + 4 * DQ_SLOTS * 4096 + 1024;
   static_assert(SMEM <= 232448, "shared memory budget");
   static constexpr uint32_t ST_COL = 0;
@@ -596,10 +593,8 @@ __global__ void __launch_bounds__(448, 1)
                     const __grid_constant__ CUtensorMap tm_dq, const __grid_constant__ CUtensorMap tm_dkv,
                     const AttnArgs args) {
   using C = BwdCfg<D>;
-  // mma2_done[g & 1]: tile g's dK / dQ MMAs are done (its dS^T tile is free, dQ is in
-  // TMEM); p_free: its dV MMA is done (the P^T tile is free)
-  __shared__ __align__(8) uint64_t kv_full, kv_empty, qd_full[2], qd_empty[2], st_full, ds_ready, mma2_done[2], p_free,
-      dq_free, acc_done, acc_free, drain_bar, st_free, dpt_free;
+  __shared__ __align__(8) uint64_t kv_full, kv_empty, qd_full[2], qd_empty[2], st_full, ds_ready, mma2_done, dq_free,
+      acc_done, acc_free, drain_bar, st_free, dpt_free;
   __shared__ uint32_t tmem_sh;
   __shared__ volatile int abort_sh;
   extern __shared__ uint8_t dyn[];
@@ -614,9 +609,7 @@ __global__ void __launch_bounds__(448, 1)
     }
     mbar_init(&st_full, 1);
     mbar_init(&ds_ready, 8);
-    mbar_init(&mma2_done[0], 1);
-    mbar_init(&mma2_done[1], 1);
-    mbar_init(&p_free, 1);
+    mbar_init(&mma2_done, 1);
     mbar_init(&dq_free, 4);
     mbar_init(&acc_done, 1);
     mbar_init(&acc_free, 8);
@@ -742,22 +735,15 @@ __global__ void __launch_bounds__(448, 1)
           const bool first = qt == kt;
           trace_ev(args.trace, 3, g);
           tc_fence_after();
-          const uint32_t dsb = dsa + (g % C::DS_BUFS) * 32768;
-          // dV += P^T dO first: its commit frees the P^T tile for the next tile
 #pragma unroll
           for (int kk = 0; kk < 8; ++kk) {
             const uint32_t aoff = (kk >> 2) * 16384 + (kk & 3) * 32;  // K-major A over q (K dim)
             const uint32_t boff = kk * 2048;                          // MN-major B: 16 q rows
+            const uint32_t acc = (first && kk == 0) ? 0u : 1u;
             umma_ss(tmem + C::DV_COL, sdesc_sw128(pa + aoff, 16, 1024), sdesc_sw128(da + boff, 16384, 1024),
-                    C::IDESC_KV, (first && kk == 0) ? 0u : 1u);
-          }
-          umma_commit(&p_free);
-#pragma unroll
-          for (int kk = 0; kk < 8; ++kk) {
-            const uint32_t aoff = (kk >> 2) * 16384 + (kk & 3) * 32;
-            const uint32_t boff = kk * 2048;
-            umma_ss(tmem + C::DK_COL, sdesc_sw128(dsb + aoff, 16, 1024), sdesc_sw128(qa + boff, 16384, 1024),
-                    C::IDESC_KV, (first && kk == 0) ? 0u : 1u);
+                    C::IDESC_KV, acc);
+            umma_ss(tmem + C::DK_COL, sdesc_sw128(dsa + aoff, 16, 1024), sdesc_sw128(qa + boff, 16384, 1024),
+                    C::IDESC_KV, acc);
           }
           if (C::SPLIT_DQ && g > 0 && !mbar_wait(&dq_free, (g - 1) & 1, args.status, 226, &abort_sh)) {
             ok = false;
@@ -767,10 +753,10 @@ __global__ void __launch_bounds__(448, 1)
 #pragma unroll
           for (int kk = 0; kk < 8; ++kk) {
             const uint32_t off = kk * 2048;  // 16 kv rows
-            umma_ss(tmem + C::DQ_COL, sdesc_sw128(dsb + off, 16384, 1024), sdesc_sw128(ka + off, 16384, 1024),
+            umma_ss(tmem + C::DQ_COL, sdesc_sw128(dsa + off, 16384, 1024), sdesc_sw128(ka + off, 16384, 1024),
                     C::IDESC_DQ, kk > 0 ? 1u : 0u);
           }
-          umma_commit(&mma2_done[g & 1]);
+          umma_commit(&mma2_done);
           umma_commit(&qd_empty[s]);
           trace_ev(args.trace, 4, g);
           if (!C::SPLIT_DQ && qt < qhi && !issue_st(g + 1)) {
@@ -852,8 +838,8 @@ __global__ void __launch_bounds__(448, 1)
             pp[cc * 16 + i] = pack_bf16x2(p2[0], p2[1]);
           }
         }
-        // The previous tile's dV MMA reads P^T from shared memory.
-        if (g > 0 && !mbar_wait_warp(&p_free, (g - 1) & 1, args.status, 230, &abort_sh)) {
+        // The previous tile's dV/dK/dQ MMAs read P/dS from shared memory.
+        if (g > 0 && !mbar_wait_warp(&mma2_done, (g - 1) & 1, args.status, 230, &abort_sh)) {
           ok = false;
           break;
         }
@@ -862,15 +848,6 @@ __global__ void __launch_bounds__(448, 1)
 #pragma unroll
         for (int k = 0; k < 8; ++k)
           st_swz_chunk(ptile, r, grp * 8 + k, make_uint4(pp[4 * k], pp[4 * k + 1], pp[4 * k + 2], pp[4 * k + 3]));
-        // dS^T buffer g % DS_BUFS: the dK / dQ MMAs of tile g - DS_BUFS read it
-        uint8_t* dsg = dstile + (g % C::DS_BUFS) * 32768;
-        if (g >= static_cast<uint32_t>(C::DS_BUFS)) {
-          const uint32_t gb = g - C::DS_BUFS;
-          if (!mbar_wait_warp(&mma2_done[gb & 1], (gb >> 1) & 1, args.status, 236, &abort_sh)) {
-            ok = false;
-            break;
-          }
-        }
         // dP^T -> dS^T = P^T (dP^T - delta), 32 columns at a time
 #pragma unroll
         for (int cc = 0; cc < 2; ++cc) {
@@ -894,7 +871,7 @@ __global__ void __launch_bounds__(448, 1)
           }
 #pragma unroll
           for (int k = 0; k < 4; ++k)
-            st_swz_chunk(dsg, r, grp * 8 + cc * 4 + k, make_uint4(dd[4 * k], dd[4 * k + 1], dd[4 * k + 2], dd[4 * k + 3]));
+            st_swz_chunk(dstile, r, grp * 8 + cc * 4 + k, make_uint4(dd[4 * k], dd[4 * k + 1], dd[4 * k + 2], dd[4 * k + 3]));
         }
         fence_async_smem();
         tc_fence_before();
@@ -945,7 +922,7 @@ __global__ void __launch_bounds__(448, 1)
       const int kt = nx.x, h = nx.y, qhi = nx.z;
       if (it + (int)gridDim.x < args.n_items) nx = checked_item(ld_item(args.items, it + gridDim.x), args.T, args.H, args.status);
       for (int qt = kt; qt <= qhi; ++qt, ++g) {
-        if (!mbar_wait_warp(&mma2_done[g & 1], (g >> 1) & 1, args.status, 231, &abort_sh)) {
+        if (!mbar_wait_warp(&mma2_done, g & 1, args.status, 231, &abort_sh)) {
           ok = false;
           break;
         }
