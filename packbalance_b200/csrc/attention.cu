@@ -192,7 +192,6 @@ __global__ void __launch_bounds__(448, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  pdl_enter();  // set-up above overlaps the previous kernel; global memory only from here
   const uint32_t tmem = tmem_sh;
   const int H = args.H, Hkv = args.Hkv, T = args.T;
   const int group = H / Hkv;
@@ -631,7 +630,6 @@ __global__ void __launch_bounds__(448, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  pdl_enter();  // set-up above overlaps the previous kernel; global memory only from here
   const uint32_t tmem = tmem_sh;
   const int H = args.H, Hkv = args.Hkv, T = args.T;
   const int group = H / Hkv;
@@ -968,7 +966,6 @@ __global__ void __launch_bounds__(448, 1)
 __global__ void attn_delta_kernel(const __nv_bfloat16* __restrict__ o, const __nv_bfloat16* __restrict__ dout,
                                   float* __restrict__ delta, int T, int H, int D, float* __restrict__ dq_acc,
                                   float* __restrict__ dkv_acc, int Hkv) {
-  pdl_enter();
   const long idx = blockIdx.x * (long)blockDim.x + threadIdx.x;
   const long nthreads = static_cast<long>(gridDim.x) * blockDim.x;
   {
@@ -1010,7 +1007,6 @@ __global__ void dqkv_finalize_kernel(const float* __restrict__ dq_acc, const flo
                                      __nv_bfloat16* __restrict__ dqkv, long ld, const int* __restrict__ pos,
                                      const float* __restrict__ cos_t, const float* __restrict__ sin_t, int n_pos,
                                      int T, int H, int Hkv, int D) {
-  pdl_enter();
   const int half = D / 2, g4 = half / 4;
   const int heads = H + 2 * Hkv;
   const long total = static_cast<long>(T) * heads * g4;
@@ -1088,10 +1084,10 @@ std::vector<at::Tensor> attn_fwd(at::Tensor qkv, at::Tensor doc_start, at::Tenso
   auto s = at::cuda::getCurrentCUDAStream();
   if (D == 64) {
     set_smem(attn_fwd_kernel<64>, FwdCfg<64>::SMEM);
-    pb::launch_pdl(attn_fwd_kernel<64>, dim3(pb::smem_max(attn_fwd_kernel<64>, grid)), dim3(448), FwdCfg<64>::SMEM, s, tm, a);
+    attn_fwd_kernel<64><<<pb::smem_max(attn_fwd_kernel<64>, grid), 448, FwdCfg<64>::SMEM, s>>>(tm, a);
   } else {
     set_smem(attn_fwd_kernel<128>, FwdCfg<128>::SMEM);
-    pb::launch_pdl(attn_fwd_kernel<128>, dim3(pb::smem_max(attn_fwd_kernel<128>, grid)), dim3(448), FwdCfg<128>::SMEM, s, tm, a);
+    attn_fwd_kernel<128><<<pb::smem_max(attn_fwd_kernel<128>, grid), 448, FwdCfg<128>::SMEM, s>>>(tm, a);
   }
   PB_CUDA_CHECK(cudaGetLastError());
   return {out, lse};
@@ -1115,10 +1111,10 @@ void attn_bwd(at::Tensor qkv, at::Tensor out, at::Tensor dout, at::Tensor lse, a
   if (T == 0) return;
   auto s = at::cuda::getCurrentCUDAStream();
   const long pairs = static_cast<long>(T) * H;
-  pb::launch_pdl(attn_delta_kernel, dim3((unsigned)((pairs + 255) / 256)), dim3(256), 0, s,
-                 reinterpret_cast<const __nv_bfloat16*>(out.data_ptr()),
-                 reinterpret_cast<const __nv_bfloat16*>(dout.data_ptr()), delta.data_ptr<float>(), T, (int)H,
-                 (int)D, dq_acc.data_ptr<float>(), dkv_acc.data_ptr<float>(), (int)Hkv);
+  attn_delta_kernel<<<(pairs + 255) / 256, 256, 0, s>>>(reinterpret_cast<const __nv_bfloat16*>(out.data_ptr()),
+                                                      reinterpret_cast<const __nv_bfloat16*>(dout.data_ptr()),
+                                                      delta.data_ptr<float>(), T, (int)H, (int)D,
+                                                      dq_acc.data_ptr<float>(), dkv_acc.data_ptr<float>(), (int)Hkv);
   PB_CUDA_CHECK(cudaGetLastError());
   CUtensorMap tq = make_tmap_bf16_2d(qkv.data_ptr(), qkv.size(1), T, qkv.stride(0) * 2, 64, 128);
   CUtensorMap td = make_tmap_bf16_2d(dout.data_ptr(), dout.size(1), T, dout.stride(0) * 2, 64, 128);
@@ -1144,23 +1140,20 @@ void attn_bwd(at::Tensor qkv, at::Tensor out, at::Tensor dout, at::Tensor lse, a
   const int grid = std::min<int>(a.n_items, num_sms(qkv.device().index()));
   if (D == 64) {
     set_smem(attn_bwd_kernel<64>, BwdCfg<64>::SMEM);
-    pb::launch_pdl(attn_bwd_kernel<64>, dim3(pb::smem_max(attn_bwd_kernel<64>, grid)), dim3(448), BwdCfg<64>::SMEM, s, tq, td, tdq,
-                   tdkv, a);
+    attn_bwd_kernel<64><<<pb::smem_max(attn_bwd_kernel<64>, grid), 448, BwdCfg<64>::SMEM, s>>>(tq, td, tdq, tdkv, a);
   } else {
     set_smem(attn_bwd_kernel<128>, BwdCfg<128>::SMEM);
-    pb::launch_pdl(attn_bwd_kernel<128>, dim3(pb::smem_max(attn_bwd_kernel<128>, grid)), dim3(448), BwdCfg<128>::SMEM, s, tq, td,
-                   tdq, tdkv, a);
+    attn_bwd_kernel<128><<<pb::smem_max(attn_bwd_kernel<128>, grid), 448, BwdCfg<128>::SMEM, s>>>(tq, td, tdq, tdkv, a);
   }
   PB_CUDA_CHECK(cudaGetLastError());
   const long n4 = static_cast<long>(T) * (H + 2 * Hkv) * (D / 8);
-  pb::launch_pdl(dqkv_finalize_kernel,
-                 dim3((unsigned)std::max<long>(1, std::min<long>((n4 + 255) / 256, 8L * num_sms(qkv.device().index())))),
-                 dim3(256), 0, s, dq_acc.data_ptr<float>(), dkv_acc.data_ptr<float>(),
-                 reinterpret_cast<__nv_bfloat16*>(dqkv.data_ptr()), (long)dqkv.stride(0),
-                 pos.has_value() ? pos->data_ptr<int>() : (int*)nullptr,
-                 cos_t.has_value() ? cos_t->data_ptr<float>() : (float*)nullptr,
-                 sin_t.has_value() ? sin_t->data_ptr<float>() : (float*)nullptr,
-                 cos_t.has_value() ? (int)cos_t->size(0) : 1, T, (int)H, (int)Hkv, (int)D);
+  dqkv_finalize_kernel<<<std::max<long>(1, std::min<long>((n4 + 255) / 256, 8L * num_sms(qkv.device().index()))),
+                         256, 0, s>>>(dq_acc.data_ptr<float>(), dkv_acc.data_ptr<float>(),
+                                      reinterpret_cast<__nv_bfloat16*>(dqkv.data_ptr()), dqkv.stride(0),
+                                      pos.has_value() ? pos->data_ptr<int>() : nullptr,
+                                      cos_t.has_value() ? cos_t->data_ptr<float>() : nullptr,
+                                      sin_t.has_value() ? sin_t->data_ptr<float>() : nullptr,
+                                      cos_t.has_value() ? (int)cos_t->size(0) : 1, T, (int)H, (int)Hkv, (int)D);
   PB_CUDA_CHECK(cudaGetLastError());
 }
 

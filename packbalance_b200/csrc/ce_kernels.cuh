@@ -26,7 +26,6 @@ static __global__ void __launch_bounds__(kCeRows * kCeGroups) ce_finalize_kernel
     const float* __restrict__ pmax, const float* __restrict__ psum, int ntiles, int rows,
     const float* __restrict__ tlogit, const int64_t* __restrict__ targets, int64_t ignore_index, float z,
     float* __restrict__ lse, float* __restrict__ loss) {
-  pdl_enter();
   __shared__ float sm[kCeGroups][kCeRows], ss[kCeGroups][kCeRows];
   const int rl = threadIdx.x % kCeRows, grp = threadIdx.x / kCeRows;
   const int r = blockIdx.x * kCeRows + rl;

@@ -49,19 +49,6 @@ __device__ __forceinline__ uint64_t globaltimer() {
   return t;
 }
 
-// Programmatic dependent launch.  A kernel launched with pb::launch_pdl may start while
-// its predecessor in the stream is still running: it does its setup (barriers, tensor
-// memory, descriptor prefetch) first and calls pdl_wait() before it reads or writes any
-// global memory, which returns once the predecessor grid has completed and its memory
-// is visible.  pdl_trigger() (after the wait) lets the next kernel launch early in the
-// same way, so at most two grids overlap.  Both are no-ops for a normal launch.
-__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
-__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
-__device__ __forceinline__ void pdl_enter() {
-  pdl_wait();
-  pdl_trigger();
-}
-
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }

@@ -46,7 +46,6 @@ template <typename TI, typename TO>
 __global__ void add_rmsnorm_kernel(const TI* __restrict__ xp, const __nv_bfloat16* __restrict__ delta,
                                    const float* __restrict__ w, float* __restrict__ x_out, TO* __restrict__ y,
                                    float* __restrict__ rstd, int rows, int n, float eps) {
-  pdl_enter();
   const int row = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
   if (row >= rows) return;
@@ -80,7 +79,6 @@ __global__ void rmsnorm_bwd_kernel(const TD* __restrict__ dy, const TI* __restri
                                    const float* __restrict__ rstd, const float* __restrict__ dres,
                                    float* __restrict__ dx, __nv_bfloat16* __restrict__ dx_bf16,
                                    float* __restrict__ dw_out, int rows, int n, float* __restrict__ dw_part) {
-  pdl_enter();
   extern __shared__ float sdw[];  // [warps][n]
   const int warps = blockDim.x / 32;
   const int wid = threadIdx.x / 32, lane = threadIdx.x % 32;
@@ -130,7 +128,6 @@ __global__ void __launch_bounds__(256) add_rmsnorm_reg_kernel(const TI* __restri
                                                                const float* __restrict__ w, float* __restrict__ x_out,
                                                                TO* __restrict__ y, float* __restrict__ rstd, int rows,
                                                                float eps) {
-  pdl_enter();
   constexpr int n = 128 * CH;
   const int lane = threadIdx.x & 31;
   const int warps = blockDim.x / 32;
@@ -169,7 +166,6 @@ __global__ void __launch_bounds__(256) rmsnorm_bwd_reg_kernel(const TD* __restri
                                                                __nv_bfloat16* __restrict__ dx_bf16,
                                                                float* __restrict__ dw_out, int rows,
                                                                float* __restrict__ dw_part) {
-  pdl_enter();
   constexpr int n = 128 * CH;
   __shared__ float sdw[8][n];
   const int lane = threadIdx.x & 31, wid = threadIdx.x / 32;
@@ -227,7 +223,6 @@ __global__ void __launch_bounds__(256) rmsnorm_bwd_reg_kernel(const TD* __restri
 // Deterministic mode: dw_out[c] (+)= sum over blocks b = 0, 1, ... of part[b, c], always in
 // that order.
 __global__ void dw_reduce_kernel(const float* __restrict__ part, int blocks, int n, float* __restrict__ dw_out) {
-  pdl_enter();
   for (int c = blockIdx.x * blockDim.x + threadIdx.x; c < n; c += gridDim.x * blockDim.x) {
     float t = 0.f;
     for (int b = 0; b < blocks; ++b) t += part[static_cast<long>(b) * n + c];
@@ -276,7 +271,7 @@ std::vector<at::Tensor> add_rmsnorm_fwd(at::Tensor x, c10::optional<at::Tensor> 
     bool done = true;
     switch (n / 128) {
 #define PB_FWD_CH(C) \
-  case C: pb::launch_pdl(add_rmsnorm_reg_kernel<C, float, __nv_bfloat16>, dim3(g2), dim3(256), 0, s, xp, dp, w.data_ptr<float>(), xop, yp, rstd.data_ptr<float>(), rows, (float)eps); break;
+  case C: add_rmsnorm_reg_kernel<C, float, __nv_bfloat16><<<g2, 256, 0, s>>>(xp, dp, w.data_ptr<float>(), xop, yp, rstd.data_ptr<float>(), rows, (float)eps); break;
       PB_FWD_CH(2) PB_FWD_CH(4) PB_FWD_CH(6) PB_FWD_CH(8) PB_FWD_CH(12) PB_FWD_CH(16) PB_FWD_CH(32)
 #undef PB_FWD_CH
       default: done = false;
@@ -288,16 +283,16 @@ std::vector<at::Tensor> add_rmsnorm_fwd(at::Tensor x, c10::optional<at::Tensor> 
   }
   if (x.scalar_type() == at::kFloat) {
     if (out_bf16)
-      pb::launch_pdl(add_rmsnorm_kernel<float, __nv_bfloat16>, dim3(grid), dim3(warps * 32), 0, s, 
+      add_rmsnorm_kernel<float, __nv_bfloat16><<<grid, warps * 32, 0, s>>>(
           x.data_ptr<float>(), dp, w.data_ptr<float>(), xop, reinterpret_cast<__nv_bfloat16*>(y.data_ptr()),
           rstd.data_ptr<float>(), rows, n, (float)eps);
     else
-      pb::launch_pdl(add_rmsnorm_kernel<float, float>, dim3(grid), dim3(warps * 32), 0, s, x.data_ptr<float>(), dp, w.data_ptr<float>(), xop,
+      add_rmsnorm_kernel<float, float><<<grid, warps * 32, 0, s>>>(x.data_ptr<float>(), dp, w.data_ptr<float>(), xop,
                                                                    y.data_ptr<float>(), rstd.data_ptr<float>(), rows,
                                                                    n, (float)eps);
   } else {
     TORCH_CHECK(x.scalar_type() == at::kBFloat16 && !delta.has_value(), "rmsnorm: fp32 or bf16 input");
-    pb::launch_pdl(add_rmsnorm_kernel<__nv_bfloat16, __nv_bfloat16>, dim3(grid), dim3(warps * 32), 0, s, 
+    add_rmsnorm_kernel<__nv_bfloat16, __nv_bfloat16><<<grid, warps * 32, 0, s>>>(
         reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), nullptr, w.data_ptr<float>(), nullptr,
         reinterpret_cast<__nv_bfloat16*>(y.data_ptr()), rstd.data_ptr<float>(), rows, n, (float)eps);
   }
@@ -324,7 +319,7 @@ at::Tensor rmsnorm_bwd(at::Tensor dy, at::Tensor x, at::Tensor w, at::Tensor rst
   if (rows == 0) return dx;
   // deterministic mode: per-block dw partials, then one ordered sum (dw_reduce_kernel)
   auto reduce_parts = [&](const at::Tensor& part, int blocks) {
-    pb::launch_pdl(dw_reduce_kernel, dim3((n + 255) / 256), dim3(256), 0, s, part.data_ptr<float>(), blocks, n, dw_out.data_ptr<float>());
+    dw_reduce_kernel<<<(n + 255) / 256, 256, 0, s>>>(part.data_ptr<float>(), blocks, n, dw_out.data_ptr<float>());
   };
   if (x.scalar_type() == at::kFloat && dy.scalar_type() == at::kFloat && n % 128 == 0 && n / 128 <= 8) {
     // one persistent wave: 1 CTA of 8 warps per SM for CH >= 6 (register-bound), else 2
@@ -337,7 +332,7 @@ at::Tensor rmsnorm_bwd(at::Tensor dy, at::Tensor x, at::Tensor w, at::Tensor rst
     bool done = true;
     switch (n / 128) {
 #define PB_BWD_CH(C) \
-  case C: pb::launch_pdl(rmsnorm_bwd_reg_kernel<C, float, float>, dim3(g2), dim3(256), 0, s, dy.data_ptr<float>(), x.data_ptr<float>(), w.data_ptr<float>(), rstd.data_ptr<float>(), dres_q, dx.data_ptr<float>(), dxq, dw_out.data_ptr<float>(), rows, pp); break;
+  case C: rmsnorm_bwd_reg_kernel<C, float, float><<<g2, 256, 0, s>>>(dy.data_ptr<float>(), x.data_ptr<float>(), w.data_ptr<float>(), rstd.data_ptr<float>(), dres_q, dx.data_ptr<float>(), dxq, dw_out.data_ptr<float>(), rows, pp); break;
       PB_BWD_CH(2) PB_BWD_CH(4) PB_BWD_CH(6) PB_BWD_CH(8)
 #undef PB_BWD_CH
       default: done = false;
@@ -361,7 +356,7 @@ at::Tensor rmsnorm_bwd(at::Tensor dy, at::Tensor x, at::Tensor w, at::Tensor rst
   do {                                                                                                        \
     auto k = rmsnorm_bwd_kernel<TI, TD>;                                                                      \
     if (smem > 48 * 1024) PB_CUDA_CHECK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)); \
-    pb::launch_pdl(k, dim3(nb), dim3(warps * 32), smem, s, reinterpret_cast<const TD*>(dy.data_ptr()), reinterpret_cast<const TI*>(x.data_ptr()), \
+    k<<<nb, warps * 32, smem, s>>>(reinterpret_cast<const TD*>(dy.data_ptr()), reinterpret_cast<const TI*>(x.data_ptr()), \
                                    w.data_ptr<float>(), rstd.data_ptr<float>(), dres_p, dx.data_ptr<float>(), dxb,      \
                                    dw_out.data_ptr<float>(), rows, n, pp);                                    \
   } while (0)
@@ -380,7 +375,6 @@ at::Tensor rmsnorm_bwd(at::Tensor dy, at::Tensor x, at::Tensor w, at::Tensor rst
 // -> dgu = [dg | du] (bf16 [M, 2F]).  8 elements per thread.
 __global__ void swiglu_bwd_packed_kernel(const __nv_bfloat16* __restrict__ dh, const __nv_bfloat16* __restrict__ gu,
                                          __nv_bfloat16* __restrict__ dgu, long rows, int F) {
-  pdl_enter();
   const int f8 = F / 8;
   const long total = rows * f8;
   for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
@@ -413,7 +407,8 @@ void swiglu_bwd_packed(at::Tensor dh, at::Tensor gu, at::Tensor dgu) {
   TORCH_CHECK(F % 8 == 0 && gu.size(1) == 2 * F && dgu.size(1) == 2 * F);
   const long total = rows * (F / 8);
   if (total == 0) return;
-  pb::launch_pdl(swiglu_bwd_packed_kernel, dim3((int)std::min<long>((total + 255) / 256, 16L * num_sms(dh.device().index()))), dim3(256), 0, at::cuda::getCurrentCUDAStream(), 
+  swiglu_bwd_packed_kernel<<<(int)std::min<long>((total + 255) / 256, 16L * num_sms(dh.device().index())), 256, 0,
+                             at::cuda::getCurrentCUDAStream()>>>(
       reinterpret_cast<const __nv_bfloat16*>(dh.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(gu.data_ptr()),
       reinterpret_cast<__nv_bfloat16*>(dgu.data_ptr()), rows, F);
   PB_CUDA_CHECK(cudaGetLastError());
@@ -535,7 +530,6 @@ __device__ __forceinline__ int64_t checked_id(int64_t id, int64_t vocab, int* st
 
 __global__ void embedding_fwd_kernel(const int64_t* __restrict__ ids, const float* __restrict__ w,
                                      float* __restrict__ out, int rows, int d, int64_t vocab, int* status) {
-  pdl_enter();
   const int d4 = d / 4;
   const long total = static_cast<long>(rows) * d4;
   for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
@@ -546,7 +540,6 @@ __global__ void embedding_fwd_kernel(const int64_t* __restrict__ ids, const floa
 
 __global__ void embedding_bwd_kernel(const int64_t* __restrict__ ids, const float* __restrict__ dx,
                                      float* __restrict__ grad, int rows, int d, int64_t vocab, int* status) {
-  pdl_enter();
   const int d4 = d / 4;
   const long total = static_cast<long>(rows) * d4;
   for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
@@ -562,7 +555,6 @@ __global__ void embedding_bwd_kernel(const int64_t* __restrict__ ids, const floa
 __global__ void embedding_bwd_sorted_kernel(const int64_t* __restrict__ sorted_ids, const int64_t* __restrict__ pos,
                                             const int64_t* __restrict__ starts, int runs, const float* __restrict__ dx,
                                             float* __restrict__ grad, int d, int64_t vocab, int* status) {
-  pdl_enter();
   const int d4 = d / 4;
   const long total = static_cast<long>(runs) * d4;
   for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
@@ -588,7 +580,7 @@ at::Tensor embedding_fwd(at::Tensor ids, at::Tensor w) {
   auto out = at::empty({rows, d}, w.options());
   if (rows == 0) return out;
   const long total = (long)rows * d / 4;
-  pb::launch_pdl(embedding_fwd_kernel, dim3(ew_grid(total, w.device().index())), dim3(256), 0, at::cuda::getCurrentCUDAStream(), 
+  embedding_fwd_kernel<<<ew_grid(total, w.device().index()), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
       ids.data_ptr<int64_t>(), w.data_ptr<float>(), out.data_ptr<float>(), rows, d, w.size(0),
       status_ptr(w.device().index()));
   PB_CUDA_CHECK(cudaGetLastError());
@@ -612,14 +604,15 @@ void embedding_bwd(at::Tensor ids, at::Tensor dx, at::Tensor grad, bool accumula
     auto starts = at::cat({at::zeros({1}, counts.options()), at::cumsum(counts, 0)});
     const int runs = static_cast<int>(counts.numel());
     const long total = (long)runs * d / 4;
-    pb::launch_pdl(embedding_bwd_sorted_kernel, dim3(ew_grid(total, grad.device().index())), dim3(256), 0, at::cuda::getCurrentCUDAStream(), 
+    embedding_bwd_sorted_kernel<<<ew_grid(total, grad.device().index()), 256, 0,
+                                  at::cuda::getCurrentCUDAStream()>>>(
         sid.data_ptr<int64_t>(), pos.data_ptr<int64_t>(), starts.data_ptr<int64_t>(), runs, dx.data_ptr<float>(),
         grad.data_ptr<float>(), d, grad.size(0), status_ptr(grad.device().index()));
     PB_CUDA_CHECK(cudaGetLastError());
     return;
   }
   const long total = (long)rows * d / 4;
-  pb::launch_pdl(embedding_bwd_kernel, dim3(ew_grid(total, grad.device().index())), dim3(256), 0, at::cuda::getCurrentCUDAStream(), 
+  embedding_bwd_kernel<<<ew_grid(total, grad.device().index()), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
       ids.data_ptr<int64_t>(), dx.data_ptr<float>(), grad.data_ptr<float>(), rows, d, grad.size(0),
       status_ptr(grad.device().index()));
   PB_CUDA_CHECK(cudaGetLastError());
@@ -630,7 +623,7 @@ void ce_finalize(at::Tensor pmax, at::Tensor psum, at::Tensor tlogit, at::Tensor
   const c10::cuda::CUDAGuard guard(pmax.device());
   const int ntiles = pmax.size(0), rows = pmax.size(1);
   if (rows == 0) return;
-  pb::launch_pdl(ce_finalize_kernel, dim3(ce_finalize_blocks(rows)), dim3(kCeRows * kCeGroups), 0, at::cuda::getCurrentCUDAStream(), 
+  ce_finalize_kernel<<<ce_finalize_blocks(rows), kCeRows * kCeGroups, 0, at::cuda::getCurrentCUDAStream()>>>(
       pmax.data_ptr<float>(), psum.data_ptr<float>(), ntiles, rows, tlogit.data_ptr<float>(),
       targets.data_ptr<int64_t>(), ignore_index, (float)z, lse.data_ptr<float>(), loss.data_ptr<float>());
   PB_CUDA_CHECK(cudaGetLastError());
@@ -638,7 +631,6 @@ void ce_finalize(at::Tensor pmax, at::Tensor psum, at::Tensor tlogit, at::Tensor
 
 __global__ void ce_row_scale_kernel(const int64_t* __restrict__ targets, int64_t ignore_index,
                                     const float* __restrict__ g, float* __restrict__ scale, int rows) {
-  pdl_enter();
   const int r = blockIdx.x * blockDim.x + threadIdx.x;
   if (r < rows) scale[r] = targets[r] != ignore_index ? *g : 0.f;
 }
@@ -647,7 +639,7 @@ void ce_row_scale(at::Tensor targets, int64_t ignore_index, at::Tensor grad_out,
   const c10::cuda::CUDAGuard guard(targets.device());
   const int rows = targets.numel();
   if (rows == 0) return;
-  pb::launch_pdl(ce_row_scale_kernel, dim3((rows + 255) / 256), dim3(256), 0, at::cuda::getCurrentCUDAStream(), 
+  ce_row_scale_kernel<<<(rows + 255) / 256, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
       targets.data_ptr<int64_t>(), ignore_index, grad_out.data_ptr<float>(), scale.data_ptr<float>(), rows);
   PB_CUDA_CHECK(cudaGetLastError());
 }
@@ -702,7 +694,6 @@ __global__ void adamw_kernel(float* __restrict__ p, const float* __restrict__ g,
                              float* __restrict__ v, __nv_bfloat16* __restrict__ shadow, long n,
                              const float* __restrict__ norm, int* __restrict__ skipped, float lr, float b1, float b2,
                              float eps, float wd, float bc1, float bc2, float max_norm, const float* __restrict__ hp) {
-  pdl_enter();
   if (hp != nullptr) {  // per-step values from device memory (CUDA-graph replay)
     lr = hp[0];
     bc1 = hp[1];
@@ -759,7 +750,7 @@ void adamw_step(at::Tensor p, at::Tensor g, at::Tensor m, at::Tensor v, at::Tens
   const c10::cuda::CUDAGuard guard(p.device());
   const long n = p.numel();
   TORCH_CHECK(reinterpret_cast<uintptr_t>(p.data_ptr()) % 16 == 0 && reinterpret_cast<uintptr_t>(g.data_ptr()) % 16 == 0);
-  pb::launch_pdl(adamw_kernel, dim3(4 * num_sms(p.device().index())), dim3(256), 0, at::cuda::getCurrentCUDAStream(), 
+  adamw_kernel<<<4 * num_sms(p.device().index()), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
       p.data_ptr<float>(), g.data_ptr<float>(), m.data_ptr<float>(), v.data_ptr<float>(),
       write_shadow ? reinterpret_cast<__nv_bfloat16*>(shadow.data_ptr()) : nullptr, n, norm.data_ptr<float>(),
       skipped.data_ptr<int>(), (float)lr, (float)b1, (float)b2, (float)eps, (float)wd, (float)bc1, (float)bc2,
@@ -768,7 +759,6 @@ void adamw_step(at::Tensor p, at::Tensor g, at::Tensor m, at::Tensor v, at::Tens
 }
 
 __global__ void sumsq_kernel(const float* __restrict__ x, long n, float* __restrict__ out, float* __restrict__ part) {
-  pdl_enter();
   float s = 0.f;
   const long n4 = n / 4;
   for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < n4; i += (long)gridDim.x * blockDim.x) {
@@ -799,10 +789,10 @@ at::Tensor l2_norm(at::Tensor x) {
   at::Tensor part;
   if (g_deterministic) part = at::empty({blocks}, x.options().dtype(at::kFloat));
   if (n > 0) {
-    pb::launch_pdl(sumsq_kernel, dim3(blocks), dim3(512), 0, at::cuda::getCurrentCUDAStream(), 
+    sumsq_kernel<<<blocks, 512, 0, at::cuda::getCurrentCUDAStream()>>>(
         x.data_ptr<float>(), n, acc.data_ptr<float>(), g_deterministic ? part.data_ptr<float>() : nullptr);
     if (g_deterministic)
-      pb::launch_pdl(dw_reduce_kernel, dim3(1), dim3(32), 0, at::cuda::getCurrentCUDAStream(), part.data_ptr<float>(), blocks, 1,
+      dw_reduce_kernel<<<1, 32, 0, at::cuda::getCurrentCUDAStream()>>>(part.data_ptr<float>(), blocks, 1,
                                                                          acc.data_ptr<float>());
   }
   PB_CUDA_CHECK(cudaGetLastError());

@@ -48,7 +48,8 @@ static void launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const CUte
     PB_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES));
     configured[dev] = true;
   }
-  pb::launch_pdl(kern, dim3(pb::smem_max(kern, grid)), dim3(threads), C::SMEM_BYTES, stream, ta, tb, to, tx, args);
+  kern<<<pb::smem_max(kern, grid), threads, C::SMEM_BYTES, stream>>>(ta, tb, to, tx, args);
+  PB_CUDA_CHECK(cudaGetLastError());
 }
 
 template <int BN, bool A_MN, bool B_MN, int STAGES, int NSLOT>
@@ -81,12 +82,6 @@ static void launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const CUte
   int clusters = std::min(tiles, max_clusters[dev]);
   if (max_ctas > 0) clusters = std::min(clusters, std::max(1, max_ctas / 2));
   cfg.gridDim = pb::smem_max(kern, dim3(2 * std::max(clusters, 1), 1, 1));
-  // programmatic dependent launch (the kernel calls pdl_wait after its set-up)
-  cudaLaunchAttribute attrs[2] = {attr[0], {}};
-  attrs[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attrs[1].val.programmaticStreamSerializationAllowed = pb::pdl_enabled() ? 1 : 0;
-  cfg.attrs = attrs;
-  cfg.numAttrs = 2;
   PB_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kern, ta, tb, to, tx, args));
 }
 

@@ -536,7 +536,6 @@ __global__ void __launch_bounds__(256, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  pdl_enter();  // set-up above overlaps the previous kernel; global memory only from here
   const uint32_t tmem_base = tmem_base_sh;
   const int num_tiles = args.m_tiles * args.n_tiles * args.splits;
   const bool swiglu = args.epi == EPI_SWIGLU;

@@ -9,10 +9,8 @@
 #include <cudaTypedefs.h>
 #include <c10/util/Exception.h>
 
-#include <cstdlib>
 #include <mutex>
 #include <set>
-#include <string>
 #include <utility>
 
 #define PB_CUDA_CHECK(expr)                                                              \
@@ -100,35 +98,6 @@ inline int* status_ptr(int dev) {
 // collective from holding back the compute kernels in practice is its width: see
 // parallel/comm.py.)  Returns ``value``, used as the first launch argument:
 // ``k<<<pb::smem_max(k, grid), ...>>>``; one attribute call per (device, kernel).
-// Programmatic dependent launch (common.cuh: pdl_wait / pdl_trigger) for the kernels of
-// the training step's main chain; PB_PDL=0 turns it off (plain stream order).
-inline bool pdl_enabled() {
-  static const bool on = [] {
-    const char* e = std::getenv("PB_PDL");
-    return e == nullptr || std::string(e) != "0";
-  }();
-  return on;
-}
-
-// ``kernel<<<grid, block, smem, stream>>>(args...)`` with the programmatic-serialization
-// attribute: the kernel may be scheduled while its stream predecessor finishes.  Every
-// kernel launched this way calls pdl_wait() before its first global memory access.
-template <typename... KArgs, typename... Args>
-inline void launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
-                       Args&&... args) {
-  cudaLaunchConfig_t cfg{};
-  cfg.gridDim = grid;
-  cfg.blockDim = block;
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  PB_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...));
-}
-
 template <typename K, typename V>
 inline V smem_max(K* kernel, V value) {
   static std::mutex mu;
