@@ -47,6 +47,31 @@ def _deal_order(n: int, g: int) -> np.ndarray:
     return r0 + np.where((p // g) % 2 == 0, m - 1 - b, b)
 
 
+_DEAL_CACHE: dict[tuple[int, int, str], torch.Tensor] = {}
+
+
+def _deal_tensor(n: int, g: int, dev: torch.device) -> torch.Tensor:
+    """:func:`_deal_order` as a device tensor, cached per (items, CTAs, device): the
+    device-built plans copy it to the GPU once, not on every call."""
+    key = (n, g, str(dev))
+    t = _DEAL_CACHE.get(key)
+    if t is None:
+        if len(_DEAL_CACHE) >= 64:
+            _DEAL_CACHE.clear()
+        t = _DEAL_CACHE[key] = torch.from_numpy(_deal_order(n, g)).to(dev)
+    return t
+
+
+def plan_ctas(device: torch.device) -> int:
+    """Persistent CTAs the attention kernels run on ``device`` (its SM count; PLAN_CTAS
+    off the GPU)."""
+    if device.type != "cuda":
+        return PLAN_CTAS
+    from packbalance_b200.ops.gemm import sm_count
+
+    return sm_count(device)
+
+
 def doc_end_from_start(doc_start: torch.Tensor) -> torch.Tensor:
     t = doc_start.numel()
     idx = torch.arange(t, device=doc_start.device, dtype=torch.int64)
@@ -58,13 +83,15 @@ def doc_end_from_start(doc_start: torch.Tensor) -> torch.Tensor:
 
 
 def attention_plan(doc_start: torch.Tensor, n_heads: int, n_kv_heads: int,
-                   n_ctas: int = PLAN_CTAS) -> dict[str, torch.Tensor]:
+                   n_ctas: int | None = None) -> dict[str, torch.Tensor]:
     """Cost-ordered work lists: ``fwd`` int32 [nq*H, 3] = (q tile, head, first kv tile);
     ``bwd`` int32 [nk*H, 3] = (kv tile, q head, last q tile), dealt to ``n_ctas``
     persistent CTAs by :func:`_deal_order`.  The GQA heads of a kv head are separate
     backward items; their dK/dV add up in an fp32 accumulator.  Also returns
     ``doc_end`` (last token of each token's document)."""
     dev = doc_start.device
+    if n_ctas is None:
+        n_ctas = plan_ctas(dev)
     t = doc_start.numel()
     n_tiles = -(-t // TILE)
     tiles = torch.arange(n_tiles, device=dev, dtype=torch.int64)
@@ -85,7 +112,7 @@ def attention_plan(doc_start: torch.Tensor, n_heads: int, n_kv_heads: int,
         [korder.repeat_interleave(n_heads), heads.repeat(n_tiles), q_hi[korder].repeat_interleave(n_heads)],
         dim=1,
     ).to(torch.int32)
-    deal = torch.from_numpy(_deal_order(n_tiles * n_heads, n_ctas)).to(dev)
+    deal = _deal_tensor(n_tiles * n_heads, n_ctas, dev)
     fwd = fwd[deal].contiguous()
     bwd = bwd[deal].contiguous()
     return {
@@ -202,7 +229,7 @@ def attn_backward_packed(
     dqkv = torch.empty_like(qkv)
     dq_acc = torch.empty(tp, n_heads * head_dim, device=qkv.device, dtype=torch.float32)
     dkv_acc = torch.empty(tp, 2 * n_kv_heads * head_dim, device=qkv.device, dtype=torch.float32)
-    delta = torch.empty(n_heads, tp, device=qkv.device, dtype=torch.float32)
+    delta = torch.empty(2, n_heads, tp, device=qkv.device, dtype=torch.float32)  # delta, -lse * log2(e)
     _native.module().attn_bwd(
         qkv, out, dout.contiguous(), lse.contiguous(), pl["doc_start"], pl["doc_end"], pl["bwd"], n_heads,
         n_kv_heads, head_dim, 1.0 / math.sqrt(head_dim), dqkv, dq_acc, dkv_acc, delta,

@@ -2,12 +2,19 @@
 
     python -m packbalance_b200.profiling.profile_kernels [--tokens 8192] [--warmup 1]
 
-Runs each kernel ``--warmup`` times and then once more (the launch to capture, e.g.
-``ncu --set full --clock-control none -k regex:pb:: -s <warm-up launches> ...``) on the
+Runs each kernel ``--warmup`` times and then once more (the launch to capture) on the
 shapes of BASELINE config #2 (d_model 768, 12/4 heads of 64, SwiGLU 2048, vocab 32000,
 8192 tokens = 4 packs of 2048 from the bench corpus's document-length law), and prints
 each kernel's CUDA-event time of the last launch with its algorithmic FLOPs or bytes.
 Inputs total a few hundred MB, above the 126 MB L2.
+
+Capture one kernel per ncu run, after the same command has run once without ncu:
+
+    ncu --set full --clock-control none -k <one kernel name> -s <its warm-up launches> -c 1 \
+        -o prof python -m packbalance_b200.profiling.profile_kernels --warmup 1
+
+and read the others' times from this script's CUDA-event output (or an ncu run with
+``--metrics gpu__time_duration.sum`` only, which takes one pass per launch).
 
 Kernels: QKV GEMM with the RoPE epilogue, gate|up GEMM with the SwiGLU epilogue,
 down-projection dgrad GEMM, wgrad GEMM (split-K, fp32 reduce-add), LM-head GEMM with the
