@@ -588,8 +588,9 @@ __device__ __forceinline__ void reduce_box(const CUtensorMap* map, const uint8_t
 }
 
 template <int D>
-// 448 threads x 144 registers = 64512 of the SM's 65536 (launch bounds alone cap at 128)
-__global__ void __maxnreg__(144)
+// 128 registers per thread: each SM sub-partition holds 16K registers and takes four of
+// the 14 warps (4 x 32 x 128)
+__global__ void __launch_bounds__(448, 1)
     attn_bwd_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __grid_constant__ CUtensorMap tm_do,
                     const __grid_constant__ CUtensorMap tm_dq, const __grid_constant__ CUtensorMap tm_dkv,
                     const AttnArgs args) {
