@@ -588,8 +588,6 @@ __device__ __forceinline__ void reduce_box(const CUtensorMap* map, const uint8_t
 }
 
 template <int D>
-// 128 registers per thread: each SM sub-partition holds 16K registers and takes four of
-// the 14 warps (4 x 32 x 128)
 __global__ void __launch_bounds__(448, 1)
     attn_bwd_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __grid_constant__ CUtensorMap tm_do,
                     const __grid_constant__ CUtensorMap tm_dq, const __grid_constant__ CUtensorMap tm_dkv,
@@ -809,14 +807,8 @@ __global__ void __launch_bounds__(448, 1)
           break;
         }
         if (warp == 2 && lane == 0) trace_ev(args.trace, 5, g);
-        // -lse * log2(e) and delta of the tile's 128 queries (attn_delta_kernel)
-        const float* s_nl = reinterpret_cast<const float*>(smem + C::VSTAGE_OFF + s * 1024);
-        const float* s_delta = s_nl + 128;
-        // Tiles whose 64 query columns all attend this key row (inside its document's
-        // causal window: most tiles of long documents) skip the mask and the selects;
-        // the test is warp-uniform.
-        const int c0 = q0 + grp * 64;
-        const bool inside = __all_sync(0xffffffff, c0 >= kv && c0 + 63 <= de);
+        const float* s_lse = reinterpret_cast<const float*>(smem + C::VSTAGE_OFF + s * 1024);
+        const float* s_delta = s_lse + 128;
         tc_fence_after();
         // S^T -> P^T (bf16, this group's 64 query columns), then release S^T's TMEM
         // columns so the next tile's S^T MMA can run while this tile's gradient math does.
@@ -833,24 +825,17 @@ __global__ void __launch_bounds__(448, 1)
             __syncwarp();
             if (lane == 0) mbar_arrive(&st_free);
           }
-          const float4* nl4 = reinterpret_cast<const float4*>(s_nl + grp * 64 + cc * 32);
 #pragma unroll
-          for (int i4 = 0; i4 < 8; ++i4) {
-            const float4 nl = nl4[i4];
-            float p[4] = {fast_exp2(fmaf(__uint_as_float(sv[4 * i4]), args.scale_log2, nl.x)),
-                          fast_exp2(fmaf(__uint_as_float(sv[4 * i4 + 1]), args.scale_log2, nl.y)),
-                          fast_exp2(fmaf(__uint_as_float(sv[4 * i4 + 2]), args.scale_log2, nl.z)),
-                          fast_exp2(fmaf(__uint_as_float(sv[4 * i4 + 3]), args.scale_log2, nl.w))};
-            if (!inside) {
-              // select (not multiply): -lse past T is stale shared memory
+          for (int i = 0; i < 16; ++i) {
+            float p2[2];
 #pragma unroll
-              for (int e = 0; e < 4; ++e) {
-                const int q = c0 + cc * 32 + 4 * i4 + e;
-                if (!(q >= kv && q <= de)) p[e] = 0.f;
-              }
+            for (int e = 0; e < 2; ++e) {
+              const int j = grp * 64 + cc * 32 + 2 * i + e;
+              const int q = q0 + j;
+              const bool allowed = q >= kv && q <= de;
+              p2[e] = allowed ? fast_exp2(__uint_as_float(sv[2 * i + e]) * args.scale_log2 - s_lse[j] * kLog2e) : 0.f;
             }
-            pp[cc * 16 + 2 * i4] = pack_bf16x2(p[0], p[1]);
-            pp[cc * 16 + 2 * i4 + 1] = pack_bf16x2(p[2], p[3]);
+            pp[cc * 16 + i] = pack_bf16x2(p2[0], p2[1]);
           }
         }
         // The previous tile's dV/dK/dQ MMAs read P/dS from shared memory.
@@ -875,22 +860,14 @@ __global__ void __launch_bounds__(448, 1)
             if (lane == 0) mbar_arrive(&dpt_free);
           }
           uint32_t dd[16];
-          const float4* d4 = reinterpret_cast<const float4*>(s_delta + grp * 64 + cc * 32);
 #pragma unroll
-          for (int i4 = 0; i4 < 8; ++i4) {
-            const float4 dl = d4[i4];
-            const float2 pa = unpack_bf16x2(pp[cc * 16 + 2 * i4]), pb = unpack_bf16x2(pp[cc * 16 + 2 * i4 + 1]);
-            float d[4] = {pa.x * (__uint_as_float(dv[4 * i4]) - dl.x), pa.y * (__uint_as_float(dv[4 * i4 + 1]) - dl.y),
-                          pb.x * (__uint_as_float(dv[4 * i4 + 2]) - dl.z), pb.y * (__uint_as_float(dv[4 * i4 + 3]) - dl.w)};
-            if (!inside) {
-              // select (not multiply): delta past T is stale shared memory; masked P is exactly 0
-              d[0] = pa.x != 0.f ? d[0] : 0.f;
-              d[1] = pa.y != 0.f ? d[1] : 0.f;
-              d[2] = pb.x != 0.f ? d[2] : 0.f;
-              d[3] = pb.y != 0.f ? d[3] : 0.f;
-            }
-            dd[2 * i4] = pack_bf16x2(d[0], d[1]);
-            dd[2 * i4 + 1] = pack_bf16x2(d[2], d[3]);
+          for (int i = 0; i < 16; ++i) {
+            const float2 p = unpack_bf16x2(pp[cc * 16 + i]);
+            const int j = grp * 64 + cc * 32 + 2 * i;
+            // select (not multiply): delta past T is stale smem; masked P is exactly 0
+            const float d0 = p.x != 0.f ? p.x * (__uint_as_float(dv[2 * i]) - s_delta[j]) : 0.f;
+            const float d1 = p.y != 0.f ? p.y * (__uint_as_float(dv[2 * i + 1]) - s_delta[j + 1]) : 0.f;
+            dd[i] = pack_bf16x2(d0, d1);
           }
 #pragma unroll
           for (int k = 0; k < 4; ++k)
@@ -988,8 +965,7 @@ __global__ void __launch_bounds__(448, 1)
 // 16-byte words.
 __global__ void attn_delta_kernel(const __nv_bfloat16* __restrict__ o, const __nv_bfloat16* __restrict__ dout,
                                   float* __restrict__ delta, int T, int H, int D, float* __restrict__ dq_acc,
-                                  float* __restrict__ dkv_acc, int Hkv, const float* __restrict__ lse,
-                                  float* __restrict__ nlse2) {
+                                  float* __restrict__ dkv_acc, int Hkv) {
   const long idx = blockIdx.x * (long)blockDim.x + threadIdx.x;
   const long nthreads = static_cast<long>(gridDim.x) * blockDim.x;
   {
@@ -1023,7 +999,6 @@ __global__ void attn_delta_kernel(const __nv_bfloat16* __restrict__ o, const __n
     }
   }
   delta[static_cast<long>(h) * T + t] = s;
-  nlse2[static_cast<long>(h) * T + t] = -lse[static_cast<long>(h) * T + t] * kLog2e;
 }
 
 // dQ and dK (fp32 accumulators) -> bf16 into dqkv rotated back by the inverse RoPE
@@ -1131,8 +1106,7 @@ void attn_bwd(at::Tensor qkv, at::Tensor out, at::Tensor dout, at::Tensor lse, a
   TORCH_CHECK(doc_end.scalar_type() == at::kInt && doc_end.numel() == qkv.size(0), "attention: doc_end");
   const c10::cuda::CUDAGuard guard(qkv.device());
   const int T = qkv.size(0);
-  // delta: [2, H, T] fp32 = delta, then -lse * log2(e) (both written by attn_delta_kernel)
-  TORCH_CHECK(dq_acc.size(0) == T && dkv_acc.size(0) == T && delta.numel() == 2 * static_cast<long>(T) * H,
+  TORCH_CHECK(dq_acc.size(0) == T && dkv_acc.size(0) == T && delta.numel() == static_cast<long>(T) * H,
               "attention: accumulator rows");
   if (T == 0) return;
   auto s = at::cuda::getCurrentCUDAStream();
@@ -1140,8 +1114,7 @@ void attn_bwd(at::Tensor qkv, at::Tensor out, at::Tensor dout, at::Tensor lse, a
   attn_delta_kernel<<<(pairs + 255) / 256, 256, 0, s>>>(reinterpret_cast<const __nv_bfloat16*>(out.data_ptr()),
                                                       reinterpret_cast<const __nv_bfloat16*>(dout.data_ptr()),
                                                       delta.data_ptr<float>(), T, (int)H, (int)D,
-                                                      dq_acc.data_ptr<float>(), dkv_acc.data_ptr<float>(), (int)Hkv,
-                                                      lse.data_ptr<float>(), delta.data_ptr<float>() + pairs);
+                                                      dq_acc.data_ptr<float>(), dkv_acc.data_ptr<float>(), (int)Hkv);
   PB_CUDA_CHECK(cudaGetLastError());
   CUtensorMap tq = make_tmap_bf16_2d(qkv.data_ptr(), qkv.size(1), T, qkv.stride(0) * 2, 64, 128);
   CUtensorMap td = make_tmap_bf16_2d(dout.data_ptr(), dout.size(1), T, dout.stride(0) * 2, 64, 128);
@@ -1161,7 +1134,7 @@ void attn_bwd(at::Tensor qkv, at::Tensor out, at::Tensor dout, at::Tensor lse, a
   a.doc_end = doc_end.data_ptr<int>();
   a.items = items.data_ptr<int>();
   a.n_items = items.size(0);
-  a.lse = delta.data_ptr<float>() + pairs;  // the backward kernel reads -lse * log2(e)
+  a.lse = lse.data_ptr<float>();
   a.delta = delta.data_ptr<float>();
   a.status = status_ptr(qkv.device().index());
   const int grid = std::min<int>(a.n_items, num_sms(qkv.device().index()));

@@ -229,7 +229,7 @@ def attn_backward_packed(
     dqkv = torch.empty_like(qkv)
     dq_acc = torch.empty(tp, n_heads * head_dim, device=qkv.device, dtype=torch.float32)
     dkv_acc = torch.empty(tp, 2 * n_kv_heads * head_dim, device=qkv.device, dtype=torch.float32)
-    delta = torch.empty(2, n_heads, tp, device=qkv.device, dtype=torch.float32)  # delta, -lse * log2(e)
+    delta = torch.empty(n_heads, tp, device=qkv.device, dtype=torch.float32)
     _native.module().attn_bwd(
         qkv, out, dout.contiguous(), lse.contiguous(), pl["doc_start"], pl["doc_end"], pl["bwd"], n_heads,
         n_kv_heads, head_dim, 1.0 / math.sqrt(head_dim), dqkv, dq_acc, dkv_acc, delta,
