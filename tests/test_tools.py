@@ -92,3 +92,23 @@ def test_step_profiler_writes_window_trace_and_summary(tmp_path: Path) -> None:
     summary = json.loads((tmp_path / "prof" / "summary_steps2-3.json").read_text())
     assert summary["profiled_steps"] == 2
     assert summary["phases_ms"]["packbalance/forward"] > 0
+
+
+def test_attn_trace_summary_of_synthetic_stamps() -> None:
+    """The attention trace summary on hand-made stamps: two CTAs, three forward tiles."""
+    import numpy as np
+
+    from packbalance_b200.profiling.attn_trace import N_EV, N_ROLES, summarize
+
+    tr = np.zeros((2, N_ROLES, N_EV), dtype=np.int64)
+    for c in range(2):
+        tr[c, 0, N_EV - 1] = 1000  # start
+        tr[c, 2, :3] = [1100, 1500, 1900]  # S issued
+        tr[c, 4, :3] = [1200, 1600, 2000]  # S read
+        tr[c, 5, :3] = [1450, 1850, 2250]  # P ready
+        tr[c, 6, :1] = [2300]
+        tr[c, 7, :1] = [2400]
+    s = summarize(tr, "fwd")
+    assert s["s_issue_to_read"] == 100 and s["softmax_per_tile"] == 250
+    assert s["idle_between_tiles"] == 150 and s["tile_period"] == 400 and s["epilogue_per_item"] == 100
+    assert s["span_per_cta_median"] == 1400 and s["span_per_cta_max"] == 1400
