@@ -544,14 +544,6 @@ __global__ void __launch_bounds__(448, 1)
 // softmax-gradient math overlap.
 template <int D>
 struct BwdCfg {
-  // Gradient warps: GGROUPS groups of four (one per TMEM lane quarter), each on GCOLS of a
-  // tile's 128 query columns.  Four groups (16 warps) keep four warps of gradient math on
-  // every SM sub-partition; each thread then has 80 registers (22 warps).
-  static constexpr int GGROUPS = 4;
-  static constexpr int GCOLS = 128 / GGROUPS;
-  static constexpr int DQ_WARP0 = 2 + 4 * GGROUPS;  // first of the four dQ warps
-  static constexpr int THREADS = 32 * (DQ_WARP0 + 4);
-  static constexpr int STG_SLOTS = 4 / GGROUPS;     // 4 KB dK/dV staging slots per gradient warp
   static constexpr int TILE_BYTES = 128 * D * 2;
   static constexpr bool SPLIT_DQ = 256 + 3 * D <= 512;  // dQ in its own TMEM columns
   static constexpr int QSTAGES = D == 64 ? 2 : 1;
@@ -596,7 +588,7 @@ __device__ __forceinline__ void reduce_box(const CUtensorMap* map, const uint8_t
 }
 
 template <int D>
-__global__ void __launch_bounds__(BwdCfg<D>::THREADS, 1)
+__global__ void __launch_bounds__(448, 1)
     attn_bwd_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __grid_constant__ CUtensorMap tm_do,
                     const __grid_constant__ CUtensorMap tm_dq, const __grid_constant__ CUtensorMap tm_dkv,
                     const AttnArgs args) {
@@ -616,14 +608,14 @@ __global__ void __launch_bounds__(BwdCfg<D>::THREADS, 1)
       mbar_init(&qd_empty[i], 1);
     }
     mbar_init(&st_full, 1);
-    mbar_init(&ds_ready, 4 * C::GGROUPS);
+    mbar_init(&ds_ready, 8);
     mbar_init(&mma2_done, 1);
     mbar_init(&dq_free, 4);
     mbar_init(&acc_done, 1);
-    mbar_init(&acc_free, 4 * C::GGROUPS);
+    mbar_init(&acc_free, 8);
     mbar_init(&drain_bar, 1);
-    mbar_init(&st_free, 4 * C::GGROUPS);   // the gradient warps have read S^T out of TMEM
-    mbar_init(&dpt_free, 4 * C::GGROUPS);  // ... and dP^T
+    mbar_init(&st_free, 8);   // the gradient warps have read S^T out of TMEM
+    mbar_init(&dpt_free, 8);  // ... and dP^T
     abort_sh = 0;
     fence_mbar_init();
   }
@@ -779,9 +771,9 @@ __global__ void __launch_bounds__(BwdCfg<D>::THREADS, 1)
       umma_commit(&drain_bar);
       mbar_wait(&drain_bar, 0, args.status, 228, nullptr);
     }
-  } else if (warp < C::DQ_WARP0) {
+  } else if (warp < 10) {
     // ---------------- P^T / dS^T (thread = key row) ----------------
-    const int grp = (warp - 2) / 4;  // query columns [GCOLS grp, GCOLS (grp + 1))
+    const int grp = (warp - 2) / 4;  // query columns [64 grp, 64 grp + 64)
     const int q4 = warp & 3;
     const int r = q4 * 32 + lane;
     const uint32_t lane_off = static_cast<uint32_t>(q4 * 32) << 16;
@@ -818,17 +810,17 @@ __global__ void __launch_bounds__(BwdCfg<D>::THREADS, 1)
         const float* s_lse = reinterpret_cast<const float*>(smem + C::VSTAGE_OFF + s * 1024);
         const float* s_delta = s_lse + 128;
         tc_fence_after();
-        // S^T -> P^T (bf16, this group's query columns), then release S^T's TMEM columns
-        // so the next tile's S^T MMA can run while this tile's gradient math does.  dS^T
-        // below uses the same bf16 P^T that the dV MMA reads.
-        constexpr int NCC = C::GCOLS / 32;
-        uint32_t pp[C::GCOLS / 2];
+        // S^T -> P^T (bf16, this group's 64 query columns), then release S^T's TMEM
+        // columns so the next tile's S^T MMA can run while this tile's gradient math does.
+        // dS^T below uses the same bf16 P^T that the dV MMA reads (registers: 14 warps
+        // leave 128 per thread).
+        uint32_t pp[32];
 #pragma unroll
-        for (int cc = 0; cc < NCC; ++cc) {
+        for (int cc = 0; cc < 2; ++cc) {
           uint32_t sv[32];
-          tmem_ld32(tmem + lane_off + C::ST_COL + grp * C::GCOLS + cc * 32, sv);
+          tmem_ld32(tmem + lane_off + C::ST_COL + grp * 64 + cc * 32, sv);
           tmem_wait_ld();
-          if (cc == NCC - 1) {
+          if (cc == 1) {
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&st_free);
@@ -838,7 +830,7 @@ __global__ void __launch_bounds__(BwdCfg<D>::THREADS, 1)
             float p2[2];
 #pragma unroll
             for (int e = 0; e < 2; ++e) {
-              const int j = grp * C::GCOLS + cc * 32 + 2 * i + e;
+              const int j = grp * 64 + cc * 32 + 2 * i + e;
               const int q = q0 + j;
               const bool allowed = q >= kv && q <= de;
               p2[e] = allowed ? fast_exp2(__uint_as_float(sv[2 * i + e]) * args.scale_log2 - s_lse[j] * kLog2e) : 0.f;
@@ -854,16 +846,15 @@ __global__ void __launch_bounds__(BwdCfg<D>::THREADS, 1)
         if (lane == 0) bulk_wait_read<0>();  // dK/dV staging of the previous item used these tiles
         __syncwarp();
 #pragma unroll
-        for (int k = 0; k < C::GCOLS / 8; ++k)
-          st_swz_chunk(ptile, r, grp * (C::GCOLS / 8) + k,
-                       make_uint4(pp[4 * k], pp[4 * k + 1], pp[4 * k + 2], pp[4 * k + 3]));
+        for (int k = 0; k < 8; ++k)
+          st_swz_chunk(ptile, r, grp * 8 + k, make_uint4(pp[4 * k], pp[4 * k + 1], pp[4 * k + 2], pp[4 * k + 3]));
         // dP^T -> dS^T = P^T (dP^T - delta), 32 columns at a time
 #pragma unroll
-        for (int cc = 0; cc < NCC; ++cc) {
+        for (int cc = 0; cc < 2; ++cc) {
           uint32_t dv[32];
-          tmem_ld32(tmem + lane_off + C::DPT_COL + grp * C::GCOLS + cc * 32, dv);
+          tmem_ld32(tmem + lane_off + C::DPT_COL + grp * 64 + cc * 32, dv);
           tmem_wait_ld();
-          if (cc == NCC - 1) {
+          if (cc == 1) {
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&dpt_free);
@@ -872,7 +863,7 @@ __global__ void __launch_bounds__(BwdCfg<D>::THREADS, 1)
 #pragma unroll
           for (int i = 0; i < 16; ++i) {
             const float2 p = unpack_bf16x2(pp[cc * 16 + i]);
-            const int j = grp * C::GCOLS + cc * 32 + 2 * i;
+            const int j = grp * 64 + cc * 32 + 2 * i;
             // select (not multiply): delta past T is stale smem; masked P is exactly 0
             const float d0 = p.x != 0.f ? p.x * (__uint_as_float(dv[2 * i]) - s_delta[j]) : 0.f;
             const float d1 = p.y != 0.f ? p.y * (__uint_as_float(dv[2 * i + 1]) - s_delta[j + 1]) : 0.f;
@@ -880,8 +871,7 @@ __global__ void __launch_bounds__(BwdCfg<D>::THREADS, 1)
           }
 #pragma unroll
           for (int k = 0; k < 4; ++k)
-            st_swz_chunk(dstile, r, grp * (C::GCOLS / 8) + cc * 4 + k,
-                         make_uint4(dd[4 * k], dd[4 * k + 1], dd[4 * k + 2], dd[4 * k + 3]));
+            st_swz_chunk(dstile, r, grp * 8 + cc * 4 + k, make_uint4(dd[4 * k], dd[4 * k + 1], dd[4 * k + 2], dd[4 * k + 3]));
         }
         fence_async_smem();
         tc_fence_before();
@@ -893,26 +883,21 @@ __global__ void __launch_bounds__(BwdCfg<D>::THREADS, 1)
       // dK (scaled) and dV rows of this key tile -> fp32 accumulators (TMA reduce-add).
       if (!mbar_wait_warp(&acc_done, item_n & 1, args.status, 232, &abort_sh)) break;
       tc_fence_after();
-      // Staging in this warp's own slots of the P and dS tiles (64 KB, free after
-      // acc_done); the 2D columns of dK | dV go out in 32-column boxes, group g taking
-      // boxes g, g + GGROUPS, ...
-      uint8_t* stg = smem + C::P_OFF + ((warp - 2) * C::STG_SLOTS) * 4096;
+      // Staging in this group's own halves of the P and dS tiles (free after acc_done).
+      uint8_t* stg = smem + (q4 < 2 ? C::P_OFF : C::DS_OFF) + grp * 16384 + (q4 & 1) * 8192;
       int slot = 0;
 #pragma unroll 1
-      for (int c = grp * 32; c < 2 * D; c += C::GGROUPS * 32) {
+      for (int c = grp * D; c < grp * D + D; c += 32) {
         const bool is_k = c < D;
         uint32_t v[32];
         tmem_ld32(tmem + lane_off + (is_k ? C::DK_COL + c : C::DV_COL + c - D), v);
         tmem_wait_ld();
-        if (lane == 0) {
-          if (C::STG_SLOTS == 2) bulk_wait_read<1>();
-          else bulk_wait_read<0>();
-        }
+        if (lane == 0) bulk_wait_read<1>();
         __syncwarp();
         uint8_t* sl = stg + slot * 4096;
         stage_row_f32(sl, v, is_k ? args.scale : 1.f);
         reduce_box(&tm_dkv, sl, is_k ? hk * D + c : (Hkv + hk) * D + c - D, kt * 128 + q4 * 32);
-        if (C::STG_SLOTS == 2) slot ^= 1;
+        slot ^= 1;
       }
       // The staging areas overlap other warps' P^T / dS^T rows: they may be rewritten
       // (next item) only after these stores have read them; acc_free orders that.
@@ -942,30 +927,24 @@ __global__ void __launch_bounds__(BwdCfg<D>::THREADS, 1)
           break;
         }
         tc_fence_after();
-        // 64 columns at a time (registers); dQ's TMEM is released after the last load
-#pragma unroll 1
-        for (int c0 = 0; c0 < D; c0 += 64) {
-          uint32_t v[64];
-          tmem_ld32(tmem + lane_off + C::DQ_COL + c0, *reinterpret_cast<uint32_t(*)[32]>(v));
-          tmem_ld32(tmem + lane_off + C::DQ_COL + c0 + 32, *reinterpret_cast<uint32_t(*)[32]>(v + 32));
-          tmem_wait_ld();
-          if (c0 + 64 >= D) {
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&dq_free);
-          }
+        uint32_t v[D];
 #pragma unroll
-          for (int c = 0; c < 64; c += 32) {
-            if (lane == 0) {
-              if (C::DQ_SLOTS == 2) bulk_wait_read<1>();
-              else bulk_wait_read<0>();
-            }
-            __syncwarp();
-            uint8_t* sl = stg + slot * 4096;
-            stage_row_f32(sl, *reinterpret_cast<uint32_t(*)[32]>(v + c), args.scale);
-            reduce_box(&tm_dq, sl, h * D + c0 + c, qt * 128 + q4 * 32);
-            if (C::DQ_SLOTS == 2) slot ^= 1;
+        for (int c = 0; c < D; c += 32) tmem_ld32(tmem + lane_off + C::DQ_COL + c, *reinterpret_cast<uint32_t(*)[32]>(v + c));
+        tmem_wait_ld();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&dq_free);
+#pragma unroll
+        for (int c = 0; c < D; c += 32) {
+          if (lane == 0) {
+            if (C::DQ_SLOTS == 2) bulk_wait_read<1>();
+            else bulk_wait_read<0>();
           }
+          __syncwarp();
+          uint8_t* sl = stg + slot * 4096;
+          stage_row_f32(sl, *reinterpret_cast<uint32_t(*)[32]>(v + c), args.scale);
+          reduce_box(&tm_dq, sl, h * D + c, qt * 128 + q4 * 32);
+          if (C::DQ_SLOTS == 2) slot ^= 1;
         }
       }
     }
@@ -1161,12 +1140,10 @@ void attn_bwd(at::Tensor qkv, at::Tensor out, at::Tensor dout, at::Tensor lse, a
   const int grid = std::min<int>(a.n_items, num_sms(qkv.device().index()));
   if (D == 64) {
     set_smem(attn_bwd_kernel<64>, BwdCfg<64>::SMEM);
-    attn_bwd_kernel<64><<<pb::smem_max(attn_bwd_kernel<64>, grid), BwdCfg<64>::THREADS, BwdCfg<64>::SMEM, s>>>(tq, td, tdq,
-                                                                                                              tdkv, a);
+    attn_bwd_kernel<64><<<pb::smem_max(attn_bwd_kernel<64>, grid), 448, BwdCfg<64>::SMEM, s>>>(tq, td, tdq, tdkv, a);
   } else {
     set_smem(attn_bwd_kernel<128>, BwdCfg<128>::SMEM);
-    attn_bwd_kernel<128><<<pb::smem_max(attn_bwd_kernel<128>, grid), BwdCfg<128>::THREADS, BwdCfg<128>::SMEM, s>>>(
-        tq, td, tdq, tdkv, a);
+    attn_bwd_kernel<128><<<pb::smem_max(attn_bwd_kernel<128>, grid), 448, BwdCfg<128>::SMEM, s>>>(tq, td, tdq, tdkv, a);
   }
   PB_CUDA_CHECK(cudaGetLastError());
   const long n4 = static_cast<long>(T) * (H + 2 * Hkv) * (D / 8);
