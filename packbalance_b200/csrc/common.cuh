@@ -104,43 +104,13 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* s
   }
 }
 
-// Non-suspending test of a phase (the waiting thread keeps polling, no wake-up latency).
-__device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-
-// Bounded polling wait (mbar_wait without suspending), for the latency-critical
-// hand-offs between the warps of one CTA.
-__device__ __forceinline__ bool mbar_spin(uint64_t* bar, uint32_t parity, int* status, int code, volatile int* abort) {
-  if (mbar_test_wait(bar, parity)) return true;
-  const uint64_t t0 = globaltimer();
-  while (true) {
-    for (int i = 0; i < 64; ++i)
-      if (mbar_test_wait(bar, parity)) return true;
-    if (abort != nullptr && *abort) return false;
-    if (globaltimer() - t0 > PB_WAIT_TIMEOUT_NS) {
-      report_error(status, code);
-      if (abort != nullptr) *abort = 1;
-      return false;
-    }
-  }
-}
-
 // Warp-collective bounded wait: lane 0 polls, the verdict is broadcast, so every lane
 // of the warp takes the same path afterwards (the tcgen05.ld/st that follow are
 // .sync.aligned and must never be reached by a subset of the warp).
 __device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, int* status, int code,
                                                volatile int* abort) {
   int ok = 1;
-  if ((threadIdx.x & 31) == 0) ok = mbar_spin(bar, parity, status, code, abort) ? 1 : 0;
+  if ((threadIdx.x & 31) == 0) ok = mbar_wait(bar, parity, status, code, abort) ? 1 : 0;
   ok = __shfl_sync(0xffffffff, ok, 0);
   __syncwarp();
   return ok != 0;
