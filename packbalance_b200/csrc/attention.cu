@@ -531,7 +531,7 @@ __global__ void __launch_bounds__(448, 1)
 }
 
 // =================================== backward =====================================
-// Items = (key tile, query head, last query tile).  Warp roles (448 threads):
+// Items = (key tile, query head, last query tile).  Warp roles (320 threads):
 //   0      TMA: K/V once per item, Q/dO per query tile (QSTAGES-deep ring)
 //   1      tcgen05.mma: S^T = K Q^T, dP^T = V dO^T; then dV += P^T dO, dK += dS^T Q,
 //          dQ = dS K
@@ -540,38 +540,31 @@ __global__ void __launch_bounds__(448, 1)
 //          at item end dK (group 0) and dV (group 1) rows -> TMA reduce-add into the
 //          fp32 dK|dV accumulator (the GQA heads of a group add up there)
 //   10..13 dQ, thread = query row -> TMA reduce-add into the fp32 dQ accumulator
-// Tile g's dQ accumulates in the TMEM columns of its own S^T (read out by then).  At
-// head_dim 64 S^T and the dS^T tile have two buffers each: the next tile's S^T / dP^T
-// MMAs go out before this tile's dV / dK / dQ, and the gradient warps write the next
-// tile's dS^T while this tile's dK / dQ MMAs still read the other one; the P^T tile is
-// released after the dV MMA alone.  At 128 there is room for one of each, and the MMA
-// warp keeps the tile order (S^T(g + 1) after dQ(g) has been read).
+// so the next tile's S^T/dP^T MMAs, this tile's dQ write-out and the next tile's
+// softmax-gradient math overlap.
 template <int D>
 struct BwdCfg {
   static constexpr int TILE_BYTES = 128 * D * 2;
-  static constexpr int ST_BUFS = D == 64 ? 2 : 1;  // S^T (and dQ) TMEM buffers
-  static constexpr int DS_BUFS = D == 64 ? 2 : 1;  // dS^T shared-memory tiles
+  static constexpr bool SPLIT_DQ = 256 + 3 * D <= 512;  // dQ in its own TMEM columns
   static constexpr int QSTAGES = D == 64 ? 2 : 1;
-  static constexpr int DQ_SLOTS = 1;                // 4 KB staging slot per dQ warp
+  static constexpr int DQ_SLOTS = D == 64 ? 2 : 1;      // 4 KB staging slots per dQ warp
   static constexpr int K_OFF = 0;
   static constexpr int V_OFF = TILE_BYTES;
   static constexpr int Q_OFF = 2 * TILE_BYTES;  // stage s: Q at Q_OFF + 2*s*TILE, dO right after
   static constexpr int VSTAGE_OFF = Q_OFF + QSTAGES * 2 * TILE_BYTES;  // stage s: lse[128], delta[128] fp32
   static constexpr int P_OFF = VSTAGE_OFF + 2048;                      // P^T  [128 kv x 128 q] bf16
-  static constexpr int DS_OFF = P_OFF + 32768;                   // dS^T [128 kv x 128 q] bf16, DS_BUFS
-  static constexpr int DQS_OFF = DS_OFF + DS_BUFS * 32768;       // dQ staging, 4 warps
+  static constexpr int DS_OFF = P_OFF + 32768;                   // dS^T [128 kv x 128 q] bf16
+  static constexpr int DQS_OFF = DS_OFF + 32768;                 // dQ staging, 4 warps
   static constexpr int SMEM = DQS_OFF + 4 * DQ_SLOTS * 4096 + 1024;
   static_assert(SMEM <= 232448, "shared memory budget");
-  // TMEM columns: S^T[ST_BUFS] x 128 (dQ of the same tile in its first D columns), dP^T
-  // 128, dK D, dV D: 512 at both head dims.
-  static constexpr uint32_t DPT_COL = ST_BUFS * 128;
-  static constexpr uint32_t DK_COL = DPT_COL + 128;
+  static constexpr uint32_t ST_COL = 0;
+  static constexpr uint32_t DPT_COL = 128;
+  static constexpr uint32_t DQ_COL = SPLIT_DQ ? 256 : 0;
+  static constexpr uint32_t DK_COL = SPLIT_DQ ? 256 + D : 256;
   static constexpr uint32_t DV_COL = DK_COL + D;
-  static_assert(DV_COL + D <= 512, "TMEM budget");
   static constexpr uint32_t IDESC_SQ = idesc_bf16_f32(128, 128, false, false);  // S^T, dP^T
   static constexpr uint32_t IDESC_KV = idesc_bf16_f32(128, D, false, true);     // dV, dK
   static constexpr uint32_t IDESC_DQ = idesc_bf16_f32(128, D, true, true);      // dQ
-  __device__ static constexpr uint32_t st_col(uint32_t g) { return (g % ST_BUFS) * 128; }
 };
 
 // 32 fp32 of this lane's row -> 128B-swizzled [32 x 32] fp32 staging box.
@@ -600,12 +593,8 @@ __global__ void __launch_bounds__(448, 1)
                     const __grid_constant__ CUtensorMap tm_dq, const __grid_constant__ CUtensorMap tm_dkv,
                     const AttnArgs args) {
   using C = BwdCfg<D>;
-  // st_full[g % ST_BUFS]: S^T(g) computed; dpt_full / dpt_free: dP^T(g) computed / read
-  // out; ds_ready: the gradient warps wrote tile g's P^T and dS^T; p_free: dV(g) done
-  // (the P^T tile may be rewritten); mma2_done[g & 1]: dK(g) and dQ(g) done (dS^T tile
-  // g % DS_BUFS free, dQ in TMEM); dq_free: the dQ warps read dQ(g) out of TMEM.
-  __shared__ __align__(8) uint64_t kv_full, kv_empty, qd_full[2], qd_empty[2], st_full[2], dpt_full, dpt_free,
-      ds_ready, p_free, mma2_done[2], dq_free, acc_done, acc_free, drain_bar;
+  __shared__ __align__(8) uint64_t kv_full, kv_empty, qd_full[2], qd_empty[2], st_full, ds_ready, mma2_done, dq_free,
+      acc_done, acc_free, drain_bar, st_free, dpt_free;
   __shared__ uint32_t tmem_sh;
   __shared__ volatile int abort_sh;
   extern __shared__ uint8_t dyn[];
@@ -617,17 +606,16 @@ __global__ void __launch_bounds__(448, 1)
     for (int i = 0; i < 2; ++i) {
       mbar_init(&qd_full[i], 1);
       mbar_init(&qd_empty[i], 1);
-      mbar_init(&st_full[i], 1);
-      mbar_init(&mma2_done[i], 1);
     }
-    mbar_init(&dpt_full, 1);
-    mbar_init(&dpt_free, 8);
+    mbar_init(&st_full, 1);
     mbar_init(&ds_ready, 8);
-    mbar_init(&p_free, 1);
+    mbar_init(&mma2_done, 1);
     mbar_init(&dq_free, 4);
     mbar_init(&acc_done, 1);
     mbar_init(&acc_free, 8);
     mbar_init(&drain_bar, 1);
+    mbar_init(&st_free, 8);   // the gradient warps have read S^T out of TMEM
+    mbar_init(&dpt_free, 8);  // ... and dP^T
     abort_sh = 0;
     fence_mbar_init();
   }
@@ -646,7 +634,7 @@ __global__ void __launch_bounds__(448, 1)
   const int H = args.H, Hkv = args.Hkv, T = args.T;
   const int group = H / Hkv;
   // trace roles: 0 K/V load issued (per item; slot 127: start), 1 Q/dO load issued, 2
-  // S^T issued, 3 ds_ready seen by the MMA warp, 4 dV/dK/dQ issued (per tile), 5
+  // S^T / dP^T issued, 3 ds_ready seen by the MMA warp, 4 dV/dK/dQ issued (per tile), 5
   // S^T read by gradient warp 2, 6 its dS^T ready (per tile), 7 its dK/dV written (item)
   if (threadIdx.x == 0) trace_ev(args.trace, 0, kTraceMax - 1);
 
@@ -690,28 +678,23 @@ __global__ void __launch_bounds__(448, 1)
       bool ok = true;
       const uint32_t ka = smem_u32(smem + C::K_OFF), va = smem_u32(smem + C::V_OFF);
       const uint32_t pa = smem_u32(smem + C::P_OFF), dsa = smem_u32(smem + C::DS_OFF);
-      // S^T(gx) = K Q^T into its S^T buffer, once the dQ warps have read tile ``dq_tile``'s
-      // dQ (the last dQ that used the buffer, or a later one; -1: none).
-      auto issue_s = [&](uint32_t gx, int dq_tile) -> bool {
+      // S^T(gx) = K Q^T and dP^T(gx) = V dO^T of global tile gx: each overwrites its TMEM
+      // columns once the gradient warps have read out tile gx - 1's.
+      auto issue_st = [&](uint32_t gx) -> bool {
         const int sx = gx % C::QSTAGES;
         const uint32_t qa = smem_u32(smem + C::Q_OFF + sx * 2 * C::TILE_BYTES);
+        const uint32_t da = qa + C::TILE_BYTES;
         if (!mbar_wait(&qd_full[sx], (gx / C::QSTAGES) & 1, args.status, 225, &abort_sh)) return false;
-        if (dq_tile >= 0 && !mbar_wait(&dq_free, dq_tile & 1, args.status, 226, &abort_sh)) return false;
+        // Without separate dQ columns, dQ(gx-1) lives where S^T(gx) goes.
+        if (!C::SPLIT_DQ && gx > 0 && !mbar_wait(&dq_free, (gx - 1) & 1, args.status, 226, &abort_sh)) return false;
+        if (gx > 0 && !mbar_wait(&st_free, (gx - 1) & 1, args.status, 234, &abort_sh)) return false;
         tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
-          umma_ss(tmem + C::st_col(gx), sdesc_sw128(ka + off, 16, 1024), sdesc_sw128(qa + off, 16, 1024),
-                  C::IDESC_SQ, kk > 0 ? 1u : 0u);
+          umma_ss(tmem + C::ST_COL, sdesc_sw128(ka + off, 16, 1024), sdesc_sw128(qa + off, 16, 1024), C::IDESC_SQ,
+                  kk > 0 ? 1u : 0u);
         }
-        umma_commit(&st_full[gx % C::ST_BUFS]);
-        trace_ev(args.trace, 2, gx);
-        return true;
-      };
-      // dP^T(gx) = V dO^T, once the gradient warps have read dP^T(gx - 1).
-      auto issue_dp = [&](uint32_t gx) -> bool {
-        const int sx = gx % C::QSTAGES;
-        const uint32_t da = smem_u32(smem + C::Q_OFF + sx * 2 * C::TILE_BYTES) + C::TILE_BYTES;
         if (gx > 0 && !mbar_wait(&dpt_free, (gx - 1) & 1, args.status, 235, &abort_sh)) return false;
         tc_fence_after();
 #pragma unroll
@@ -720,7 +703,8 @@ __global__ void __launch_bounds__(448, 1)
           umma_ss(tmem + C::DPT_COL, sdesc_sw128(va + off, 16, 1024), sdesc_sw128(da + off, 16, 1024), C::IDESC_SQ,
                   kk > 0 ? 1u : 0u);
         }
-        umma_commit(&dpt_full);
+        umma_commit(&st_full);
+        trace_ev(args.trace, 2, gx);
         return true;
       };
       int3 nx = blockIdx.x < args.n_items ? checked_item(ld_item(args.items, blockIdx.x), args.T, args.H, args.status) : make_int3(0, 0, 0);
@@ -732,18 +716,15 @@ __global__ void __launch_bounds__(448, 1)
         // before this item's first S^T (whose completion lets the gradient warps write
         // the P^T / dS^T tiles that double as that staging).
         if (!mbar_wait(&acc_free, (item_n & 1) ^ 1, args.status, 224, &abort_sh)) break;
-        // The previous item's last dQ (tile g - 1) has been issued: wait for its read-out,
-        // which also covers tile g - 2's (the other S^T buffer).
-        if (!issue_s(g, g > 0 ? static_cast<int>(g) - 1 : -1) || !issue_dp(g)) break;
+        if (!issue_st(g)) break;
         for (int qt = kt; qt <= qhi; ++qt, ++g) {
           const int s = g % C::QSTAGES;
           const uint32_t qa = smem_u32(smem + C::Q_OFF + s * 2 * C::TILE_BYTES);
           const uint32_t da = qa + C::TILE_BYTES;
-          // Two S^T buffers: the next tile's S^T / dP^T go to the tensor pipe now (its S^T
-          // buffer last held tile g - 1, whose dQ is already issued), so they run while the
-          // gradient warps compute this tile's P^T / dS^T.
-          if (C::ST_BUFS == 2 && qt < qhi &&
-              (!issue_s(g + 1, g > 0 ? static_cast<int>(g) - 1 : -1) || !issue_dp(g + 1))) {
+          // The next tile's S^T / dP^T go to the tensor pipe now, so they run while the
+          // gradient warps compute this tile's P^T / dS^T.  (With dQ in the S^T columns
+          // the order must stay tile by tile.)
+          if (C::SPLIT_DQ && qt < qhi && !issue_st(g + 1)) {
             ok = false;
             break;
           }
@@ -754,35 +735,31 @@ __global__ void __launch_bounds__(448, 1)
           const bool first = qt == kt;
           trace_ev(args.trace, 3, g);
           tc_fence_after();
-          const uint32_t dsb = dsa + (g % C::DS_BUFS) * 32768;
-          // dV += P^T dO first: its commit frees the P^T tile for the next tile
 #pragma unroll
           for (int kk = 0; kk < 8; ++kk) {
             const uint32_t aoff = (kk >> 2) * 16384 + (kk & 3) * 32;  // K-major A over q (K dim)
             const uint32_t boff = kk * 2048;                          // MN-major B: 16 q rows
+            const uint32_t acc = (first && kk == 0) ? 0u : 1u;
             umma_ss(tmem + C::DV_COL, sdesc_sw128(pa + aoff, 16, 1024), sdesc_sw128(da + boff, 16384, 1024),
-                    C::IDESC_KV, (first && kk == 0) ? 0u : 1u);
+                    C::IDESC_KV, acc);
+            umma_ss(tmem + C::DK_COL, sdesc_sw128(dsa + aoff, 16, 1024), sdesc_sw128(qa + boff, 16384, 1024),
+                    C::IDESC_KV, acc);
           }
-          umma_commit(&p_free);
-#pragma unroll
-          for (int kk = 0; kk < 8; ++kk) {
-            const uint32_t aoff = (kk >> 2) * 16384 + (kk & 3) * 32;
-            const uint32_t boff = kk * 2048;
-            umma_ss(tmem + C::DK_COL, sdesc_sw128(dsb + aoff, 16, 1024), sdesc_sw128(qa + boff, 16384, 1024),
-                    C::IDESC_KV, (first && kk == 0) ? 0u : 1u);
+          if (C::SPLIT_DQ && g > 0 && !mbar_wait(&dq_free, (g - 1) & 1, args.status, 226, &abort_sh)) {
+            ok = false;
+            break;
           }
-          // dQ(g) = dS K into tile g's S^T columns (the gradient warps have read S^T(g))
+          tc_fence_after();
 #pragma unroll
           for (int kk = 0; kk < 8; ++kk) {
             const uint32_t off = kk * 2048;  // 16 kv rows
-            umma_ss(tmem + C::st_col(g), sdesc_sw128(dsb + off, 16384, 1024), sdesc_sw128(ka + off, 16384, 1024),
+            umma_ss(tmem + C::DQ_COL, sdesc_sw128(dsa + off, 16384, 1024), sdesc_sw128(ka + off, 16384, 1024),
                     C::IDESC_DQ, kk > 0 ? 1u : 0u);
           }
-          umma_commit(&mma2_done[g & 1]);
+          umma_commit(&mma2_done);
           umma_commit(&qd_empty[s]);
           trace_ev(args.trace, 4, g);
-          // One S^T buffer: the next tile's S^T waits for this tile's dQ read-out.
-          if (C::ST_BUFS == 1 && qt < qhi && (!issue_s(g + 1, static_cast<int>(g)) || !issue_dp(g + 1))) {
+          if (!C::SPLIT_DQ && qt < qhi && !issue_st(g + 1)) {
             ok = false;
             break;
           }
@@ -819,7 +796,7 @@ __global__ void __launch_bounds__(448, 1)
       for (int qt = kt; qt <= qhi; ++qt, ++g) {
         const int q0 = qt * 128;
         const int s = g % C::QSTAGES;
-        if (!mbar_wait_warp(&st_full[g % C::ST_BUFS], (g / C::ST_BUFS) & 1, args.status, 229, &abort_sh)) {
+        if (!mbar_wait_warp(&st_full, g & 1, args.status, 229, &abort_sh)) {
           ok = false;
           break;
         }
@@ -833,14 +810,21 @@ __global__ void __launch_bounds__(448, 1)
         const float* s_lse = reinterpret_cast<const float*>(smem + C::VSTAGE_OFF + s * 1024);
         const float* s_delta = s_lse + 128;
         tc_fence_after();
-        // S^T -> P^T (bf16, this group's 64 query columns).  dS^T below uses the same
-        // bf16 P^T that the dV MMA reads (registers: 14 warps leave 128 per thread).
+        // S^T -> P^T (bf16, this group's 64 query columns), then release S^T's TMEM
+        // columns so the next tile's S^T MMA can run while this tile's gradient math does.
+        // dS^T below uses the same bf16 P^T that the dV MMA reads (registers: 14 warps
+        // leave 128 per thread).
         uint32_t pp[32];
 #pragma unroll
         for (int cc = 0; cc < 2; ++cc) {
           uint32_t sv[32];
-          tmem_ld32(tmem + lane_off + C::st_col(g) + grp * 64 + cc * 32, sv);
+          tmem_ld32(tmem + lane_off + C::ST_COL + grp * 64 + cc * 32, sv);
           tmem_wait_ld();
+          if (cc == 1) {
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&st_free);
+          }
 #pragma unroll
           for (int i = 0; i < 16; ++i) {
             float p2[2];
@@ -854,8 +838,8 @@ __global__ void __launch_bounds__(448, 1)
             pp[cc * 16 + i] = pack_bf16x2(p2[0], p2[1]);
           }
         }
-        // The previous tile's dV MMA reads the P^T tile.
-        if (g > 0 && !mbar_wait_warp(&p_free, (g - 1) & 1, args.status, 230, &abort_sh)) {
+        // The previous tile's dV/dK/dQ MMAs read P/dS from shared memory.
+        if (g > 0 && !mbar_wait_warp(&mma2_done, (g - 1) & 1, args.status, 230, &abort_sh)) {
           ok = false;
           break;
         }
@@ -864,20 +848,6 @@ __global__ void __launch_bounds__(448, 1)
 #pragma unroll
         for (int k = 0; k < 8; ++k)
           st_swz_chunk(ptile, r, grp * 8 + k, make_uint4(pp[4 * k], pp[4 * k + 1], pp[4 * k + 2], pp[4 * k + 3]));
-        // dS^T tile g % DS_BUFS: the dK / dQ MMAs of tile g - DS_BUFS read it
-        uint8_t* dsg = dstile + (g % C::DS_BUFS) * 32768;
-        if (g >= static_cast<uint32_t>(C::DS_BUFS)) {
-          const uint32_t gb = g - C::DS_BUFS;
-          if (!mbar_wait_warp(&mma2_done[gb & 1], (gb >> 1) & 1, args.status, 236, &abort_sh)) {
-            ok = false;
-            break;
-          }
-        }
-        if (!mbar_wait_warp(&dpt_full, g & 1, args.status, 237, &abort_sh)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
         // dP^T -> dS^T = P^T (dP^T - delta), 32 columns at a time
 #pragma unroll
         for (int cc = 0; cc < 2; ++cc) {
@@ -901,7 +871,7 @@ __global__ void __launch_bounds__(448, 1)
           }
 #pragma unroll
           for (int k = 0; k < 4; ++k)
-            st_swz_chunk(dsg, r, grp * 8 + cc * 4 + k, make_uint4(dd[4 * k], dd[4 * k + 1], dd[4 * k + 2], dd[4 * k + 3]));
+            st_swz_chunk(dstile, r, grp * 8 + cc * 4 + k, make_uint4(dd[4 * k], dd[4 * k + 1], dd[4 * k + 2], dd[4 * k + 3]));
         }
         fence_async_smem();
         tc_fence_before();
@@ -952,14 +922,14 @@ __global__ void __launch_bounds__(448, 1)
       const int kt = nx.x, h = nx.y, qhi = nx.z;
       if (it + (int)gridDim.x < args.n_items) nx = checked_item(ld_item(args.items, it + gridDim.x), args.T, args.H, args.status);
       for (int qt = kt; qt <= qhi; ++qt, ++g) {
-        if (!mbar_wait_warp(&mma2_done[g & 1], (g >> 1) & 1, args.status, 231, &abort_sh)) {
+        if (!mbar_wait_warp(&mma2_done, g & 1, args.status, 231, &abort_sh)) {
           ok = false;
           break;
         }
         tc_fence_after();
         uint32_t v[D];
 #pragma unroll
-        for (int c = 0; c < D; c += 32) tmem_ld32(tmem + lane_off + C::st_col(g) + c, *reinterpret_cast<uint32_t(*)[32]>(v + c));
+        for (int c = 0; c < D; c += 32) tmem_ld32(tmem + lane_off + C::DQ_COL + c, *reinterpret_cast<uint32_t(*)[32]>(v + c));
         tmem_wait_ld();
         tc_fence_before();
         __syncwarp();
