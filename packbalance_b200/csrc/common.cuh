@@ -310,9 +310,11 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&v);
 }
+// bf16 -> fp32 is exact: the bf16 bits are the high half of the fp32 bits.  Two integer
+// operations instead of two conversions (those issue to the MUFU / conversion pipe,
+// which the attention kernels' exponentials already saturate).
 __device__ __forceinline__ float2 unpack_bf16x2(uint32_t v) {
-  __nv_bfloat162 h = *reinterpret_cast<__nv_bfloat162*>(&v);
-  return __bfloat1622float2(h);
+  return make_float2(__uint_as_float(v << 16), __uint_as_float(v & 0xffff0000u));
 }
 // Logistic function with the fast exp and divide intrinsics (a few ulp; the callers
 // round the results to bf16).  Large negative x: 1 + exp(-x) overflows to inf and the
