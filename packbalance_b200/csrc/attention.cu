@@ -32,9 +32,6 @@
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 
-#include <cstdlib>
-#include <string>
-
 #include "common.cuh"
 #include "host_utils.h"
 
@@ -47,13 +44,6 @@ __device__ __forceinline__ float fast_exp2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
-}
-
-// bf16 pair packing: PI = integer rounding (off the conversion pipe), else cvt.
-template <bool PI>
-__device__ __forceinline__ uint32_t pk2(float lo, float hi) {
-  if constexpr (PI) return pack_bf16x2_int(lo, hi);
-  else return pack_bf16x2(lo, hi);
 }
 
 __device__ __forceinline__ void fence_proxy_async_smem() {
@@ -153,7 +143,7 @@ __device__ __forceinline__ int3 checked_item(int3 it, int T, int H, int* status)
   return it;
 }
 
-template <int D, bool PI>
+template <int D>
 __global__ void __launch_bounds__(448, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tmap, const AttnArgs args) {
   using C = FwdCfg<D>;
@@ -417,7 +407,7 @@ __global__ void __launch_bounds__(448, 1)
           const float p0 = fast_exp2(fmaf(PB_S(2 * i), sl2, nb));
           const float p1 = fast_exp2(fmaf(PB_S(2 * i + 1), sl2, nb));
           sum4[i & 3] += p0 + p1;
-          pk[i] = pk2<PI>(p0, p1);
+          pk[i] = pack_bf16x2(p0, p1);
         }
 #undef PB_S
         const float sum = (sum4[0] + sum4[1]) + (sum4[2] + sum4[3]);
@@ -515,7 +505,7 @@ __global__ void __launch_bounds__(448, 1)
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
               const int e = 8 * k + 2 * i;
-              pk[i] = pk2<PI>(__uint_as_float(oa[e]) * sa + __uint_as_float(obv[e]) * sbb,
+              pk[i] = pack_bf16x2(__uint_as_float(oa[e]) * sa + __uint_as_float(obv[e]) * sbb,
                                   __uint_as_float(oa[e + 1]) * sa + __uint_as_float(obv[e + 1]) * sbb);
             }
             dst[k] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
@@ -597,7 +587,7 @@ __device__ __forceinline__ void reduce_box(const CUtensorMap* map, const uint8_t
   }
 }
 
-template <int D, bool PI>
+template <int D>
 __global__ void __launch_bounds__(448, 1)
     attn_bwd_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __grid_constant__ CUtensorMap tm_do,
                     const __grid_constant__ CUtensorMap tm_dq, const __grid_constant__ CUtensorMap tm_dkv,
@@ -845,7 +835,7 @@ __global__ void __launch_bounds__(448, 1)
               const bool allowed = q >= kv && q <= de;
               p2[e] = allowed ? fast_exp2(__uint_as_float(sv[2 * i + e]) * args.scale_log2 - s_lse[j] * kLog2e) : 0.f;
             }
-            pp[cc * 16 + i] = pk2<PI>(p2[0], p2[1]);
+            pp[cc * 16 + i] = pack_bf16x2(p2[0], p2[1]);
           }
         }
         // The previous tile's dV/dK/dQ MMAs read P/dS from shared memory.
@@ -877,7 +867,7 @@ __global__ void __launch_bounds__(448, 1)
             // select (not multiply): delta past T is stale smem; masked P is exactly 0
             const float d0 = p.x != 0.f ? p.x * (__uint_as_float(dv[2 * i]) - s_delta[j]) : 0.f;
             const float d1 = p.y != 0.f ? p.y * (__uint_as_float(dv[2 * i + 1]) - s_delta[j + 1]) : 0.f;
-            dd[i] = pk2<PI>(d0, d1);
+            dd[i] = pack_bf16x2(d0, d1);
           }
 #pragma unroll
           for (int k = 0; k < 4; ++k)
@@ -1059,16 +1049,6 @@ static void set_smem(K kern, int bytes) {
   PB_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
 }
 
-// bf16 packing of P / dS in the attention kernels: integer rounding (default) or the
-// conversion instruction (PB_ATTN_PACK=cvt), chosen once per process.
-static bool attn_pack_int() {
-  static const bool v = [] {
-    const char* e = std::getenv("PB_ATTN_PACK");
-    return !(e != nullptr && std::string(e) == "cvt");
-  }();
-  return v;
-}
-
 // Event-trace buffer of the next attention launches (0: off), set by attn_trace().
 static unsigned long long* g_attn_trace = nullptr;
 
@@ -1102,20 +1082,13 @@ std::vector<at::Tensor> attn_fwd(at::Tensor qkv, at::Tensor doc_start, at::Tenso
   a.status = status_ptr(qkv.device().index());
   const int grid = std::min<int>(a.n_items, num_sms(qkv.device().index()));
   auto s = at::cuda::getCurrentCUDAStream();
-#define PB_FWD(DD, PP)                                                                                     \
-  do {                                                                                                     \
-    set_smem(attn_fwd_kernel<DD, PP>, FwdCfg<DD>::SMEM);                                                  \
-    attn_fwd_kernel<DD, PP><<<pb::smem_max(attn_fwd_kernel<DD, PP>, grid), 448, FwdCfg<DD>::SMEM, s>>>(tm, a); \
-  } while (0)
-  const bool pi = attn_pack_int();
   if (D == 64) {
-    if (pi) PB_FWD(64, true);
-    else PB_FWD(64, false);
+    set_smem(attn_fwd_kernel<64>, FwdCfg<64>::SMEM);
+    attn_fwd_kernel<64><<<pb::smem_max(attn_fwd_kernel<64>, grid), 448, FwdCfg<64>::SMEM, s>>>(tm, a);
   } else {
-    if (pi) PB_FWD(128, true);
-    else PB_FWD(128, false);
+    set_smem(attn_fwd_kernel<128>, FwdCfg<128>::SMEM);
+    attn_fwd_kernel<128><<<pb::smem_max(attn_fwd_kernel<128>, grid), 448, FwdCfg<128>::SMEM, s>>>(tm, a);
   }
-#undef PB_FWD
   PB_CUDA_CHECK(cudaGetLastError());
   return {out, lse};
 }
@@ -1165,21 +1138,13 @@ void attn_bwd(at::Tensor qkv, at::Tensor out, at::Tensor dout, at::Tensor lse, a
   a.delta = delta.data_ptr<float>();
   a.status = status_ptr(qkv.device().index());
   const int grid = std::min<int>(a.n_items, num_sms(qkv.device().index()));
-#define PB_BWD(DD, PP)                                                                                          \
-  do {                                                                                                          \
-    set_smem(attn_bwd_kernel<DD, PP>, BwdCfg<DD>::SMEM);                                                       \
-    attn_bwd_kernel<DD, PP><<<pb::smem_max(attn_bwd_kernel<DD, PP>, grid), 448, BwdCfg<DD>::SMEM, s>>>(tq, td, tdq, \
-                                                                                                     tdkv, a);  \
-  } while (0)
-  const bool pi = attn_pack_int();
   if (D == 64) {
-    if (pi) PB_BWD(64, true);
-    else PB_BWD(64, false);
+    set_smem(attn_bwd_kernel<64>, BwdCfg<64>::SMEM);
+    attn_bwd_kernel<64><<<pb::smem_max(attn_bwd_kernel<64>, grid), 448, BwdCfg<64>::SMEM, s>>>(tq, td, tdq, tdkv, a);
   } else {
-    if (pi) PB_BWD(128, true);
-    else PB_BWD(128, false);
+    set_smem(attn_bwd_kernel<128>, BwdCfg<128>::SMEM);
+    attn_bwd_kernel<128><<<pb::smem_max(attn_bwd_kernel<128>, grid), 448, BwdCfg<128>::SMEM, s>>>(tq, td, tdq, tdkv, a);
   }
-#undef PB_BWD
   PB_CUDA_CHECK(cudaGetLastError());
   const long n4 = static_cast<long>(T) * (H + 2 * Hkv) * (D / 8);
   dqkv_finalize_kernel<<<std::max<long>(1, std::min<long>((n4 + 255) / 256, 8L * num_sms(qkv.device().index()))),
