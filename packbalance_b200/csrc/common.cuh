@@ -310,17 +310,6 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&v);
 }
-// fp32 -> bf16 round-to-nearest-even of two finite values, packed (lo in the low half),
-// with integer operations: add 0x7fff plus the lowest kept bit, keep the high half (the
-// usual bit-level rounding; ties go to the even bf16).  Takes the pair off the
-// conversion pipe, which the attention kernels' exponentials saturate.  NaN payloads are
-// not preserved (a NaN may come out as an infinity); the callers pack finite values.
-__device__ __forceinline__ uint32_t pack_bf16x2_int(float lo, float hi) {
-  uint32_t a = __float_as_uint(lo), b = __float_as_uint(hi);
-  a += 0x7fffu + ((a >> 16) & 1u);
-  b += 0x7fffu + ((b >> 16) & 1u);
-  return __byte_perm(a, b, 0x7632);
-}
 // bf16 -> fp32 is exact: the bf16 bits are the high half of the fp32 bits.  Two integer
 // operations instead of two conversions (those issue to the MUFU / conversion pipe,
 // which the attention kernels' exponentials already saturate).
