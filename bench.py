@@ -3,7 +3,7 @@
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
     torchrun --nproc-per-node N --master-addr 127.0.0.1 ... bench.py --gpus N ...
 
-Config: BASELINE config #2 (``configs/b2_100m.yaml``): 12 layers, d_model 768, 12/4
+Config: benchmark config #2 (``configs/b2_100m.yaml``): 12 layers, d_model 768, 12/4
 heads, SwiGLU 2048, vocab 32000, tied embeddings, random init; synthetic heavy-tail
 documents (lognormal median 256, sigma 1.2, clipped [16, 2048], Zipf(1.1) ids),
 ``pack_ffd`` packing to 2048 tokens, balanced schedule, 4 packs per rank per step,

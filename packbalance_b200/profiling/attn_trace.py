@@ -5,7 +5,7 @@
 Runs the forward and backward kernels once more after warm-up with the kernels' event
 trace switched on (``_C.attn_trace``: lane 0 of each role stamps the SM clock at its
 steps, ``csrc/attention.cu``), on the bench corpus's document-length law (or fixed
-``--doc-len`` documents), 12/4 heads of 64 as in BASELINE config #2, and prints per-step
+``--doc-len`` documents), 12/4 heads of 64 as in benchmark config #2, and prints per-step
 medians over all CTAs and tiles, in SM clock cycles:
 
 forward   S issued -> S read by softmax warp 2 (TMEM result latency), softmax of one

@@ -3,7 +3,7 @@
     python -m packbalance_b200.profiling.profile_kernels [--tokens 8192] [--warmup 1]
 
 Runs each kernel ``--warmup`` times and then once more (the launch to capture) on the
-shapes of BASELINE config #2 (d_model 768, 12/4 heads of 64, SwiGLU 2048, vocab 32000,
+shapes of benchmark config #2 (d_model 768, 12/4 heads of 64, SwiGLU 2048, vocab 32000,
 8192 tokens = 4 packs of 2048 from the bench corpus's document-length law), and prints
 each kernel's CUDA-event time of the last launch with its algorithmic FLOPs or bytes.
 Inputs total a few hundred MB, above the 126 MB L2.

@@ -3,7 +3,7 @@
     python -m packbalance_b200.profiling.step_timeline [--config configs/b2_100m.yaml]
     torchrun --nproc-per-node N -m packbalance_b200.profiling.step_timeline --output-dir T
 
-Builds the benchmark's engine and data (BASELINE config #2 by default), runs warm-up steps
+Builds the benchmark's engine and data (benchmark config #2 by default), runs warm-up steps
 (so the step is a CUDA-graph replay where the engine captures one), then records two steps
 with ``torch.profiler`` (CUPTI kernel records, device timestamps) and summarises the second
 one per rank into ``<output-dir>/step_timeline_w{W}_r{rank}.json``:

@@ -1,4 +1,4 @@
-"""BASELINE config #1 against the reference itself (CPU, gloo, world size 2, fp32).
+"""benchmark config #1 against the reference itself (CPU, gloo, world size 2, fp32).
 
 Both frameworks read the same corpus; the test checks that the packs and the balanced
 schedule are identical, starts both models from the same weights (the reference's

@@ -47,7 +47,7 @@ def test_layer_segments_follow_the_fused_gemms(model_cfg: ModelConfig) -> None:
 
 
 def test_8b_config_fits_on_b200_at_8_ranks() -> None:
-    """BASELINE config #5 (Llama-3-8B shape) on 8 ranks: the sharded engine's persistent
+    """benchmark config #5 (Llama-3-8B shape) on 8 ranks: the sharded engine's persistent
     buffers per rank (bf16 gathered weights, fp32 gradient, fp32 master + moments +
     reduced-gradient shards) leave most of a B200's 180 GB for activations.  Built on
     the meta device: no memory is allocated."""
