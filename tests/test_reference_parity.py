@@ -1,4 +1,4 @@
-"""benchmark config #1 against the reference itself (CPU, gloo, world size 2, fp32).
+"""Benchmark config #1 against the reference itself (CPU, gloo, world size 2, fp32).
 
 Both frameworks read the same corpus; the test checks that the packs and the balanced
 schedule are identical, starts both models from the same weights (the reference's
@@ -148,3 +148,53 @@ def test_config1_matches_reference_losses(tmp_path: Path) -> None:
         assert abs(ref - ours) <= 2e-5 * abs(ref) + 1e-6, losses
     # the model trains: last loss below the first
     assert losses[-1][0] < losses[0][0]
+
+
+@pytest.mark.parametrize("mode", ["pad", "pack_random", "pack_ffd", "isoflop"])
+@pytest.mark.parametrize("schedule", ["random", "balanced"])
+@pytest.mark.parametrize("world", [1, 4])
+def test_packs_and_schedules_match_reference(tmp_path: Path, mode: str, schedule: str, world: int) -> None:
+    """Every packing mode and both schedules give the reference's packs and step plans on
+    a corpus with long (split) and one-token documents (no process group needed)."""
+    import sys as _sys
+
+    _sys.path.insert(1, str(REF))
+    from packbalance.config import DataConfig as RData
+    from packbalance.config import ModelConfig as RModel
+    from packbalance.data.cost import FlopModel as RFlop
+    from packbalance.data.packer import build_packs as rbuild_packs
+    from packbalance.data.sampler import build_schedule as rbuild_schedule
+    from packbalance.data.store import TokenStore as RStore
+
+    from packbalance_b200.config import DataConfig, ModelConfig
+    from packbalance_b200.data.cost import FlopModel
+    from packbalance_b200.data.packer import build_packs
+    from packbalance_b200.data.prepare import prepare_synthetic
+    from packbalance_b200.data.sampler import build_schedule
+    from packbalance_b200.data.store import TokenStore
+
+    d = DataConfig(dataset="synthetic", data_dir=str(tmp_path / "c"), seq_len=96, mode=mode, schedule=schedule,
+                   max_doc_len=96, min_doc_len=1, synthetic_num_docs=300, synthetic_mu=3.4, synthetic_sigma=1.1,
+                   synthetic_min_len=1, synthetic_max_len=250, synthetic_vocab_size=97, num_workers=0,
+                   val_fraction=0.1, seed=5, pad_batch_size=4)
+    m = ModelConfig(vocab_size=97, d_model=32, n_layers=2, n_heads=4, n_kv_heads=2, d_ff=64, max_seq_len=96)
+    prepare_synthetic(d, Path(d.data_dir))
+    rd = RData(dataset="synthetic", data_dir=d.data_dir, seq_len=d.seq_len, mode=mode, schedule=schedule,
+               max_doc_len=d.max_doc_len, min_doc_len=d.min_doc_len, val_fraction=d.val_fraction, seed=d.seed,
+               num_workers=0, pad_batch_size=d.pad_batch_size)
+    rm = RModel(vocab_size=m.vocab_size, d_model=m.d_model, n_layers=m.n_layers, n_heads=m.n_heads,
+                n_kv_heads=m.n_kv_heads, d_ff=m.d_ff, max_seq_len=m.max_seq_len)
+    key = lambda ps: [[(s.doc_id, s.start, s.length) for s in p.segments] for p in ps]  # noqa: E731
+    built = {}
+    for split in ("train", "val"):
+        packs = build_packs(TokenStore.open(d.data_dir), d, FlopModel.from_config(m), split=split)
+        rpacks = rbuild_packs(RStore.open(d.data_dir), rd, RFlop.from_config(rm), split=split)
+        assert key(packs) == key(rpacks), (split, mode)
+        built[split] = (packs, rpacks)
+    packs, rpacks = built["train"]
+    accum = 2
+    sched = build_schedule(packs, world, accum, seed=d.seed, mode=schedule)
+    rsched = rbuild_schedule(rpacks, world, accum, seed=d.seed, mode=schedule)
+    assert len(sched.steps) > 0
+    assert [s.rank_packs for s in sched.steps] == [s.rank_packs for s in rsched.steps]
+    assert [s.step_tokens for s in sched.steps] == [s.step_tokens for s in rsched.steps]
