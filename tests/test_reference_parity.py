@@ -198,3 +198,32 @@ def test_packs_and_schedules_match_reference(tmp_path: Path, mode: str, schedule
     assert len(sched.steps) > 0
     assert [s.rank_packs for s in sched.steps] == [s.rank_packs for s in rsched.steps]
     assert [s.step_tokens for s in sched.steps] == [s.step_tokens for s in rsched.steps]
+
+
+def test_greedy_generation_matches_reference() -> None:
+    """The KV-cache generate gives the reference's greedy continuation (which recomputes
+    the whole prefix every token) from the same weights."""
+    import sys as _sys
+
+    import torch
+
+    _sys.path.insert(1, str(REF))
+    from packbalance.config import ModelConfig as RModel
+    from packbalance.model.llama import LlamaForCausalLM as RModelCls
+
+    from packbalance_b200.config import ModelConfig
+    from packbalance_b200.models.llama import LlamaForCausalLM
+
+    kw = dict(vocab_size=113, d_model=48, n_layers=2, n_heads=6, n_kv_heads=2, d_ff=80, max_seq_len=40)
+    torch.manual_seed(4)
+    ref = RModelCls(RModel(**kw, attention_backend="eager", use_fused_ce=False))
+    ours = LlamaForCausalLM(ModelConfig(**kw, attention_backend="eager", use_fused_ce=False))
+    ours.load_state_dict(ref.state_dict())
+    prompt = torch.randint(1, 113, (2, 7), generator=torch.Generator().manual_seed(9))
+    with torch.no_grad():
+        a = ref.generate(prompt, max_new_tokens=20)
+        b = ours.generate(prompt, max_new_tokens=20)
+    assert torch.equal(a, b)
+    # stops at max_seq_len like the reference
+    with torch.no_grad():
+        assert torch.equal(ref.generate(prompt, max_new_tokens=50), ours.generate(prompt, max_new_tokens=50))
