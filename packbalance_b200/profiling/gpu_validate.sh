@@ -26,6 +26,8 @@ python -m pytest tests -m gpu -q
 
 echo "== kernel microbenchmarks =="
 python -m packbalance_b200.profiling.bench_kernels --output "$OUT/kernel_bench.json"
+echo "== attention event traces =="
+python -m packbalance_b200.profiling.attn_trace --json "$OUT/attn_trace.json"
 echo "== scheduler ablation =="
 python -m packbalance_b200.profiling.bench_schedule --config configs/bench.yaml --world-size 8 \
   --output "$OUT/schedule_bench.json"
@@ -48,10 +50,18 @@ if [[ "$NGPU" -ge 2 ]]; then
   timeout -k 60 600 python -m torch.distributed.run --nnodes=1 --nproc-per-node "$NGPU" --master-addr 127.0.0.1 \
     --master-port 29541 -m packbalance_b200.train.train --config configs/tiny.yaml --max-steps 2 \
     --output-dir "$OUT/ddp_smoke"
-  echo "== $NGPU-GPU sharded smoke =="
+  echo "== $NGPU-GPU sharded smoke (persistent weights, then two weight windows) =="
   timeout -k 60 600 python -m torch.distributed.run --nnodes=1 --nproc-per-node "$NGPU" --master-addr 127.0.0.1 \
     --master-port 29542 -m packbalance_b200.train.train --config configs/tiny.yaml --max-steps 2 --fsdp \
     --output-dir "$OUT/fsdp_smoke"
+  timeout -k 60 600 python -m torch.distributed.run --nnodes=1 --nproc-per-node "$NGPU" --master-addr 127.0.0.1 \
+    --master-port 29545 -m packbalance_b200.train.train --config configs/tiny.yaml --max-steps 2 --fsdp \
+    --set train.fsdp_weight_windows=2 --output-dir "$OUT/fsdp_windows_smoke"
+  echo "== $NGPU-GPU headline bench (fp32 and bf16 gradient wire) =="
+  timeout -k 60 600 python -m torch.distributed.run --nnodes=1 --nproc-per-node "$NGPU" --master-addr 127.0.0.1 \
+    --master-port 29546 bench.py --gpus "$NGPU" --steps 20 --warmup 5
+  timeout -k 60 600 python -m torch.distributed.run --nnodes=1 --nproc-per-node "$NGPU" --master-addr 127.0.0.1 \
+    --master-port 29547 bench.py --gpus "$NGPU" --steps 20 --warmup 5 --set train.grad_reduce_dtype=bf16
   echo "== collectives =="
   timeout -k 60 600 python -m torch.distributed.run --nnodes=1 --nproc-per-node "$NGPU" --master-addr 127.0.0.1 \
     --master-port 29543 -m packbalance_b200.profiling.bench_comm
