@@ -34,7 +34,7 @@ from torch.profiler import record_function
 
 from packbalance_b200.config import PackBalanceConfig, apply_overrides, load_config, save_config
 from packbalance_b200.data.cost import FlopModel
-from packbalance_b200.data.dataset import build_dataloader, concat_packs, to_device
+from packbalance_b200.data.dataset import build_dataloader, to_device
 from packbalance_b200.data.packer import build_packs, pack_stats
 from packbalance_b200.data.sampler import build_schedule
 from packbalance_b200.data.store import TokenStore
