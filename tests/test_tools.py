@@ -112,3 +112,26 @@ def test_attn_trace_summary_of_synthetic_stamps() -> None:
     assert s["s_issue_to_read"] == 100 and s["softmax_per_tile"] == 250
     assert s["idle_between_tiles"] == 150 and s["tile_period"] == 400 and s["epilogue_per_item"] == 100
     assert s["span_per_cta_median"] == 1400 and s["span_per_cta_max"] == 1400
+
+
+def test_step_timeline_summary_of_synthetic_events() -> None:
+    """The step-timeline summary: collectives with the compute that ran beside them, the
+    optimizer start, idle time of the attention stream, per-kernel totals."""
+    from packbalance_b200.profiling.step_timeline import summarize
+
+    ev = [
+        (0.0, 10.0, "pb::gemm_pair_kernel", 7),
+        (12.0, 30.0, "pb::attn_bwd_kernel<64>", 7),
+        (14.0, 24.0, "pb::nvls_allreduce_kernel", 9),   # 10 us, all of it beside attn_bwd
+        (30.0, 40.0, "void pb::fused_allreduce_kernel<2>", 9),  # nothing beside it
+        (35.0, 38.0, "pb::gemm_pair_kernel", 7),
+        (41.0, 50.0, "pb::adamw_kernel", 7),
+    ]
+    s = summarize(ev)
+    assert s["step_span_us"] == 50.0 and s["optimizer_start_us"] == 41.0
+    beside = {c["start_us"]: c["compute_beside_us"] for c in s["collectives"]}
+    assert beside == {14.0: 10.0, 30.0: 3.0 + 0.0}
+    # the attention stream (7) idles 0-10 -> 12 and 30 -> 35 and 38 -> 41
+    assert s["main_stream_gaps_us"] == 2.0 + 5.0 + 3.0
+    tops = {t["name"]: t for t in s["top_kernels"]}
+    assert tops["pb::gemm_pair_kernel"]["count"] == 2 and tops["pb::gemm_pair_kernel"]["us"] == 13.0
