@@ -126,3 +126,39 @@ def test_plan_deals_every_item_once_and_balances() -> None:
     cost = (fwd[:, 0] - fwd[:, 2] + 1).astype(float)
     loads = np.bincount(np.arange(len(cost)) % 148, weights=cost, minlength=148)
     assert loads.max() / loads.mean() < 1.12
+
+
+def test_plan_covers_exactly_the_needed_tiles_property() -> None:
+    """For random packed layouts (one-token documents, documents crossing tiles, ragged
+    ends), every forward item (q tile, head, first kv tile) starts at the kv tile of the
+    tile's earliest document start, every backward item (kv tile, head, last q tile)
+    ends at the q tile of the kv tile's latest document end, and each (tile, head) pair
+    appears exactly once in each list; brute force over the dense mask."""
+    import numpy as np
+    from hypothesis import given, settings
+    from hypothesis import strategies as st
+
+    from packbalance_b200.ops.attention import TILE, attention_plan_host
+
+    @settings(max_examples=40, deadline=None)
+    @given(st.lists(st.integers(1, 300), min_size=1, max_size=30), st.integers(1, 4), st.integers(1, 148))
+    def check(lengths, heads, ctas):
+        ds = np.concatenate([np.full(n, s) for n, s in zip(lengths, np.cumsum([0] + lengths[:-1]))]).astype(np.int64)
+        t = ds.size
+        nt = -(-t // TILE)
+        plan = attention_plan_host(ds, heads, ctas)
+        fwd, bwd = plan["fwd"].numpy(), plan["bwd"].numpy()
+        assert sorted((int(a), int(b)) for a, b, _ in fwd) == [(i, h) for i in range(nt) for h in range(heads)]
+        assert sorted((int(a), int(b)) for a, b, _ in bwd) == [(i, h) for i in range(nt) for h in range(heads)]
+        q = np.arange(t)
+        allowed = (q[None, :] >= ds[:, None]) & (q[None, :] <= q[:, None])  # [query, key]
+        for qt, _, kt0 in fwd:
+            rows = allowed[qt * TILE : (qt + 1) * TILE]
+            need = np.nonzero(rows.any(axis=0))[0] // TILE
+            assert kt0 == need.min() and need.max() <= qt
+        for kt, _, qhi in bwd:
+            cols = allowed[:, kt * TILE : (kt + 1) * TILE]
+            need = np.nonzero(cols.any(axis=1))[0] // TILE
+            assert qhi == need.max() and need.min() >= kt
+
+    check()
