@@ -366,7 +366,6 @@ class ShardedParameters(GradWindow):
         self._issued: set[int] = set()
         self.ready_hook = None
         self.hold_ready = False  # set while a non-final microbatch runs its backward pass
-        self.hold_prefetch = False  # tests: no backward-pass prefetch
         # the first fetches read the peers' owned chunks written above
         torch.cuda.synchronize(dev)
         dist.barrier(group=self.group)
@@ -482,7 +481,7 @@ class ShardedParameters(GradWindow):
         beside this layer's kernels; the window's last reader (the layer ``windows``
         positions later) was enqueued on the current stream before this point."""
         u = self.unit_of.get(id(params[0]))
-        if u is None or u.wwin < 0 or self.hold_prefetch:
+        if u is None or u.wwin < 0:
             return
         prev = next((v for v in self.units if v.order == u.order - 1), None)
         if prev is None or prev.wwin < 0 or all(seg in self._gathered_segs for seg in prev.segments):
