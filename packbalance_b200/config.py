@@ -190,8 +190,10 @@ class TrainConfig:
     # Native sharded engine (fsdp on CUDA): 0 keeps every unit's gathered bf16 weights
     # for the whole step (2 B/param per rank, no second all-gather); K >= 2 rotates the
     # decoder layers' gathered weights through K windows of one layer, fetched again for
-    # the backward pass one layer ahead (the reference's FSDP2 resharding after forward).
-    fsdp_weight_windows: int = 0
+    # the backward pass one layer ahead (the reference's FSDP2 resharding after forward);
+    # -1 (auto) keeps them when they take at most a quarter of the device's memory, else
+    # uses two windows.
+    fsdp_weight_windows: int = -1
 
     def __post_init__(self) -> None:
         if self.dtype not in DTYPES:
@@ -206,8 +208,8 @@ class TrainConfig:
             raise ValueError("keep_last must be >= 0")
         if self.grad_reduce_dtype not in ("fp32", "bf16"):
             raise ValueError("grad_reduce_dtype must be fp32 or bf16")
-        if self.fsdp_weight_windows < 0 or self.fsdp_weight_windows == 1:
-            raise ValueError("fsdp_weight_windows must be 0 or at least 2")
+        if self.fsdp_weight_windows < -1 or self.fsdp_weight_windows == 1:
+            raise ValueError("fsdp_weight_windows must be -1 (auto), 0 or at least 2")
 
 
 @dataclass

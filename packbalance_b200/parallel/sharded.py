@@ -178,6 +178,12 @@ def plan_grad_storage(layout: Layout, world: int, windows: int) -> GradStorage:
     return GradStorage(off, win_numel, windows if rotate else 0)
 
 
+def auto_weight_windows(n_params: int, device_bytes: int, share: float = 0.25) -> int:
+    """Weight windows for ``fsdp_weight_windows: -1``: persistent gathered bf16 weights
+    (0) while they take at most ``share`` of the device's memory, else two windows."""
+    return 0 if 2 * n_params <= share * device_bytes else 2
+
+
 @dataclass
 class WeightStorage:
     fixed_numel: int  # the non-layer units (all units without windows), then the windows

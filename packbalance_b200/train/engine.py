@@ -219,12 +219,16 @@ class TrainEngine:
         if self.fsdp and native_ok:
             # Native sharded path: per-unit shards in symmetric memory, all-gather fused
             # into the consuming GEMMs, reduce-scatter fused with the sharded AdamW.
-            from packbalance_b200.parallel.sharded import ShardedAdamW, ShardedParameters
+            from packbalance_b200.parallel.sharded import ShardedAdamW, ShardedParameters, auto_weight_windows
 
+            ww = cfg.train.fsdp_weight_windows
+            if ww < 0:
+                n_params = sum(p.numel() for p in self.model.parameters())
+                ww = auto_weight_windows(n_params, torch.cuda.get_device_properties(device).total_memory)
             # rotating gradient windows need one backward per step (the microbatch loop
             # keeps every unit's gradient until the optimizer step)
             self.sharded = ShardedParameters(self.model, grad_windows=None if cfg.train.fuse_microbatches else 0,
-                                             weight_windows=cfg.train.fsdp_weight_windows)
+                                             weight_windows=ww)
             self.model.flat = self.sharded
             self.flat = self.sharded
             self.dp = None

@@ -53,6 +53,7 @@ def test_overrides_parse_yaml_values_and_validate() -> None:
     assert cfg.train.fsdp_weight_windows == 2 and cfg.train.grad_reduce_dtype == "bf16"
     assert cfg.model.tie_embeddings is False and cfg.data.seq_len == 1024
     for bad in ("train.nope=1", "train.fsdp_weight_windows", "nope.x=1", "train.fsdp_weight_windows=1",
+                "train.fsdp_weight_windows=-2",
                 "train.grad_reduce_dtype=fp16"):
         with pytest.raises(ValueError):
             apply_overrides(PackBalanceConfig(), [bad])

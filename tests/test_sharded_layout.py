@@ -167,3 +167,15 @@ def test_8b_weight_windows_shrink_the_per_rank_footprint() -> None:
     grad_bytes = 4 * (gs.fixed_numel + gs.windows * gs.win_numel)
     per_rank = weight_bytes + grad_bytes + 18 * lay.shard_numel
     assert per_rank < 30e9, per_rank / 1e9  # 41 GB with persistent weights
+
+
+def test_auto_weight_windows_keeps_small_models_persistent() -> None:
+    """fsdp_weight_windows: -1 keeps the gathered bf16 weights while they fit in a quarter
+    of the device (1.1B and 8B on a 180 GB B200), else rotates two windows (30B)."""
+    from packbalance_b200.parallel.sharded import auto_weight_windows
+
+    b200 = 183_359 * 2**20
+    assert auto_weight_windows(1_100_000_000, b200) == 0
+    assert auto_weight_windows(8_000_000_000, b200) == 0
+    assert auto_weight_windows(30_000_000_000, b200) == 2
+    assert auto_weight_windows(8_000_000_000, 40 * 2**30) == 2
