@@ -262,7 +262,14 @@ def apply_overrides(config: PackBalanceConfig, items: list[str]) -> PackBalanceC
             raise ValueError(f"override {item!r}: expected section.key=value")
         if name not in raw[section]:
             raise ValueError(f"unknown {section} key in override: {name}")
-        raw[section][name] = yaml.safe_load(value)
+        parsed = yaml.safe_load(value)
+        old = raw[section][name]
+        if isinstance(old, float) and isinstance(parsed, (int, str)) and not isinstance(parsed, bool):
+            try:  # YAML reads "3e-4" as a string and "2" as an int
+                parsed = float(parsed)
+            except ValueError as exc:
+                raise ValueError(f"override {item!r}: {section}.{name} takes a number") from exc
+        raw[section][name] = parsed
     return config_from_dict(raw)
 
 

@@ -57,3 +57,14 @@ def test_overrides_parse_yaml_values_and_validate() -> None:
                 "train.grad_reduce_dtype=fp16"):
         with pytest.raises(ValueError):
             apply_overrides(PackBalanceConfig(), [bad])
+
+
+def test_overrides_coerce_float_fields() -> None:
+    from packbalance_b200.config import PackBalanceConfig, apply_overrides
+
+    cfg = apply_overrides(PackBalanceConfig(), ["train.lr=3e-4", "train.grad_clip=2", "train.min_lr=1.5e-5"])
+    assert cfg.train.lr == 3e-4 and isinstance(cfg.train.lr, float)
+    assert cfg.train.grad_clip == 2.0 and isinstance(cfg.train.grad_clip, float)
+    assert cfg.train.min_lr == 1.5e-5
+    with pytest.raises(ValueError):
+        apply_overrides(PackBalanceConfig(), ["train.lr=fast"])
